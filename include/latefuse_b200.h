@@ -1,0 +1,239 @@
+/*
+ * latefuse_b200.h -- C ABI of the B200-native late-fusion LoRA serving path.
+ *
+ * LateFuse serves many LoRA-adapted encoders in one mixed-tenant forward pass:
+ * every row (sequence) of a batch carries its own tenant, whose low-rank delta
+ *     y = W0 x + B_t (A_t x)
+ * is added to each targeted projection output, and whose classification head is
+ * applied to the pooled output.  The reference library does this in pure
+ * PyTorch (torch.bmm shrink/expand plus an index_select gather of per-tenant
+ * factors, and a zero-padded head bmm).  This library replaces those ops with
+ * hand-written sm_100a kernels reached through the plain C entry points below:
+ * plain pointers, sizes and a cudaStream_t passed as void*; no exceptions cross
+ * the boundary; every function returns LF_OK (0) or an LF_ERR_* code, with a
+ * message available from lf_last_error().
+ *
+ * Memory ownership: the caller owns every buffer passed in (inputs, outputs,
+ * workspaces, the adapter cache).  The LoRA, head and gather entry points
+ * allocate nothing; only the lf_arena_* functions allocate (they back the
+ * adapter cache with CUDA virtual memory so it can grow without moving).
+ *
+ * Layout conventions
+ *   dtype            LF_DTYPE_F32 / LF_DTYPE_BF16 / LF_DTYPE_F16 for every
+ *                    floating-point buffer of one call.
+ *   tokens           a batch is n_tokens rows; row t of x starts at x + t*ldx
+ *                    (elements).  A padded (B, S) batch is n_tokens = B*S.
+ *   segments         seg_start/seg_len/seg_slot (device int32 arrays, n_segs
+ *                    entries) name runs of consecutive tokens that share one
+ *                    adapter slot.  Segments are sorted by start and do not
+ *                    overlap; tokens covered by no segment get no delta.  For a
+ *                    padded (B, S) batch, segment b is {b*S, S, slot of row b}.
+ *   adapter cache    for slot s and op-module m the shrink factor A is the
+ *                    (hidden x rank) row-major matrix at
+ *                        cache_a + s*a_slot_stride + modules[m]*a_module_stride
+ *                    and the expand factor B is the (rank x hidden) row-major
+ *                    matrix at
+ *                        cache_b + s*b_slot_stride + modules[m]*b_module_stride
+ *                    (strides in elements).  These are the reference's
+ *                    LoraWeight.wa[m][layer] / wb[m][layer] layouts
+ *                    (src/latefuse/weights/store.py:22-39), so a per-tenant
+ *                    adapter is addressed in place, never gathered.
+ *   status           optional device int32; kernels OR LF_STATUS_* bits into
+ *                    it instead of faulting on a bad slot id, a bad segment or
+ *                    a wait that timed out.
+ */
+#ifndef LATEFUSE_B200_H
+#define LATEFUSE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* return codes */
+#define LF_OK 0
+#define LF_ERR_INVALID 1     /* an argument is out of range or inconsistent */
+#define LF_ERR_UNSUPPORTED 2 /* valid, but not a configuration this build handles */
+#define LF_ERR_CUDA 3        /* a CUDA runtime or driver call failed */
+#define LF_ERR_WORKSPACE 4   /* the workspace passed is smaller than required */
+#define LF_ERR_DRIVER 5      /* a driver entry point could not be resolved */
+
+/* dtypes */
+#define LF_DTYPE_F32 0
+#define LF_DTYPE_BF16 1
+#define LF_DTYPE_F16 2
+
+/* device status bits (written by kernels into *status) */
+#define LF_STATUS_BAD_SLOT 1    /* a segment named a slot outside [0, n_slots) */
+#define LF_STATUS_BAD_SEGMENT 2 /* a segment lies outside [0, n_tokens) or has len < 0 */
+#define LF_STATUS_TIMEOUT 4     /* an on-chip wait exceeded its time limit; output invalid */
+#define LF_STATUS_BAD_HEAD 8    /* a head row range lies outside [0, head_rows) */
+
+/* pooling modes of lf_head_forward (src/latefuse/ops/pooling.py:23) */
+#define LF_POOL_CLS 0    /* hidden[b, 0, :] */
+#define LF_POOL_MEAN 1   /* mask-weighted mean over the sequence, count clamped at 1e-9 */
+#define LF_POOL_NONE 2   /* hidden is already pooled: (B, H) */
+
+/* options for lf_set_option */
+#define LF_OPT_FORCE_SIMT 1     /* 1: run the CUDA-core LoRA kernels even where the
+                                   tcgen05 kernels apply (cross-checking) */
+#define LF_OPT_SHRINK_CLUSTER 2 /* 0 = automatic, else the shrink's split-K cluster size */
+#define LF_OPT_REQUIRE_TC 3     /* 1: fail with LF_ERR_UNSUPPORTED instead of running the
+                                   CUDA-core kernels where the tcgen05 kernels do not apply */
+
+/* ------------------------------------------------------------------------ */
+/* library                                                                   */
+/* ------------------------------------------------------------------------ */
+
+/* Version string of this build. */
+const char* lf_version(void);
+
+/* Message describing the last failing call on this host thread ("" if none). */
+const char* lf_last_error(void);
+
+/* 1 if `device` is an sm_100 GPU this build has kernels for, else 0. */
+int lf_device_supported(int device);
+
+/* Set a process-wide option (LF_OPT_*).  Returns LF_ERR_INVALID for an unknown key. */
+int lf_set_option(int key, int value);
+
+/* Number of kernels this library has launched in this process. */
+uint64_t lf_launch_count(void);
+
+/* ------------------------------------------------------------------------ */
+/* LoRA delta (replaces LoraOps.shrink / expand / output,                   */
+/* src/latefuse/ops/lora.py:29-80, the hook body                            */
+/* src/latefuse/model/hf_wrapper.py:212-217 and the "bert" engine block     */
+/* src/latefuse/model/encoder.py:70-80)                                     */
+/* ------------------------------------------------------------------------ */
+
+/* Shrink: u[m][t][:] = x[t] . A(slot(t), m) for every token t of a segment
+ * (0 for tokens in no segment), rounded to dtype.  u is a dense
+ * (n_modules, n_tokens, rank) device buffer.  Replaces LoraOps.shrink
+ * (src/latefuse/ops/lora.py:29-57, torch.bmm(x, a_weights, out=_out_A)) and the
+ * per-layer torch.cat / index_select gather of A that feeds it
+ * (src/latefuse/weights/batch.py:186-220): A is read in place from the cache.
+ * n_modules <= 4; `modules` is a host array of n_modules cache module indices. */
+int lf_lora_shrink(void* stream, int dtype,
+                   const void* x, int64_t ldx,
+                   int64_t n_tokens, int hidden, int rank,
+                   const void* cache_a, int64_t a_slot_stride, int64_t a_module_stride,
+                   int n_slots, int n_modules, const int32_t* modules,
+                   const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot,
+                   int n_segs,
+                   void* u, int32_t* status);
+
+/* Expand: for every token t and op-module m,
+ *     delta = round(u[m][t] . B(slot(t), m))
+ *     y[t, y_col_offsets[m] + n] = accumulate ? round(y + delta) : delta     (n < hidden)
+ * where round() rounds to dtype (the reference materialises the delta in the
+ * model dtype before adding it).  Tokens in no segment get delta = 0.  Replaces
+ * LoraOps.expand (src/latefuse/ops/lora.py:59-75, torch.bmm(out_A, b_weights,
+ * out=_out_B)) plus `output + owner.lora_ops.output`
+ * (src/latefuse/model/hf_wrapper.py:217; src/latefuse/model/encoder.py:80).
+ * `modules` and `y_col_offsets` are host arrays of n_modules entries. */
+int lf_lora_expand(void* stream, int dtype,
+                   const void* u,
+                   void* y, int64_t ldy,
+                   int64_t n_tokens, int hidden, int rank,
+                   const void* cache_b, int64_t b_slot_stride, int64_t b_module_stride,
+                   int n_slots, int n_modules, const int32_t* modules,
+                   const int64_t* y_col_offsets,
+                   const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot,
+                   int n_segs, int accumulate, int32_t* status);
+
+/* Device workspace bytes lf_lora_apply needs for these sizes. */
+size_t lf_lora_workspace_bytes(int dtype, int64_t n_tokens, int rank, int n_modules);
+
+/* Fused late-fusion delta: shrink into `workspace`, then expand-accumulate into
+ * y, i.e. y[t, off_m + :] += B(slot(t), m)^T (A(slot(t), m)^T x[t]) for up to 4
+ * modules that share the input x (query/key/value of one layer share one read of
+ * x).  One call replaces, per layer, the reference's cat -> bmm -> bmm -> add
+ * sequence of every hook (src/latefuse/model/hf_wrapper.py:213-217). */
+int lf_lora_apply(void* stream, int dtype,
+                  const void* x, int64_t ldx,
+                  void* y, int64_t ldy,
+                  int64_t n_tokens, int hidden, int rank,
+                  const void* cache_a, int64_t a_slot_stride, int64_t a_module_stride,
+                  const void* cache_b, int64_t b_slot_stride, int64_t b_module_stride,
+                  int n_slots, int n_modules, const int32_t* modules,
+                  const int64_t* y_col_offsets,
+                  const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot,
+                  int n_segs,
+                  void* workspace, size_t workspace_bytes, int32_t* status);
+
+/* ------------------------------------------------------------------------ */
+/* Adapter cache                                                            */
+/* ------------------------------------------------------------------------ */
+
+/* Gather: dst[i][:] = src + slots[i]*slot_stride + offset, n_elems elements of
+ * elem_bytes each, for i < n.  Bit-exact materialisation of per-row adapter
+ * factors, the equivalent of IndexSelectBatchAssembler.assemble_lora's
+ * wa[m].index_select(0, idx) (src/latefuse/weights/batch.py:186-203); the
+ * serving path never needs it (kernels read the cache by slot). */
+int lf_cache_gather(void* stream, const void* src, int64_t slot_stride, int64_t offset,
+                    int64_t n_elems, int elem_bytes, int n_slots,
+                    const int32_t* slots, int n, void* dst, int32_t* status);
+
+/* Copy nbytes from src (host or device) into slot `slot` of a cache whose slots
+ * are slot_stride_bytes apart, at byte offset `offset` within the slot, on
+ * `stream`.  Registration of a pre-packed adapter
+ * (src/latefuse/weights/store.py:158-167 AdapterStore.insert). */
+int lf_cache_write_slot(void* stream, void* cache_base, int64_t slot_stride_bytes, int slot,
+                        int n_slots, size_t offset, const void* src, size_t nbytes);
+
+/* Growable device arena backing the slot cache: reserves reserve_bytes of
+ * device virtual address space and maps physical memory on demand, so the cache
+ * grows without moving (views handed out earlier stay valid).  The reference
+ * instead repacks the whole store after every registration
+ * (src/latefuse/tasks/base.py:181-190, src/latefuse/weights/batch.py:163-170). */
+int lf_arena_create(int device, size_t reserve_bytes, void** handle);
+int lf_arena_grow(void* handle, size_t mapped_bytes);   /* ensure >= mapped_bytes are mapped */
+void* lf_arena_base(void* handle);
+size_t lf_arena_mapped_bytes(void* handle);
+int lf_arena_destroy(void* handle);
+
+/* ------------------------------------------------------------------------ */
+/* Pooling, normalisation and per-tenant heads                              */
+/* ------------------------------------------------------------------------ */
+
+/* One kernel per batch: pooling (pool_tokens, src/latefuse/ops/pooling.py:36-73)
+ * -> optional L2 normalisation (F.normalize(p=2, eps=1e-12),
+ * src/latefuse/tasks/embedding.py:69-70) -> optional per-tenant head, a
+ * gather-GEMV over a packed head cache: for row b the head is rows
+ * [head_off[b], head_off[b] + head_n[b]) of coef (head_rows x hidden) and bias,
+ *     logits[b][j] = round(round(pooled[b] . coef[off+j]) + bias[off+j])   j < n
+ *     logits[b][j] = 0                                                      n <= j < n_max
+ * which is the zero-padded bmm + add of LRHeadOps.predict_proba
+ * (src/latefuse/ops/head.py:50-51) after HeadStore.assemble
+ * (src/latefuse/tasks/heads.py:125-158) without materialising the padding; and
+ * probs[b][:n] = softmax over the row's own n logits (max-shifted), or the
+ * sigmoid when n == 1 (src/latefuse/tasks/classification.py:72-84,109-119),
+ * 0 in padded lanes.
+ *
+ *   hidden     (B, S, H) with row strides (ld_batch, ld_seq) for CLS/MEAN, or
+ *              (B, H) with row stride ld_batch for LF_POOL_NONE
+ *   mask       (B, S) int64 attention mask (1 = real token); may be NULL for
+ *              CLS/NONE and for MEAN when there is no padding
+ *   pooled_out (B, H) dtype or NULL: the pooled rows, before normalisation
+ *   normed_out (B, H) dtype or NULL: the L2-normalised pooled rows
+ *   coef/bias  NULL to skip the head; else head_off/head_n device int32 (B,)
+ *   logits_out (B, n_max) dtype, probs_out (B, n_max) float32 (either may be NULL)
+ */
+int lf_head_forward(void* stream, int dtype,
+                    const void* hidden, int64_t ld_batch, int64_t ld_seq,
+                    const int64_t* mask, int batch, int seq, int hidden_size,
+                    int pooling,
+                    void* pooled_out, void* normed_out,
+                    const void* coef, const void* bias, int64_t head_rows,
+                    const int32_t* head_off, const int32_t* head_n, int n_max,
+                    void* logits_out, float* probs_out,
+                    int32_t* status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LATEFUSE_B200_H */

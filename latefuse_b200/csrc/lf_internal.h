@@ -1,0 +1,103 @@
+// Internal declarations shared by the LateFuse-B200 translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/latefuse_b200.h"
+
+namespace lf {
+
+constexpr int kMaxModules = 4;
+
+// Kernel parameter blocks (passed as __grid_constant__, so the TMA descriptors
+// live in parameter space as cp.async.bulk.tensor requires).
+struct alignas(64) ShrinkTcParams {
+  CUtensorMap x_map;                 // 2D {hidden, n_tokens}, box {64, 128}, SW128
+  CUtensorMap a_map[kMaxModules];    // 3D {rank, hidden, n_slots}, box {rank, 64, 1}
+  int64_t n_tokens;
+  int32_t hidden;
+  int32_t kchunk;                    // hidden columns handled by one CTA of the cluster
+  int32_t n_modules;
+  int32_t n_slots;
+  uint32_t tmem_cols;
+  const int32_t* seg_start;
+  const int32_t* seg_len;
+  const int32_t* seg_slot;
+  int32_t n_segs;
+  void* u;                           // (n_modules, n_tokens, rank)
+  int32_t* status;
+};
+
+struct alignas(64) ExpandTcParams {
+  CUtensorMap y_map;                 // 2D {y_cols, n_tokens}, box {64, 128}, SW128
+  CUtensorMap b_map[kMaxModules];    // 3D {hidden, rank, n_slots}, box {64, rank, 1}, SW128
+  int64_t n_tokens;
+  int64_t y_col_off[kMaxModules];
+  int32_t hidden;
+  int32_t n_modules;
+  int32_t n_slots;
+  int32_t accumulate;
+  const int32_t* seg_start;
+  const int32_t* seg_len;
+  const int32_t* seg_slot;
+  int32_t n_segs;
+  const void* u;                     // (n_modules, n_tokens, rank)
+  int32_t* status;
+};
+
+struct SimtParams {
+  const void* x;
+  int64_t ldx;
+  void* y;
+  int64_t ldy;
+  int64_t n_tokens;
+  int32_t hidden;
+  int32_t rank;
+  const void* cache_a[kMaxModules];  // per-module base for slot 0
+  const void* cache_b[kMaxModules];
+  int64_t a_slot_stride;
+  int64_t b_slot_stride;
+  int64_t y_col_off[kMaxModules];
+  int32_t n_modules;
+  int32_t n_slots;
+  const int32_t* seg_start;
+  const int32_t* seg_len;
+  const int32_t* seg_slot;
+  int32_t n_segs;
+  void* u;
+  int32_t accumulate;
+  int32_t* status;
+};
+
+// error reporting (thread-local message, see lf_last_error)
+int set_error(int code, const char* fmt, ...);
+int cuda_error(cudaError_t e, const char* what);
+void count_launch();
+
+// tcgen05 path
+int run_shrink_tc(int dtype, const ShrinkTcParams& p, int rank, int csize, cudaStream_t s);
+int run_expand_tc(int dtype, const ExpandTcParams& p, int rank, int nt, cudaStream_t s);
+size_t shrink_tc_smem(int dtype, int rank, int kchunk, int n_mod);
+uint32_t shrink_tc_tmem_cols(int rank, int n_mod);
+CUtensorMapSwizzle a_tma_swizzle(int rank);
+
+// CUDA-core path
+int run_shrink_simt(int dtype, const SimtParams& p, cudaStream_t s);
+int run_expand_simt(int dtype, const SimtParams& p, cudaStream_t s);
+
+// driver entry points
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+PFN_encodeTiled get_encode_tiled();
+void* get_driver_fn(const char* name);
+
+// options
+int option_force_simt();
+int option_shrink_cluster();
+
+}  // namespace lf

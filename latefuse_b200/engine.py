@@ -1,0 +1,468 @@
+"""Encoders that apply per-row LoRA deltas with the native kernels.
+
+Two engines, as in the reference:
+
+* :class:`HFEncoderWithLora` (``engine="hf"``, the default) runs a stock
+  HuggingFace ``AutoModel`` and adds each row's delta inside forward hooks on the
+  targeted ``nn.Linear`` modules, in place on the projection output (the
+  reference's hook does ``cat -> bmm -> bmm -> output + delta``,
+  ``src/latefuse/model/hf_wrapper.py:169-219``).
+* :class:`EncoderWithLora` (``engine="bert"``) is a BERT/RoBERTa/XLM-R encoder
+  written for this path: one fused QKV GEMM per layer whose LoRA deltas for
+  query/key/value come from one shrink pass over the shared input, then the
+  expand adds into the fused output; the attention-output projection gets its
+  own delta; attention runs through ``scaled_dot_product_attention``.  The
+  reference's version (``src/latefuse/model/encoder.py``) skips ``dense``
+  targets; this one applies them.
+
+Both accept either a :class:`~latefuse_b200.batch.BatchLora` (slot ids; the
+serving path) or the reference's ``list[LayerwiseBatchedWeights]``.
+"""
+
+from __future__ import annotations
+
+import weakref
+
+import torch
+import torch.nn.functional as F
+from torch import Tensor, nn
+from torch.utils.hooks import RemovableHandle
+
+from latefuse_b200.batch import BatchedLRWeights, BatchLora, LayerwiseBatchedWeights
+from latefuse_b200.config import LoraServingConfig
+from latefuse_b200.head import LRHeadOps, pool_tokens, validate_pooling
+from latefuse_b200.lora import FactorCache, SegmentTable, lora_apply, per_row_cache, workspace_bytes
+
+# Per-layer module paths (relative to "encoder.layer.{i}.") for each logical target.
+# "dense" is the attention-output projection.
+_TARGET_SUFFIXES: dict[str, dict[str, str]] = {
+    "default": {
+        "query": "attention.self.query",
+        "key": "attention.self.key",
+        "value": "attention.self.value",
+        "dense": "attention.output.dense",
+    },
+    "deberta-v2": {
+        "query": "attention.self.query_proj",
+        "key": "attention.self.key_proj",
+        "value": "attention.self.value_proj",
+        "dense": "attention.output.dense",
+    },
+}
+
+
+def _detach_hooks(handles: tuple[RemovableHandle, ...]) -> None:
+    for handle in handles:
+        handle.remove()
+
+
+class _DeltaRunner:
+    """Per-engine state for applying deltas: workspace, status word, and the
+    conversion of the reference's layer-wise weight lists into factor caches."""
+
+    def __init__(self, config: LoraServingConfig):
+        self.config = config
+        self._ws: Tensor | None = None
+        self.status: Tensor | None = None
+
+    def workspace(self, n_tokens: int, n_modules: int, device, dtype) -> Tensor:
+        need = workspace_bytes(dtype, n_tokens, self.config.lora_rank, n_modules)
+        if self._ws is None or self._ws.numel() < need or self._ws.device != device:
+            self._ws = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
+        if self.status is None or self.status.device != device:
+            self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        return self._ws
+
+    @staticmethod
+    def layerwise_cache(layer_w: LayerwiseBatchedWeights, module: str) -> FactorCache:
+        a = torch.cat(layer_w.a[module], dim=0)
+        b = torch.cat(layer_w.b[module], dim=0)
+        return per_row_cache(a, b)
+
+
+def _identity_segments(B: int, S: int, device) -> SegmentTable:
+    return SegmentTable.for_padded(list(range(B)), S, device)
+
+
+class HFEncoderWithLora(nn.Module):
+    """Stock HF encoder with per-row LoRA deltas added in forward hooks (native kernels).
+
+    Same constructor, ``encode_pooled`` / ``forward`` contract, hook guards and
+    lifetime rules as the reference (``src/latefuse/model/hf_wrapper.py:56-370``).
+    """
+
+    def __init__(self, base: nn.Module, serving_config: LoraServingConfig):
+        super().__init__()
+        self.base = base
+        self.config = serving_config
+        self._runner = _DeltaRunner(serving_config)
+        self._batch: BatchLora | list[LayerwiseBatchedWeights] | None = None
+        self._segs: SegmentTable | None = None
+        self._expected_shape: tuple[int, int, int] | None = None
+        self._fired: set[tuple[int, str]] = set()
+        self.shared_projection_skips = 0
+        self._num_hooks = 0
+        self._hook_handles: list[RemovableHandle] = []
+
+        duplicates = sorted({t for t in serving_config.target_modules if serving_config.target_modules.count(t) > 1})
+        if duplicates:
+            raise ValueError(
+                f"target_modules contains duplicate entries {duplicates}: {serving_config.target_modules}. "
+                "Each projection may be hooked at most once."
+            )
+        suffixes = _TARGET_SUFFIXES.get(base.config.model_type, _TARGET_SUFFIXES["default"])
+        modules = dict(base.named_modules())
+        try:
+            for logical in serving_config.target_modules:
+                if logical not in suffixes:
+                    raise ValueError(
+                        f"target module '{logical}' has no mapping for model_type '{base.config.model_type}' "
+                        f"(known: {sorted(suffixes)})"
+                    )
+                for layer_idx in range(serving_config.num_layers):
+                    name = f"encoder.layer.{layer_idx}.{suffixes[logical]}"
+                    if name not in modules:
+                        raise ValueError(
+                            f"module '{name}' not found in {base.config.model_type} model — cannot attach LoRA hook"
+                        )
+                    self._hook_handles.append(modules[name].register_forward_hook(self._make_hook(layer_idx, logical)))
+                    self._num_hooks += 1
+        except BaseException:
+            _detach_hooks(tuple(self._hook_handles))
+            self._hook_handles.clear()
+            raise
+        self._finalizer = weakref.finalize(self, _detach_hooks, tuple(self._hook_handles))
+        self._finalizer.atexit = False
+
+    def _make_hook(self, layer_idx: int, logical: str):
+        key = (layer_idx, logical)
+        wref = weakref.ref(self)  # no reference cycle through base's hook dicts
+
+        def hook(module: nn.Module, inputs: tuple, output: Tensor):
+            owner = wref()
+            if owner is None or owner._batch is None:
+                return None
+            x = inputs[0]
+            if key in owner._fired or x.shape != owner._expected_shape:
+                owner.shared_projection_skips += 1
+                return None
+            owner._fired.add(key)
+            owner._apply(layer_idx, logical, x, output)
+            return output
+
+        return hook
+
+    def _apply(self, layer_idx: int, logical: str, x: Tensor, out: Tensor) -> None:
+        batch = self._batch
+        T = x.shape[0] * x.shape[1]
+        ws = self._runner.workspace(T, 1, x.device, x.dtype)
+        if isinstance(batch, BatchLora):
+            store = batch.store
+            cache = store.factor_cache(layer_idx)
+            mod = store.module_index(logical)
+            lora_apply(x, out, cache, batch.segments, [mod], [0], ws, self._runner.status)
+        else:
+            cache = _DeltaRunner.layerwise_cache(batch[layer_idx], logical)
+            lora_apply(x, out, cache, self._segs, [0], [0], ws, self._runner.status)
+
+    @classmethod
+    def from_pretrained_serving(cls, serving_config: LoraServingConfig, attn_implementation: str | None = None):
+        """Load the stock HF base model and attach LoRA hooks."""
+        from transformers import AutoModel
+
+        kwargs: dict = {"dtype": serving_config.dtype}
+        if attn_implementation is not None:
+            kwargs["attn_implementation"] = attn_implementation
+        base = AutoModel.from_pretrained(serving_config.model_name, **kwargs)
+        base.eval()
+        return cls(base, serving_config).to(serving_config.device)
+
+    def close(self) -> None:
+        """Detach the LoRA hooks and drop the base model. Idempotent."""
+        self._finalizer()
+        self._hook_handles.clear()
+        self.base = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, exc_type, exc, tb) -> None:
+        self.close()
+
+    def encode_pooled(self, input_ids: Tensor, attention_mask: Tensor | None, lora_weights,
+                      token_type_ids: Tensor | None = None, apply_lora: bool = True,
+                      pooling: str = "auto") -> Tensor:
+        """Base forward with LoRA deltas, up to the ``(B, H)`` pooled output.
+
+        Raises ``RuntimeError`` if the adapter was not applied at every target
+        projection, as the reference does.
+        """
+        validate_pooling(pooling)
+        if self.base is None:
+            raise RuntimeError(
+                "this HFEncoderWithLora has been closed; its base model was released and it cannot run a "
+                "forward pass. Build a new one with from_pretrained_serving()."
+            )
+        B, S = input_ids.shape
+        cfg = self.config
+        self._batch = lora_weights if apply_lora else None
+        if apply_lora and not isinstance(lora_weights, BatchLora):
+            self._segs = _identity_segments(B, S, input_ids.device)
+        self._expected_shape = (B, S, cfg.hidden_size)
+        self._fired = set()
+        skips_before = self.shared_projection_skips
+        try:
+            kwargs = {}
+            if token_type_ids is not None:
+                kwargs["token_type_ids"] = token_type_ids
+            out = self.base(input_ids=input_ids, attention_mask=attention_mask, **kwargs)
+            fired = len(self._fired)
+        finally:
+            self._batch = None
+            self._segs = None
+            self._expected_shape = None
+            self._fired = set()
+        if apply_lora and fired != self._num_hooks:
+            raise RuntimeError(
+                f"LoRA hooks fired {fired}/{self._num_hooks} times on {self.base.config.model_type}: every target "
+                f"projection was expected to be called on a tensor of shape {(B, S, cfg.hidden_size)}, and "
+                f"{self.shared_projection_skips - skips_before} call(s) took the skip path instead. The base "
+                "forward ran without the adapter delta, so anything measured from it would be wrong."
+            )
+        if pooling == "auto":
+            pooled = getattr(out, "pooler_output", None)
+            if pooled is None:
+                pooled = out.last_hidden_state[:, 0]
+            return pooled
+        return pool_tokens(out.last_hidden_state, attention_mask, pooling)
+
+    def forward(self, input_ids: Tensor, attention_mask: Tensor | None, lora_weights,
+                lr_weights: BatchedLRWeights, output_lr: Tensor, token_type_ids: Tensor | None = None,
+                apply_lora: bool = True, pooling: str = "auto") -> Tensor:
+        """Encoder + batched per-tenant LR heads; fills ``output_lr (B, 1, max_labels)``."""
+        pooled = self.encode_pooled(input_ids, attention_mask, lora_weights, token_type_ids, apply_lora, pooling)
+        LRHeadOps.predict_proba(pooled.unsqueeze(1), lr_weights.coef, lr_weights.intercept, output_lr)
+        return output_lr
+
+
+# ---------------------------------------------------------------------------
+# native encoder
+# ---------------------------------------------------------------------------
+_OFFSET_POSITION_TYPES = {"roberta", "xlm-roberta", "xlm-roberta-xl", "camembert", "mpnet"}
+_QKV = ("query", "key", "value")
+
+
+class _Layer(nn.Module):
+    def __init__(self, H: int, I: int, eps: float):
+        super().__init__()
+        self.wqkv = nn.Parameter(torch.empty(3 * H, H))
+        self.bqkv = nn.Parameter(torch.empty(3 * H))
+        self.wo = nn.Parameter(torch.empty(H, H))
+        self.bo = nn.Parameter(torch.empty(H))
+        self.ln1 = nn.LayerNorm(H, eps=eps)
+        self.wi = nn.Parameter(torch.empty(I, H))
+        self.bi = nn.Parameter(torch.empty(I))
+        self.wo2 = nn.Parameter(torch.empty(H, I))
+        self.bo2 = nn.Parameter(torch.empty(H))
+        self.ln2 = nn.LayerNorm(H, eps=eps)
+
+
+class EncoderWithLora(nn.Module):
+    """BERT-family encoder (BERT, RoBERTa, XLM-R, bge-m3 ...) with per-row LoRA deltas.
+
+    Same ``encode_pooled`` / ``forward`` contract as the reference's
+    ``EncoderWithLora`` (``src/latefuse/model/encoder.py:145-321``) and loads the
+    same checkpoints (strictly: a checkpoint without a pooler is rejected, use the
+    ``"hf"`` engine for those).
+    """
+
+    def __init__(self, hf_config, serving_config: LoraServingConfig):
+        super().__init__()
+        from transformers.activations import ACT2FN
+
+        H, I = serving_config.hidden_size, serving_config.intermediate_size
+        self.config = serving_config
+        self.hf_config = hf_config
+        self.num_heads = serving_config.num_heads
+        self.head_dim = serving_config.head_dim
+        self.eps = serving_config.layer_norm_eps
+        self.pad_idx = hf_config.pad_token_id if hf_config.pad_token_id is not None else 0
+        self.offset_positions = hf_config.model_type in _OFFSET_POSITION_TYPES
+        self.word_embeddings = nn.Embedding(hf_config.vocab_size, H, padding_idx=hf_config.pad_token_id)
+        self.position_embeddings = nn.Embedding(hf_config.max_position_embeddings, H)
+        self.token_type_embeddings = nn.Embedding(max(1, hf_config.type_vocab_size), H)
+        self.emb_ln = nn.LayerNorm(H, eps=self.eps)
+        self.layers = nn.ModuleList([_Layer(H, I, self.eps) for _ in range(serving_config.num_layers)])
+        self.pooler_w = nn.Parameter(torch.empty(H, H))
+        self.pooler_b = nn.Parameter(torch.empty(H))
+        self.act = ACT2FN[serving_config.hidden_act]
+        self._runner = _DeltaRunner(serving_config)
+        targets = serving_config.target_modules
+        self._qkv_targets = [(m, _QKV.index(m)) for m in targets if m in _QKV]
+        self._dense_target = "dense" in targets
+        unknown = sorted(set(targets) - set(_QKV) - {"dense"})
+        if unknown:
+            raise ValueError(f"target modules {unknown} have no mapping in the native encoder "
+                             f"(known: {sorted(_QKV) + ['dense']})")
+
+    # -- construction ----------------------------------------------------------
+    @torch.no_grad()
+    def load_hf_state_dict(self, sd: dict[str, Tensor]) -> None:
+        """Copy weights from a HuggingFace BERT-family state dict (strict)."""
+        sd = {k.removeprefix("bert.").removeprefix("roberta."): v for k, v in sd.items()}
+        used: set[str] = set()
+
+        def take(key: str) -> Tensor:
+            if key not in sd:
+                hint = " — the checkpoint ships no pooler; use the HF hook engine ('hf')" if key.startswith("pooler.") else ""
+                raise RuntimeError(f"{self.config.model_name} does not match the BERT-family layout: missing {key}{hint}")
+            used.add(key)
+            return sd[key]
+
+        self.word_embeddings.weight.copy_(take("embeddings.word_embeddings.weight"))
+        self.position_embeddings.weight.copy_(take("embeddings.position_embeddings.weight"))
+        self.token_type_embeddings.weight.copy_(take("embeddings.token_type_embeddings.weight"))
+        self.emb_ln.weight.copy_(take("embeddings.LayerNorm.weight"))
+        self.emb_ln.bias.copy_(take("embeddings.LayerNorm.bias"))
+        for i, layer in enumerate(self.layers):
+            p = f"encoder.layer.{i}."
+            layer.wqkv.copy_(torch.cat([take(p + f"attention.self.{m}.weight") for m in _QKV], 0))
+            layer.bqkv.copy_(torch.cat([take(p + f"attention.self.{m}.bias") for m in _QKV], 0))
+            layer.wo.copy_(take(p + "attention.output.dense.weight"))
+            layer.bo.copy_(take(p + "attention.output.dense.bias"))
+            layer.ln1.weight.copy_(take(p + "attention.output.LayerNorm.weight"))
+            layer.ln1.bias.copy_(take(p + "attention.output.LayerNorm.bias"))
+            layer.wi.copy_(take(p + "intermediate.dense.weight"))
+            layer.bi.copy_(take(p + "intermediate.dense.bias"))
+            layer.wo2.copy_(take(p + "output.dense.weight"))
+            layer.bo2.copy_(take(p + "output.dense.bias"))
+            layer.ln2.weight.copy_(take(p + "output.LayerNorm.weight"))
+            layer.ln2.bias.copy_(take(p + "output.LayerNorm.bias"))
+        self.pooler_w.copy_(take("pooler.dense.weight"))
+        self.pooler_b.copy_(take("pooler.dense.bias"))
+        ignorable = {"embeddings.position_ids", "embeddings.token_type_ids"}
+        unexpected = sorted(k for k in sd if k not in used and k not in ignorable)
+        if unexpected:
+            raise RuntimeError(f"{self.config.model_name} does not match the BERT-family layout: unexpected={unexpected}")
+
+    @classmethod
+    def from_hf_model(cls, base: nn.Module, serving_config: LoraServingConfig) -> EncoderWithLora:
+        model = cls(base.config, serving_config)
+        model.load_hf_state_dict(base.state_dict())
+        return model.to(device=serving_config.device, dtype=serving_config.dtype).eval()
+
+    @classmethod
+    def from_pretrained_serving(cls, serving_config: LoraServingConfig) -> EncoderWithLora:
+        """Create the model and load base weights from HuggingFace."""
+        from transformers import AutoModel
+
+        base = AutoModel.from_pretrained(serving_config.model_name, dtype=serving_config.dtype)
+        return cls.from_hf_model(base, serving_config)
+
+    @classmethod
+    @torch.no_grad()
+    def random_init(cls, hf_config, serving_config: LoraServingConfig, seed: int = 0) -> EncoderWithLora:
+        """A randomly initialised model (N(0, initializer_range) weights, zero biases, unit
+        LayerNorms), drawn directly on the serving device: synthetic serving workloads."""
+        model = cls(hf_config, serving_config).to(device=serving_config.device, dtype=serving_config.dtype)
+        gen = torch.Generator(device=serving_config.device).manual_seed(seed)
+        std = getattr(hf_config, "initializer_range", 0.02)
+        ones = ("ln1.weight", "ln2.weight", "emb_ln.weight")
+        zeros = ("ln1.bias", "ln2.bias", "emb_ln.bias", "bqkv", "bo", "bi", "bo2", "pooler_b")
+        for name, p in model.named_parameters():
+            if name.endswith(ones):
+                p.fill_(1.0)
+            elif name.split(".")[-1] in zeros or name.endswith(zeros[:3]):
+                p.zero_()
+            else:
+                p.normal_(0.0, std, generator=gen)
+        if hf_config.pad_token_id is not None:
+            model.word_embeddings.weight[hf_config.pad_token_id].zero_()
+        return model.eval()
+
+    # -- forward -------------------------------------------------------------
+    def position_ids(self, input_ids: Tensor) -> Tensor:
+        """arange for BERT; mask-offset positions for the RoBERTa family (pad -> pad_idx)."""
+        B, S = input_ids.shape
+        if not self.offset_positions:
+            return torch.arange(S, device=input_ids.device).unsqueeze(0).expand(B, -1)
+        mask = input_ids.ne(self.pad_idx).int()
+        return (torch.cumsum(mask, dim=1) * mask).long() + self.pad_idx
+
+    def _resolve(self, lora_weights, B: int, S: int, device):
+        """(per-layer cache getter, segment table) for this batch."""
+        if isinstance(lora_weights, BatchLora):
+            store = lora_weights.store
+            qkv_idx = [store.module_index(m) for m, _ in self._qkv_targets]
+            dense_idx = [store.module_index("dense")] if self._dense_target else []
+            return (lambda l, _m=None: store.factor_cache(l)), lora_weights.segments, qkv_idx, dense_idx, True
+        segs = _identity_segments(B, S, device)
+        return None, segs, None, None, False
+
+    def encode_pooled(self, input_ids: Tensor, attention_mask: Tensor | None, lora_weights,
+                      token_type_ids: Tensor | None = None, apply_lora: bool = True,
+                      pooling: str = "auto") -> Tensor:
+        """Base forward with LoRA deltas, up to the ``(B, H)`` pooled output."""
+        validate_pooling(pooling)
+        hidden = self.encode(input_ids, attention_mask, lora_weights, token_type_ids, apply_lora)
+        if pooling == "auto":
+            return torch.tanh(F.linear(hidden[:, 0], self.pooler_w, self.pooler_b))
+        return pool_tokens(hidden, attention_mask, pooling)
+
+    def encode(self, input_ids: Tensor, attention_mask: Tensor | None, lora_weights,
+               token_type_ids: Tensor | None = None, apply_lora: bool = True) -> Tensor:
+        """Final hidden states ``(B, S, H)``."""
+        B, S = input_ids.shape
+        H, nh, hd = self.config.hidden_size, self.num_heads, self.head_dim
+        dev = input_ids.device
+        T = B * S
+        if token_type_ids is None:
+            token_type_ids = torch.zeros(B, S, dtype=torch.long, device=dev)
+        x = self.word_embeddings(input_ids) + self.token_type_embeddings(token_type_ids)
+        x = x + self.position_embeddings(self.position_ids(input_ids))
+        h = F.layer_norm(x, (H,), self.emb_ln.weight, self.emb_ln.bias, self.eps).view(T, H)
+
+        attn_mask = None
+        if attention_mask is not None:
+            attn_mask = attention_mask.to(torch.bool).view(B, 1, 1, S)
+
+        do_lora = apply_lora and (self._qkv_targets or self._dense_target)
+        if do_lora:
+            getter, segs, qkv_idx, dense_idx, sloted = self._resolve(lora_weights, B, S, dev)
+            n_mod = max(1, len(self._qkv_targets))
+            ws = self._runner.workspace(T, n_mod, dev, h.dtype)
+            status = self._runner.status
+            qkv_offs = [j * H for _, j in self._qkv_targets]
+
+        for l, layer in enumerate(self.layers):
+            qkv = F.linear(h, layer.wqkv, layer.bqkv)  # (T, 3H)
+            if do_lora and self._qkv_targets:
+                if sloted:
+                    lora_apply(h, qkv, getter(l), segs, qkv_idx, qkv_offs, ws, status)
+                else:
+                    for (m, j) in self._qkv_targets:
+                        cache = _DeltaRunner.layerwise_cache(lora_weights[l], m)
+                        lora_apply(h, qkv, cache, segs, [0], [j * H], ws, status)
+            q, k, v = qkv.view(B, S, 3, nh, hd).permute(2, 0, 3, 1, 4).unbind(0)
+            ctx = F.scaled_dot_product_attention(q, k, v, attn_mask=attn_mask)
+            ctx = ctx.transpose(1, 2).reshape(T, H)
+            ao = F.linear(ctx, layer.wo, layer.bo)
+            if do_lora and self._dense_target:
+                if sloted:
+                    lora_apply(ctx, ao, getter(l), segs, dense_idx, [0], ws, status)
+                else:
+                    cache = _DeltaRunner.layerwise_cache(lora_weights[l], "dense")
+                    lora_apply(ctx, ao, cache, segs, [0], [0], ws, status)
+            h1 = F.layer_norm(ao + h, (H,), layer.ln1.weight, layer.ln1.bias, self.eps)
+            mid = self.act(F.linear(h1, layer.wi, layer.bi))
+            o = F.linear(mid, layer.wo2, layer.bo2)
+            h = F.layer_norm(o + h1, (H,), layer.ln2.weight, layer.ln2.bias, self.eps)
+        return h.view(B, S, H)
+
+    def forward(self, input_ids: Tensor, attention_mask: Tensor | None, lora_weights,
+                lr_weights: BatchedLRWeights, output_lr: Tensor, token_type_ids: Tensor | None = None,
+                apply_lora: bool = True, pooling: str = "auto") -> Tensor:
+        """Full mixed-tenant forward: encoder + batched per-tenant LR heads."""
+        pooled = self.encode_pooled(input_ids, attention_mask, lora_weights, token_type_ids, apply_lora, pooling)
+        LRHeadOps.predict_proba(pooled.unsqueeze(1), lr_weights.coef, lr_weights.intercept, output_lr)
+        return output_lr

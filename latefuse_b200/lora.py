@@ -1,0 +1,237 @@
+"""The late-fusion LoRA delta on the GPU, and the reference's ``LoraOps`` API over it.
+
+For a mixed-tenant batch every token row ``t`` belongs to one adapter slot, and
+each targeted projection output gets
+
+    y[t] += B_slot(t) (A_slot(t) x[t])
+
+The reference computes this with a per-layer ``torch.cat``/``index_select``
+gather of the per-row factors followed by two ``torch.bmm`` calls and an add
+(``src/latefuse/ops/lora.py:57,75``, ``src/latefuse/model/hf_wrapper.py:213-217``).
+Here one :func:`lora_apply` call runs the sm_100a shrink and expand kernels,
+which read each tenant's factors in place from the slot cache.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+from torch import Tensor
+
+from latefuse_b200 import _native as nat
+from latefuse_b200.config import LoraServingConfig
+
+
+# ---------------------------------------------------------------------------
+# segment tables
+# ---------------------------------------------------------------------------
+class SegmentTable:
+    """Runs of consecutive tokens that share one adapter slot, as device int32 arrays.
+
+    For a padded ``(B, S)`` batch row ``b`` is the segment ``{b*S, len_b, slot_b}``
+    with ``len_b = S`` (every position gets its delta, as in the reference) or the
+    row's real length when padding is skipped (right-padded rows only: real
+    tokens first).  Skipping padding changes no real token's output, because
+    padded keys are masked out of attention and every other op is per token.
+    """
+
+    def __init__(self, starts, lengths, slots, n_tokens: int, device: torch.device):
+        starts, lengths, slots = list(starts), list(lengths), list(slots)
+        if not (len(starts) == len(lengths) == len(slots)):
+            raise ValueError("starts, lengths and slots must have equal length")
+        self.n_segs = len(starts)
+        self.n_tokens = int(n_tokens)
+        self.device = torch.device(device)
+        self.host = torch.tensor([starts, lengths, slots], dtype=torch.int32).reshape(3, -1)
+        if self.device.type == "cuda":
+            self.table = self.host.pin_memory().to(self.device, non_blocking=True)
+        else:
+            self.table = self.host.clone()
+        self.slots = slots
+
+    @classmethod
+    def for_padded(cls, slots, seq_len: int, device, lengths=None) -> SegmentTable:
+        B = len(slots)
+        lens = [seq_len] * B if lengths is None else [int(min(seq_len, max(0, n))) for n in lengths]
+        return cls([b * seq_len for b in range(B)], lens, slots, B * seq_len, device)
+
+    def ptrs(self) -> tuple[int, int, int]:
+        base = self.table.data_ptr()
+        step = self.table.stride(0) * 4
+        return base, base + step, base + 2 * step
+
+
+# ---------------------------------------------------------------------------
+# cache views
+# ---------------------------------------------------------------------------
+@dataclass
+class FactorCache:
+    """Where the shrink (A, hidden x rank) and expand (B, rank x hidden) factors of
+    every slot live, for one layer.  Strides are in elements.
+
+    ``a``/``b`` are tensors whose ``data_ptr()`` is the address of slot 0, module 0.
+    """
+
+    a: Tensor
+    b: Tensor
+    a_offset: int          # element offset of (slot 0, module 0) from a.data_ptr()
+    b_offset: int
+    a_slot_stride: int
+    b_slot_stride: int
+    a_module_stride: int
+    b_module_stride: int
+    n_slots: int
+    hidden: int
+    rank: int
+
+    @property
+    def a_ptr(self) -> int:
+        return self.a.data_ptr() + self.a_offset * self.a.element_size()
+
+    @property
+    def b_ptr(self) -> int:
+        return self.b.data_ptr() + self.b_offset * self.b.element_size()
+
+
+def workspace_bytes(dtype: torch.dtype, n_tokens: int, rank: int, n_modules: int) -> int:
+    return int(nat.lib().lf_lora_workspace_bytes(nat.dtype_code(dtype), n_tokens, rank, n_modules))
+
+
+def _rows(t: Tensor) -> tuple[Tensor, int]:
+    """``t`` as a 2-D tensor of rows with unit column stride, and its row stride."""
+    if t.dim() == 2 and t.stride(-1) == 1:
+        return t, t.stride(0)
+    t = t.contiguous()
+    return t.reshape(-1, t.shape[-1]), t.shape[-1]
+
+
+def lora_apply(x: Tensor, y: Tensor, cache: FactorCache, segs: SegmentTable, modules, y_col_offsets,
+               workspace: Tensor, status: Tensor | None = None) -> None:
+    """``y[:, off_m : off_m + H] += B(A x)`` for each op module, in place, on the current stream.
+
+    Args:
+        x:  ``(..., H)`` input of the projections (the rows of one batch).
+        y:  ``(..., C)`` projection output(s), updated in place; module ``m`` owns
+            columns ``y_col_offsets[m] : y_col_offsets[m] + H``.
+        modules: cache module indices, one per op module (<= 4).
+    """
+    dev = nat.require_cuda(x, y, workspace, segs.table)
+    x2, ldx = _rows(x)
+    if not y.is_contiguous() and y.stride(-1) != 1:
+        raise ValueError("y must have unit stride in its last dimension")
+    y2 = y.reshape(-1, y.shape[-1])
+    if y2.data_ptr() != y.data_ptr():
+        raise ValueError("y must be viewable as rows without a copy")
+    ldy = y2.stride(0)
+    n = len(modules)
+    rc = nat.lib().lf_lora_apply(
+        nat.stream_ptr(dev), nat.dtype_code(x.dtype),
+        x2.data_ptr(), ldx, y2.data_ptr(), ldy, x2.shape[0], cache.hidden, cache.rank,
+        cache.a_ptr, cache.a_slot_stride, cache.a_module_stride,
+        cache.b_ptr, cache.b_slot_stride, cache.b_module_stride,
+        cache.n_slots, n, nat.i32_array(modules), nat.i64_array(y_col_offsets),
+        *segs.ptrs(), segs.n_segs,
+        workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+        nat.ptr(status))
+    nat.check(rc, "lf_lora_apply")
+
+
+def lora_shrink(x: Tensor, u: Tensor, cache: FactorCache, segs: SegmentTable, modules,
+                status: Tensor | None = None) -> None:
+    """``u[m, t] = A_m(slot(t))^T x[t]`` rounded to the dtype; ``u`` is ``(n_mod, T, R)``."""
+    dev = nat.require_cuda(x, u, segs.table)
+    x2, ldx = _rows(x)
+    rc = nat.lib().lf_lora_shrink(
+        nat.stream_ptr(dev), nat.dtype_code(x.dtype), x2.data_ptr(), ldx, x2.shape[0],
+        cache.hidden, cache.rank, cache.a_ptr, cache.a_slot_stride, cache.a_module_stride,
+        cache.n_slots, len(modules), nat.i32_array(modules), *segs.ptrs(), segs.n_segs,
+        u.data_ptr(), nat.ptr(status))
+    nat.check(rc, "lf_lora_shrink")
+
+
+def lora_expand(u: Tensor, y: Tensor, cache: FactorCache, segs: SegmentTable, modules, y_col_offsets,
+                accumulate: bool, status: Tensor | None = None) -> None:
+    """``y = [y +] round(u B)`` per op module (see :func:`lora_apply` for the column layout)."""
+    dev = nat.require_cuda(u, y, segs.table)
+    y2 = y.reshape(-1, y.shape[-1])
+    if y2.data_ptr() != y.data_ptr() or y2.stride(-1) != 1:
+        raise ValueError("y must be viewable as rows without a copy")
+    rc = nat.lib().lf_lora_expand(
+        nat.stream_ptr(dev), nat.dtype_code(y.dtype), u.data_ptr(), y2.data_ptr(), y2.stride(0),
+        y2.shape[0], cache.hidden, cache.rank, cache.b_ptr, cache.b_slot_stride, cache.b_module_stride,
+        cache.n_slots, len(modules), nat.i32_array(modules), nat.i64_array(y_col_offsets),
+        *segs.ptrs(), segs.n_segs, 1 if accumulate else 0, nat.ptr(status))
+    nat.check(rc, "lf_lora_expand")
+
+
+def per_row_cache(a: Tensor, b: Tensor) -> FactorCache:
+    """A factor cache over materialised per-row factors ``a (B,H,R)``, ``b (B,R,H)``:
+    slot ``i`` is row ``i`` (what the reference's assemblers hand to ``LoraOps``)."""
+    a = a.contiguous()
+    b = b.contiguous()
+    Bn, H, R = a.shape
+    return FactorCache(a=a, b=b, a_offset=0, b_offset=0, a_slot_stride=H * R, b_slot_stride=R * H,
+                       a_module_stride=0, b_module_stride=0, n_slots=Bn, hidden=H, rank=R)
+
+
+class LoraOps:
+    """Batched LoRA operations over buffers pre-allocated from the config.
+
+    Same interface and contract as the reference's ``LoraOps``
+    (``src/latefuse/ops/lora.py:7-80``): ``shrink(x, a_weights)`` fills ``out_A``
+    ``(B, S, R)``, ``expand(b_weights)`` fills ``out_B`` ``(B, S, H)`` and ``output``
+    returns it.  Both steps run the sm_100a kernels with row ``i`` of the batch
+    using factor row ``i``; ``out_A`` is rounded to the model dtype exactly as the
+    reference's ``bmm(..., out=_out_A)`` is.
+    """
+
+    def __init__(self, config: LoraServingConfig):
+        B, S, H, R = config.batch_size, config.max_seq_len, config.hidden_size, config.lora_rank
+        self._out_A = torch.empty(B, S, R, dtype=config.dtype, device=config.device)
+        self._out_B = torch.empty(B, S, H, dtype=config.dtype, device=config.device)
+        self._segs = SegmentTable.for_padded(list(range(B)), S, config.device)
+        self._a: Tensor | None = None
+
+    def shrink(self, x: Tensor, a_weights: Tensor) -> None:
+        """First LoRA step: ``out_A = bmm(x, a_weights)``.
+
+        Args:
+            x:         (B, S, H) input hidden states
+            a_weights: (B, H, R) stacked A matrices, one per sample
+        """
+        assert x.device == self._out_A.device, f"x on {x.device} but LoraOps buffers on {self._out_A.device}"
+        assert a_weights.device == self._out_A.device, (
+            f"a_weights on {a_weights.device} but buffers on {self._out_A.device}")
+        B, S, R = self._out_A.shape
+        H = self._out_B.shape[2]
+        assert x.shape == (B, S, H), (
+            f"x shape {tuple(x.shape)} != buffer shape {(B, S, H)}; "
+            "LoraOps buffers are sized from config at init")
+        assert a_weights.shape == (B, H, R), f"a_weights shape {tuple(a_weights.shape)} != expected {(B, H, R)}"
+        a = a_weights.to(self._out_A.dtype).contiguous()
+        self._a = a
+        cache = FactorCache(a=a, b=a, a_offset=0, b_offset=0, a_slot_stride=H * R, b_slot_stride=R * H,
+                            a_module_stride=0, b_module_stride=0, n_slots=B, hidden=H, rank=R)
+        lora_shrink(x.to(self._out_A.dtype), self._out_A, cache, self._segs, [0])
+
+    def expand(self, b_weights: Tensor) -> None:
+        """Second LoRA step: ``out_B = bmm(out_A, b_weights)``; call ``shrink`` first.
+
+        Args:
+            b_weights: (B, R, H) stacked B matrices, one per sample
+        """
+        assert b_weights.device == self._out_B.device, (
+            f"b_weights on {b_weights.device} but buffers on {self._out_B.device}")
+        B, S, R = self._out_A.shape
+        H = self._out_B.shape[2]
+        assert b_weights.shape == (B, R, H), f"b_weights shape {tuple(b_weights.shape)} != expected {(B, R, H)}"
+        b = b_weights.to(self._out_B.dtype).contiguous()
+        cache = FactorCache(a=b, b=b, a_offset=0, b_offset=0, a_slot_stride=H * R, b_slot_stride=R * H,
+                            a_module_stride=0, b_module_stride=0, n_slots=B, hidden=H, rank=R)
+        lora_expand(self._out_A, self._out_B, cache, self._segs, [0], [0], accumulate=False)
+
+    @property
+    def output(self) -> Tensor:
+        """The (B, S, H) LoRA delta from the last expand() call."""
+        return self._out_B

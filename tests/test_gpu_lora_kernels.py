@@ -1,0 +1,253 @@
+"""Parity of the native LoRA kernels (tcgen05 and CUDA-core paths) with the oracle.
+
+Tolerances: f32 1e-5 absolute; bf16/f16 2e-2 relative (max-abs error over the
+max-abs of the oracle's delta), as stated for the serving path.  The oracle
+reproduces the reference's rounding points (shrink output and delta stored in
+the model dtype, add in the model dtype).
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from latefuse_b200 import _native as nat
+from latefuse_b200.lora import FactorCache, SegmentTable, lora_apply, lora_expand, lora_shrink, workspace_bytes
+from oracle.lora import segmented_apply
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: 1e-5, torch.bfloat16: 2e-2, torch.float16: 2e-2}
+
+
+def make_cache(n_slots, n_mod, H, R, dtype, dev, seed=0, std=0.05):
+    """Cache in the store's slot layout with one layer: [slot][module][A (H,R) | B (R,H)]."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    buf = (torch.randn(n_slots, n_mod, 2, H * R, generator=g) * std).to(dtype).to(dev)
+    fc = FactorCache(a=buf, b=buf, a_offset=0, b_offset=H * R, a_slot_stride=buf.stride(0),
+                     b_slot_stride=buf.stride(0), a_module_stride=buf.stride(1), b_module_stride=buf.stride(1),
+                     n_slots=n_slots, hidden=H, rank=R)
+    cpu = buf.cpu()
+
+    def a_of(slot, m):
+        return cpu[slot, m, 0].view(H, R)
+
+    def b_of(slot, m):
+        return cpu[slot, m, 1].view(R, H)
+
+    return fc, a_of, b_of
+
+
+def segments_padded(B, S, n_slots, seed, lengths=None):
+    g = torch.Generator().manual_seed(seed)
+    slots = torch.randint(0, n_slots, (B,), generator=g).tolist()
+    lens = [S] * B if lengths is None else lengths
+    return [(b * S, lens[b], slots[b]) for b in range(B)]
+
+
+def run_apply(x, y, fc, segs, modules, offs):
+    dev = x.device
+    st = SegmentTable([s for s, _, _ in segs], [l for _, l, _ in segs], [k for _, _, k in segs], x.shape[0], dev)
+    ws = torch.empty(workspace_bytes(x.dtype, x.shape[0], fc.rank, len(modules)), dtype=torch.uint8, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = y.clone()
+    lora_apply(x, out, fc, st, modules, offs, ws, status)
+    torch.cuda.synchronize()
+    assert status.item() == 0, nat.decode_status(status.item())
+    return out
+
+
+def check(ours, ref, base, dtype):
+    d_ours = ours.float() - base.float()
+    d_ref = ref.float() - base.float()
+    scale = max(d_ref.abs().max().item(), 1e-6)
+    err = (ours.float() - ref.float()).abs().max().item()
+    if dtype == torch.float32:
+        assert err <= TOL[dtype], f"max abs err {err}"
+    else:
+        # the final add rounds to the output dtype: allow one output ulp on top of the relative bound
+        ulp = base.float().abs().max().item() * 2 ** -7
+        assert err <= TOL[dtype] * scale + ulp, f"max abs err {err} vs delta scale {scale}"
+        rel = (d_ours - d_ref).norm() / d_ref.norm().clamp_min(1e-12)
+        assert rel.item() <= TOL[dtype], f"relative delta error {rel.item()}"
+
+
+@pytest.fixture(autouse=True)
+def _reset_options(request):
+    # tests named test_tc_* must run on the tcgen05 kernels: falling back is an error
+    nat.set_option(nat.LF_OPT_REQUIRE_TC, 1 if request.node.name.startswith("test_tc_") else 0)
+    nat.set_option(nat.LF_OPT_FORCE_SIMT, 0)
+    nat.set_option(nat.LF_OPT_SHRINK_CLUSTER, 0)
+    yield
+    nat.set_option(nat.LF_OPT_REQUIRE_TC, 0)
+    nat.set_option(nat.LF_OPT_FORCE_SIMT, 0)
+    nat.set_option(nat.LF_OPT_SHRINK_CLUSTER, 0)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("R", [8, 16, 32, 64])
+def test_tc_padded_one_segment_per_tile(cuda, dtype, R):
+    B, S, H, n_slots = 4, 128, 256, 7
+    fc, a_of, b_of = make_cache(n_slots, 1, H, R, dtype, cuda, seed=R)
+    x = torch.randn(B * S, H, generator=torch.Generator().manual_seed(1)).to(dtype).to(cuda)
+    y = torch.randn(B * S, H, generator=torch.Generator().manual_seed(2)).to(dtype).to(cuda)
+    segs = segments_padded(B, S, n_slots, seed=3)
+    ours = run_apply(x, y, fc, segs, [0], [0]).cpu()
+    ref = segmented_apply(x.cpu(), y.cpu(), a_of, b_of, segs)
+    check(ours, ref, y.cpu(), dtype)
+
+
+@pytest.mark.parametrize("R", [8, 16, 64])
+def test_tc_delta_only_precision(cuda, R):
+    """accumulate=0 isolates the delta: bf16 relative error well inside 2e-2."""
+    dtype = torch.bfloat16
+    T, H, n_slots = 384, 512, 5
+    fc, a_of, b_of = make_cache(n_slots, 1, H, R, dtype, cuda, seed=11)
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(4)).to(dtype).to(cuda)
+    segs = [(0, 128, 1), (128, 200, 4), (328, 56, 0)]
+    st = SegmentTable([s for s, _, _ in segs], [l for _, l, _ in segs], [k for _, _, k in segs], T, cuda)
+    u = torch.empty(1, T, R, dtype=dtype, device=cuda)
+    y = torch.full((T, H), 7.0, dtype=dtype, device=cuda)
+    lora_shrink(x, u, fc, st, [0])
+    lora_expand(u, y, fc, st, [0], [0], accumulate=False)
+    torch.cuda.synchronize()
+    ref = segmented_apply(x.cpu(), torch.zeros(T, H, dtype=dtype), a_of, b_of, segs, accumulate=False)
+    rel = (y.cpu().float() - ref.float()).norm() / ref.float().norm()
+    assert rel.item() < 5e-3, rel.item()
+
+
+@pytest.mark.parametrize("H", [64, 192, 320])
+def test_tc_hidden_not_multiple_of_128(cuda, H):
+    dtype = torch.bfloat16
+    B, S, R, n_slots = 3, 128, 16, 4
+    fc, a_of, b_of = make_cache(n_slots, 1, H, R, dtype, cuda, seed=H)
+    x = torch.randn(B * S, H, generator=torch.Generator().manual_seed(5)).to(dtype).to(cuda)
+    y = torch.randn(B * S, H, generator=torch.Generator().manual_seed(6)).to(dtype).to(cuda)
+    segs = segments_padded(B, S, n_slots, seed=7)
+    ours = run_apply(x, y, fc, segs, [0], [0]).cpu()
+    ref = segmented_apply(x.cpu(), y.cpu(), a_of, b_of, segs)
+    check(ours, ref, y.cpu(), dtype)
+
+
+@pytest.mark.parametrize("S", [16, 100, 200, 513])
+def test_tc_ragged_segments_cross_tiles(cuda, S):
+    """Sequences shorter/longer than a 128-token tile, a ragged last tile, skipped padding."""
+    dtype = torch.bfloat16
+    B, H, R, n_slots = 5, 256, 16, 9
+    fc, a_of, b_of = make_cache(n_slots, 1, H, R, dtype, cuda, seed=S)
+    g = torch.Generator().manual_seed(S)
+    lengths = torch.randint(1, S + 1, (B,), generator=g).tolist()
+    x = torch.randn(B * S, H, generator=g).to(dtype).to(cuda)
+    y = torch.randn(B * S, H, generator=g).to(dtype).to(cuda)
+    segs = segments_padded(B, S, n_slots, seed=S + 1, lengths=lengths)
+    ours = run_apply(x, y, fc, segs, [0], [0]).cpu()
+    ref = segmented_apply(x.cpu(), y.cpu(), a_of, b_of, segs)
+    check(ours, ref, y.cpu(), dtype)
+    # rows outside every segment are bit-identical to the input
+    covered = torch.zeros(B * S, dtype=torch.bool)
+    for s, l, _ in segs:
+        covered[s : s + l] = True
+    assert torch.equal(ours[~covered], y.cpu()[~covered])
+
+
+@pytest.mark.parametrize("modules,offs", [([0, 1, 2], [0, 1, 2]), ([0, 2], [0, 2]), ([1], [2])])
+def test_tc_fused_qkv_modules(cuda, modules, offs):
+    dtype = torch.bfloat16
+    B, S, H, R, n_slots = 2, 256, 256, 16, 6
+    fc, a_of, b_of = make_cache(n_slots, 3, H, R, dtype, cuda, seed=21)
+    x = torch.randn(B * S, H, generator=torch.Generator().manual_seed(8)).to(dtype).to(cuda)
+    y = torch.randn(B * S, 3 * H, generator=torch.Generator().manual_seed(9)).to(dtype).to(cuda)
+    segs = segments_padded(B, S, n_slots, seed=10)
+    col = [o * H for o in offs]
+    ours = run_apply(x, y, fc, segs, modules, col).cpu()
+    ref = segmented_apply(x.cpu(), y.cpu(), a_of, b_of, segs, col_offsets=col, modules=modules)
+    check(ours, ref, y.cpu(), dtype)
+    untouched = [j for j in range(3) if j not in offs]
+    for j in untouched:
+        assert torch.equal(ours[:, j * H : (j + 1) * H], y.cpu()[:, j * H : (j + 1) * H])
+
+
+@pytest.mark.parametrize("csize", [1, 2, 4])
+def test_tc_cluster_split_is_deterministic_and_equal(cuda, csize):
+    dtype = torch.bfloat16
+    B, S, H, R, n_slots = 2, 128, 256, 16, 3
+    fc, a_of, b_of = make_cache(n_slots, 1, H, R, dtype, cuda, seed=31)
+    x = torch.randn(B * S, H, generator=torch.Generator().manual_seed(12)).to(dtype).to(cuda)
+    y = torch.randn(B * S, H, generator=torch.Generator().manual_seed(13)).to(dtype).to(cuda)
+    segs = segments_padded(B, S, n_slots, seed=14)
+    nat.set_option(nat.LF_OPT_SHRINK_CLUSTER, csize)
+    a = run_apply(x, y, fc, segs, [0], [0])
+    b = run_apply(x, y, fc, segs, [0], [0])
+    assert torch.equal(a, b)
+    ref = segmented_apply(x.cpu(), y.cpu(), a_of, b_of, segs)
+    check(a.cpu(), ref, y.cpu(), dtype)
+
+
+def test_tc_matches_simt(cuda):
+    dtype = torch.bfloat16
+    B, S, H, R, n_slots = 3, 160, 256, 32, 5
+    fc, _, _ = make_cache(n_slots, 2, H, R, dtype, cuda, seed=41)
+    x = torch.randn(B * S, H, generator=torch.Generator().manual_seed(15)).to(dtype).to(cuda)
+    y = torch.randn(B * S, 2 * H, generator=torch.Generator().manual_seed(16)).to(dtype).to(cuda)
+    segs = segments_padded(B, S, n_slots, seed=17)
+    tc = run_apply(x, y, fc, segs, [0, 1], [0, H])
+    nat.set_option(nat.LF_OPT_REQUIRE_TC, 0)
+    nat.set_option(nat.LF_OPT_FORCE_SIMT, 1)
+    simt = run_apply(x, y, fc, segs, [0, 1], [0, H])
+    d = (tc.float() - y.float())
+    e = (simt.float() - y.float())
+    rel = (d - e).norm() / e.norm()
+    assert rel.item() < 2e-2
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("H,R", [(32, 4), (48, 8), (256, 16), (100, 3)])
+def test_simt_any_shape(cuda, dtype, H, R):
+    """f32 (exact arithmetic) and shapes the tensor-core path does not tile."""
+    B, S, n_slots = 3, 16, 4
+    fc, a_of, b_of = make_cache(n_slots, 1, H, R, dtype, cuda, seed=H + R)
+    x = torch.randn(B * S, H, generator=torch.Generator().manual_seed(18)).to(dtype).to(cuda)
+    y = torch.randn(B * S, H, generator=torch.Generator().manual_seed(19)).to(dtype).to(cuda)
+    segs = segments_padded(B, S, n_slots, seed=20, lengths=[16, 5, 0])
+    ours = run_apply(x, y, fc, segs, [0], [0]).cpu()
+    ref = segmented_apply(x.cpu(), y.cpu(), a_of, b_of, segs)
+    check(ours, ref, y.cpu(), dtype)
+
+
+def test_bad_slot_sets_status_without_fault(cuda):
+    dtype = torch.bfloat16
+    T, H, R = 256, 256, 16
+    fc, _, _ = make_cache(2, 1, H, R, dtype, cuda)
+    x = torch.randn(T, H, device=cuda, dtype=dtype)
+    y = torch.randn(T, H, device=cuda, dtype=dtype)
+    st = SegmentTable([0, 128], [128, 128], [1, 5], T, cuda)  # slot 5 is out of range
+    ws = torch.empty(workspace_bytes(dtype, T, R, 1), dtype=torch.uint8, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = y.clone()
+    lora_apply(x, out, fc, st, [0], [0], ws, status)
+    torch.cuda.synchronize()
+    assert status.item() & 1
+    assert torch.equal(out[128:], y[128:])  # the bad segment got no delta
+
+
+def test_large_cfg2_shape_vs_gathered_bmm(cuda):
+    """(64, 256, 1024) bf16, r=16, 1,000 slots: the kernels against the reference's
+    own GPU arithmetic (gather + bmm + add), on the same device."""
+    dtype = torch.bfloat16
+    B, S, H, R, n_slots = 64, 256, 1024, 16, 1000
+    fc, _, _ = make_cache(n_slots, 1, H, R, dtype, cuda, seed=51, std=0.02)
+    x = torch.randn(B * S, H, device=cuda, dtype=dtype)
+    y = torch.randn(B * S, H, device=cuda, dtype=dtype)
+    segs = segments_padded(B, S, n_slots, seed=52)
+    ours = run_apply(x, y, fc, segs, [0], [0])
+    slots = torch.tensor([k for _, _, k in segs], device=cuda)
+    buf = fc.a
+    a = buf[slots, 0, 0].view(B, H, R)
+    b = buf[slots, 0, 1].view(B, R, H)
+    out_a = torch.bmm(x.view(B, S, H), a)
+    out_b = torch.bmm(out_a, b)
+    ref = (y.view(B, S, H) + out_b).view(B * S, H)
+    d1 = ours.float() - y.float()
+    d2 = ref.float() - y.float()
+    rel = (d1 - d2).norm() / d2.norm()
+    assert rel.item() < 2e-2, rel.item()
