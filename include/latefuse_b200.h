@@ -38,6 +38,10 @@
  *                    LoraWeight.wa[m][layer] / wb[m][layer] layouts
  *                    (src/latefuse/weights/store.py:22-39), so a per-tenant
  *                    adapter is addressed in place, never gathered.
+ *   tiles            optional device int32 list of the row tiles (tokens
+ *                    [i*LF_TILE_TOKENS, (i+1)*LF_TILE_TOKENS)) that hold any
+ *                    segment token, so tiles of pure padding are never
+ *                    launched; NULL (n_tiles = 0) means every tile.
  *   status           optional device int32; kernels OR LF_STATUS_* bits into
  *                    it instead of faulting on a bad slot id, a bad segment or
  *                    a wait that timed out.
@@ -64,6 +68,9 @@ extern "C" {
 #define LF_DTYPE_F32 0
 #define LF_DTYPE_BF16 1
 #define LF_DTYPE_F16 2
+
+/* tokens per row tile of the LoRA kernels (the unit of the optional tile list) */
+#define LF_TILE_TOKENS 128
 
 /* device status bits (written by kernels into *status) */
 #define LF_STATUS_BAD_SLOT 1    /* a segment named a slot outside [0, n_slots) */
@@ -122,7 +129,7 @@ int lf_lora_shrink(void* stream, int dtype,
                    const void* cache_a, int64_t a_slot_stride, int64_t a_module_stride,
                    int n_slots, int n_modules, const int32_t* modules,
                    const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot,
-                   int n_segs,
+                   int n_segs, const int32_t* tiles, int n_tiles,
                    void* u, int32_t* status);
 
 /* Expand: for every token t and op-module m,
@@ -142,7 +149,8 @@ int lf_lora_expand(void* stream, int dtype,
                    int n_slots, int n_modules, const int32_t* modules,
                    const int64_t* y_col_offsets,
                    const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot,
-                   int n_segs, int accumulate, int32_t* status);
+                   int n_segs, const int32_t* tiles, int n_tiles,
+                   int accumulate, int32_t* status);
 
 /* Device workspace bytes lf_lora_apply needs for these sizes. */
 size_t lf_lora_workspace_bytes(int dtype, int64_t n_tokens, int rank, int n_modules);
@@ -161,7 +169,7 @@ int lf_lora_apply(void* stream, int dtype,
                   int n_slots, int n_modules, const int32_t* modules,
                   const int64_t* y_col_offsets,
                   const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot,
-                  int n_segs,
+                  int n_segs, const int32_t* tiles, int n_tiles,
                   void* workspace, size_t workspace_bytes, int32_t* status);
 
 /* ------------------------------------------------------------------------ */

@@ -18,6 +18,7 @@ import torch
 from latefuse_b200._build import LIB_PATH
 
 LF_OK = 0
+TILE_TOKENS = 128
 LF_DTYPE = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 LF_POOL = {"cls": 0, "mean": 1, "none": 2}
 LF_OPT_FORCE_SIMT = 1
@@ -41,17 +42,17 @@ SIGNATURES: dict[str, tuple] = {
     "lf_lora_shrink": (c_int, [
         c_void_p, c_int, c_void_p, c_int64, c_int64, c_int, c_int,
         c_void_p, c_int64, c_int64, c_int, c_int, POINTER(c_int32),
-        c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+        c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p]),
     "lf_lora_expand": (c_int, [
         c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int,
         c_void_p, c_int64, c_int64, c_int, c_int, POINTER(c_int32), POINTER(c_int64),
-        c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+        c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p]),
     "lf_lora_workspace_bytes": (c_size_t, [c_int, c_int64, c_int, c_int]),
     "lf_lora_apply": (c_int, [
         c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_int,
         c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int,
         POINTER(c_int32), POINTER(c_int64), c_void_p, c_void_p, c_void_p, c_int,
-        c_void_p, c_size_t, c_void_p]),
+        c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     "lf_cache_gather": (c_int, [
         c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_int, c_void_p, c_int,
         c_void_p, c_void_p]),

@@ -88,6 +88,15 @@ static int check_common(const char* fn, int dtype, int64_t n_tokens, int hidden,
   if (n_segs < 0) return set_error(LF_ERR_INVALID, "%s: n_segs < 0", fn);
   if (n_segs > 0 && (seg_start == nullptr || seg_len == nullptr || seg_slot == nullptr))
     return set_error(LF_ERR_INVALID, "%s: segment arrays are NULL", fn);
+  const int64_t all_tiles = (n_tokens + LF_TILE_TOKENS - 1) / LF_TILE_TOKENS;
+  if (all_tiles > 65535) return set_error(LF_ERR_UNSUPPORTED, "%s: more than 65535 token tiles", fn);
+  return LF_OK;
+}
+
+static int check_tiles(const char* fn, const int32_t* tiles, int n_tiles, int64_t n_tokens) {
+  const int64_t all_tiles = (n_tokens + LF_TILE_TOKENS - 1) / LF_TILE_TOKENS;
+  if (n_tiles < 0 || n_tiles > all_tiles || (tiles == nullptr && n_tiles != 0))
+    return set_error(LF_ERR_INVALID, "%s: tile list of %d entries for %lld tiles", fn, n_tiles, (long long)all_tiles);
   return LF_OK;
 }
 
@@ -124,7 +133,7 @@ static int shrink_impl(cudaStream_t stream, int dtype, const void* x, int64_t ld
                        int hidden, int rank, const void* cache_a, int64_t a_slot_stride,
                        int64_t a_module_stride, int n_slots, int n_modules, const int32_t* modules,
                        const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot,
-                       int n_segs, void* u, int32_t* status) {
+                       int n_segs, const int32_t* tiles, int n_tiles, void* u, int32_t* status) {
   const int es = elem_size(dtype);
   const bool tc = !option_force_simt() && dtype != LF_DTYPE_F32 && tc_rank(rank) && hidden % 64 == 0 &&
                   aligned16(x) && aligned16(cache_a) && aligned16(u) && (ldx * es) % 16 == 0 &&
@@ -187,9 +196,12 @@ static int shrink_impl(cudaStream_t stream, int dtype, const void* x, int64_t ld
     p.seg_len = seg_len;
     p.seg_slot = seg_slot;
     p.n_segs = n_segs;
+    p.tiles = tiles;
     p.u = static_cast<uint8_t*>(u) + int64_t(m0) * n_tokens * rank * es;
     p.status = status;
-    int rc = run_shrink_tc(dtype, p, rank, csize, stream);
+    const int grid_tiles = tiles != nullptr ? n_tiles : int((n_tokens + LF_TILE_TOKENS - 1) / LF_TILE_TOKENS);
+    if (grid_tiles == 0) return LF_OK;
+    int rc = run_shrink_tc(dtype, p, rank, csize, grid_tiles, stream);
     if (rc) return rc;
   }
   return LF_OK;
@@ -202,7 +214,8 @@ static int expand_impl(cudaStream_t stream, int dtype, const void* u, void* y, i
                        int hidden, int rank, const void* cache_b, int64_t b_slot_stride,
                        int64_t b_module_stride, int n_slots, int n_modules, const int32_t* modules,
                        const int64_t* y_col_offsets, const int32_t* seg_start, const int32_t* seg_len,
-                       const int32_t* seg_slot, int n_segs, int accumulate, int32_t* status) {
+                       const int32_t* seg_slot, int n_segs, const int32_t* tiles, int n_tiles, int accumulate,
+                       int32_t* status) {
   const int es = elem_size(dtype);
   int64_t y_cols = 0;
   bool offs_aligned = true;
@@ -269,8 +282,12 @@ static int expand_impl(cudaStream_t stream, int dtype, const void* u, void* y, i
   p.seg_len = seg_len;
   p.seg_slot = seg_slot;
   p.n_segs = n_segs;
+  // with accumulate == 0 every tile must be written (rows outside segments become 0)
+  p.tiles = accumulate ? tiles : nullptr;
+  p.n_tiles = (accumulate && tiles != nullptr) ? n_tiles : int((n_tokens + LF_TILE_TOKENS - 1) / LF_TILE_TOKENS);
   p.u = u;
   p.status = status;
+  if (p.n_tiles == 0) return LF_OK;
   const int nt = hidden % 128 == 0 ? 128 : 64;
   return run_expand_tc(dtype, p, rank, nt, stream);
 }
@@ -315,42 +332,47 @@ size_t lf_lora_workspace_bytes(int dtype, int64_t n_tokens, int rank, int n_modu
 int lf_lora_shrink(void* stream, int dtype, const void* x, int64_t ldx, int64_t n_tokens, int hidden, int rank,
                    const void* cache_a, int64_t a_slot_stride, int64_t a_module_stride, int n_slots,
                    int n_modules, const int32_t* modules, const int32_t* seg_start, const int32_t* seg_len,
-                   const int32_t* seg_slot, int n_segs, void* u, int32_t* status) {
+                   const int32_t* seg_slot, int n_segs, const int32_t* tiles, int n_tiles, void* u,
+                   int32_t* status) {
   int rc = check_common("lf_lora_shrink", dtype, n_tokens, hidden, rank, n_slots, n_modules, modules, seg_start,
                         seg_len, seg_slot, n_segs);
   if (rc) return rc;
+  if ((rc = check_tiles("lf_lora_shrink", tiles, n_tiles, n_tokens))) return rc;
   if (x == nullptr || cache_a == nullptr || u == nullptr) return set_error(LF_ERR_INVALID, "lf_lora_shrink: NULL buffer");
   if (ldx < hidden) return set_error(LF_ERR_INVALID, "lf_lora_shrink: ldx < hidden");
   if (n_tokens == 0) return LF_OK;
   return shrink_impl(static_cast<cudaStream_t>(stream), dtype, x, ldx, n_tokens, hidden, rank, cache_a,
                      a_slot_stride, a_module_stride, n_slots, n_modules, modules, seg_start, seg_len, seg_slot,
-                     n_segs, u, status);
+                     n_segs, tiles, n_tiles, u, status);
 }
 
 int lf_lora_expand(void* stream, int dtype, const void* u, void* y, int64_t ldy, int64_t n_tokens, int hidden,
                    int rank, const void* cache_b, int64_t b_slot_stride, int64_t b_module_stride, int n_slots,
                    int n_modules, const int32_t* modules, const int64_t* y_col_offsets, const int32_t* seg_start,
-                   const int32_t* seg_len, const int32_t* seg_slot, int n_segs, int accumulate, int32_t* status) {
+                   const int32_t* seg_len, const int32_t* seg_slot, int n_segs, const int32_t* tiles, int n_tiles,
+                   int accumulate, int32_t* status) {
   int rc = check_common("lf_lora_expand", dtype, n_tokens, hidden, rank, n_slots, n_modules, modules, seg_start,
                         seg_len, seg_slot, n_segs);
   if (rc) return rc;
+  if ((rc = check_tiles("lf_lora_expand", tiles, n_tiles, n_tokens))) return rc;
   if (u == nullptr || y == nullptr || cache_b == nullptr || y_col_offsets == nullptr)
     return set_error(LF_ERR_INVALID, "lf_lora_expand: NULL buffer");
   if (n_tokens == 0) return LF_OK;
   return expand_impl(static_cast<cudaStream_t>(stream), dtype, u, y, ldy, n_tokens, hidden, rank, cache_b,
                      b_slot_stride, b_module_stride, n_slots, n_modules, modules, y_col_offsets, seg_start, seg_len,
-                     seg_slot, n_segs, accumulate, status);
+                     seg_slot, n_segs, tiles, n_tiles, accumulate, status);
 }
 
 int lf_lora_apply(void* stream, int dtype, const void* x, int64_t ldx, void* y, int64_t ldy, int64_t n_tokens,
                   int hidden, int rank, const void* cache_a, int64_t a_slot_stride, int64_t a_module_stride,
                   const void* cache_b, int64_t b_slot_stride, int64_t b_module_stride, int n_slots, int n_modules,
                   const int32_t* modules, const int64_t* y_col_offsets, const int32_t* seg_start,
-                  const int32_t* seg_len, const int32_t* seg_slot, int n_segs, void* workspace,
-                  size_t workspace_bytes, int32_t* status) {
+                  const int32_t* seg_len, const int32_t* seg_slot, int n_segs, const int32_t* tiles, int n_tiles,
+                  void* workspace, size_t workspace_bytes, int32_t* status) {
   int rc = check_common("lf_lora_apply", dtype, n_tokens, hidden, rank, n_slots, n_modules, modules, seg_start,
                         seg_len, seg_slot, n_segs);
   if (rc) return rc;
+  if ((rc = check_tiles("lf_lora_apply", tiles, n_tiles, n_tokens))) return rc;
   if (x == nullptr || y == nullptr || cache_a == nullptr || cache_b == nullptr || y_col_offsets == nullptr)
     return set_error(LF_ERR_INVALID, "lf_lora_apply: NULL buffer");
   if (ldx < hidden) return set_error(LF_ERR_INVALID, "lf_lora_apply: ldx < hidden");
@@ -360,10 +382,11 @@ int lf_lora_apply(void* stream, int dtype, const void* x, int64_t ldx, void* y, 
     return set_error(LF_ERR_WORKSPACE, "lf_lora_apply: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   rc = shrink_impl(s, dtype, x, ldx, n_tokens, hidden, rank, cache_a, a_slot_stride, a_module_stride, n_slots,
-                   n_modules, modules, seg_start, seg_len, seg_slot, n_segs, workspace, status);
+                   n_modules, modules, seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles, workspace, status);
   if (rc) return rc;
   return expand_impl(s, dtype, workspace, y, ldy, n_tokens, hidden, rank, cache_b, b_slot_stride, b_module_stride,
-                     n_slots, n_modules, modules, y_col_offsets, seg_start, seg_len, seg_slot, n_segs, 1, status);
+                     n_slots, n_modules, modules, y_col_offsets, seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles,
+                     1, status);
 }
 
 }  // extern "C"

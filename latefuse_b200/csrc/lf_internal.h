@@ -27,6 +27,7 @@ struct alignas(64) ShrinkTcParams {
   const int32_t* seg_len;
   const int32_t* seg_slot;
   int32_t n_segs;
+  const int32_t* tiles;              // row tiles to process (NULL: all)
   void* u;                           // (n_modules, n_tokens, rank)
   int32_t* status;
 };
@@ -44,6 +45,8 @@ struct alignas(64) ExpandTcParams {
   const int32_t* seg_len;
   const int32_t* seg_slot;
   int32_t n_segs;
+  const int32_t* tiles;              // row tiles to process (NULL: all)
+  int32_t n_tiles;                   // grid rows (tiles listed, or all tiles)
   const void* u;                     // (n_modules, n_tokens, rank)
   int32_t* status;
 };
@@ -78,7 +81,7 @@ int cuda_error(cudaError_t e, const char* what);
 void count_launch();
 
 // tcgen05 path
-int run_shrink_tc(int dtype, const ShrinkTcParams& p, int rank, int csize, cudaStream_t s);
+int run_shrink_tc(int dtype, const ShrinkTcParams& p, int rank, int csize, int n_tiles, cudaStream_t s);
 int run_expand_tc(int dtype, const ExpandTcParams& p, int rank, int nt, cudaStream_t s);
 size_t shrink_tc_smem(int dtype, int rank, int kchunk, int n_mod);
 uint32_t shrink_tc_tmem_cols(int rank, int n_mod);

@@ -119,7 +119,7 @@ lora_shrink_tc_kernel(const __grid_constant__ ShrinkTcParams p) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int csize = gridDim.x;                 // cluster size (split-K factor)
   const int crank = blockIdx.x;                // == %cluster_ctarank for cluster dims (csize,1,1)
-  const int64_t row0 = int64_t(blockIdx.y) * kTileM;
+  const int64_t row0 = int64_t(p.tiles != nullptr ? p.tiles[blockIdx.y] : int32_t(blockIdx.y)) * kTileM;
   const int kchunk = p.kchunk;
   const int nkb = kchunk / kKBlock;
   const int k0 = crank * kchunk;
@@ -319,7 +319,7 @@ lora_expand_tc_kernel(const __grid_constant__ ExpandTcParams p) {
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ct = blockIdx.x;
-  const int64_t row0 = int64_t(blockIdx.y) * kTileM;
+  const int64_t row0 = int64_t(p.tiles != nullptr ? p.tiles[blockIdx.y] : int32_t(blockIdx.y)) * kTileM;
   const int m = blockIdx.z;
   const int32_t col0 = int32_t(p.y_col_off[m] + int64_t(ct) * NT);
   const bool acc_y = p.accumulate != 0;
@@ -499,7 +499,7 @@ static size_t occupancy_capped_smem(size_t need, int cap) {
 }
 
 template <typename T, int R>
-static int launch_shrink_tc(const ShrinkTcParams& p, int csize, cudaStream_t stream) {
+static int launch_shrink_tc(const ShrinkTcParams& p, int csize, int n_tiles, cudaStream_t stream) {
   const size_t need = ShrinkTc<T, R>::smem_bytes(p.kchunk, p.n_modules);
   const int cap = 512 / int(p.tmem_cols);
   const size_t smem = occupancy_capped_smem(need, cap);
@@ -508,7 +508,7 @@ static int launch_shrink_tc(const ShrinkTcParams& p, int csize, cudaStream_t str
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(shrink)");
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(csize, unsigned((p.n_tokens + kTileM - 1) / kTileM), 1);
+  cfg.gridDim = dim3(csize, unsigned(n_tiles), 1);
   cfg.blockDim = dim3(128, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -532,7 +532,7 @@ static int launch_expand_tc(const ExpandTcParams& p, cudaStream_t stream) {
   auto kern = lora_expand_tc_kernel<T, R, NT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(expand)");
-  dim3 grid(unsigned(p.hidden / NT), unsigned((p.n_tokens + kTileM - 1) / kTileM), unsigned(p.n_modules));
+  dim3 grid(unsigned(p.hidden / NT), unsigned(p.n_tiles), unsigned(p.n_modules));
   kern<<<grid, 128, smem, stream>>>(p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "launch lora_expand_tc");
@@ -565,19 +565,19 @@ CUtensorMapSwizzle a_tma_swizzle(int rank) {
 }
 
 template <typename T>
-static int dispatch_shrink_rank(const ShrinkTcParams& p, int rank, int csize, cudaStream_t s) {
+static int dispatch_shrink_rank(const ShrinkTcParams& p, int rank, int csize, int n_tiles, cudaStream_t s) {
   switch (rank) {
-    case 8: return launch_shrink_tc<T, 8>(p, csize, s);
-    case 16: return launch_shrink_tc<T, 16>(p, csize, s);
-    case 32: return launch_shrink_tc<T, 32>(p, csize, s);
-    case 64: return launch_shrink_tc<T, 64>(p, csize, s);
+    case 8: return launch_shrink_tc<T, 8>(p, csize, n_tiles, s);
+    case 16: return launch_shrink_tc<T, 16>(p, csize, n_tiles, s);
+    case 32: return launch_shrink_tc<T, 32>(p, csize, n_tiles, s);
+    case 64: return launch_shrink_tc<T, 64>(p, csize, n_tiles, s);
   }
   return set_error(LF_ERR_UNSUPPORTED, "tcgen05 shrink: rank %d", rank);
 }
 
-int run_shrink_tc(int dtype, const ShrinkTcParams& p, int rank, int csize, cudaStream_t s) {
-  if (dtype == LF_DTYPE_BF16) return dispatch_shrink_rank<__nv_bfloat16>(p, rank, csize, s);
-  return dispatch_shrink_rank<__half>(p, rank, csize, s);
+int run_shrink_tc(int dtype, const ShrinkTcParams& p, int rank, int csize, int n_tiles, cudaStream_t s) {
+  if (dtype == LF_DTYPE_BF16) return dispatch_shrink_rank<__nv_bfloat16>(p, rank, csize, n_tiles, s);
+  return dispatch_shrink_rank<__half>(p, rank, csize, n_tiles, s);
 }
 
 template <typename T, int R>

@@ -147,12 +147,12 @@ class HFEncoderWithLora(nn.Module):
                 owner.shared_projection_skips += 1
                 return None
             owner._fired.add(key)
-            owner._apply(layer_idx, logical, x, output)
+            owner._apply_delta(layer_idx, logical, x, output)
             return output
 
         return hook
 
-    def _apply(self, layer_idx: int, logical: str, x: Tensor, out: Tensor) -> None:
+    def _apply_delta(self, layer_idx: int, logical: str, x: Tensor, out: Tensor) -> None:
         batch = self._batch
         T = x.shape[0] * x.shape[1]
         ws = self._runner.workspace(T, 1, x.device, x.dtype)
@@ -297,6 +297,9 @@ class EncoderWithLora(nn.Module):
         self.pooler_b = nn.Parameter(torch.empty(H))
         self.act = ACT2FN[serving_config.hidden_act]
         self._runner = _DeltaRunner(serving_config)
+        #: when a list, every LoRA delta op appends (start, end) CUDA events recorded
+        #: around it on the current stream (used by the benchmark's roofline timing)
+        self.lora_events: list | None = None
         targets = serving_config.target_modules
         self._qkv_targets = [(m, _QKV.index(m)) for m in targets if m in _QKV]
         self._dense_target = "dense" in targets
@@ -399,6 +402,14 @@ class EncoderWithLora(nn.Module):
         segs = _identity_segments(B, S, device)
         return None, segs, None, None, False
 
+    def _event_pair(self, kind: str):
+        if self.lora_events is None:
+            return None
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        self.lora_events.append((kind, start, end))
+        return start, end
+
     def encode_pooled(self, input_ids: Tensor, attention_mask: Tensor | None, lora_weights,
                       token_type_ids: Tensor | None = None, apply_lora: bool = True,
                       pooling: str = "auto") -> Tensor:
@@ -438,7 +449,10 @@ class EncoderWithLora(nn.Module):
             qkv = F.linear(h, layer.wqkv, layer.bqkv)  # (T, 3H)
             if do_lora and self._qkv_targets:
                 if sloted:
+                    ev = self._event_pair("qkv")
                     lora_apply(h, qkv, getter(l), segs, qkv_idx, qkv_offs, ws, status)
+                    if ev is not None:
+                        ev[1].record()
                 else:
                     for (m, j) in self._qkv_targets:
                         cache = _DeltaRunner.layerwise_cache(lora_weights[l], m)
@@ -449,7 +463,10 @@ class EncoderWithLora(nn.Module):
             ao = F.linear(ctx, layer.wo, layer.bo)
             if do_lora and self._dense_target:
                 if sloted:
+                    ev = self._event_pair("dense")
                     lora_apply(ctx, ao, getter(l), segs, dense_idx, [0], ws, status)
+                    if ev is not None:
+                        ev[1].record()
                 else:
                     cache = _DeltaRunner.layerwise_cache(lora_weights[l], "dense")
                     lora_apply(ctx, ao, cache, segs, [0], [0], ws, status)

@@ -34,6 +34,11 @@ class SegmentTable:
     row's real length when padding is skipped (right-padded rows only: real
     tokens first).  Skipping padding changes no real token's output, because
     padded keys are masked out of attention and every other op is per token.
+
+    The table also lists the 128-token row tiles that hold any segment token, so
+    the kernels never launch work for tiles of pure padding.  Everything lives in
+    one int32 buffer, ``[starts | lengths | slots | tiles]``, copied to the device
+    once per batch.
     """
 
     def __init__(self, starts, lengths, slots, n_tokens: int, device: torch.device):
@@ -43,12 +48,17 @@ class SegmentTable:
         self.n_segs = len(starts)
         self.n_tokens = int(n_tokens)
         self.device = torch.device(device)
-        self.host = torch.tensor([starts, lengths, slots], dtype=torch.int32).reshape(3, -1)
+        tile = nat.TILE_TOKENS
+        tiles = sorted({t for s, n in zip(starts, lengths) if n > 0
+                        for t in range(s // tile, (s + n - 1) // tile + 1)})
+        self.n_tiles = len(tiles)
+        self.host = torch.tensor(starts + lengths + slots + tiles, dtype=torch.int32)
         if self.device.type == "cuda":
             self.table = self.host.pin_memory().to(self.device, non_blocking=True)
         else:
             self.table = self.host.clone()
         self.slots = slots
+        self.real_tokens = int(sum(max(0, n) for n in lengths))
 
     @classmethod
     def for_padded(cls, slots, seq_len: int, device, lengths=None) -> SegmentTable:
@@ -56,10 +66,11 @@ class SegmentTable:
         lens = [seq_len] * B if lengths is None else [int(min(seq_len, max(0, n))) for n in lengths]
         return cls([b * seq_len for b in range(B)], lens, slots, B * seq_len, device)
 
-    def ptrs(self) -> tuple[int, int, int]:
+    def ptrs(self) -> tuple[int, int, int, int, int]:
+        """(seg_start, seg_len, seg_slot, tiles, n_tiles) device pointers/count for the C ABI."""
         base = self.table.data_ptr()
-        step = self.table.stride(0) * 4
-        return base, base + step, base + 2 * step
+        n = self.n_segs
+        return base, base + 4 * n, base + 8 * n, base + 12 * n, self.n_tiles
 
 
 # ---------------------------------------------------------------------------
@@ -92,6 +103,11 @@ class FactorCache:
     @property
     def b_ptr(self) -> int:
         return self.b.data_ptr() + self.b_offset * self.b.element_size()
+
+
+def _seg_args(segs: SegmentTable) -> tuple:
+    s, l, k, t, nt = segs.ptrs()
+    return s, l, k, segs.n_segs, t, nt
 
 
 def workspace_bytes(dtype: torch.dtype, n_tokens: int, rank: int, n_modules: int) -> int:
@@ -131,7 +147,7 @@ def lora_apply(x: Tensor, y: Tensor, cache: FactorCache, segs: SegmentTable, mod
         cache.a_ptr, cache.a_slot_stride, cache.a_module_stride,
         cache.b_ptr, cache.b_slot_stride, cache.b_module_stride,
         cache.n_slots, n, nat.i32_array(modules), nat.i64_array(y_col_offsets),
-        *segs.ptrs(), segs.n_segs,
+        *_seg_args(segs),
         workspace.data_ptr(), workspace.numel() * workspace.element_size(),
         nat.ptr(status))
     nat.check(rc, "lf_lora_apply")
@@ -145,7 +161,7 @@ def lora_shrink(x: Tensor, u: Tensor, cache: FactorCache, segs: SegmentTable, mo
     rc = nat.lib().lf_lora_shrink(
         nat.stream_ptr(dev), nat.dtype_code(x.dtype), x2.data_ptr(), ldx, x2.shape[0],
         cache.hidden, cache.rank, cache.a_ptr, cache.a_slot_stride, cache.a_module_stride,
-        cache.n_slots, len(modules), nat.i32_array(modules), *segs.ptrs(), segs.n_segs,
+        cache.n_slots, len(modules), nat.i32_array(modules), *_seg_args(segs),
         u.data_ptr(), nat.ptr(status))
     nat.check(rc, "lf_lora_shrink")
 
@@ -161,7 +177,7 @@ def lora_expand(u: Tensor, y: Tensor, cache: FactorCache, segs: SegmentTable, mo
         nat.stream_ptr(dev), nat.dtype_code(y.dtype), u.data_ptr(), y2.data_ptr(), y2.stride(0),
         y2.shape[0], cache.hidden, cache.rank, cache.b_ptr, cache.b_slot_stride, cache.b_module_stride,
         cache.n_slots, len(modules), nat.i32_array(modules), nat.i64_array(y_col_offsets),
-        *segs.ptrs(), segs.n_segs, 1 if accumulate else 0, nat.ptr(status))
+        *_seg_args(segs), 1 if accumulate else 0, nat.ptr(status))
     nat.check(rc, "lf_lora_expand")
 
 

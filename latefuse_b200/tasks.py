@@ -84,11 +84,7 @@ class TaskPipeline:
         self.config = config
         self.pooling = pooling
         self.skip_padding = skip_padding
-        if tokenizer is None:
-            from transformers import AutoTokenizer
-
-            tokenizer = AutoTokenizer.from_pretrained(config.model_name)
-        self.tokenizer = tokenizer
+        self._tokenizer = tokenizer
         if model is None:
             cls = HFEncoderWithLora if engine == "hf" else EncoderWithLora
             model = cls.from_pretrained_serving(config)
@@ -96,6 +92,19 @@ class TaskPipeline:
         self.store = store if store is not None else AdapterStore(config)
         self._assembler_kind = assembler
         self._assembler = None
+
+    @property
+    def tokenizer(self):
+        """The HF tokenizer of ``model_name`` (loaded on first use; pre-tokenized calls never need it)."""
+        if self._tokenizer is None:
+            from transformers import AutoTokenizer
+
+            self._tokenizer = AutoTokenizer.from_pretrained(self.config.model_name)
+        return self._tokenizer
+
+    @tokenizer.setter
+    def tokenizer(self, value) -> None:
+        self._tokenizer = value
 
     @classmethod
     def from_pretrained(cls, model_name: str, *, lora_rank: int = 8, batch_size: int = 32,

@@ -1,0 +1,273 @@
+"""Host-side logic on the CPU: stores, assemblers, heads, loaders, batching, segment tables.
+
+Mirrors the reference's own CPU tests (``tests/test_weights.py``,
+``tests/test_tasks.py`` sections 1, 5, 8, 9) for the parts that involve no kernel:
+the serving path itself only runs on the GPU.
+"""
+
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import pytest
+import torch
+from transformers import BertConfig
+
+import latefuse_b200 as lf
+from latefuse_b200.batch import BatchAssembler, IndexSelectBatchAssembler
+from latefuse_b200.lora import SegmentTable
+from latefuse_b200.tasks import chunk_and_pad, right_padded_lengths
+
+GOLD = Path(__file__).resolve().parent / "golden"
+TINY = dict(vocab_size=100, hidden_size=32, num_hidden_layers=2, num_attention_heads=4, intermediate_size=64,
+            max_position_embeddings=64, pad_token_id=0)
+
+
+def cfg(rank=4, dtype=torch.float32, targets=("query", "value")):
+    return lf.LoraServingConfig(model_name="tiny", lora_rank=rank, batch_size=4, max_seq_len=16,
+                                target_modules=list(targets), device=torch.device("cpu"), dtype=dtype,
+                                hf_config=BertConfig(**TINY))
+
+
+# ---------------------------------------------------------------- batching ---
+def test_chunk_and_pad_matches_reference_cases():
+    cases = json.loads((GOLD / "chunking.json").read_text())
+    for key, want in cases.items():
+        n, bs = map(int, key.split("_"))
+        assert [[c, k] for c, k in chunk_and_pad(list(range(n)), bs)] == want
+    with pytest.raises(ValueError, match="must be positive"):
+        list(chunk_and_pad([1], 0))
+
+
+def test_right_padded_lengths():
+    m = torch.tensor([[1, 1, 1, 0], [1, 0, 0, 0], [1, 1, 1, 1]])
+    assert right_padded_lengths(m) == [3, 1, 4]
+    assert right_padded_lengths(torch.tensor([[0, 1, 1, 1]])) is None  # left padding is not a suffix
+
+
+def test_segment_table_layout_and_tiles():
+    st = SegmentTable.for_padded([5, 0, 5], 200, "cpu", lengths=[200, 10, 0])
+    n = st.n_segs
+    h = st.host
+    assert h[:n].tolist() == [0, 200, 400]
+    assert h[n : 2 * n].tolist() == [200, 10, 0]
+    assert h[2 * n : 3 * n].tolist() == [5, 0, 5]
+    # tiles of 128 tokens holding any segment token: [0,200) -> 0,1 ; [200,210) -> 1 ; empty -> none
+    assert h[3 * n :].tolist() == [0, 1]
+    assert st.n_tiles == 2 and st.real_tokens == 210
+
+
+# ------------------------------------------------------------ adapter store ---
+def test_store_shapes_and_accounting():
+    c = cfg()
+    store = lf.AdapterStore(c)
+    store.load_synthetic("a0", seed=0)
+    store.load_synthetic("a1", seed=1)
+    L, H, R = c.num_layers, c.hidden_size, c.lora_rank
+    w = store.get("a0")
+    for m in c.target_modules:
+        assert w.wa[m].shape == (L, H, R) and w.wa[m].is_contiguous()
+        assert w.wb[m].shape == (L, R, H) and w.wb[m].is_contiguous()
+    assert store.memory_bytes() == len(c.target_modules) * 2 * (L * H * R * 4) * 2
+    assert not torch.equal(store.get("a0").wa["query"], store.get("a1").wa["query"])
+
+
+def test_store_synthetic_draws_match_reference_fixture():
+    g = torch.load(GOLD / "synthetic_rng.pt", weights_only=False)
+    store = lf.AdapterStore(cfg())
+    store.load_synthetic("a", seed=g["seed"])
+    for m in g["wa"]:
+        assert torch.equal(store.get("a").wa[m], g["wa"][m])
+        assert torch.equal(store.get("a").wb[m], g["wb"][m])
+
+
+def test_store_errors_name_the_adapter():
+    store = lf.AdapterStore(cfg())
+    with pytest.raises(KeyError, match="not found"):
+        store.get("nonexistent")
+    with pytest.raises(KeyError, match="nobody"):
+        store.slots(["nobody"])
+    with pytest.raises(KeyError, match="not resident"):
+        store.evict("ghost")
+
+
+def test_store_slot_reuse_and_growth_keeps_views_valid():
+    store = lf.AdapterStore(cfg(), capacity=2)
+    for i in range(5):  # grows past the initial capacity
+        store.load_synthetic(f"t{i}", seed=i)
+    w1 = store.get("t1")
+    before = w1.wa["query"].clone()
+    for i in range(5, 40):
+        store.load_synthetic(f"t{i}", seed=i)
+    assert torch.equal(store.get("t1").wa["query"], before)
+    assert store.get("t1") is w1
+    slot3 = store.slot_of("t3")
+    store.evict("t3")
+    store.load_synthetic("new", seed=99)
+    assert store.slot_of("new") == slot3  # freed slot is reused
+    assert store.adapter_ids()[-1] == "new" and "t3" not in store
+
+
+def test_store_insert_aliases_the_slot():
+    c = cfg()
+    store = lf.AdapterStore(c)
+    w = lf.LoraWeight(c)
+    torch.nn.init.normal_(w.wa["query"], std=1.0)
+    ref = w.wa["query"].clone()
+    store.insert("x", w)
+    assert torch.equal(store.get("x").wa["query"], ref)
+    w.wb["value"].fill_(3.0)  # later edits through the object reach the cache
+    slot = store.slot_of("x")
+    vi = store.module_index("value")
+    assert torch.all(store.cache[slot, vi, 1] == 3.0)
+
+
+def test_load_from_state_dict_folds_alpha_and_transposes():
+    c = cfg(rank=4)
+    L, H, R = c.num_layers, c.hidden_size, c.lora_rank
+    sd = {}
+    g = torch.Generator().manual_seed(3)
+    for m in c.target_modules:
+        for i in range(L):
+            key_a, key_b = lf.peft_key_fn("bert")(i, m)
+            sd[key_a] = torch.randn(R, H, generator=g)
+            sd[key_b] = torch.randn(H, R, generator=g)
+    store = lf.AdapterStore(c)
+    store.load_from_state_dict("p", sd, lf.peft_key_fn("bert"), lora_alpha=8)
+    w = store.get("p")
+    ka, kb = lf.peft_key_fn("bert")(1, "value")
+    assert torch.equal(w.wa["value"][1], sd[ka].t())
+    assert torch.allclose(w.wb["value"][1], sd[kb].t() * 2.0)
+    with pytest.raises(KeyError, match="has no tensor"):
+        store.load_from_state_dict("q", {}, lf.peft_key_fn("bert"))
+
+
+def test_assemblers_match_reference_fixture():
+    g = torch.load(GOLD / "assembler.pt", weights_only=False)
+    c = cfg()
+    store = lf.AdapterStore(c)
+    for aid, w in g["weights"].items():
+        lw = lf.LoraWeight(c)
+        for m in c.target_modules:
+            lw.wa[m].copy_(w["wa"][m])
+            lw.wb[m].copy_(w["wb"][m])
+        store.insert(aid, lw)
+    base = BatchAssembler(store, c).assemble_lora(g["ids"])
+    for m, layers in g["per_layer_a"].items():
+        for layer, ref in enumerate(layers):
+            assert torch.equal(torch.cat(base[layer].a[m], 0), ref)
+    fast = IndexSelectBatchAssembler(store, c)
+    assert fast.batch_index(["adapter_2", "adapter_0", "adapter_2"]).tolist() == g["batch_index"]
+    got = fast.assemble_lora(g["ids"])  # CPU store: index_select over the slot views
+    for m, (pa, pb) in g["packed"].items():
+        assert torch.equal(got[m][0], pa) and torch.equal(got[m][1], pb)
+    assert store.memory_bytes() == g["memory_bytes"]
+
+
+# ------------------------------------------------------------------- heads ---
+def test_head_store_validation_and_accounting():
+    c = cfg()
+    heads = lf.HeadStore(c, capacity_rows=2)
+    heads.load("small", torch.randn(3, 32), torch.zeros(3))
+    heads.load("big", torch.randn(10, 32), torch.zeros(10))  # forces a regrow
+    heads.load("one", torch.randn(32), torch.tensor(0.5))
+    assert heads.num_labels("small") == 3 and heads.num_labels("one") == 1
+    with pytest.raises(ValueError, match="hidden size"):
+        heads.load("bad", torch.randn(3, 33), torch.zeros(3))
+    with pytest.raises(ValueError, match="intercept"):
+        heads.load("bad", torch.randn(3, 32), torch.zeros(5))
+    with pytest.raises(KeyError, match="headless"):
+        heads.get("headless")
+    table, nl, n_max = heads.head_table(["big", "small", "one"])
+    assert nl == [10, 3, 1] and n_max == 10
+    coef, bias = heads.packed
+    off = table[0].tolist()
+    assert torch.equal(coef[off[1] : off[1] + 3], heads.get("small").coef)
+    assert heads.memory_bytes() == (3 + 10 + 1) * 33 * 4
+    batched = heads.assemble(["small", "big"])
+    assert batched.coef.shape == (2, 10, 32) and batched.num_labels == [3, 10]
+    assert torch.count_nonzero(batched.coef[0, 3:]) == 0
+    heads.evict("small")
+    assert "small" not in heads and len(heads) == 2
+    heads.load("small2", torch.randn(3, 32), torch.zeros(3))
+    assert heads.head_table(["small2"])[0][0].item() == off[1]  # freed rows reused
+
+
+# ----------------------------------------------------------------- loaders ---
+def test_peft_key_fn_naming():
+    ka, kb = lf.peft_key_fn("bert")(3, "value")
+    assert ka == "base_model.model.encoder.layer.3.attention.self.value.lora_A.weight"
+    assert kb == "base_model.model.encoder.layer.3.attention.self.value.lora_B.weight"
+    assert "query_proj" in lf.peft_key_fn("deberta-v2")(0, "query")[0]
+    assert "attention.output.dense" in lf.peft_key_fn("xlm-roberta")(0, "dense")[0]
+
+
+@pytest.mark.parametrize("conf,match", [({"r": 8, "lora_alpha": 8, "target_modules": ["query", "value"]}, "rank"),
+                                        ({"r": 4, "lora_alpha": 4, "target_modules": ["query", "key"]},
+                                         "wrong projections")])
+def test_peft_loader_rejects_mismatch(tmp_path, conf, match):
+    d = tmp_path / "adapter"
+    d.mkdir()
+    (d / "adapter_config.json").write_text(json.dumps(conf))
+    (d / "adapter_model.bin").write_bytes(b"")
+    with pytest.raises(ValueError, match=match):
+        lf.load_peft_adapter(lf.AdapterStore(cfg()), "t", str(d))
+
+
+# ------------------------------------------------------------------- misc ---
+def test_pooling_validation():
+    assert lf.validate_pooling("mean") == "mean"
+    with pytest.raises(ValueError, match="unknown pooling"):
+        lf.validate_pooling("first_token")
+
+
+def test_every_export_is_importable():
+    missing = [n for n in lf.__all__ if not hasattr(lf, n)]
+    assert not missing
+
+
+def test_reference_api_surface_is_mirrored():
+    """Every name the reference exports has a counterpart here."""
+    reference_all = ["MultiTenantEmbedder", "MultiTenantClassifier", "MultiTenantReranker", "RerankResult",
+                     "TaskPipeline", "LoraServingConfig", "load_peft_adapter", "peft_key_fn", "POOLING_STRATEGIES",
+                     "AdapterStore", "LoraWeight", "HeadStore", "LRHead", "EncoderWithLora", "HFEncoderWithLora",
+                     "BatchAssembler", "IndexSelectBatchAssembler", "BatchedLRWeights", "LayerwiseBatchedWeights",
+                     "LoraOps", "LRHeadOps", "__version__"]
+    assert not [n for n in reference_all if n not in lf.__all__]
+    for cls, methods in {
+        lf.TaskPipeline: ["from_pretrained", "register_adapter", "register_synthetic", "evict_adapter", "tenant_ids"],
+        lf.MultiTenantEmbedder: ["embed"],
+        lf.MultiTenantClassifier: ["logits", "predict_proba", "predict", "encode"],
+        lf.MultiTenantReranker: ["score", "rerank"],
+        lf.AdapterStore: ["load_from_file", "load_from_state_dict", "load_synthetic", "insert", "get", "evict",
+                          "adapter_ids", "memory_bytes", "memory_gb", "config"],
+        lf.HeadStore: ["load", "load_from_sklearn", "load_from_file", "assemble", "get", "evict", "tenant_ids",
+                       "num_labels", "memory_bytes"],
+        lf.IndexSelectBatchAssembler: ["batch_index", "assemble_lora", "to_layerwise"],
+        lf.BatchAssembler: ["assemble_lora", "assemble_lr", "assemble"],
+        lf.LoraOps: ["shrink", "expand", "output"],
+        lf.HFEncoderWithLora: ["encode_pooled", "forward", "close", "from_pretrained_serving"],
+        lf.EncoderWithLora: ["encode_pooled", "forward", "from_pretrained_serving", "position_ids"],
+    }.items():
+        assert not [m for m in methods if not hasattr(cls, m)], cls
+
+
+def test_unknown_engine_and_assembler_are_rejected():
+    class Dummy(torch.nn.Module):
+        pass
+
+    with pytest.raises(ValueError, match="unknown engine"):
+        lf.TaskPipeline(cfg(), engine="tensorrt", tokenizer=object(), model=Dummy())
+    with pytest.raises(ValueError, match="unknown assembler"):
+        lf.TaskPipeline(cfg(), assembler="magic", tokenizer=object(), model=Dummy())
+    with pytest.raises(ValueError, match="unknown pooling"):
+        lf.TaskPipeline(cfg(), pooling="first_token", tokenizer=object(), model=Dummy())
+
+
+def test_cpu_serving_path_fails_loudly():
+    """No CPU fallback: the kernels refuse CPU tensors."""
+    from latefuse_b200._native import NativeLibraryError
+
+    with pytest.raises(NativeLibraryError, match="CUDA"):
+        lf.pool_tokens(torch.randn(2, 3, 32), None, "cls")
