@@ -172,6 +172,33 @@ int lf_lora_apply(void* stream, int dtype,
                   int n_segs, const int32_t* tiles, int n_tiles,
                   void* workspace, size_t workspace_bytes, int32_t* status);
 
+/* Bytes of the static device scratch behind lf_lora_apply_noalloc (8 MiB). */
+#define LF_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/* lf_lora_apply without a caller-provided workspace, for callers that cannot
+ * allocate device memory (a host framework that owns every allocation, or code
+ * that must not call cudaMalloc while serving).  It has no counterpart in the
+ * reference.  Same arguments, contract and results as lf_lora_apply minus the
+ * workspace: the shrink output lives in a file-scope device array of
+ * LF_NOALLOC_SCRATCH_BYTES that every GPU using the library holds until the
+ * process exits.  Batches needing more scratch than that
+ * (lf_lora_workspace_bytes) are rejected with LF_ERR_WORKSPACE.  The first call
+ * on each device, with that device current, resolves the array's device
+ * address (cudaGetSymbolAddress); make it before any stream capture.  All calls
+ * share the array, so calls whose kernels can overlap on the GPU race; order
+ * them on one stream.  It allocates nothing. */
+int lf_lora_apply_noalloc(void* stream, int dtype,
+                          const void* x, int64_t ldx,
+                          void* y, int64_t ldy,
+                          int64_t n_tokens, int hidden, int rank,
+                          const void* cache_a, int64_t a_slot_stride, int64_t a_module_stride,
+                          const void* cache_b, int64_t b_slot_stride, int64_t b_module_stride,
+                          int n_slots, int n_modules, const int32_t* modules,
+                          const int64_t* y_col_offsets,
+                          const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot,
+                          int n_segs, const int32_t* tiles, int n_tiles,
+                          int32_t* status);
+
 /* ------------------------------------------------------------------------ */
 /* Adapter cache                                                            */
 /* ------------------------------------------------------------------------ */
