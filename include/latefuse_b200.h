@@ -38,10 +38,17 @@
  *                    LoraWeight.wa[m][layer] / wb[m][layer] layouts
  *                    (src/latefuse/weights/store.py:22-39), so a per-tenant
  *                    adapter is addressed in place, never gathered.
- *   tiles            optional device int32 list of the row tiles (tokens
- *                    [i*LF_TILE_TOKENS, (i+1)*LF_TILE_TOKENS)) that hold any
- *                    segment token, so tiles of pure padding are never
- *                    launched; NULL (n_tiles = 0) means every tile.
+ *   tiles            optional device array of n_tiles tile records, 16-byte
+ *                    aligned, one per row tile (tokens [i*LF_TILE_TOKENS,
+ *                    (i+1)*LF_TILE_TOKENS)) that holds any segment token:
+ *                    int32 {i, index of the first segment overlapping the
+ *                    tile, number of segments overlapping it, slot of that
+ *                    first segment}.  Tiles of pure padding are then never
+ *                    launched and each tile's loads issue after one read.
+ *                    NULL (n_tiles = 0) means every tile (segments found by
+ *                    binary search).  A record that disagrees with the
+ *                    segment arrays gives its tile no delta and sets
+ *                    LF_STATUS_BAD_SEGMENT.
  *   status           optional device int32; kernels OR LF_STATUS_* bits into
  *                    it instead of faulting on a bad slot id, a bad segment or
  *                    a wait that timed out.

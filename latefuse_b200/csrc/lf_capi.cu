@@ -97,6 +97,8 @@ static int check_tiles(const char* fn, const int32_t* tiles, int n_tiles, int64_
   const int64_t all_tiles = (n_tokens + LF_TILE_TOKENS - 1) / LF_TILE_TOKENS;
   if (n_tiles < 0 || n_tiles > all_tiles || (tiles == nullptr && n_tiles != 0))
     return set_error(LF_ERR_INVALID, "%s: tile list of %d entries for %lld tiles", fn, n_tiles, (long long)all_tiles);
+  if (tiles != nullptr && (reinterpret_cast<uintptr_t>(tiles) & 15u) != 0)
+    return set_error(LF_ERR_INVALID, "%s: tile records must be 16-byte aligned", fn);
   return LF_OK;
 }
 

@@ -36,35 +36,70 @@ struct TileSegs {
   int16_t hi[kMaxSegPerTile];
 };
 
-__device__ void build_tile_segments(TileSegs* ts, int64_t row0, int64_t n_tokens,
+// Where a CTA's 128-token tile starts, and (with a caller-built tile record)
+// which segments overlap it and the slot of the first one, so that every load
+// of the tile can be issued after a single 16-byte read.
+struct TileInfo {
+  int64_t row0;
+  int32_t first;  // first overlapping segment (record path), -1 otherwise
+  int32_t count;  // number of overlapping segments (record path)
+  int32_t slot0;  // slot of the first overlapping segment (record path)
+};
+
+__device__ __forceinline__ TileInfo load_tile_info(const int32_t* __restrict__ tiles) {
+  if (tiles != nullptr) {
+    const int4 r = __ldg(reinterpret_cast<const int4*>(tiles) + blockIdx.y);
+    return {int64_t(r.x) * kTileM, r.y, r.z, r.w};
+  }
+  return {int64_t(blockIdx.y) * kTileM, -1, 0, -1};
+}
+
+__device__ __forceinline__ void add_segment(TileSegs* ts, int& cnt, int64_t s, int64_t l, int32_t slot,
+                                            int64_t row0, int64_t row_end, int64_t n_tokens, int n_slots,
+                                            int32_t* status) {
+  if (l <= 0) {
+    if (l < 0) set_status(status, LF_STATUS_BAD_SEGMENT);
+    return;
+  }
+  if (s < 0 || s + l > n_tokens) set_status(status, LF_STATUS_BAD_SEGMENT);
+  const int64_t lo = max(s, row0), hi = min(s + l, row_end);
+  if (lo >= hi) return;
+  if (slot < 0 || slot >= n_slots) {
+    set_status(status, LF_STATUS_BAD_SLOT);
+    return;
+  }
+  if (cnt < kMaxSegPerTile) {
+    ts->slot[cnt] = slot;
+    ts->lo[cnt] = static_cast<int16_t>(lo - row0);
+    ts->hi[cnt] = static_cast<int16_t>(hi - row0);
+    ++cnt;
+  }
+}
+
+// Segments overlapping the tile, into smem.  With a tile record the overlapping
+// segments are named directly (their loads issue together); without one, a
+// binary search over the sorted segment starts finds the first.
+__device__ void build_tile_segments(TileSegs* ts, const TileInfo& ti, int64_t n_tokens,
                                     const int32_t* __restrict__ seg_start,
                                     const int32_t* __restrict__ seg_len,
                                     const int32_t* __restrict__ seg_slot, int n_segs, int n_slots,
                                     int32_t* status) {
+  const int64_t row0 = ti.row0;
   const int64_t row_end = min(row0 + kTileM, n_tokens);
   int cnt = 0;
-  int g = first_seg_ending_after(seg_start, seg_len, n_segs, row0);
-  for (; g < n_segs; ++g) {
-    const int64_t s = seg_start[g];
-    const int64_t l = seg_len[g];
-    if (s >= row_end) break;
-    if (l <= 0) {
-      if (l < 0) set_status(status, LF_STATUS_BAD_SEGMENT);
-      continue;
+  if (ti.first >= 0) {
+    if (ti.count < 0 || int64_t(ti.first) + ti.count > n_segs) {
+      set_status(status, LF_STATUS_BAD_SEGMENT);
+      ts->n = 0;
+      return;
     }
-    if (s < 0 || s + l > n_tokens) set_status(status, LF_STATUS_BAD_SEGMENT);
-    const int64_t lo = max(s, row0), hi = min(s + l, row_end);
-    if (lo >= hi) continue;
-    const int32_t slot = seg_slot[g];
-    if (slot < 0 || slot >= n_slots) {
-      set_status(status, LF_STATUS_BAD_SLOT);
-      continue;
-    }
-    if (cnt < kMaxSegPerTile) {
-      ts->slot[cnt] = slot;
-      ts->lo[cnt] = static_cast<int16_t>(lo - row0);
-      ts->hi[cnt] = static_cast<int16_t>(hi - row0);
-      ++cnt;
+    for (int g = ti.first; g < ti.first + ti.count; ++g)
+      add_segment(ts, cnt, seg_start[g], seg_len[g], seg_slot[g], row0, row_end, n_tokens, n_slots, status);
+  } else {
+    for (int g = first_seg_ending_after(seg_start, seg_len, n_segs, row0); g < n_segs; ++g) {
+      const int64_t st = seg_start[g];
+      if (st >= row_end) break;
+      add_segment(ts, cnt, st, seg_len[g], seg_slot[g], row0, row_end, n_tokens, n_slots, status);
     }
   }
   ts->n = cnt;
@@ -119,7 +154,6 @@ lora_shrink_tc_kernel(const __grid_constant__ ShrinkTcParams p) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int csize = gridDim.x;                 // cluster size (split-K factor)
   const int crank = blockIdx.x;                // == %cluster_ctarank for cluster dims (csize,1,1)
-  const int64_t row0 = int64_t(p.tiles != nullptr ? p.tiles[blockIdx.y] : int32_t(blockIdx.y)) * kTileM;
   const int kchunk = p.kchunk;
   const int nkb = kchunk / kKBlock;
   const int k0 = crank * kchunk;
@@ -140,19 +174,37 @@ lora_shrink_tc_kernel(const __grid_constant__ ShrinkTcParams p) {
 
   const uint32_t tmem_cols = p.tmem_cols;
   bool ok = true;
+  int32_t* s_pref = reinterpret_cast<int32_t*>(&bars[4]);  // 1 if the first A was prefetched
+  const TileInfo ti = load_tile_info(p.tiles);
+  const int64_t row0 = ti.row0;
+
+  auto issue_a = [&](int32_t slot) {
+    mbar_arrive_expect_tx(bar_a, n_mod * nkb * S::kABox);
+    for (int m = 0; m < n_mod; ++m)
+      for (int kb = 0; kb < nkb; ++kb)
+        tma_load_3d(s_a + (m * nkb + kb) * S::kABox, &p.a_map[m], bar_a, 0, k0 + kb * kKBlock, slot);
+  };
 
   if (tid == 0) {
     mbar_init(bar_x, 1);
     mbar_init(bar_a, 1);
     mbar_init(bar_mma, 1);
     fence_mbar_init();
-    prefetch_tmap(&p.x_map);
     // x chunk: rows [row0, row0+128) x cols [k0, k0+kchunk); rows past n_tokens read as 0
     mbar_arrive_expect_tx(bar_x, nkb * S::kXBox);
     for (int kb = 0; kb < nkb; ++kb)
       tma_load_2d(s_x + kb * S::kXBox, &p.x_map, bar_x, k0 + kb * kKBlock, int32_t(row0));
-    build_tile_segments(segs, row0, p.n_tokens, p.seg_start, p.seg_len, p.seg_slot, p.n_segs,
+    // the record names the first segment's slot: start its A factor now
+    const bool pref = ti.first >= 0 && ti.count > 0 && ti.slot0 >= 0 && ti.slot0 < p.n_slots;
+    if (pref) issue_a(ti.slot0);
+    build_tile_segments(segs, ti, p.n_tokens, p.seg_start, p.seg_len, p.seg_slot, p.n_segs,
                         p.n_slots, p.status);
+    if (pref && (segs->n == 0 || segs->slot[0] != ti.slot0)) {
+      // the record disagrees with the segment table: no delta for this tile
+      if (segs->n != 0) set_status(p.status, LF_STATUS_BAD_SEGMENT);
+      segs->n = 0;
+    }
+    *s_pref = pref ? 1 : 0;
   }
   // zero the fp32 partials (rows in no segment contribute 0) and the R=8 pad
   for (int i = tid; i < kTileM * n_mod * RP; i += blockDim.x) s_part[i] = 0.f;
@@ -161,7 +213,7 @@ lora_shrink_tc_kernel(const __grid_constant__ ShrinkTcParams p) {
     for (int i = tid; i < 1024 / 16; i += blockDim.x) z[i] = make_uint4(0, 0, 0, 0);
     fence_proxy_async_smem();
   }
-  if (warp == 0) {
+  if (warp == 1) {
     __syncwarp();
     tmem_alloc(smem_u32(tmem_slot), tmem_cols);
   }
@@ -169,18 +221,14 @@ lora_shrink_tc_kernel(const __grid_constant__ ShrinkTcParams p) {
   tc_fence_after();
   const uint32_t taddr = *tmem_slot;
   const int nseg = segs->n;
+  const bool prefetched = *s_pref != 0;
 
   constexpr uint32_t idesc = umma_idesc_f16(DT<T>::umma_fmt, kTileM, RP, /*a_mn=*/0, /*b_mn=*/1);
   using A = MnOperand<R>;
 
   for (int g = 0; g < nseg; ++g) {
     if (tid == 0) {
-      const int32_t slot = segs->slot[g];
-      mbar_arrive_expect_tx(bar_a, n_mod * nkb * S::kABox);
-      for (int m = 0; m < n_mod; ++m)
-        for (int kb = 0; kb < nkb; ++kb)
-          tma_load_3d(s_a + (m * nkb + kb) * S::kABox, &p.a_map[m], bar_a, 0, k0 + kb * kKBlock,
-                      slot);
+      if (g > 0 || !prefetched) issue_a(segs->slot[g]);
       bool w = mbar_wait(bar_a, g & 1);
       if (g == 0) w = w && mbar_wait(bar_x, 0);
       if (!w) {
@@ -241,8 +289,9 @@ lora_shrink_tc_kernel(const __grid_constant__ ShrinkTcParams p) {
   }
 
   if (nseg == 0 && tid == 0) {
-    // the x tile was never consumed: its TMA writes must land before the CTA exits
+    // loads that nothing consumed must land before the CTA exits
     if (!mbar_wait(bar_x, 0)) set_status(p.status, LF_STATUS_TIMEOUT);
+    if (prefetched && !mbar_wait(bar_a, 0)) set_status(p.status, LF_STATUS_TIMEOUT);
   }
   __syncthreads();
 
@@ -279,7 +328,7 @@ lora_shrink_tc_kernel(const __grid_constant__ ShrinkTcParams p) {
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 1) {
     __syncwarp();
     tmem_dealloc(taddr, tmem_cols);
   }
@@ -319,7 +368,8 @@ lora_expand_tc_kernel(const __grid_constant__ ExpandTcParams p) {
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ct = blockIdx.x;
-  const int64_t row0 = int64_t(p.tiles != nullptr ? p.tiles[blockIdx.y] : int32_t(blockIdx.y)) * kTileM;
+  const TileInfo ti = load_tile_info(p.tiles);  // every thread: row0 is needed for the U loads
+  const int64_t row0 = ti.row0;
   const int m = blockIdx.z;
   const int32_t col0 = int32_t(p.y_col_off[m] + int64_t(ct) * NT);
   const bool acc_y = p.accumulate != 0;
@@ -335,6 +385,13 @@ lora_expand_tc_kernel(const __grid_constant__ ExpandTcParams p) {
   const uint32_t bar_y = smem_u32(&bars[0]), bar_b = smem_u32(&bars[1]), bar_mma = smem_u32(&bars[2]);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(&bars[3]);
   int32_t* s_fail = reinterpret_cast<int32_t*>(&bars[4]);
+  int32_t* s_pref = reinterpret_cast<int32_t*>(&bars[4]) + 1;  // 1 if the first B was prefetched
+
+  auto issue_b = [&](int32_t slot) {
+    mbar_arrive_expect_tx(bar_b, E::kNBox * E::kBBox);
+    for (int j = 0; j < E::kNBox; ++j)
+      tma_load_3d(s_b + j * E::kBBox, &p.b_map[m], bar_b, ct * NT + j * 64, 0, slot);
+  };
 
   if (tid == 0) {
     *s_fail = 0;
@@ -348,14 +405,35 @@ lora_expand_tc_kernel(const __grid_constant__ ExpandTcParams p) {
       for (int j = 0; j < E::kNBox; ++j)
         tma_load_2d(s_y + j * E::kYBox, &p.y_map, bar_y, col0 + j * 64, int32_t(row0));
     }
-    build_tile_segments(segs, row0, p.n_tokens, p.seg_start, p.seg_len, p.seg_slot, p.n_segs,
+    // the record names the first segment's slot: start its B factor now
+    const bool pref = ti.first >= 0 && ti.count > 0 && ti.slot0 >= 0 && ti.slot0 < p.n_slots;
+    if (pref) issue_b(ti.slot0);
+    build_tile_segments(segs, ti, p.n_tokens, p.seg_start, p.seg_len, p.seg_slot, p.n_segs,
                         p.n_slots, p.status);
+    if (pref && (segs->n == 0 || segs->slot[0] != ti.slot0)) {
+      // the record disagrees with the segment table: no delta for this tile
+      if (segs->n != 0) set_status(p.status, LF_STATUS_BAD_SEGMENT);
+      segs->n = 0;
+    }
+    *s_pref = pref ? 1 : 0;
+  }
+  // This thread's U row, read now (in parallel with the y / B loads).  Every row
+  // of a launched tile was written by the shrink (0 for rows in no segment).
+  const int row = warp * 32 + lane;     // this thread's tile row (U operand and epilogue)
+  const int64_t t = row0 + row;
+  uint4 u_reg[RP / 8];
+  {
+    const T* __restrict__ u_row = reinterpret_cast<const T*>(p.u) + (int64_t(m) * p.n_tokens + t) * R;
+#pragma unroll
+    for (int kc = 0; kc < RP / 8; ++kc)
+      u_reg[kc] = (t < p.n_tokens && kc * 8 < R) ? *reinterpret_cast<const uint4*>(u_row + kc * 8)
+                                                 : make_uint4(0, 0, 0, 0);
   }
   if (R == 8) {
     uint4* z = reinterpret_cast<uint4*>(gbase + (s_z - base));
     for (int i = tid; i < E::kZBytes / 16; i += blockDim.x) z[i] = make_uint4(0, 0, 0, 0);
   }
-  if (warp == 0) {
+  if (warp == 1) {
     __syncwarp();
     tmem_alloc(smem_u32(tmem_slot), NT);
   }
@@ -363,33 +441,24 @@ lora_expand_tc_kernel(const __grid_constant__ ExpandTcParams p) {
   tc_fence_after();
   const uint32_t taddr = *tmem_slot;
   const int nseg = segs->n;
+  const bool prefetched = *s_pref != 0;
 
   constexpr uint32_t idesc = umma_idesc_f16(DT<T>::umma_fmt, kTileM, NT, /*a_mn=*/0, /*b_mn=*/1);
-  const int row = warp * 32 + lane;     // this thread's tile row (U operand and epilogue)
-  const int64_t t = row0 + row;
-  const T* __restrict__ u_m = reinterpret_cast<const T*>(p.u) + int64_t(m) * p.n_tokens * R;
 
   for (int g = 0; g < nseg; ++g) {
     if (g > 0) {
       // the previous MMA must have finished reading the U and B buffers
       if (!mbar_wait(bar_mma, (g - 1) & 1)) atomicOr(s_fail, 1);
     }
-    if (tid == 0) {
-      mbar_arrive_expect_tx(bar_b, E::kNBox * E::kBBox);
-      for (int j = 0; j < E::kNBox; ++j)
-        tma_load_3d(s_b + j * E::kBBox, &p.b_map[m], bar_b, ct * NT + j * 64, 0, segs->slot[g]);
-    }
+    if (tid == 0 && (g > 0 || !prefetched)) issue_b(segs->slot[g]);
     // U operand, K-major without swizzle: core matrices of 8 rows x 16 bytes;
     // K chunks (8 elements) are LBO = 128 B apart, 8-row groups SBO = RP*16 B apart.
     {
       const bool mine = row >= segs->lo[g] && row < segs->hi[g];
       uint8_t* ub = gbase + (s_u - base) + (row >> 3) * (RP * 16) + (row & 7) * 16;
 #pragma unroll
-      for (int kc = 0; kc < RP / 8; ++kc) {
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (mine && kc * 8 < R) v = *reinterpret_cast<const uint4*>(u_m + t * R + kc * 8);
-        *reinterpret_cast<uint4*>(ub + kc * 128) = v;
-      }
+      for (int kc = 0; kc < RP / 8; ++kc)
+        *reinterpret_cast<uint4*>(ub + kc * 128) = mine ? u_reg[kc] : make_uint4(0, 0, 0, 0);
     }
     fence_proxy_async_smem();
     __syncthreads();
@@ -428,6 +497,10 @@ lora_expand_tc_kernel(const __grid_constant__ ExpandTcParams p) {
     // give copies still in flight one more bounded chance to land before teardown
     if (nseg > 0) mbar_wait(bar_mma, (nseg - 1) & 1);
     if (acc_y) mbar_wait(bar_y, 0);
+  }
+  if (nseg == 0 && prefetched && tid == 0) {
+    // a prefetched B that no MMA consumed must land before the CTA exits
+    if (!mbar_wait(bar_b, 0)) set_status(p.status, LF_STATUS_TIMEOUT);
   }
   tc_fence_after();
   __syncwarp();
@@ -474,7 +547,7 @@ lora_expand_tc_kernel(const __grid_constant__ ExpandTcParams p) {
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 1) {
     __syncwarp();
     tmem_dealloc(taddr, NT);
   }

@@ -35,24 +35,25 @@ class SegmentTable:
     tokens first).  Skipping padding changes no real token's output, because
     padded keys are masked out of attention and every other op is per token.
 
-    The table also lists the 128-token row tiles that hold any segment token, so
-    the kernels never launch work for tiles of pure padding.  Everything lives in
-    one int32 buffer, ``[starts | lengths | slots | tiles]``, copied to the device
-    once per batch.
+    The table also carries one record per 128-token row tile that holds any
+    segment token -- ``{tile, first overlapping segment, number of overlapping
+    segments, slot of the first}`` -- so the kernels launch nothing for tiles of
+    pure padding and issue every load of a tile after one 16-byte read.
+    Everything lives in one int32 buffer, ``[records | starts | lengths | slots]``,
+    copied to the device once per batch.
     """
 
-    def __init__(self, starts, lengths, slots, n_tokens: int, device: torch.device):
+    def __init__(self, starts, lengths, slots, n_tokens: int, device: torch.device, records: bool = True):
         starts, lengths, slots = list(starts), list(lengths), list(slots)
         if not (len(starts) == len(lengths) == len(slots)):
             raise ValueError("starts, lengths and slots must have equal length")
         self.n_segs = len(starts)
         self.n_tokens = int(n_tokens)
         self.device = torch.device(device)
-        tile = nat.TILE_TOKENS
-        tiles = sorted({t for s, n in zip(starts, lengths) if n > 0
-                        for t in range(s // tile, (s + n - 1) // tile + 1)})
-        self.n_tiles = len(tiles)
-        self.host = torch.tensor(starts + lengths + slots + tiles, dtype=torch.int32)
+        self.use_records = records
+        records = _tile_records(starts, lengths, slots) if records else []
+        self.n_tiles = len(records) // 4
+        self.host = torch.tensor(records + starts + lengths + slots, dtype=torch.int32)
         if self.device.type == "cuda":
             self.table = self.host.pin_memory().to(self.device, non_blocking=True)
         else:
@@ -67,10 +68,33 @@ class SegmentTable:
         return cls([b * seq_len for b in range(B)], lens, slots, B * seq_len, device)
 
     def ptrs(self) -> tuple[int, int, int, int, int]:
-        """(seg_start, seg_len, seg_slot, tiles, n_tiles) device pointers/count for the C ABI."""
+        """(seg_start, seg_len, seg_slot, tile records, n_tiles) device pointers/count for the C ABI."""
         base = self.table.data_ptr()
+        r = 16 * self.n_tiles
         n = self.n_segs
-        return base, base + 4 * n, base + 8 * n, base + 12 * n, self.n_tiles
+        if not self.use_records:
+            return base, base + 4 * n, base + 8 * n, None, 0
+        return base + r, base + r + 4 * n, base + r + 8 * n, base, self.n_tiles
+
+
+def _tile_records(starts, lengths, slots) -> list[int]:
+    """Flattened ``{tile, first segment, segment count, first slot}`` records of the
+    tiles that hold segment tokens, in tile order (segments sorted by start)."""
+    tile = nat.TILE_TOKENS
+    first: dict[int, int] = {}
+    count: dict[int, int] = {}
+    for g, (s, n) in enumerate(zip(starts, lengths)):
+        if n <= 0:
+            continue
+        for t in range(s // tile, (s + n - 1) // tile + 1):
+            if t not in first:
+                first[t] = g
+                count[t] = 0
+            count[t] = g - first[t] + 1
+    out: list[int] = []
+    for t in sorted(first):
+        out += [t, first[t], count[t], slots[first[t]]]
+    return out
 
 
 # ---------------------------------------------------------------------------

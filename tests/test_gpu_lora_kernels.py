@@ -45,9 +45,10 @@ def segments_padded(B, S, n_slots, seed, lengths=None):
     return [(b * S, lens[b], slots[b]) for b in range(B)]
 
 
-def run_apply(x, y, fc, segs, modules, offs):
+def run_apply(x, y, fc, segs, modules, offs, records=True):
     dev = x.device
-    st = SegmentTable([s for s, _, _ in segs], [l for _, l, _ in segs], [k for _, _, k in segs], x.shape[0], dev)
+    st = SegmentTable([s for s, _, _ in segs], [l for _, l, _ in segs], [k for _, _, k in segs], x.shape[0], dev,
+                      records=records)
     ws = torch.empty(workspace_bytes(x.dtype, x.shape[0], fc.rank, len(modules)), dtype=torch.uint8, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     out = y.clone()
@@ -251,3 +252,38 @@ def test_large_cfg2_shape_vs_gathered_bmm(cuda):
     d2 = ref.float() - y.float()
     rel = (d1 - d2).norm() / d2.norm()
     assert rel.item() < 2e-2, rel.item()
+
+
+@pytest.mark.parametrize("S", [100, 512])
+def test_tc_tile_records_equal_segment_search(cuda, S):
+    """Per-tile records (one read per CTA) and the binary search over the segment
+    table (no records) give bit-identical results."""
+    dtype = torch.bfloat16
+    B, H, R, n_slots = 4, 256, 16, 6
+    fc, _, _ = make_cache(n_slots, 3, H, R, dtype, cuda, seed=61)
+    g = torch.Generator().manual_seed(S)
+    lengths = torch.randint(1, S + 1, (B,), generator=g).tolist()
+    x = torch.randn(B * S, H, generator=g).to(dtype).to(cuda)
+    y = torch.randn(B * S, 3 * H, generator=g).to(dtype).to(cuda)
+    segs = segments_padded(B, S, n_slots, seed=S, lengths=lengths)
+    a = run_apply(x, y, fc, segs, [0, 1, 2], [0, H, 2 * H], records=True)
+    b = run_apply(x, y, fc, segs, [0, 1, 2], [0, H, 2 * H], records=False)
+    assert torch.equal(a, b)
+
+
+def test_record_that_disagrees_with_segments_is_flagged(cuda):
+    dtype = torch.bfloat16
+    T, H, R = 256, 256, 16
+    fc, _, _ = make_cache(4, 1, H, R, dtype, cuda)
+    x = torch.randn(T, H, device=cuda, dtype=dtype)
+    y = torch.randn(T, H, device=cuda, dtype=dtype)
+    st = SegmentTable([0, 128], [128, 128], [1, 2], T, cuda)
+    st.table[7] = 3  # tile 1's record names slot 3, the segment table says slot 2
+    ws = torch.empty(workspace_bytes(dtype, T, R, 1), dtype=torch.uint8, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = y.clone()
+    lora_apply(x, out, fc, st, [0], [0], ws, status)
+    torch.cuda.synchronize()
+    assert status.item() & 2
+    assert torch.equal(out[128:], y[128:])       # that tile got no delta
+    assert not torch.equal(out[:128], y[:128])   # the consistent tile did

@@ -48,14 +48,18 @@ def test_right_padded_lengths():
 
 def test_segment_table_layout_and_tiles():
     st = SegmentTable.for_padded([5, 0, 5], 200, "cpu", lengths=[200, 10, 0])
-    n = st.n_segs
-    h = st.host
-    assert h[:n].tolist() == [0, 200, 400]
-    assert h[n : 2 * n].tolist() == [200, 10, 0]
-    assert h[2 * n : 3 * n].tolist() == [5, 0, 5]
-    # tiles of 128 tokens holding any segment token: [0,200) -> 0,1 ; [200,210) -> 1 ; empty -> none
-    assert h[3 * n :].tolist() == [0, 1]
-    assert st.n_tiles == 2 and st.real_tokens == 210
+    h = st.host.tolist()
+    # tile records first (16-byte aligned): {tile, first segment, count, slot of first}
+    # [0,200) -> tiles 0,1 ; [200,210) -> tile 1 ; the empty segment -> none
+    assert st.n_tiles == 2
+    assert h[:8] == [0, 0, 1, 5, 1, 0, 2, 5]
+    assert h[8:11] == [0, 200, 400] and h[11:14] == [200, 10, 0] and h[14:17] == [5, 0, 5]
+    assert st.real_tokens == 210
+    s, l, k, t, nt = st.ptrs()
+    assert (t - st.table.data_ptr()) == 0 and s - t == 32 and nt == 2
+    # several short segments in one tile
+    st2 = SegmentTable([0, 10, 130], [10, 100, 5], [1, 2, 3], 200, "cpu")
+    assert st2.host.tolist()[:8] == [0, 0, 2, 1, 1, 2, 1, 3]
 
 
 # ------------------------------------------------------------ adapter store ---
