@@ -74,6 +74,7 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--ranks", default="8,16,64", help="--mode op: LoRA ranks to measure")
+    ap.add_argument("--persistent", type=int, default=1, help="0: per-tile expand kernel only")
     return ap.parse_args()
 
 
@@ -423,11 +424,12 @@ def run_op(args):
     with 10,000 resident adapters and Zipf(1.1) tenants.  Reports the delta's
     achieved HBM bandwidth (algorithmic bytes 3*T*H*2 + U*4*H*r) and the whole op."""
     from latefuse_b200 import _native as nat
-    from latefuse_b200.lora import FactorCache, SegmentTable, lora_apply, workspace_bytes
+    from latefuse_b200.lora import FactorCache, SegmentTable, lora_apply, lora_expand, lora_shrink, workspace_bytes
     from latefuse_b200.synthetic import zipf_tenants
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    nat.set_option(nat.LF_OPT_PERSISTENT, args.persistent)
     B, S, H = 64, 256, 1024
     T = B * S
     g = torch.Generator(device=dev).manual_seed(args.seed)
@@ -467,6 +469,22 @@ def run_op(args):
         torch.cuda.synchronize()
         delta_ms = statistics.median(a.elapsed_time(b) for a, b in ev)
         op_ms = statistics.median(a.elapsed_time(b) for a, b in ops)
+        launches = (nat.launch_count() - n0) / args.steps
+        # each launch of the delta on its own (same inputs, L2 flushed before each)
+        u = ws[: T * R * 2].view(torch.bfloat16).view(1, T, R)
+        sh, ex = [], []
+        for _ in range(args.steps):
+            for fn, acc in ((lambda: lora_shrink(x, u, fc, segs, [0]), sh),
+                            (lambda: lora_expand(u, y, fc, segs, [0], [0], True), ex)):
+                flush.zero_()
+                a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a_.record()
+                fn()
+                b_.record()
+                acc.append((a_, b_))
+        torch.cuda.synchronize()
+        shrink_ms = statistics.median(a.elapsed_time(b) for a, b in sh)
+        expand_ms = statistics.median(a.elapsed_time(b) for a, b in ex)
         U = len(set(slots))
         algo = 3 * T * H * 2 + U * 4 * H * R
         flops = 2 * T * H * H + 4 * T * H * R
@@ -474,7 +492,10 @@ def run_op(args):
         out[f"r{R}"] = {"delta_us": delta_ms * 1e3, "delta_gbs": algo / (delta_ms * 1e-3) / 1e9,
                         "delta_frac_of_hbm": algo / (delta_ms * 1e-3) / 1e9 / peak, "algorithmic_bytes": algo,
                         "unique_tenants": U, "op_us": op_ms * 1e3, "op_tflops": flops / (op_ms * 1e-3) / 1e12,
-                        "launches_per_op": (nat.launch_count() - n0) / args.steps}
+                        "shrink_us": shrink_ms * 1e3, "shrink_gbs": (T * H * 2 + U * 2 * H * R) / (shrink_ms * 1e-3) / 1e9,
+                        "expand_us": expand_ms * 1e3,
+                        "expand_gbs": (2 * T * H * 2 + U * 2 * H * R) / (expand_ms * 1e-3) / 1e9,
+                        "launches_per_op": launches}
         del cache, x, y, w, ws, flush
         torch.cuda.empty_cache()
     print(json.dumps({"mode": "op", "workload": "Y = X W + (X A_t) B_t, X (64,256,1024) bf16, "

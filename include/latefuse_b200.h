@@ -45,6 +45,8 @@
  *                    tile, number of segments overlapping it, slot of that
  *                    first segment}.  Tiles of pure padding are then never
  *                    launched and each tile's loads issue after one read.
+ *                    Records of tiles with exactly one segment come first;
+ *                    the last n_multi records are the tiles with several.
  *                    NULL (n_tiles = 0) means every tile (segments found by
  *                    binary search).  A record that disagrees with the
  *                    segment arrays gives its tile no delta and sets
@@ -96,6 +98,7 @@ extern "C" {
 #define LF_OPT_SHRINK_CLUSTER 2 /* 0 = automatic, else the shrink's split-K cluster size */
 #define LF_OPT_REQUIRE_TC 3     /* 1: fail with LF_ERR_UNSUPPORTED instead of running the
                                    CUDA-core kernels where the tcgen05 kernels do not apply */
+#define LF_OPT_PERSISTENT 4     /* 0: do not use the persistent expand kernel (default 1) */
 
 /* ------------------------------------------------------------------------ */
 /* library                                                                   */
@@ -136,7 +139,7 @@ int lf_lora_shrink(void* stream, int dtype,
                    const void* cache_a, int64_t a_slot_stride, int64_t a_module_stride,
                    int n_slots, int n_modules, const int32_t* modules,
                    const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot,
-                   int n_segs, const int32_t* tiles, int n_tiles,
+                   int n_segs, const int32_t* tiles, int n_tiles, int n_multi,
                    void* u, int32_t* status);
 
 /* Expand: for every token t and op-module m,
@@ -156,7 +159,7 @@ int lf_lora_expand(void* stream, int dtype,
                    int n_slots, int n_modules, const int32_t* modules,
                    const int64_t* y_col_offsets,
                    const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot,
-                   int n_segs, const int32_t* tiles, int n_tiles,
+                   int n_segs, const int32_t* tiles, int n_tiles, int n_multi,
                    int accumulate, int32_t* status);
 
 /* Device workspace bytes lf_lora_apply needs for these sizes. */
@@ -176,7 +179,7 @@ int lf_lora_apply(void* stream, int dtype,
                   int n_slots, int n_modules, const int32_t* modules,
                   const int64_t* y_col_offsets,
                   const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot,
-                  int n_segs, const int32_t* tiles, int n_tiles,
+                  int n_segs, const int32_t* tiles, int n_tiles, int n_multi,
                   void* workspace, size_t workspace_bytes, int32_t* status);
 
 /* Bytes of the static device scratch behind lf_lora_apply_noalloc (8 MiB). */
@@ -203,7 +206,7 @@ int lf_lora_apply_noalloc(void* stream, int dtype,
                           int n_slots, int n_modules, const int32_t* modules,
                           const int64_t* y_col_offsets,
                           const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot,
-                          int n_segs, const int32_t* tiles, int n_tiles,
+                          int n_segs, const int32_t* tiles, int n_tiles, int n_multi,
                           int32_t* status);
 
 /* ------------------------------------------------------------------------ */

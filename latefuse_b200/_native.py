@@ -24,6 +24,7 @@ LF_POOL = {"cls": 0, "mean": 1, "none": 2}
 LF_OPT_FORCE_SIMT = 1
 LF_OPT_SHRINK_CLUSTER = 2
 LF_OPT_REQUIRE_TC = 3
+LF_OPT_PERSISTENT = 4
 
 STATUS_BITS = {
     1: "segment names a slot outside the cache",
@@ -42,22 +43,22 @@ SIGNATURES: dict[str, tuple] = {
     "lf_lora_shrink": (c_int, [
         c_void_p, c_int, c_void_p, c_int64, c_int64, c_int, c_int,
         c_void_p, c_int64, c_int64, c_int, c_int, POINTER(c_int32),
-        c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p]),
+        c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "lf_lora_expand": (c_int, [
         c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int,
         c_void_p, c_int64, c_int64, c_int, c_int, POINTER(c_int32), POINTER(c_int64),
-        c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p]),
+        c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_void_p]),
     "lf_lora_workspace_bytes": (c_size_t, [c_int, c_int64, c_int, c_int]),
     "lf_lora_apply": (c_int, [
         c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_int,
         c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int,
         POINTER(c_int32), POINTER(c_int64), c_void_p, c_void_p, c_void_p, c_int,
-        c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+        c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "lf_lora_apply_noalloc": (c_int, [
         c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_int,
         c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int,
         POINTER(c_int32), POINTER(c_int64), c_void_p, c_void_p, c_void_p, c_int,
-        c_void_p, c_int, c_void_p]),
+        c_void_p, c_int, c_int, c_void_p]),
     "lf_cache_gather": (c_int, [
         c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_int, c_void_p, c_int,
         c_void_p, c_void_p]),

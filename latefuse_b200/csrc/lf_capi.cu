@@ -17,6 +17,7 @@ static std::atomic<uint64_t> g_launches{0};
 static std::atomic<int> g_force_simt{0};
 static std::atomic<int> g_shrink_cluster{0};
 static std::atomic<int> g_require_tc{0};
+static std::atomic<int> g_persistent{1};
 
 int set_error(int code, const char* fmt, ...) {
   va_list ap;
@@ -93,8 +94,10 @@ static int check_common(const char* fn, int dtype, int64_t n_tokens, int hidden,
   return LF_OK;
 }
 
-static int check_tiles(const char* fn, const int32_t* tiles, int n_tiles, int64_t n_tokens) {
+static int check_tiles(const char* fn, const int32_t* tiles, int n_tiles, int n_multi, int64_t n_tokens) {
   const int64_t all_tiles = (n_tokens + LF_TILE_TOKENS - 1) / LF_TILE_TOKENS;
+  if (n_multi < 0 || n_multi > n_tiles)
+    return set_error(LF_ERR_INVALID, "%s: n_multi %d not in [0, n_tiles]", fn, n_multi);
   if (n_tiles < 0 || n_tiles > all_tiles || (tiles == nullptr && n_tiles != 0))
     return set_error(LF_ERR_INVALID, "%s: tile list of %d entries for %lld tiles", fn, n_tiles, (long long)all_tiles);
   if (tiles != nullptr && (reinterpret_cast<uintptr_t>(tiles) & 15u) != 0)
@@ -135,7 +138,7 @@ static int shrink_impl(cudaStream_t stream, int dtype, const void* x, int64_t ld
                        int hidden, int rank, const void* cache_a, int64_t a_slot_stride,
                        int64_t a_module_stride, int n_slots, int n_modules, const int32_t* modules,
                        const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot,
-                       int n_segs, const int32_t* tiles, int n_tiles, void* u, int32_t* status) {
+                       int n_segs, const int32_t* tiles, int n_tiles, int n_multi, void* u, int32_t* status) {
   const int es = elem_size(dtype);
   const bool tc = !option_force_simt() && dtype != LF_DTYPE_F32 && tc_rank(rank) && hidden % 64 == 0 &&
                   aligned16(x) && aligned16(cache_a) && aligned16(u) && (ldx * es) % 16 == 0 &&
@@ -163,8 +166,48 @@ static int shrink_impl(cudaStream_t stream, int dtype, const void* x, int64_t ld
     p.status = status;
     return run_shrink_simt(dtype, p, stream);
   }
-  // tcgen05 path; modules are processed in groups whose fp32 partials fit on chip
+  // tcgen05 path.  Tiles with one segment go to the persistent kernel (all
+  // modules in one pass over x); the rest to the per-tile cluster kernel.
   const int rp = rank < 16 ? 16 : rank;
+  if (tiles != nullptr && g_persistent.load() && n_tiles - n_multi > 0) {
+    ShrinkPersistParams q;
+    memset(&q, 0, sizeof(q));
+    {
+      cuuint64_t dims[2] = {cuuint64_t(hidden), cuuint64_t(n_tokens)};
+      cuuint64_t strides[1] = {cuuint64_t(ldx) * es};
+      cuuint32_t box[2] = {64, 128};
+      int rc = encode(&q.x_map, dtype, 2, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "x");
+      if (rc) return rc;
+    }
+    for (int m = 0; m < n_modules; ++m) {
+      const void* a = static_cast<const uint8_t*>(cache_a) + int64_t(modules[m]) * a_module_stride * es;
+      const int64_t ss = n_slots == 1 ? int64_t(hidden) * rank : a_slot_stride;
+      cuuint64_t dims[3] = {cuuint64_t(rank), cuuint64_t(hidden), cuuint64_t(n_slots)};
+      cuuint64_t strides[2] = {cuuint64_t(rank) * es, cuuint64_t(ss) * es};
+      cuuint32_t box[3] = {cuuint32_t(rank), 64, 1};
+      int rc = encode(&q.a_map[m], dtype, 3, a, dims, strides, box, a_tma_swizzle(rank), "a");
+      if (rc) return rc;
+    }
+    q.n_tokens = n_tokens;
+    q.hidden = hidden;
+    q.n_modules = n_modules;
+    q.n_slots = n_slots;
+    q.n_tiles = n_tiles - n_multi;
+    q.acc_cols = uint32_t(n_modules * rp);
+    q.tiles = tiles;
+    q.seg_start = seg_start;
+    q.seg_len = seg_len;
+    q.seg_slot = seg_slot;
+    q.n_segs = n_segs;
+    q.u = u;
+    q.status = status;
+    int rc = run_shrink_persist(dtype, q, rank, stream);
+    if (rc) return rc;
+    if (n_multi == 0) return LF_OK;
+    tiles += 4 * (n_tiles - n_multi);  // the per-tile kernel takes the rest
+    n_tiles = n_multi;
+  }
+  // per-tile cluster kernel; modules in groups whose fp32 partials fit on chip
   const int group = rp * n_modules <= 64 ? n_modules : (64 / rp > 0 ? 64 / rp : 1);
   for (int m0 = 0; m0 < n_modules; m0 += group) {
     const int gm = (n_modules - m0) < group ? (n_modules - m0) : group;
@@ -216,8 +259,8 @@ static int expand_impl(cudaStream_t stream, int dtype, const void* u, void* y, i
                        int hidden, int rank, const void* cache_b, int64_t b_slot_stride,
                        int64_t b_module_stride, int n_slots, int n_modules, const int32_t* modules,
                        const int64_t* y_col_offsets, const int32_t* seg_start, const int32_t* seg_len,
-                       const int32_t* seg_slot, int n_segs, const int32_t* tiles, int n_tiles, int accumulate,
-                       int32_t* status) {
+                       const int32_t* seg_slot, int n_segs, const int32_t* tiles, int n_tiles, int n_multi,
+                       int accumulate, int32_t* status) {
   const int es = elem_size(dtype);
   int64_t y_cols = 0;
   bool offs_aligned = true;
@@ -284,13 +327,46 @@ static int expand_impl(cudaStream_t stream, int dtype, const void* u, void* y, i
   p.seg_len = seg_len;
   p.seg_slot = seg_slot;
   p.n_segs = n_segs;
-  // with accumulate == 0 every tile must be written (rows outside segments become 0)
-  p.tiles = accumulate ? tiles : nullptr;
-  p.n_tiles = (accumulate && tiles != nullptr) ? n_tiles : int((n_tokens + LF_TILE_TOKENS - 1) / LF_TILE_TOKENS);
   p.u = u;
   p.status = status;
-  if (p.n_tiles == 0) return LF_OK;
   const int nt = hidden % 128 == 0 ? 128 : 64;
+  if (!accumulate || tiles == nullptr) {
+    // with accumulate == 0 every tile must be written (rows outside segments become 0)
+    p.tiles = accumulate ? tiles : nullptr;
+    p.n_tiles = (accumulate && tiles != nullptr) ? n_tiles : int((n_tokens + LF_TILE_TOKENS - 1) / LF_TILE_TOKENS);
+    if (p.n_tiles == 0) return LF_OK;
+    return run_expand_tc(dtype, p, rank, nt, stream);
+  }
+  const int n_single = n_tiles - n_multi;
+  int first_old = 0;  // records the one-tile-per-CTA kernel handles: [first_old, n_tiles)
+  if (g_persistent.load() && nt == 128 && n_single > 0) {
+    ExpandPersistParams q;
+    memset(&q, 0, sizeof(q));
+    q.y_map = p.y_map;
+    for (int m = 0; m < n_modules; ++m) {
+      q.b_map[m] = p.b_map[m];
+      q.y_col_off[m] = p.y_col_off[m];
+    }
+    {
+      cuuint64_t dims[2] = {cuuint64_t(rank), cuuint64_t(n_modules) * cuuint64_t(n_tokens)};
+      cuuint64_t strides[1] = {cuuint64_t(rank) * es};
+      cuuint32_t box[2] = {cuuint32_t(rank), 128};
+      int rc = encode(&q.u_map, dtype, 2, u, dims, strides, box, a_tma_swizzle(rank), "u");
+      if (rc) return rc;
+    }
+    q.n_tokens = n_tokens;
+    q.n_modules = n_modules;
+    q.n_col_blocks = hidden / 128;
+    q.n_tiles = n_single;
+    q.tiles = tiles;
+    q.status = status;
+    int rc = run_expand_persist(dtype, q, rank, 128, stream);
+    if (rc) return rc;
+    first_old = n_single;
+  }
+  if (first_old == n_tiles) return LF_OK;
+  p.tiles = tiles + 4 * first_old;
+  p.n_tiles = n_tiles - first_old;
   return run_expand_tc(dtype, p, rank, nt, stream);
 }
 
@@ -314,6 +390,7 @@ int lf_set_option(int key, int value) {
   switch (key) {
     case LF_OPT_FORCE_SIMT: g_force_simt.store(value ? 1 : 0); return LF_OK;
     case LF_OPT_REQUIRE_TC: g_require_tc.store(value ? 1 : 0); return LF_OK;
+    case LF_OPT_PERSISTENT: g_persistent.store(value ? 1 : 0); return LF_OK;
     case LF_OPT_SHRINK_CLUSTER:
       if (value < 0 || value > 8 || (value & (value - 1)) != 0)
         return set_error(LF_ERR_INVALID, "LF_OPT_SHRINK_CLUSTER must be 0 or a power of two <= 8");
@@ -334,35 +411,35 @@ size_t lf_lora_workspace_bytes(int dtype, int64_t n_tokens, int rank, int n_modu
 int lf_lora_shrink(void* stream, int dtype, const void* x, int64_t ldx, int64_t n_tokens, int hidden, int rank,
                    const void* cache_a, int64_t a_slot_stride, int64_t a_module_stride, int n_slots,
                    int n_modules, const int32_t* modules, const int32_t* seg_start, const int32_t* seg_len,
-                   const int32_t* seg_slot, int n_segs, const int32_t* tiles, int n_tiles, void* u,
-                   int32_t* status) {
+                   const int32_t* seg_slot, int n_segs, const int32_t* tiles, int n_tiles, int n_multi,
+                   void* u, int32_t* status) {
   int rc = check_common("lf_lora_shrink", dtype, n_tokens, hidden, rank, n_slots, n_modules, modules, seg_start,
                         seg_len, seg_slot, n_segs);
   if (rc) return rc;
-  if ((rc = check_tiles("lf_lora_shrink", tiles, n_tiles, n_tokens))) return rc;
+  if ((rc = check_tiles("lf_lora_shrink", tiles, n_tiles, n_multi, n_tokens))) return rc;
   if (x == nullptr || cache_a == nullptr || u == nullptr) return set_error(LF_ERR_INVALID, "lf_lora_shrink: NULL buffer");
   if (ldx < hidden) return set_error(LF_ERR_INVALID, "lf_lora_shrink: ldx < hidden");
   if (n_tokens == 0) return LF_OK;
   return shrink_impl(static_cast<cudaStream_t>(stream), dtype, x, ldx, n_tokens, hidden, rank, cache_a,
                      a_slot_stride, a_module_stride, n_slots, n_modules, modules, seg_start, seg_len, seg_slot,
-                     n_segs, tiles, n_tiles, u, status);
+                     n_segs, tiles, n_tiles, n_multi, u, status);
 }
 
 int lf_lora_expand(void* stream, int dtype, const void* u, void* y, int64_t ldy, int64_t n_tokens, int hidden,
                    int rank, const void* cache_b, int64_t b_slot_stride, int64_t b_module_stride, int n_slots,
                    int n_modules, const int32_t* modules, const int64_t* y_col_offsets, const int32_t* seg_start,
                    const int32_t* seg_len, const int32_t* seg_slot, int n_segs, const int32_t* tiles, int n_tiles,
-                   int accumulate, int32_t* status) {
+                   int n_multi, int accumulate, int32_t* status) {
   int rc = check_common("lf_lora_expand", dtype, n_tokens, hidden, rank, n_slots, n_modules, modules, seg_start,
                         seg_len, seg_slot, n_segs);
   if (rc) return rc;
-  if ((rc = check_tiles("lf_lora_expand", tiles, n_tiles, n_tokens))) return rc;
+  if ((rc = check_tiles("lf_lora_expand", tiles, n_tiles, n_multi, n_tokens))) return rc;
   if (u == nullptr || y == nullptr || cache_b == nullptr || y_col_offsets == nullptr)
     return set_error(LF_ERR_INVALID, "lf_lora_expand: NULL buffer");
   if (n_tokens == 0) return LF_OK;
   return expand_impl(static_cast<cudaStream_t>(stream), dtype, u, y, ldy, n_tokens, hidden, rank, cache_b,
                      b_slot_stride, b_module_stride, n_slots, n_modules, modules, y_col_offsets, seg_start, seg_len,
-                     seg_slot, n_segs, tiles, n_tiles, accumulate, status);
+                     seg_slot, n_segs, tiles, n_tiles, n_multi, accumulate, status);
 }
 
 int lf_lora_apply(void* stream, int dtype, const void* x, int64_t ldx, void* y, int64_t ldy, int64_t n_tokens,
@@ -370,11 +447,11 @@ int lf_lora_apply(void* stream, int dtype, const void* x, int64_t ldx, void* y, 
                   const void* cache_b, int64_t b_slot_stride, int64_t b_module_stride, int n_slots, int n_modules,
                   const int32_t* modules, const int64_t* y_col_offsets, const int32_t* seg_start,
                   const int32_t* seg_len, const int32_t* seg_slot, int n_segs, const int32_t* tiles, int n_tiles,
-                  void* workspace, size_t workspace_bytes, int32_t* status) {
+                  int n_multi, void* workspace, size_t workspace_bytes, int32_t* status) {
   int rc = check_common("lf_lora_apply", dtype, n_tokens, hidden, rank, n_slots, n_modules, modules, seg_start,
                         seg_len, seg_slot, n_segs);
   if (rc) return rc;
-  if ((rc = check_tiles("lf_lora_apply", tiles, n_tiles, n_tokens))) return rc;
+  if ((rc = check_tiles("lf_lora_apply", tiles, n_tiles, n_multi, n_tokens))) return rc;
   if (x == nullptr || y == nullptr || cache_a == nullptr || cache_b == nullptr || y_col_offsets == nullptr)
     return set_error(LF_ERR_INVALID, "lf_lora_apply: NULL buffer");
   if (ldx < hidden) return set_error(LF_ERR_INVALID, "lf_lora_apply: ldx < hidden");
@@ -384,11 +461,12 @@ int lf_lora_apply(void* stream, int dtype, const void* x, int64_t ldx, void* y, 
     return set_error(LF_ERR_WORKSPACE, "lf_lora_apply: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   rc = shrink_impl(s, dtype, x, ldx, n_tokens, hidden, rank, cache_a, a_slot_stride, a_module_stride, n_slots,
-                   n_modules, modules, seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles, workspace, status);
+                   n_modules, modules, seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles, n_multi, workspace,
+                   status);
   if (rc) return rc;
   return expand_impl(s, dtype, workspace, y, ldy, n_tokens, hidden, rank, cache_b, b_slot_stride, b_module_stride,
                      n_slots, n_modules, modules, y_col_offsets, seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles,
-                     1, status);
+                     n_multi, 1, status);
 }
 
 }  // extern "C"

@@ -51,6 +51,39 @@ struct alignas(64) ExpandTcParams {
   int32_t* status;
 };
 
+// Persistent expand over single-segment tiles (see lf_lora_persist.cu).
+struct alignas(64) ExpandPersistParams {
+  CUtensorMap y_map;                 // 2D {y_cols, n_tokens}, box {64, 128}, SW128
+  CUtensorMap b_map[kMaxModules];    // 3D {hidden, rank, n_slots}, box {64, rank, 1}, SW128
+  CUtensorMap u_map;                 // 2D {rank, n_modules * n_tokens}, box {rank, 128}, swizzle by rank
+  int64_t n_tokens;
+  int64_t y_col_off[kMaxModules];
+  int32_t n_modules;
+  int32_t n_col_blocks;              // hidden / NT
+  int32_t n_tiles;                   // single-segment tile records
+  const int32_t* tiles;              // records {tile, first segment, 1, slot}
+  int32_t* status;
+};
+
+// Persistent shrink over single-segment tiles (see lf_lora_persist.cu).
+struct alignas(64) ShrinkPersistParams {
+  CUtensorMap x_map;                 // 2D {hidden, n_tokens}, box {64, 128}, SW128
+  CUtensorMap a_map[kMaxModules];    // 3D {rank, hidden, n_slots}, box {rank, 64, 1}
+  int64_t n_tokens;
+  int32_t hidden;
+  int32_t n_modules;
+  int32_t n_slots;
+  int32_t n_tiles;                   // single-segment tile records
+  uint32_t acc_cols;                 // TMEM columns of one accumulator (n_modules * rank, padded)
+  const int32_t* tiles;              // records {tile, first segment, 1, slot}
+  const int32_t* seg_start;
+  const int32_t* seg_len;
+  const int32_t* seg_slot;
+  int32_t n_segs;
+  void* u;                           // (n_modules, n_tokens, rank)
+  int32_t* status;
+};
+
 struct SimtParams {
   const void* x;
   int64_t ldx;
@@ -86,6 +119,9 @@ int run_expand_tc(int dtype, const ExpandTcParams& p, int rank, int nt, cudaStre
 size_t shrink_tc_smem(int dtype, int rank, int kchunk, int n_mod);
 uint32_t shrink_tc_tmem_cols(int rank, int n_mod);
 CUtensorMapSwizzle a_tma_swizzle(int rank);
+
+int run_expand_persist(int dtype, const ExpandPersistParams& p, int rank, int nt, cudaStream_t s);
+int run_shrink_persist(int dtype, const ShrinkPersistParams& p, int rank, cudaStream_t s);
 
 // CUDA-core path
 int run_shrink_simt(int dtype, const SimtParams& p, cudaStream_t s);

@@ -1,0 +1,550 @@
+// Persistent, warp-specialised LoRA kernels for tiles that hold one segment.
+//
+// Both kernels run one CTA per SM that loops over work items, with three roles:
+//   warp 0      producer: streams the item's operands by TMA into a ring of
+//               shared-memory stages (mbarrier "full"/"empty" per stage);
+//   warp 1      MMA issuer: tcgen05.mma into one of two TMEM accumulators;
+//   warps 2-5   epilogue: drains the accumulator (each warp owns the 32 TMEM
+//               lanes = tile rows of its quadrant) while the next item's loads
+//               and MMAs are already in flight.
+//
+// Shrink  (item = 128-token tile):  u[m][t] = round(x[t] . A(slot, m)) for every
+//         module, the hidden dimension streamed in 64-wide K blocks; the
+//         epilogue writes u (0 for tile rows outside the tile's segment, which
+//         the expand relies on).
+// Expand  (item = tile x module x 128 columns):  y += round(u . B(slot, m)); the
+//         y tile, the B factor tile and the u tile (canonical K-major layout,
+//         straight from the shrink output) arrive by TMA; the epilogue adds in
+//         f32, rounds, writes a separate double-buffered output tile and stores
+//         it by TMA, so an input stage is free as soon as it has been read.
+//
+// Tiles with several segments use the one-tile-per-CTA kernels in
+// lf_lora_tc.cu.  Every wait is bounded; a timeout sets LF_STATUS_TIMEOUT and
+// the roles unwind without leaving a warp at a hardware barrier.
+#include "lf_common.cuh"
+#include "lf_internal.h"
+
+namespace lf {
+
+namespace {
+
+constexpr int kTile = 128;
+constexpr int kYBox = kTile * 64 * 2;  // one 128 x 64 bf16 box, 16 KB
+constexpr int kSmemBudget = 220 * 1024;
+
+__device__ __forceinline__ bool aborted(const int32_t* flag) {
+  return *reinterpret_cast<const volatile int32_t*>(flag) != 0;
+}
+
+template <int R>
+struct UOperand {  // K-major u tile: 128 rows of R elements
+  static constexpr uint32_t kLayout = (R == 8) ? 0u : (R == 16) ? 6u : (R == 32) ? 4u : 2u;
+  static constexpr uint32_t kSbo = (R == 8) ? 128u : 8u * R * 2u;  // 8-row group stride
+};
+
+template <int R>
+struct AOperand {  // MN-major A factor box: 64 K rows of R elements
+  static constexpr uint32_t kRowBytes = R * 2;
+  static constexpr uint32_t kLayout = (R == 8) ? 0u : (R == 16) ? 6u : (R == 32) ? 4u : 2u;
+  static constexpr uint32_t kSbo = 8 * kRowBytes;
+};
+
+// ------------------------------------------------------------------ expand
+template <int R, int NT>
+struct ExpandCfg {
+  static constexpr int kNBox = NT / 64;
+  static constexpr int kYBytes = kNBox * kYBox;
+  static constexpr int kBBox = R * 64 * 2;
+  static constexpr int kBBytes = kNBox * kBBox;
+  static constexpr int kUBytes = kTile * R * 2;
+  static constexpr int kStageBytes = kYBytes + kBBytes + kUBytes;  // multiple of 1024
+  static constexpr int kOutBytes = 2 * kYBytes;                     // double-buffered output tile
+  static constexpr int kZeroB = (R == 8) ? kNBox * 1024 : 0;
+  static constexpr int kZeroU = (R == 8) ? kTile * 16 : 0;
+  static constexpr int kRP = R < 16 ? 16 : R;
+  static constexpr int kMeta = 1024;
+  static constexpr int kStages = (kSmemBudget - 1024 - kOutBytes - kZeroB - kZeroU - kMeta) / kStageBytes;
+  static_assert(kStages >= 2, "expand stage ring does not fit");
+  static constexpr int kST = kStages > 4 ? 4 : kStages;
+  static constexpr size_t kSmem = 1024 + size_t(kST) * kStageBytes + kOutBytes + kZeroB + kZeroU + kMeta;
+};
+
+}  // namespace
+
+template <typename T, int R, int NT>
+__global__ void __launch_bounds__(192, 1)
+lora_expand_persist_kernel(const __grid_constant__ ExpandPersistParams p) {
+  using C = ExpandCfg<R, NT>;
+  constexpr int ST = C::kST;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t s_stage0 = base;
+  const uint32_t s_out0 = base + ST * C::kStageBytes;
+  const uint32_t s_zero_b = s_out0 + C::kOutBytes;
+  const uint32_t s_zero_u = s_zero_b + C::kZeroB;
+  uint8_t* meta_base = gbase + (s_zero_u + C::kZeroU - base);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(meta_base);
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  const int FULL = 0, EMPTY = ST, ACC_FULL = 2 * ST, ACC_EMPTY = 2 * ST + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(&bars[2 * ST + 4]);
+  int32_t* s_abort = reinterpret_cast<int32_t*>(tmem_slot + 1);
+  int4* s_meta = reinterpret_cast<int4*>(&bars[2 * ST + 6]);  // per stage: {row0, col0}
+
+  const int ncb = p.n_col_blocks;
+  const int64_t per_tile = int64_t(p.n_modules) * ncb;
+  const int64_t total = int64_t(p.n_tiles) * per_tile;
+
+  if (tid == 0) {
+    for (int i = 0; i < ST; ++i) {
+      mbar_init(bar(FULL + i), 1);
+      mbar_init(bar(EMPTY + i), 2);  // the MMA's commit + the epilogue's read of the y tile
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(ACC_FULL + i), 1);
+      mbar_init(bar(ACC_EMPTY + i), 4);  // one arrive per epilogue warp
+    }
+    *s_abort = 0;
+    fence_mbar_init();
+  }
+  if (R == 8) {
+    uint4* z = reinterpret_cast<uint4*>(gbase + (s_zero_b - base));
+    for (int i = tid; i < (C::kZeroB + C::kZeroU) / 16; i += blockDim.x) z[i] = make_uint4(0, 0, 0, 0);
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc(smem_u32(tmem_slot), 2 * NT);
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto fail = [&]() {
+    set_status(p.status, LF_STATUS_TIMEOUT);
+    atomicExch(s_abort, 1);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int it = 0;
+      int64_t item = blockIdx.x;
+      int4 rec = item < total ? __ldg(reinterpret_cast<const int4*>(p.tiles) + item / per_tile) : int4{};
+      for (; item < total; item += gridDim.x, ++it) {
+        const int s = it % ST;
+        const uint32_t ph = (it / ST) & 1;
+        const int rem = int(item % per_tile);
+        const int m = rem / ncb, cb = rem % ncb;
+        const int4 cur = rec;
+        const int64_t next = item + gridDim.x;  // prefetch the next item's record
+        if (next < total) rec = __ldg(reinterpret_cast<const int4*>(p.tiles) + next / per_tile);
+        if (aborted(s_abort)) break;
+        if (!mbar_wait(bar(EMPTY + s), ph ^ 1)) { fail(); break; }
+        const int32_t row0 = cur.x * kTile;
+        const int32_t col0 = int32_t(p.y_col_off[m]) + cb * NT;
+        s_meta[s] = make_int4(row0, col0, 0, 0);
+        const uint32_t st = s_stage0 + s * C::kStageBytes;
+        const uint32_t sy = st, sb = st + C::kYBytes, su = sb + C::kBBytes;
+        mbar_arrive_expect_tx(bar(FULL + s), C::kStageBytes);
+        for (int j = 0; j < C::kNBox; ++j)
+          tma_load_2d(sy + j * kYBox, &p.y_map, bar(FULL + s), col0 + j * 64, row0);
+        // an out-of-range slot reads zeros (TMA fill): the tile then gets no delta
+        for (int j = 0; j < C::kNBox; ++j)
+          tma_load_3d(sb + j * C::kBBox, &p.b_map[m], bar(FULL + s), cb * NT + j * 64, 0, cur.w);
+        tma_load_2d(su, &p.u_map, bar(FULL + s), 0, int32_t(int64_t(m) * p.n_tokens + row0));
+      }
+      if (aborted(s_abort)) {  // loads nobody consumed must land before the CTA exits (bounded)
+        for (int k = (it > ST ? it - ST : 0); k < it; ++k) mbar_wait(bar(FULL + k % ST), (k / ST) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(DT<T>::umma_fmt, kTile, NT, /*a_mn=*/0, /*b_mn=*/1);
+      using U = UOperand<R>;
+      int it = 0;
+      for (int64_t item = blockIdx.x; item < total; item += gridDim.x, ++it) {
+        const int s = it % ST;
+        const uint32_t ph = (it / ST) & 1;
+        const int a = it & 1;
+        const uint32_t aph = (it >> 1) & 1;
+        if (aborted(s_abort)) break;
+        if (!mbar_wait(bar(FULL + s), ph)) { fail(); break; }
+        if (!mbar_wait(bar(ACC_EMPTY + a), aph ^ 1)) { fail(); break; }
+        tc_fence_after();
+        const uint32_t st = s_stage0 + s * C::kStageBytes;
+        const uint32_t sb = st + C::kYBytes, su = sb + C::kBBytes;
+#pragma unroll
+        for (int k = 0; k < C::kRP / 16; ++k) {
+          uint64_t ad, bd;
+          if (R == 8) {
+            ad = smem_desc(su, s_zero_u - su, U::kSbo, 0);  // K elements 8..15 read zeros
+            bd = smem_desc(sb, C::kBBox, s_zero_b - sb, 2);
+          } else {
+            ad = smem_desc(su + k * 32, 16, U::kSbo, U::kLayout);
+            bd = smem_desc(sb + k * 2048, C::kBBox, 1024, 2);
+          }
+          umma_f16(tmem + a * NT, ad, bd, idesc, k > 0 ? 1u : 0u);
+        }
+        umma_commit(bar(ACC_FULL + a));
+        umma_commit(bar(EMPTY + s));
+      }
+      if (it > 0 && aborted(s_abort))  // MMAs in flight must finish before TMEM is released (bounded)
+        mbar_wait(bar(ACC_FULL + ((it - 1) & 1)), ((it - 1) >> 1) & 1);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    // All four warps take every iteration and every named barrier, whatever
+    // happens, so that no warp can be left waiting at bar.sync.
+    const int quad = warp & 3;          // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;   // tile row
+    const bool leader = (warp == 2 && lane == 0);
+    int it = 0;
+    for (int64_t item = blockIdx.x; item < total; item += gridDim.x, ++it) {
+      const int s = it % ST;
+      const uint32_t ph = (it / ST) & 1;
+      const int a = it & 1;
+      const uint32_t aph = (it >> 1) & 1;
+      const int ob = it & 1;
+      bool ok = !aborted(s_abort);
+      if (ok && !(mbar_wait(bar(ACC_FULL + a), aph) && mbar_wait(bar(FULL + s), ph))) {
+        fail();
+        ok = false;
+      }
+      const bool work = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld is collective
+      // (B) the leader has seen the store that last read out[ob] finish (end of the previous iteration)
+      named_barrier_sync(1, 128);
+      tc_fence_after();
+      const uint32_t sy = s_stage0 + s * C::kStageBytes;
+      const uint32_t so = s_out0 + ob * C::kYBytes;
+      if (work) {
+        for (int q = 0; q < NT / 32; ++q) {
+          float v[32];
+          {
+            float lo[16], hi[16];
+            tmem_ld16(tmem + (uint32_t(quad * 32) << 16) + a * NT + q * 32, lo);
+            tmem_ld16(tmem + (uint32_t(quad * 32) << 16) + a * NT + q * 32 + 16, hi);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) { v[i] = lo[i]; v[16 + i] = hi[i]; }
+          }
+          const uint32_t roff = (q >> 1) * kYBox + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            const int chunk = (q & 1) * 4 + c4;
+            const uint32_t o = roff + ((chunk ^ (row & 7)) << 4);
+            uint4 raw16 = *reinterpret_cast<const uint4*>(gbase + (sy - base) + o);
+            T* e = reinterpret_cast<T*>(&raw16);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              e[i] = DT<T>::from_f(DT<T>::to_f(e[i]) + round_through<T>(v[c4 * 8 + i]));
+            *reinterpret_cast<uint4*>(gbase + (so - base) + o) = raw16;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(ACC_EMPTY + a));  // this warp's TMEM reads are done
+      fence_proxy_async_smem();
+      // (C) every warp has read its rows of the y stage and written out[ob]
+      named_barrier_sync(1, 128);
+      if (leader) {
+        const int4 meta = s_meta[s];  // read before the stage (and its metadata) is handed back
+        mbar_arrive(bar(EMPTY + s));  // the input stage may be refilled now
+        if (!aborted(s_abort)) {
+          for (int j = 0; j < NT / 64; ++j) tma_store_2d(&p.y_map, so + j * kYBox, meta.y + j * 64, meta.x);
+          tma_store_commit();
+        }
+        tma_store_wait_read_le1();  // the store that read the other output buffer has finished
+      }
+    }
+    if (leader) tma_store_wait_all();
+  }
+
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, 2 * NT);
+  }
+}
+
+// ------------------------------------------------------------------ shrink
+template <typename T, int R>
+__global__ void __launch_bounds__(192, 1)
+lora_shrink_persist_kernel(const __grid_constant__ ShrinkPersistParams p, int stages, int stage_bytes) {
+  constexpr int RP = R < 16 ? 16 : R;
+  constexpr int kABox = 64 * R * 2;
+  using A = AOperand<R>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ST = stages;
+  const int n_mod = p.n_modules;
+  const int nkb = p.hidden / 64;
+  const uint32_t s_stage0 = base;
+  const uint32_t s_zero = base + ST * stage_bytes;  // 1 KB of zeros (rank 8 only)
+  uint8_t* meta_base = gbase + (s_zero + 1024 - base);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(meta_base);
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  const int FULL = 0, EMPTY = ST, ACC_FULL = 2 * ST, ACC_EMPTY = 2 * ST + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(&bars[2 * ST + 4]);
+  int32_t* s_abort = reinterpret_cast<int32_t*>(tmem_slot + 1);
+  const uint32_t acc_cols = p.acc_cols;
+  uint32_t alloc_cols = 32;
+  while (alloc_cols < 2 * acc_cols) alloc_cols <<= 1;
+
+  if (tid == 0) {
+    for (int i = 0; i < ST; ++i) {
+      mbar_init(bar(FULL + i), 1);
+      mbar_init(bar(EMPTY + i), 1);  // the MMA's commit
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(ACC_FULL + i), 1);
+      mbar_init(bar(ACC_EMPTY + i), 4);
+    }
+    *s_abort = 0;
+    fence_mbar_init();
+  }
+  if (R == 8) {
+    uint4* z = reinterpret_cast<uint4*>(gbase + (s_zero - base));
+    for (int i = tid; i < 1024 / 16; i += blockDim.x) z[i] = make_uint4(0, 0, 0, 0);
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc(smem_u32(tmem_slot), alloc_cols);
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto fail = [&]() {
+    set_status(p.status, LF_STATUS_TIMEOUT);
+    atomicExch(s_abort, 1);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int kk = 0;
+      int ti = blockIdx.x;
+      int4 rec = ti < p.n_tiles ? __ldg(reinterpret_cast<const int4*>(p.tiles) + ti) : int4{};
+      bool stop = false;
+      for (; ti < p.n_tiles && !stop; ti += gridDim.x) {
+        const int4 cur = rec;
+        if (ti + int(gridDim.x) < p.n_tiles) rec = __ldg(reinterpret_cast<const int4*>(p.tiles) + ti + gridDim.x);
+        const int32_t row0 = cur.x * kTile;
+        for (int kb = 0; kb < nkb; ++kb, ++kk) {
+          const int s = kk % ST;
+          const uint32_t ph = (kk / ST) & 1;
+          if (aborted(s_abort) || !mbar_wait(bar(EMPTY + s), ph ^ 1)) {
+            if (!aborted(s_abort)) fail();
+            stop = true;
+            break;
+          }
+          const uint32_t st = s_stage0 + s * stage_bytes;
+          mbar_arrive_expect_tx(bar(FULL + s), kYBox + n_mod * kABox);
+          tma_load_2d(st, &p.x_map, bar(FULL + s), kb * 64, row0);
+          for (int m = 0; m < n_mod; ++m)
+            tma_load_3d(st + kYBox + m * kABox, &p.a_map[m], bar(FULL + s), 0, kb * 64, cur.w);
+        }
+      }
+      if (aborted(s_abort)) {
+        for (int k = (kk > ST ? kk - ST : 0); k < kk; ++k) mbar_wait(bar(FULL + k % ST), (k / ST) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(DT<T>::umma_fmt, kTile, RP, /*a_mn=*/0, /*b_mn=*/1);
+      int kk = 0, it = 0;
+      bool stop = false;
+      for (int ti = blockIdx.x; ti < p.n_tiles && !stop; ti += gridDim.x, ++it) {
+        const int a = it & 1;
+        const uint32_t aph = (it >> 1) & 1;
+        if (aborted(s_abort) || !mbar_wait(bar(ACC_EMPTY + a), aph ^ 1)) {
+          if (!aborted(s_abort)) fail();
+          break;
+        }
+        for (int kb = 0; kb < nkb; ++kb, ++kk) {
+          const int s = kk % ST;
+          const uint32_t ph = (kk / ST) & 1;
+          if (!mbar_wait(bar(FULL + s), ph)) { fail(); stop = true; break; }
+          tc_fence_after();
+          const uint32_t st = s_stage0 + s * stage_bytes;
+          for (int m = 0; m < n_mod; ++m) {
+            const uint32_t ab = st + kYBox + m * kABox;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint64_t ad = smem_desc(st + k * 32, 16, 1024, 2);
+              const uint32_t bstart = ab + k * 16 * A::kRowBytes;
+              const uint64_t bd = (R == 8) ? smem_desc(bstart, 128, s_zero + k * 256 - bstart, 0)
+                                           : smem_desc(bstart, A::kSbo, A::kSbo, A::kLayout);
+              umma_f16(tmem + a * acc_cols + m * RP, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
+          }
+          umma_commit(bar(EMPTY + s));
+        }
+        if (!stop) umma_commit(bar(ACC_FULL + a));
+      }
+      if (it > 0 && aborted(s_abort)) mbar_wait(bar(ACC_FULL + ((it - 1) & 1)), ((it - 1) >> 1) & 1);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    int it = 0;
+    for (int ti = blockIdx.x; ti < p.n_tiles; ti += gridDim.x, ++it) {
+      const int a = it & 1;
+      const uint32_t aph = (it >> 1) & 1;
+      // the tile's segment, read while the MMAs run
+      const int4 rec = __ldg(reinterpret_cast<const int4*>(p.tiles) + ti);
+      const int64_t row0 = int64_t(rec.x) * kTile;
+      int64_t lo = 0, hi = 0;
+      if (rec.y >= 0 && rec.y < p.n_segs) {
+        const int64_t s0 = __ldg(p.seg_start + rec.y), l0 = __ldg(p.seg_len + rec.y);
+        if (__ldg(p.seg_slot + rec.y) == rec.w && rec.w >= 0 && rec.w < p.n_slots) {
+          lo = max(s0, row0) - row0;
+          hi = min(min(s0 + l0, row0 + kTile), p.n_tokens) - row0;
+        } else if (row == 0 && quad == 0) {
+          set_status(p.status, (rec.w < 0 || rec.w >= p.n_slots) ? LF_STATUS_BAD_SLOT : LF_STATUS_BAD_SEGMENT);
+        }
+      } else if (row == 0 && quad == 0) {
+        set_status(p.status, LF_STATUS_BAD_SEGMENT);
+      }
+      bool ok = !aborted(s_abort);
+      if (ok && !mbar_wait(bar(ACC_FULL + a), aph)) {
+        fail();
+        ok = false;
+      }
+      const bool work = __all_sync(0xffffffffu, ok);
+      tc_fence_after();
+      const int64_t t = row0 + row;
+      const bool mine = row >= lo && row < hi;
+      if (work) {
+        for (int m = 0; m < n_mod; ++m) {
+          T* dst = reinterpret_cast<T*>(p.u) + (int64_t(m) * p.n_tokens + t) * R;
+#pragma unroll
+          for (int c = 0; c < RP / 16; ++c) {
+            float v[16];
+            tmem_ld16(tmem + (uint32_t(quad * 32) << 16) + a * acc_cols + m * RP + c * 16, v);
+            if (t < p.n_tokens) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                if (c * 16 + h * 8 < R) {
+                  uint4 pk;
+                  T* e = reinterpret_cast<T*>(&pk);
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) e[i] = DT<T>::from_f(mine ? v[h * 8 + i] : 0.f);
+                  *reinterpret_cast<uint4*>(dst + c * 16 + h * 8) = pk;
+                }
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(ACC_EMPTY + a));
+    }
+  }
+
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, alloc_cols);
+  }
+}
+
+// ------------------------------------------------------------------ launchers
+namespace {
+
+int sm_count() {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+template <typename T, int R, int NT>
+int launch_expand(const ExpandPersistParams& p, cudaStream_t stream) {
+  using C = ExpandCfg<R, NT>;
+  auto kern = lora_expand_persist_kernel<T, R, NT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(C::kSmem));
+  if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(expand_persist)");
+  const int64_t total = int64_t(p.n_tiles) * p.n_modules * p.n_col_blocks;
+  const int sms = sm_count();
+  const int grid = int(total < sms ? total : sms);
+  if (grid == 0) return LF_OK;
+  kern<<<grid, 192, C::kSmem, stream>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, "launch lora_expand_persist");
+  count_launch();
+  return LF_OK;
+}
+
+template <typename T, int R>
+int launch_shrink(const ShrinkPersistParams& p, cudaStream_t stream) {
+  const int stage_bytes = kYBox + p.n_modules * 64 * R * 2;  // multiple of 1024
+  const int fixed = 1024 + 1024 + 1024;                      // alignment, zeros, barriers
+  int stages = (kSmemBudget - fixed) / stage_bytes;
+  if (stages > 8) stages = 8;
+  if (stages < 2) return set_error(LF_ERR_UNSUPPORTED, "persistent shrink: %d modules of rank %d do not fit", p.n_modules, R);
+  const size_t smem = size_t(fixed) + size_t(stages) * stage_bytes;
+  auto kern = lora_shrink_persist_kernel<T, R>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(shrink_persist)");
+  const int sms = sm_count();
+  const int grid = p.n_tiles < sms ? p.n_tiles : sms;
+  if (grid == 0) return LF_OK;
+  kern<<<grid, 192, smem, stream>>>(p, stages, stage_bytes);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, "launch lora_shrink_persist");
+  count_launch();
+  return LF_OK;
+}
+
+template <typename T>
+int expand_rank(const ExpandPersistParams& p, int rank, cudaStream_t s) {
+  switch (rank) {
+    case 8: return launch_expand<T, 8, 128>(p, s);
+    case 16: return launch_expand<T, 16, 128>(p, s);
+    case 32: return launch_expand<T, 32, 128>(p, s);
+    case 64: return launch_expand<T, 64, 128>(p, s);
+  }
+  return set_error(LF_ERR_UNSUPPORTED, "persistent expand: rank %d", rank);
+}
+
+template <typename T>
+int shrink_rank(const ShrinkPersistParams& p, int rank, cudaStream_t s) {
+  switch (rank) {
+    case 8: return launch_shrink<T, 8>(p, s);
+    case 16: return launch_shrink<T, 16>(p, s);
+    case 32: return launch_shrink<T, 32>(p, s);
+    case 64: return launch_shrink<T, 64>(p, s);
+  }
+  return set_error(LF_ERR_UNSUPPORTED, "persistent shrink: rank %d", rank);
+}
+
+}  // namespace
+
+int run_expand_persist(int dtype, const ExpandPersistParams& p, int rank, int nt, cudaStream_t s) {
+  if (nt != 128) return set_error(LF_ERR_UNSUPPORTED, "persistent expand: column tile %d", nt);
+  if (dtype == LF_DTYPE_BF16) return expand_rank<__nv_bfloat16>(p, rank, s);
+  return expand_rank<__half>(p, rank, s);
+}
+
+int run_shrink_persist(int dtype, const ShrinkPersistParams& p, int rank, cudaStream_t s) {
+  if (dtype == LF_DTYPE_BF16) return shrink_rank<__nv_bfloat16>(p, rank, s);
+  return shrink_rank<__half>(p, rank, s);
+}
+
+}  // namespace lf

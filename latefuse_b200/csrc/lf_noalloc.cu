@@ -43,7 +43,7 @@ extern "C" int lf_lora_apply_noalloc(void* stream, int dtype,
                                      int n_slots, int n_modules, const int32_t* modules,
                                      const int64_t* y_col_offsets,
                                      const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot,
-                                     int n_segs, const int32_t* tiles, int n_tiles,
+                                     int n_segs, const int32_t* tiles, int n_tiles, int n_multi,
                                      int32_t* status) {
   using namespace lf;
   const size_t need = lf_lora_workspace_bytes(dtype, n_tokens, rank, n_modules);
@@ -70,6 +70,6 @@ extern "C" int lf_lora_apply_noalloc(void* stream, int dtype,
   }
   return lf_lora_apply(stream, dtype, x, ldx, y, ldy, n_tokens, hidden, rank, cache_a, a_slot_stride,
                        a_module_stride, cache_b, b_slot_stride, b_module_stride, n_slots, n_modules, modules,
-                       y_col_offsets, seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles, scratch,
+                       y_col_offsets, seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles, n_multi, scratch,
                        LF_NOALLOC_SCRATCH_BYTES, status);
 }

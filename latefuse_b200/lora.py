@@ -53,6 +53,7 @@ class SegmentTable:
         self.use_records = records
         records = _tile_records(starts, lengths, slots) if records else []
         self.n_tiles = len(records) // 4
+        self.n_multi = sum(1 for i in range(2, len(records), 4) if records[i] != 1)
         self.host = torch.tensor(records + starts + lengths + slots, dtype=torch.int32)
         if self.device.type == "cuda":
             self.table = self.host.pin_memory().to(self.device, non_blocking=True)
@@ -67,19 +68,20 @@ class SegmentTable:
         lens = [seq_len] * B if lengths is None else [int(min(seq_len, max(0, n))) for n in lengths]
         return cls([b * seq_len for b in range(B)], lens, slots, B * seq_len, device)
 
-    def ptrs(self) -> tuple[int, int, int, int, int]:
-        """(seg_start, seg_len, seg_slot, tile records, n_tiles) device pointers/count for the C ABI."""
+    def ptrs(self) -> tuple[int, int, int, int, int, int]:
+        """(seg_start, seg_len, seg_slot, tile records, n_tiles, n_multi) for the C ABI."""
         base = self.table.data_ptr()
         r = 16 * self.n_tiles
         n = self.n_segs
         if not self.use_records:
-            return base, base + 4 * n, base + 8 * n, None, 0
-        return base + r, base + r + 4 * n, base + r + 8 * n, base, self.n_tiles
+            return base, base + 4 * n, base + 8 * n, None, 0, 0
+        return base + r, base + r + 4 * n, base + r + 8 * n, base, self.n_tiles, self.n_multi
 
 
 def _tile_records(starts, lengths, slots) -> list[int]:
     """Flattened ``{tile, first segment, segment count, first slot}`` records of the
-    tiles that hold segment tokens, in tile order (segments sorted by start)."""
+    tiles that hold segment tokens (segments sorted by start): single-segment
+    tiles first, in tile order, then the tiles with several segments."""
     tile = nat.TILE_TOKENS
     first: dict[int, int] = {}
     count: dict[int, int] = {}
@@ -92,7 +94,8 @@ def _tile_records(starts, lengths, slots) -> list[int]:
                 count[t] = 0
             count[t] = g - first[t] + 1
     out: list[int] = []
-    for t in sorted(first):
+    # tiles with one segment first (the persistent kernel takes those), then the rest
+    for t in sorted(first, key=lambda t: (count[t] != 1, t)):
         out += [t, first[t], count[t], slots[first[t]]]
     return out
 
@@ -130,8 +133,8 @@ class FactorCache:
 
 
 def _seg_args(segs: SegmentTable) -> tuple:
-    s, l, k, t, nt = segs.ptrs()
-    return s, l, k, segs.n_segs, t, nt
+    s, l, k, t, nt, nm = segs.ptrs()
+    return s, l, k, segs.n_segs, t, nt, nm
 
 
 def workspace_bytes(dtype: torch.dtype, n_tokens: int, rank: int, n_modules: int) -> int:

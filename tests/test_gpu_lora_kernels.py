@@ -79,7 +79,9 @@ def _reset_options(request):
     nat.set_option(nat.LF_OPT_REQUIRE_TC, 1 if request.node.name.startswith("test_tc_") else 0)
     nat.set_option(nat.LF_OPT_FORCE_SIMT, 0)
     nat.set_option(nat.LF_OPT_SHRINK_CLUSTER, 0)
+    nat.set_option(nat.LF_OPT_PERSISTENT, 1)
     yield
+    nat.set_option(nat.LF_OPT_PERSISTENT, 1)
     nat.set_option(nat.LF_OPT_REQUIRE_TC, 0)
     nat.set_option(nat.LF_OPT_FORCE_SIMT, 0)
     nat.set_option(nat.LF_OPT_SHRINK_CLUSTER, 0)
@@ -176,6 +178,7 @@ def test_tc_cluster_split_is_deterministic_and_equal(cuda, csize):
     x = torch.randn(B * S, H, generator=torch.Generator().manual_seed(12)).to(dtype).to(cuda)
     y = torch.randn(B * S, H, generator=torch.Generator().manual_seed(13)).to(dtype).to(cuda)
     segs = segments_padded(B, S, n_slots, seed=14)
+    nat.set_option(nat.LF_OPT_PERSISTENT, 0)  # the split-K kernel, not the persistent one
     nat.set_option(nat.LF_OPT_SHRINK_CLUSTER, csize)
     a = run_apply(x, y, fc, segs, [0], [0])
     b = run_apply(x, y, fc, segs, [0], [0])
@@ -257,7 +260,8 @@ def test_large_cfg2_shape_vs_gathered_bmm(cuda):
 @pytest.mark.parametrize("S", [100, 512])
 def test_tc_tile_records_equal_segment_search(cuda, S):
     """Per-tile records (one read per CTA) and the binary search over the segment
-    table (no records) give bit-identical results."""
+    table (no records) give bit-identical results.  The shrink runs without a
+    K split so both paths accumulate in the same order."""
     dtype = torch.bfloat16
     B, H, R, n_slots = 4, 256, 16, 6
     fc, _, _ = make_cache(n_slots, 3, H, R, dtype, cuda, seed=61)
@@ -266,6 +270,7 @@ def test_tc_tile_records_equal_segment_search(cuda, S):
     x = torch.randn(B * S, H, generator=g).to(dtype).to(cuda)
     y = torch.randn(B * S, 3 * H, generator=g).to(dtype).to(cuda)
     segs = segments_padded(B, S, n_slots, seed=S, lengths=lengths)
+    nat.set_option(nat.LF_OPT_SHRINK_CLUSTER, 1)
     a = run_apply(x, y, fc, segs, [0, 1, 2], [0, H, 2 * H], records=True)
     b = run_apply(x, y, fc, segs, [0, 1, 2], [0, H, 2 * H], records=False)
     assert torch.equal(a, b)
@@ -287,3 +292,120 @@ def test_record_that_disagrees_with_segments_is_flagged(cuda):
     assert status.item() & 2
     assert torch.equal(out[128:], y[128:])       # that tile got no delta
     assert not torch.equal(out[:128], y[:128])   # the consistent tile did
+
+
+def run_per_tile(fn, *args, **kw):
+    """Run with the persistent kernels off and the shrink on one CTA per tile,
+    so that every fp32 accumulation runs in the persistent kernels' order."""
+    nat.set_option(nat.LF_OPT_PERSISTENT, 0)
+    nat.set_option(nat.LF_OPT_SHRINK_CLUSTER, 1)
+    try:
+        return fn(*args, **kw)
+    finally:
+        nat.set_option(nat.LF_OPT_PERSISTENT, 1)
+        nat.set_option(nat.LF_OPT_SHRINK_CLUSTER, 0)
+
+
+@pytest.mark.parametrize("R", [8, 16, 32, 64])
+def test_tc_persistent_equals_per_tile_kernel(cuda, R):
+    """The persistent shrink + expand (single-segment tiles) and the
+    one-tile-per-CTA kernels run the same MMAs on the same operands in the same
+    order: results are bit-identical."""
+    dtype = torch.bfloat16
+    B, S, H, n_slots = 6, 256, 512, 9
+    fc, a_of, b_of = make_cache(n_slots, 3, H, R, dtype, cuda, seed=70 + R)
+    g = torch.Generator().manual_seed(R)
+    lengths = torch.randint(1, S + 1, (B,), generator=g).tolist()
+    x = torch.randn(B * S, H, generator=g).to(dtype).to(cuda)
+    y = torch.randn(B * S, 3 * H, generator=g).to(dtype).to(cuda)
+    segs = segments_padded(B, S, n_slots, seed=R, lengths=lengths)
+    persistent = run_apply(x, y, fc, segs, [0, 1, 2], [0, H, 2 * H])
+    per_tile = run_per_tile(run_apply, x, y, fc, segs, [0, 1, 2], [0, H, 2 * H])
+    assert torch.equal(persistent, per_tile)
+    ref = segmented_apply(x.cpu(), y.cpu(), a_of, b_of, segs, col_offsets=[0, H, 2 * H], modules=[0, 1, 2])
+    check(persistent.cpu(), ref, y.cpu(), dtype)
+
+
+@pytest.mark.parametrize("R", [8, 16, 64])
+def test_tc_persistent_shrink_with_multi_segment_tiles(cuda, R):
+    """Packed segments: tiles holding one segment go to the persistent shrink,
+    tiles holding several to the per-tile kernel, in one call; u equals the
+    per-tile kernel's everywhere and is zero on rows outside every segment."""
+    dtype = torch.bfloat16
+    H, n_slots, n_mod = 512, 7, 2
+    g = torch.Generator().manual_seed(300 + R)
+    lengths = [300, 40, 17, 128, 256, 5, 90, 200]
+    starts, t = [], 0
+    for i, n in enumerate(lengths):
+        starts.append(t)
+        t += n + (3 if i % 3 == 0 else 0)  # a few uncovered rows between segments
+    T = t + 50
+    slots = torch.randint(0, n_slots, (len(lengths),), generator=g).tolist()
+    fc, a_of, _ = make_cache(n_slots, n_mod, H, R, dtype, cuda, seed=90 + R)
+    x = torch.randn(T, H, generator=g).to(dtype).to(cuda)
+    st = SegmentTable(starts, lengths, slots, T, cuda)
+    assert 0 < st.n_multi < st.n_tiles
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+
+    def shrink():
+        u = torch.full((n_mod, T, R), float("nan"), dtype=dtype, device=cuda)
+        lora_shrink(x, u, fc, st, [0, 1], status)
+        torch.cuda.synchronize()
+        assert status.item() == 0, nat.decode_status(status.item())
+        return u
+
+    nat.set_option(nat.LF_OPT_SHRINK_CLUSTER, 1)  # multi-segment tiles without a K split in both runs
+    persistent = shrink()
+    per_tile = run_per_tile(shrink)
+    covered = torch.zeros(T, dtype=torch.bool, device=cuda)
+    for s0, n in zip(starts, lengths):
+        covered[s0 : s0 + n] = True
+    tiles_touched = torch.zeros(T, dtype=torch.bool, device=cuda)
+    for s0, n in zip(starts, lengths):
+        tiles_touched[s0 // 128 * 128 : min(T, (s0 + n + 127) // 128 * 128)] = True
+    # rows of a tile that holds a segment are written (0 where uncovered); others are never read
+    assert torch.equal(persistent[:, tiles_touched], per_tile[:, tiles_touched])
+    assert not persistent[:, covered].isnan().any()
+    assert (persistent[:, tiles_touched & ~covered] == 0).all()
+    xc = x.cpu().float()
+    for m in range(n_mod):
+        for s0, n, k in zip(starts, lengths, slots):
+            ref = (xc[s0 : s0 + n] @ a_of(k, m).float()).to(dtype).float()
+            got = persistent[m, s0 : s0 + n].cpu().float()
+            assert (got - ref).abs().max().item() <= 2e-2 * max(ref.abs().max().item(), 1e-6)
+
+
+def test_tc_persistent_expand_many_items_per_cta(cuda):
+    """bge-m3 q/k/v shape: 256 tiles x 3 modules x 8 column blocks = 6,144 work
+    items over at most 148 CTAs, so every CTA cycles its stage ring many times;
+    the persistent shrink likewise streams 16 K blocks for each of 256 tiles."""
+    dtype = torch.bfloat16
+    B, S, H, R, n_slots = 64, 512, 1024, 16, 300
+    fc, a_of, b_of = make_cache(n_slots, 3, H, R, dtype, cuda, seed=81, std=0.02)
+    x = torch.randn(B * S, H, device=cuda, dtype=dtype)
+    y = torch.randn(B * S, 3 * H, device=cuda, dtype=dtype)
+    lengths = torch.randint(32, S + 1, (B,), generator=torch.Generator().manual_seed(3)).tolist()
+    segs = segments_padded(B, S, n_slots, seed=82, lengths=lengths)
+    st = SegmentTable([s for s, _, _ in segs], [l for _, l, _ in segs], [k for _, _, k in segs], B * S, cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    u = torch.empty(3, B * S, R, dtype=dtype, device=cuda)
+    lora_shrink(x, u, fc, st, [0, 1, 2], status)
+    # expand: persistent vs per-tile on the same u
+    persistent = y.clone()
+    lora_expand(u, persistent, fc, st, [0, 1, 2], [0, H, 2 * H], True, status)
+    per_tile = y.clone()
+    run_per_tile(lora_expand, u, per_tile, fc, st, [0, 1, 2], [0, H, 2 * H], True, status)
+    torch.cuda.synchronize()
+    assert status.item() == 0, nat.decode_status(status.item())
+    assert torch.equal(persistent, per_tile)
+    # the whole delta against the oracle on a few sequences
+    pick = [0, 17, 63]
+    sub = [segs[i] for i in pick]
+    rows = torch.cat([torch.arange(s, s + l) for s, l, _ in sub])
+    local, t0 = [], 0
+    for s, l, k in sub:
+        local.append((t0, l, k))
+        t0 += l
+    ref = segmented_apply(x.cpu()[rows], y.cpu()[rows], a_of, b_of, local, col_offsets=[0, H, 2 * H],
+                          modules=[0, 1, 2])
+    check(persistent.cpu()[rows], ref, y.cpu()[rows], dtype)

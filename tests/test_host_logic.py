@@ -51,15 +51,15 @@ def test_segment_table_layout_and_tiles():
     h = st.host.tolist()
     # tile records first (16-byte aligned): {tile, first segment, count, slot of first}
     # [0,200) -> tiles 0,1 ; [200,210) -> tile 1 ; the empty segment -> none
-    assert st.n_tiles == 2
+    assert st.n_tiles == 2 and st.n_multi == 1
     assert h[:8] == [0, 0, 1, 5, 1, 0, 2, 5]
     assert h[8:11] == [0, 200, 400] and h[11:14] == [200, 10, 0] and h[14:17] == [5, 0, 5]
     assert st.real_tokens == 210
-    s, l, k, t, nt = st.ptrs()
-    assert (t - st.table.data_ptr()) == 0 and s - t == 32 and nt == 2
-    # several short segments in one tile
+    s, l, k, t, nt, nm = st.ptrs()
+    assert (t - st.table.data_ptr()) == 0 and s - t == 32 and nt == 2 and nm == 1
+    # several short segments in one tile: single-segment tiles are listed first
     st2 = SegmentTable([0, 10, 130], [10, 100, 5], [1, 2, 3], 200, "cpu")
-    assert st2.host.tolist()[:8] == [0, 0, 2, 1, 1, 2, 1, 3]
+    assert st2.host.tolist()[:8] == [1, 2, 1, 3, 0, 0, 2, 1] and st2.n_multi == 1
 
 
 # ------------------------------------------------------------ adapter store ---

@@ -56,22 +56,22 @@ def test_argument_validation_happens_before_any_device_work(lib):
     mods = nat.i32_array([0])
     offs = nat.i64_array([0])
     # unknown dtype
-    rc = lib.lf_lora_shrink(None, 7, None, 64, 128, 64, 16, None, 0, 0, 1, 1, mods, None, None, None, 0, None, 0,
+    rc = lib.lf_lora_shrink(None, 7, None, 64, 128, 64, 16, None, 0, 0, 1, 1, mods, None, None, None, 0, None, 0, 0,
                             None, None)
     assert rc == LF_ERR_INVALID and b"dtype" in lib.lf_last_error()
     # too many modules
     rc = lib.lf_lora_expand(None, 1, None, None, 64, 128, 64, 16, None, 0, 0, 1, 5, mods, offs, None, None, None, 0,
-                            None, 0, 1, None)
+                            None, 0, 0, 1, None)
     assert rc == LF_ERR_INVALID and b"n_modules" in lib.lf_last_error()
     # workspace too small is its own error code
     buf = ctypes.create_string_buffer(64)
     addr = ctypes.addressof(buf)
     rc = lib.lf_lora_apply(None, 1, addr, 64, addr, 64, 128, 64, 16, addr, 0, 0, addr, 0, 0, 1, 1, mods, offs,
-                           None, None, None, 0, None, 0, addr, 16, None)
+                           None, None, None, 0, None, 0, 0, addr, 16, None)
     assert rc == 4 and b"workspace" in lib.lf_last_error()
     # bad tile list
     rc = lib.lf_lora_apply(None, 1, addr, 64, addr, 64, 128, 64, 16, addr, 0, 0, addr, 0, 0, 1, 1, mods, offs,
-                           None, None, None, 0, None, 3, addr, 1 << 20, None)
+                           None, None, None, 0, None, 3, 0, addr, 1 << 20, None)
     assert rc == LF_ERR_INVALID and b"tile" in lib.lf_last_error()
     # head: unknown pooling
     rc = lib.lf_head_forward(None, 1, addr, 64, 64, None, 2, 4, 64, 9, None, None, None, None, 0, None, None, 0,
