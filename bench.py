@@ -75,6 +75,7 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--ranks", default="8,16,64", help="--mode op: LoRA ranks to measure")
     ap.add_argument("--persistent", type=int, default=1, help="0: per-tile expand kernel only")
+    ap.add_argument("--no-pack", action="store_true", help="serve: run the padded forward instead of the packed one")
     return ap.parse_args()
 
 
@@ -220,12 +221,17 @@ def run_ours(args):
     lengths = mask.sum(1).tolist()
     ids_d, mask_d = ids.to(dev), mask.to(dev)
     batch = emb._get_assembler().batch_lora(tenants, args.seq, lengths)
+    packed = None if args.no_pack else model.pack(ids, lengths, store.slots(tenants))
+    emb.pack_tokens = packed is not None
     H = emb.config.hidden_size
     gathered = torch.empty(world * args.batch, H, dtype=torch.bfloat16, device=dev) if world > 1 else None
 
     def step():
         with torch.no_grad():
-            pooled = model.encode_pooled(ids_d, mask_d, batch, pooling="cls")
+            if packed is not None:
+                pooled = model.encode_pooled_packed(packed, store, pooling="cls")
+            else:
+                pooled = model.encode_pooled(ids_d, mask_d, batch, pooling="cls")
             out = lf.head.l2_normalize(pooled)
             if world > 1:
                 dist.all_gather_into_tensor(gathered, out)
@@ -264,7 +270,7 @@ def run_ours(args):
         ms, lora_ms_step = t.tolist()
     emb.check_device_status()
 
-    segs = batch.segments
+    segs = packed.segments if packed is not None else batch.segments
     n_unique = len(set(tenants))
     bytes_step, ops_step = lora_bytes_per_step(segs, n_unique, args.layers, H, args.rank)
     achieved = bytes_step / (lora_ms_step * 1e-3) / 1e9
@@ -275,7 +281,10 @@ def run_ours(args):
     if not args.no_e2e:
         ids_h, mask_h = ids.pin_memory(), mask.pin_memory()
         out_h = torch.empty(args.batch, H, dtype=torch.bfloat16).pin_memory()
-        h2d = ids_h.numel() * 8 + mask_h.numel() * 8 + segs.host.numel() * 4
+        # what embed_tokens copies to the device each step: the packed token
+        # tables and segment table, or the padded ids/mask and segment table
+        h2d = (packed.host_bytes if packed is not None
+               else ids_h.numel() * 8 + mask_h.numel() * 8 + segs.host.numel() * 4)
         d2h = out_h.numel() * 2
 
         def e2e_step():
@@ -333,6 +342,8 @@ def run_ours(args):
             "seq_len": args.seq,
             "real_tokens_per_gpu_step": segs.real_tokens,
             "padded_tokens_per_gpu_step": args.batch * args.seq,
+            "tokens_computed": "real tokens only (packed, attention per sequence)" if packed is not None
+                               else "all padded positions (LoRA on real tokens only)",
             "parallelism": f"dp{world}",
             "adapters": args.adapters,
             "rank": args.rank,

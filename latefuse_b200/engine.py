@@ -32,6 +32,7 @@ from latefuse_b200.batch import BatchedLRWeights, BatchLora, LayerwiseBatchedWei
 from latefuse_b200.config import LoraServingConfig
 from latefuse_b200.head import LRHeadOps, pool_tokens, validate_pooling
 from latefuse_b200.lora import FactorCache, SegmentTable, lora_apply, per_row_cache, workspace_bytes
+from latefuse_b200.packing import PackedBatch, pack_rows
 
 # Per-layer module paths (relative to "encoder.layer.{i}.") for each logical target.
 # "dense" is the attention-output projection.
@@ -250,6 +251,23 @@ class HFEncoderWithLora(nn.Module):
 # ---------------------------------------------------------------------------
 _OFFSET_POSITION_TYPES = {"roberta", "xlm-roberta", "xlm-roberta-xl", "camembert", "mpnet"}
 _QKV = ("query", "key", "value")
+
+
+def varlen_attention(q: Tensor, k: Tensor, v: Tensor, cu_seqlens: Tensor, max_len: int) -> Tensor:
+    """Non-causal attention of each packed sequence with itself, ``(T, heads, head_dim)``
+    in and out, scale ``1/sqrt(head_dim)`` (FlashAttention's varlen forward)."""
+    return torch.ops.aten._flash_attention_forward(q, k, v, cu_seqlens, cu_seqlens, max_len, max_len, 0.0,
+                                                   False, False)[0]
+
+
+def packed_mean(h: Tensor, pb: PackedBatch) -> Tensor:
+    """Per-row mean of packed token states, with the reference's rounding points
+    (``src/latefuse/ops/pooling.py:61-71``): the sum and the count are held in the
+    model dtype, then divided."""
+    acc = torch.zeros(pb.n_rows, h.shape[1], dtype=torch.float32, device=h.device)
+    acc.index_add_(0, pb.row_of_token, h.float())
+    counts = pb.row_lengths.to(h.dtype).clamp(min=1e-9)
+    return acc.to(h.dtype) / counts.unsqueeze(1)
 
 
 class _Layer(nn.Module):
@@ -475,6 +493,77 @@ class EncoderWithLora(nn.Module):
             o = F.linear(mid, layer.wo2, layer.bo2)
             h = F.layer_norm(o + h1, (H,), layer.ln2.weight, layer.ln2.bias, self.eps)
         return h.view(B, S, H)
+
+    # -- padding-free forward ------------------------------------------------
+    @property
+    def supports_packing(self) -> bool:
+        """Whether :meth:`encode_pooled_packed` can run: FlashAttention's varlen
+        kernel takes f16/bf16 with head_dim a multiple of 8 up to 256."""
+        return (self.config.dtype in (torch.float16, torch.bfloat16) and self.head_dim % 8 == 0
+                and self.head_dim <= 256)
+
+    def pack(self, input_ids: Tensor, lengths: list[int], slots: list[int],
+             token_type_ids: Tensor | None = None) -> PackedBatch:
+        """Pack right-padded host rows (``lengths[b]`` real tokens first) for
+        :meth:`encode_pooled_packed`; position ids follow the padded rows."""
+        return pack_rows(input_ids, lengths, slots, self.position_ids(input_ids), token_type_ids,
+                         self.config.device)
+
+    def encode_packed(self, pb: PackedBatch, store, apply_lora: bool = True) -> Tensor:
+        """Final hidden states of the real tokens, ``(n_tokens, H)`` in packed order.
+
+        Same per-token arithmetic as :meth:`encode`; attention runs per sequence
+        over ``cu_seqlens`` (FlashAttention varlen), so no padded key exists.
+        ``store`` is the :class:`~latefuse_b200.store.AdapterStore` whose slots
+        ``pb.segments`` names.
+        """
+        T = pb.n_tokens
+        H, nh, hd = self.config.hidden_size, self.num_heads, self.head_dim
+        x = self.word_embeddings(pb.ids) + self.token_type_embeddings(pb.token_types)
+        x = x + self.position_embeddings(pb.positions)
+        h = F.layer_norm(x, (H,), self.emb_ln.weight, self.emb_ln.bias, self.eps)
+
+        do_lora = apply_lora and store is not None and (self._qkv_targets or self._dense_target)
+        if do_lora:
+            qkv_idx = [store.module_index(m) for m, _ in self._qkv_targets]
+            dense_idx = [store.module_index("dense")] if self._dense_target else []
+            ws = self._runner.workspace(T, max(1, len(self._qkv_targets)), h.device, h.dtype)
+            status = self._runner.status
+            qkv_offs = [j * H for _, j in self._qkv_targets]
+            segs = pb.segments
+
+        for l, layer in enumerate(self.layers):
+            qkv = F.linear(h, layer.wqkv, layer.bqkv)  # (T, 3H)
+            if do_lora and self._qkv_targets:
+                ev = self._event_pair("qkv")
+                lora_apply(h, qkv, store.factor_cache(l), segs, qkv_idx, qkv_offs, ws, status)
+                if ev is not None:
+                    ev[1].record()
+            q, k, v = qkv.view(T, 3, nh, hd).unbind(1)
+            ctx = varlen_attention(q, k, v, pb.cu_seqlens, pb.max_len).view(T, H)
+            ao = F.linear(ctx, layer.wo, layer.bo)
+            if do_lora and self._dense_target:
+                ev = self._event_pair("dense")
+                lora_apply(ctx, ao, store.factor_cache(l), segs, dense_idx, [0], ws, status)
+                if ev is not None:
+                    ev[1].record()
+            h1 = F.layer_norm(ao + h, (H,), layer.ln1.weight, layer.ln1.bias, self.eps)
+            mid = self.act(F.linear(h1, layer.wi, layer.bi))
+            o = F.linear(mid, layer.wo2, layer.bo2)
+            h = F.layer_norm(o + h1, (H,), layer.ln2.weight, layer.ln2.bias, self.eps)
+        return h
+
+    def encode_pooled_packed(self, pb: PackedBatch, store, pooling: str = "auto",
+                             apply_lora: bool = True) -> Tensor:
+        """Pooled ``(B, H)`` rows in input order from a packed batch."""
+        validate_pooling(pooling)
+        h = self.encode_packed(pb, store, apply_lora)
+        if pooling == "mean":
+            return packed_mean(h, pb)
+        cls = h.index_select(0, pb.first_token)
+        if pooling == "auto":
+            return torch.tanh(F.linear(cls, self.pooler_w, self.pooler_b))
+        return cls
 
     def forward(self, input_ids: Tensor, attention_mask: Tensor | None, lora_weights,
                 lr_weights: BatchedLRWeights, output_lr: Tensor, token_type_ids: Tensor | None = None,

@@ -1,0 +1,117 @@
+"""Padding-free ("packed") batches for the native encoder.
+
+A right-padded ``(B, S)`` batch with real lengths ``len_b`` holds ``sum(len_b)``
+real tokens.  The reference runs every layer over all ``B*S`` positions and
+keeps padded keys out of attention with the mask
+(``src/latefuse/model/encoder.py:45-142``; the hf engine through HuggingFace's
+attention mask).  No real token's output depends on a padded position: the
+embeddings, projections, LoRA deltas, LayerNorms and FFN are per token, and
+attention never reads a padded key.  So the native encoder can run the per-token
+ops on the real tokens only and attention per sequence (``cu_seqlens``), with
+the same results on every real token.
+
+Rows are laid out sorted by adapter slot (stable), so all rows of one tenant
+are adjacent and the LoRA delta sees one segment per tenant run rather than one
+per row.  Everything the device needs (token ids, position ids, token types,
+``cu_seqlens``, the first token of each row, the row of each token, row
+lengths) goes over in one pinned host-to-device copy.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+from torch import Tensor
+
+from latefuse_b200.lora import SegmentTable
+
+
+@dataclass
+class PackedBatch:
+    """One mixed-tenant batch with its padding removed.
+
+    Packed order is the rows sorted by slot; ``order[i]`` is the input row at
+    packed position ``i``.  Device tensors are int32 views of one buffer.
+    """
+
+    n_rows: int
+    n_tokens: int
+    max_len: int
+    lengths: list[int]          # per input row
+    order: list[int]            # packed position -> input row
+    slots: list[int]            # per input row
+    ids: Tensor                 # (n_tokens,) token ids
+    positions: Tensor           # (n_tokens,) position ids
+    token_types: Tensor         # (n_tokens,) token type ids
+    cu_seqlens: Tensor          # (n_rows + 1,) sequence boundaries in packed order
+    first_token: Tensor         # (n_rows,) packed index of each input row's first token
+    row_of_token: Tensor        # (n_tokens,) input row of each packed token
+    row_lengths: Tensor         # (n_rows,) per input row
+    segments: SegmentTable      # LoRA segments: runs of rows with one slot
+    host_bytes: int             # bytes copied host -> device for this batch
+
+
+def pack_rows(input_ids: Tensor, lengths: list[int], slots: list[int], positions: Tensor,
+              token_type_ids: Tensor | None, device: torch.device) -> PackedBatch:
+    """Pack the real tokens of right-padded host rows (``1 <= lengths[b] <= S``).
+
+    ``positions`` are the model's position ids for the padded rows (computed on
+    the host by the model's own rule), so packing changes no position.
+    """
+    B, S = input_ids.shape
+    if len(lengths) != B or len(slots) != B:
+        raise ValueError(f"{B} rows but {len(lengths)} lengths and {len(slots)} slots")
+    lens = np.asarray(lengths, dtype=np.int64)
+    if B == 0 or lens.min() < 1 or lens.max() > S:
+        raise ValueError("every packed row needs 1..S real tokens")
+    order = sorted(range(B), key=lambda b: slots[b])  # stable: ties keep input order
+    olens = lens[order]
+    cu = np.zeros(B + 1, dtype=np.int64)
+    np.cumsum(olens, out=cu[1:])
+    T = int(cu[-1])
+    # flat (row * S + col) index of every real token, in packed order
+    row_base = np.repeat(np.asarray(order, dtype=np.int64) * S, olens)
+    col = np.arange(T, dtype=np.int64) - np.repeat(cu[:-1], olens)
+    sel = row_base + col
+    first = np.empty(B, dtype=np.int64)
+    first[order] = cu[:-1]
+
+    n_parts = 3 * T + (B + 1) + B + T + B
+    buf = torch.empty(n_parts, dtype=torch.int32, pin_memory=device.type == "cuda")
+    a = buf.numpy()
+    o = 0
+    a[o:o + T] = input_ids.reshape(-1).numpy()[sel]
+    o += T
+    a[o:o + T] = positions.reshape(-1).numpy()[sel]
+    o += T
+    a[o:o + T] = token_type_ids.reshape(-1).numpy()[sel] if token_type_ids is not None else 0
+    o += T
+    a[o:o + B + 1] = cu
+    o += B + 1
+    a[o:o + B] = first
+    o += B
+    a[o:o + T] = np.repeat(np.asarray(order, dtype=np.int64), olens)
+    o += T
+    a[o:o + B] = lens
+    dev_buf = buf.to(device, non_blocking=True) if device.type == "cuda" else buf.clone()
+    views, o = [], 0
+    for n in (T, T, T, B + 1, B, T, B):
+        views.append(dev_buf[o:o + n])
+        o += n
+
+    # LoRA segments: maximal runs of packed rows that share a slot
+    starts, seg_lens, seg_slots = [], [], []
+    for i, b in enumerate(order):
+        if seg_slots and seg_slots[-1] == slots[b]:
+            seg_lens[-1] += int(lens[b])
+        else:
+            starts.append(int(cu[i]))
+            seg_lens.append(int(lens[b]))
+            seg_slots.append(int(slots[b]))
+    segs = SegmentTable(starts, seg_lens, seg_slots, T, device)
+    return PackedBatch(n_rows=B, n_tokens=T, max_len=int(lens.max()), lengths=[int(n) for n in lens],
+                       order=order, slots=list(slots), ids=views[0], positions=views[1], token_types=views[2],
+                       cu_seqlens=views[3], first_token=views[4], row_of_token=views[5], row_lengths=views[6],
+                       segments=segs, host_bytes=n_parts * 4 + segs.host.numel() * 4)

@@ -6,8 +6,10 @@ forward passes (``src/latefuse/tasks/base.py``).  The wrappers add embeddings
 (L2-normalised), classification with per-tenant heads, and cross-encoder
 reranking on top.  Differences from the reference, all invisible in results:
 tenant ids map to cache slots instead of gathered weights; padded positions of
-right-padded rows get no LoRA delta (``skip_padding``); softmax/sigmoid of the
-heads run on the GPU next to the head GEMV.
+right-padded rows get no LoRA delta (``skip_padding``), and with the native
+encoder they are not computed at all (``pack_tokens``: real tokens only, rows
+grouped by tenant, attention per sequence); softmax/sigmoid of the heads run on
+the GPU next to the head GEMV.
 """
 
 from __future__ import annotations
@@ -75,7 +77,7 @@ class TaskPipeline:
 
     def __init__(self, config: LoraServingConfig, *, engine: str = "hf", assembler: str = "cpu",
                  pooling: str = "auto", tokenizer=None, model=None, store: AdapterStore | None = None,
-                 skip_padding: bool = True):
+                 skip_padding: bool = True, pack_tokens: bool = True):
         if engine not in ENGINES:
             raise ValueError(f"unknown engine {engine!r}; expected one of {', '.join(map(repr, ENGINES))}")
         if assembler not in ASSEMBLERS:
@@ -84,6 +86,7 @@ class TaskPipeline:
         self.config = config
         self.pooling = pooling
         self.skip_padding = skip_padding
+        self.pack_tokens = pack_tokens
         self._tokenizer = tokenizer
         if model is None:
             cls = HFEncoderWithLora if engine == "hf" else EncoderWithLora
@@ -170,6 +173,16 @@ class TaskPipeline:
         lengths = None
         if self.skip_padding and attention_mask is not None and attention_mask.device.type == "cpu":
             lengths = right_padded_lengths(attention_mask)
+        packable = (self.pack_tokens and lengths is not None and min(lengths, default=0) >= 1
+                    and input_ids.device.type == "cpu"
+                    and (token_type_ids is None or token_type_ids.device.type == "cpu")
+                    and getattr(self.model, "supports_packing", False))
+        if packable:
+            # padding-free forward: real tokens only, rows grouped by tenant
+            slots = self.store.slots(list(tenants))
+            pb = self.model.pack(input_ids, lengths, slots, token_type_ids)
+            with torch.no_grad():
+                return self.model.encode_pooled_packed(pb, self.store, pooling)
         batch = self._get_assembler().batch_lora(list(tenants), input_ids.shape[1], lengths)
 
         def dev(t):

@@ -75,6 +75,47 @@ def test_bf16_matches_oracle_on_gpu(cuda, engine):
     assert (ours - ref).abs().max().item() <= 2e-2 * ref.abs().max().item()
 
 
+@pytest.mark.parametrize("pooling", ["cls", "mean", "auto"])
+def test_packed_forward_matches_oracle_bf16(cuda, pooling):
+    """The padding-free forward (real tokens only, rows grouped by tenant,
+    attention per sequence) against the reference's padded forward run by the
+    oracle on the same GPU, and against this engine's padded path."""
+    model, store, c, g = setup(cuda, torch.bfloat16, "bert")
+    assert model.supports_packing
+    base_ref, _ = tiny_xlmr(torch.bfloat16)
+    oracle = HookedEncoder(base_ref.to(cuda), g["adapters"], g["targets"])
+    ids, mask = g["ids"].to(cuda), g["mask"].to(cuda)
+    lengths = g["mask"].sum(1).tolist()
+    pb = model.pack(g["ids"], lengths, store.slots(g["tenants"]))
+    assert pb.n_tokens == sum(lengths)
+    with torch.no_grad():
+        ours = model.encode_pooled_packed(pb, store, pooling).float()
+        padded = model.encode_pooled(ids, mask, batch_for(store, c, g, True), pooling=pooling).float()
+    ref = oracle.encode_pooled(ids, mask, g["tenants"], pooling).float()
+    for got in (ours, padded):
+        rel = ((got - ref).norm(dim=-1) / ref.norm(dim=-1)).max().item()
+        assert rel < 2e-2, rel
+        assert (got - ref).abs().max().item() <= 2e-2 * ref.abs().max().item()
+    assert model._runner.status.item() == 0
+
+
+def test_packed_forward_tenant_isolation_and_row_order(cuda):
+    """Each row's pooled output depends only on its own tokens and tenant:
+    permuting rows (which changes the packed layout and segment runs) permutes
+    the outputs, and a row served alone equals the same row in a mixed batch."""
+    model, store, c, g = setup(cuda, torch.bfloat16, "bert")
+    ids, mask, tenants = g["ids"], g["mask"], list(g["tenants"])
+    lengths = mask.sum(1).tolist()
+    with torch.no_grad():
+        full = model.encode_pooled_packed(model.pack(ids, lengths, store.slots(tenants)), store, "cls")
+        perm = list(reversed(range(len(tenants))))
+        pb = model.pack(ids[perm], [lengths[i] for i in perm], store.slots([tenants[i] for i in perm]))
+        permuted = model.encode_pooled_packed(pb, store, "cls")
+        alone = model.encode_pooled_packed(model.pack(ids[:1], lengths[:1], store.slots(tenants[:1])), store, "cls")
+    torch.testing.assert_close(permuted, full[perm], atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(alone[0], full[0], atol=2e-2, rtol=2e-2)
+
+
 def test_hooks_must_all_fire(cuda):
     model, store, c, g = setup(cuda, torch.float32, "hf")
     ids, mask = g["ids"].to(cuda), g["mask"].to(cuda)

@@ -63,6 +63,36 @@ def test_segment_table_layout_and_tiles():
 
 
 # ------------------------------------------------------------ adapter store ---
+def test_pack_rows_layout():
+    """Packed order = rows sorted by slot (stable); every index table agrees with
+    the padded rows; adjacent rows of one slot form one LoRA segment."""
+    from latefuse_b200.packing import pack_rows
+
+    B, S = 4, 6
+    ids = torch.arange(B * S).view(B, S) + 100
+    pos = torch.arange(S).expand(B, S) + 2
+    tt = torch.zeros(B, S, dtype=torch.long)
+    tt[:, 3:] = 1
+    lengths, slots = [6, 2, 4, 1], [5, 3, 5, 3]
+    pb = pack_rows(ids, lengths, slots, pos, tt, torch.device("cpu"))
+    assert pb.order == [1, 3, 0, 2]
+    assert pb.n_tokens == 13 and pb.max_len == 6
+    assert pb.cu_seqlens.tolist() == [0, 2, 3, 9, 13]
+    assert pb.ids.tolist() == torch.cat([ids[b, :lengths[b]] for b in pb.order]).tolist()
+    assert pb.positions.tolist() == torch.cat([pos[b, :lengths[b]] for b in pb.order]).tolist()
+    assert pb.token_types.tolist() == torch.cat([tt[b, :lengths[b]] for b in pb.order]).tolist()
+    for b in range(B):  # first token of each input row is its CLS
+        assert pb.ids[pb.first_token[b]].item() == ids[b, 0].item()
+    assert pb.row_of_token.tolist() == sum(([b] * lengths[b] for b in pb.order), [])
+    assert pb.row_lengths.tolist() == lengths
+    segs = pb.segments
+    assert segs.n_segs == 2 and segs.slots == [3, 5]
+    starts, seg_lens = segs.host[4 * segs.n_tiles:].view(3, -1)[:2].tolist()
+    assert starts == [0, 3] and seg_lens == [3, 10]
+    with pytest.raises(ValueError):
+        pack_rows(ids, [6, 0, 4, 1], slots, pos, None, torch.device("cpu"))
+
+
 def test_store_shapes_and_accounting():
     c = cfg()
     store = lf.AdapterStore(c)
