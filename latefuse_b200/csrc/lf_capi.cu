@@ -337,9 +337,8 @@ static int expand_impl(cudaStream_t stream, int dtype, const void* u, void* y, i
     if (p.n_tiles == 0) return LF_OK;
     return run_expand_tc(dtype, p, rank, nt, stream);
   }
-  const int n_single = n_tiles - n_multi;
-  int first_old = 0;  // records the one-tile-per-CTA kernel handles: [first_old, n_tiles)
-  if (g_persistent.load() && nt == 128 && n_single > 0) {
+  (void)n_multi;  // the persistent expand takes tiles with any number of segments
+  if (g_persistent.load() && nt == 128 && n_tiles > 0) {
     ExpandPersistParams q;
     memset(&q, 0, sizeof(q));
     q.y_map = p.y_map;
@@ -357,16 +356,18 @@ static int expand_impl(cudaStream_t stream, int dtype, const void* u, void* y, i
     q.n_tokens = n_tokens;
     q.n_modules = n_modules;
     q.n_col_blocks = hidden / 128;
-    q.n_tiles = n_single;
+    q.n_slots = n_slots;
+    q.n_tiles = n_tiles;
     q.tiles = tiles;
+    q.seg_start = seg_start;
+    q.seg_len = seg_len;
+    q.seg_slot = seg_slot;
+    q.n_segs = n_segs;
     q.status = status;
-    int rc = run_expand_persist(dtype, q, rank, 128, stream);
-    if (rc) return rc;
-    first_old = n_single;
+    return run_expand_persist(dtype, q, rank, 128, stream);
   }
-  if (first_old == n_tiles) return LF_OK;
-  p.tiles = tiles + 4 * first_old;
-  p.n_tiles = n_tiles - first_old;
+  p.tiles = tiles;
+  p.n_tiles = n_tiles;
   return run_expand_tc(dtype, p, rank, nt, stream);
 }
 

@@ -60,8 +60,13 @@ struct alignas(64) ExpandPersistParams {
   int64_t y_col_off[kMaxModules];
   int32_t n_modules;
   int32_t n_col_blocks;              // hidden / NT
-  int32_t n_tiles;                   // single-segment tile records
-  const int32_t* tiles;              // records {tile, first segment, 1, slot}
+  int32_t n_slots;
+  int32_t n_tiles;                   // tile records
+  const int32_t* tiles;              // records {tile, first segment, segment count, first slot}
+  const int32_t* seg_start;
+  const int32_t* seg_len;
+  const int32_t* seg_slot;
+  int32_t n_segs;
   int32_t* status;
 };
 

@@ -1,26 +1,32 @@
-// Persistent, warp-specialised LoRA kernels for tiles that hold one segment.
+// Persistent, warp-specialised LoRA kernels over the tile records.
 //
 // Both kernels run one CTA per SM that loops over work items, with three roles:
 //   warp 0      producer: streams the item's operands by TMA into a ring of
 //               shared-memory stages (mbarrier "full"/"empty" per stage);
 //   warp 1      MMA issuer: tcgen05.mma into one of two TMEM accumulators;
-//   warps 2-5   epilogue: drains the accumulator (each warp owns the 32 TMEM
-//               lanes = tile rows of its quadrant) while the next item's loads
-//               and MMAs are already in flight.
+//   epilogue    drains the accumulator (a warp may only read the 32 TMEM lanes
+//               = tile rows of its quadrant) while the next item's loads and
+//               MMAs are already in flight: 4 warps in the shrink, 8 in the
+//               expand (two per quadrant, 64 columns each).
 //
-// Shrink  (item = 128-token tile):  u[m][t] = round(x[t] . A(slot, m)) for every
-//         module, the hidden dimension streamed in 64-wide K blocks; the
-//         epilogue writes u (0 for tile rows outside the tile's segment, which
-//         the expand relies on).
+// Shrink  (item = 128-token tile holding one segment):  u[m][t] =
+//         round(x[t] . A(slot, m)) for every module, the hidden dimension
+//         streamed in 64-wide K blocks; the epilogue writes u (0 for tile rows
+//         outside the segment).  Tiles with several segments use the
+//         one-tile-per-CTA kernel in lf_lora_tc.cu.
 // Expand  (item = tile x module x 128 columns):  y += round(u . B(slot, m)); the
 //         y tile, the B factor tile and the u tile (canonical K-major layout,
 //         straight from the shrink output) arrive by TMA; the epilogue adds in
 //         f32, rounds, writes a separate double-buffered output tile and stores
 //         it by TMA, so an input stage is free as soon as it has been read.
+//         A tile that holds k segments is k sub-items, one per segment, run
+//         back to back by the same CTA: each multiplies the tile's u by its
+//         segment's B and folds that segment's rows into the one output tile,
+//         which is stored once, after the last sub-item.  Segments are sorted
+//         by start and do not overlap (the segment-table contract).
 //
-// Tiles with several segments use the one-tile-per-CTA kernels in
-// lf_lora_tc.cu.  Every wait is bounded; a timeout sets LF_STATUS_TIMEOUT and
-// the roles unwind without leaving a warp at a hardware barrier.
+// Every wait is bounded; a timeout sets LF_STATUS_TIMEOUT and the roles unwind
+// without leaving a warp at a hardware barrier.
 #include "lf_common.cuh"
 #include "lf_internal.h"
 
@@ -34,6 +40,65 @@ constexpr int kSmemBudget = 220 * 1024;
 
 __device__ __forceinline__ bool aborted(const int32_t* flag) {
   return *reinterpret_cast<const volatile int32_t*>(flag) != 0;
+}
+
+// Number of sub-items (segments) of a record, clamped to the segment table.
+__device__ __forceinline__ int sub_items(const int4& rec, int n_segs) {
+  int k = rec.z < 1 ? 1 : rec.z;
+  if (rec.y >= 0 && rec.y < n_segs && k > n_segs - rec.y) k = n_segs - rec.y;
+  return k;
+}
+
+// Slot of sub-item j (the record carries the first one); -1 reads zeros by TMA fill.
+__device__ __forceinline__ int32_t sub_slot(const int4& rec, int j, const int32_t* seg_slot, int n_segs) {
+  if (j == 0) return rec.w;
+  const int g = rec.y + j;
+  return (g >= 0 && g < n_segs) ? __ldg(seg_slot + g) : -1;
+}
+
+// Tile rows [lo, hi) that one segment covers (lo == hi: none).
+struct SubRows {
+  int lo, hi;
+};
+
+__device__ __forceinline__ SubRows clip_rows(int64_t s0, int64_t l0, int64_t row0, int64_t n_tokens) {
+  const int64_t lo = max(s0, row0) - row0;
+  const int64_t hi = min(min(s0 + l0, row0 + kTile), n_tokens) - row0;
+  if (hi <= lo) return {0, 0};
+  return {int(lo), int(hi)};
+}
+
+// {start, len, slot} of the record's first segment (slot -1 if out of range).
+__device__ __forceinline__ int4 first_seg(const int4& rec, const int32_t* seg_start, const int32_t* seg_len,
+                                          const int32_t* seg_slot, int n_segs) {
+  if (rec.y < 0 || rec.y >= n_segs) return make_int4(0, 0, -1, 0);
+  return make_int4(__ldg(seg_start + rec.y), __ldg(seg_len + rec.y), __ldg(seg_slot + rec.y), 0);
+}
+
+// Rows of sub-item j of a record; seg0 is the record's first segment, loaded
+// ahead of time.  A segment whose slot is out of range, or a first segment
+// whose slot disagrees with the record, covers no rows and is reported.
+__device__ __forceinline__ SubRows rows_of(const int4& rec, int j, const int4& seg0, int64_t row0,
+                                           int64_t n_tokens, const int32_t* seg_start, const int32_t* seg_len,
+                                           const int32_t* seg_slot, int n_segs, int n_slots, int32_t* status,
+                                           bool report) {
+  int4 sg = seg0;
+  if (j > 0) {
+    const int g = rec.y + j;
+    if (g < 0 || g >= n_segs) {
+      if (report) set_status(status, LF_STATUS_BAD_SEGMENT);
+      return {0, 0};
+    }
+    sg = make_int4(__ldg(seg_start + g), __ldg(seg_len + g), __ldg(seg_slot + g), 0);
+  } else if (rec.y < 0 || rec.y >= n_segs || sg.z != rec.w) {
+    if (report) set_status(status, LF_STATUS_BAD_SEGMENT);
+    return {0, 0};
+  }
+  if (sg.z < 0 || sg.z >= n_slots) {
+    if (report) set_status(status, LF_STATUS_BAD_SLOT);
+    return {0, 0};
+  }
+  return clip_rows(sg.x, sg.y, row0, n_tokens);
 }
 
 template <int R>
@@ -69,11 +134,15 @@ struct ExpandCfg {
   static constexpr size_t kSmem = 1024 + size_t(kST) * kStageBytes + kOutBytes + kZeroB + kZeroU + kMeta;
 };
 
+constexpr int kExpandEpiWarps = 8;
+constexpr int kExpandThreads = 64 + 32 * kExpandEpiWarps;
+
 }  // namespace
 
 template <typename T, int R, int NT>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kExpandThreads, 1)
 lora_expand_persist_kernel(const __grid_constant__ ExpandPersistParams p) {
+  static_assert(NT == 128, "two epilogue warps per quadrant, 64 columns each");
   using C = ExpandCfg<R, NT>;
   constexpr int ST = C::kST;
   extern __shared__ uint8_t smem_raw[];
@@ -97,15 +166,17 @@ lora_expand_persist_kernel(const __grid_constant__ ExpandPersistParams p) {
   const int ncb = p.n_col_blocks;
   const int64_t per_tile = int64_t(p.n_modules) * ncb;
   const int64_t total = int64_t(p.n_tiles) * per_tile;
+  const int4* recs = reinterpret_cast<const int4*>(p.tiles);
+  auto rec_at = [&](int64_t i) { return i < total ? __ldg(recs + i / per_tile) : int4{}; };
 
   if (tid == 0) {
     for (int i = 0; i < ST; ++i) {
       mbar_init(bar(FULL + i), 1);
-      mbar_init(bar(EMPTY + i), 2);  // the MMA's commit + the epilogue's read of the y tile
+      mbar_init(bar(EMPTY + i), 2);  // the MMA's commit + the epilogue's release
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(ACC_FULL + i), 1);
-      mbar_init(bar(ACC_EMPTY + i), 4);  // one arrive per epilogue warp
+      mbar_init(bar(ACC_EMPTY + i), kExpandEpiWarps);  // one arrive per epilogue warp
     }
     *s_abort = 0;
     fence_mbar_init();
@@ -132,33 +203,41 @@ lora_expand_persist_kernel(const __grid_constant__ ExpandPersistParams p) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       int it = 0;
+      bool stop = false;
       int64_t item = blockIdx.x;
-      int4 rec = item < total ? __ldg(reinterpret_cast<const int4*>(p.tiles) + item / per_tile) : int4{};
-      for (; item < total; item += gridDim.x, ++it) {
-        const int s = it % ST;
-        const uint32_t ph = (it / ST) & 1;
+      int4 rnext = rec_at(item);
+      for (; item < total && !stop; item += gridDim.x) {
         const int rem = int(item % per_tile);
         const int m = rem / ncb, cb = rem % ncb;
-        const int4 cur = rec;
-        const int64_t next = item + gridDim.x;  // prefetch the next item's record
-        if (next < total) rec = __ldg(reinterpret_cast<const int4*>(p.tiles) + next / per_tile);
-        if (aborted(s_abort)) break;
-        if (!mbar_wait(bar(EMPTY + s), ph ^ 1)) { fail(); break; }
+        const int4 cur = rnext;
+        rnext = rec_at(item + gridDim.x);  // the next item's record loads while this one issues
+        const int k = sub_items(cur, p.n_segs);
         const int32_t row0 = cur.x * kTile;
         const int32_t col0 = int32_t(p.y_col_off[m]) + cb * NT;
-        s_meta[s] = make_int4(row0, col0, 0, 0);
-        const uint32_t st = s_stage0 + s * C::kStageBytes;
-        const uint32_t sy = st, sb = st + C::kYBytes, su = sb + C::kBBytes;
-        mbar_arrive_expect_tx(bar(FULL + s), C::kStageBytes);
-        for (int j = 0; j < C::kNBox; ++j)
-          tma_load_2d(sy + j * kYBox, &p.y_map, bar(FULL + s), col0 + j * 64, row0);
-        // an out-of-range slot reads zeros (TMA fill): the tile then gets no delta
-        for (int j = 0; j < C::kNBox; ++j)
-          tma_load_3d(sb + j * C::kBBox, &p.b_map[m], bar(FULL + s), cb * NT + j * 64, 0, cur.w);
-        tma_load_2d(su, &p.u_map, bar(FULL + s), 0, int32_t(int64_t(m) * p.n_tokens + row0));
+        for (int j = 0; j < k; ++j, ++it) {
+          const int s = it % ST;
+          const uint32_t ph = (it / ST) & 1;
+          if (aborted(s_abort)) { stop = true; break; }
+          if (!mbar_wait(bar(EMPTY + s), ph ^ 1)) { fail(); stop = true; break; }
+          const uint32_t st = s_stage0 + s * C::kStageBytes;
+          const uint32_t sy = st, sb = st + C::kYBytes, su = sb + C::kBBytes;
+          // an out-of-range slot reads zeros (TMA fill); the epilogue also adds nothing for it
+          const int32_t slot = sub_slot(cur, j, p.seg_slot, p.n_segs);
+          if (j == 0) {
+            s_meta[s] = make_int4(row0, col0, 0, 0);
+            mbar_arrive_expect_tx(bar(FULL + s), C::kStageBytes);
+            for (int b = 0; b < C::kNBox; ++b)
+              tma_load_2d(sy + b * kYBox, &p.y_map, bar(FULL + s), col0 + b * 64, row0);
+          } else {
+            mbar_arrive_expect_tx(bar(FULL + s), C::kBBytes + C::kUBytes);
+          }
+          for (int b = 0; b < C::kNBox; ++b)
+            tma_load_3d(sb + b * C::kBBox, &p.b_map[m], bar(FULL + s), cb * NT + b * 64, 0, slot);
+          tma_load_2d(su, &p.u_map, bar(FULL + s), 0, int32_t(int64_t(m) * p.n_tokens + row0));
+        }
       }
       if (aborted(s_abort)) {  // loads nobody consumed must land before the CTA exits (bounded)
-        for (int k = (it > ST ? it - ST : 0); k < it; ++k) mbar_wait(bar(FULL + k % ST), (k / ST) & 1);
+        for (int q = (it > ST ? it - ST : 0); q < it; ++q) mbar_wait(bar(FULL + q % ST), (q / ST) & 1);
       }
     }
   } else if (warp == 1) {
@@ -167,95 +246,139 @@ lora_expand_persist_kernel(const __grid_constant__ ExpandPersistParams p) {
       constexpr uint32_t idesc = umma_idesc_f16(DT<T>::umma_fmt, kTile, NT, /*a_mn=*/0, /*b_mn=*/1);
       using U = UOperand<R>;
       int it = 0;
-      for (int64_t item = blockIdx.x; item < total; item += gridDim.x, ++it) {
-        const int s = it % ST;
-        const uint32_t ph = (it / ST) & 1;
-        const int a = it & 1;
-        const uint32_t aph = (it >> 1) & 1;
-        if (aborted(s_abort)) break;
-        if (!mbar_wait(bar(FULL + s), ph)) { fail(); break; }
-        if (!mbar_wait(bar(ACC_EMPTY + a), aph ^ 1)) { fail(); break; }
-        tc_fence_after();
-        const uint32_t st = s_stage0 + s * C::kStageBytes;
-        const uint32_t sb = st + C::kYBytes, su = sb + C::kBBytes;
-#pragma unroll
-        for (int k = 0; k < C::kRP / 16; ++k) {
-          uint64_t ad, bd;
-          if (R == 8) {
-            ad = smem_desc(su, s_zero_u - su, U::kSbo, 0);  // K elements 8..15 read zeros
-            bd = smem_desc(sb, C::kBBox, s_zero_b - sb, 2);
-          } else {
-            ad = smem_desc(su + k * 32, 16, U::kSbo, U::kLayout);
-            bd = smem_desc(sb + k * 2048, C::kBBox, 1024, 2);
+      bool stop = false;
+      int64_t item = blockIdx.x;
+      int4 rnext = rec_at(item);
+      for (; item < total && !stop; item += gridDim.x) {
+        const int4 rec = rnext;
+        rnext = rec_at(item + gridDim.x);
+        const int k = sub_items(rec, p.n_segs);
+        for (int j = 0; j < k; ++j, ++it) {
+          const int s = it % ST;
+          const uint32_t ph = (it / ST) & 1;
+          const int a = it & 1;
+          const uint32_t aph = (it >> 1) & 1;
+          if (aborted(s_abort)) { stop = true; break; }
+          if (!mbar_wait(bar(FULL + s), ph) || !mbar_wait(bar(ACC_EMPTY + a), aph ^ 1)) {
+            fail();
+            stop = true;
+            break;
           }
-          umma_f16(tmem + a * NT, ad, bd, idesc, k > 0 ? 1u : 0u);
+          tc_fence_after();
+          const uint32_t st = s_stage0 + s * C::kStageBytes;
+          const uint32_t sb = st + C::kYBytes, su = sb + C::kBBytes;
+#pragma unroll
+          for (int kk = 0; kk < C::kRP / 16; ++kk) {
+            uint64_t ad, bd;
+            if (R == 8) {
+              ad = smem_desc(su, s_zero_u - su, U::kSbo, 0);  // K elements 8..15 read zeros
+              bd = smem_desc(sb, C::kBBox, s_zero_b - sb, 2);
+            } else {
+              ad = smem_desc(su + kk * 32, 16, U::kSbo, U::kLayout);
+              bd = smem_desc(sb + kk * 2048, C::kBBox, 1024, 2);
+            }
+            umma_f16(tmem + a * NT, ad, bd, idesc, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(bar(ACC_FULL + a));
+          umma_commit(bar(EMPTY + s));
         }
-        umma_commit(bar(ACC_FULL + a));
-        umma_commit(bar(EMPTY + s));
       }
       if (it > 0 && aborted(s_abort))  // MMAs in flight must finish before TMEM is released (bounded)
         mbar_wait(bar(ACC_FULL + ((it - 1) & 1)), ((it - 1) >> 1) & 1);
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2..5)
-    // All four warps take every iteration and every named barrier, whatever
+    // ------------------------------------------------------------ epilogue (warps 2..9)
+    // All eight warps take every item, sub-item and named barrier, whatever
     // happens, so that no warp can be left waiting at bar.sync.
-    const int quad = warp & 3;          // TMEM lane quadrant this warp may access
-    const int row = quad * 32 + lane;   // tile row
+    constexpr int kEpi = 32 * kExpandEpiWarps;
+    const int quad = warp & 3;              // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) >> 2;       // output columns [64 * half, 64 * half + 64)
+    const int row = quad * 32 + lane;       // tile row
     const bool leader = (warp == 2 && lane == 0);
-    int it = 0;
-    for (int64_t item = blockIdx.x; item < total; item += gridDim.x, ++it) {
-      const int s = it % ST;
-      const uint32_t ph = (it / ST) & 1;
-      const int a = it & 1;
-      const uint32_t aph = (it >> 1) & 1;
-      const int ob = it & 1;
-      bool ok = !aborted(s_abort);
-      if (ok && !(mbar_wait(bar(ACC_FULL + a), aph) && mbar_wait(bar(FULL + s), ph))) {
-        fail();
-        ok = false;
-      }
-      const bool work = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld is collective
-      // (B) the leader has seen the store that last read out[ob] finish (end of the previous iteration)
-      named_barrier_sync(1, 128);
-      tc_fence_after();
-      const uint32_t sy = s_stage0 + s * C::kStageBytes;
+    const uint32_t taddr = tmem + (uint32_t(quad * 32) << 16) + half * 64;
+    const uint32_t rbase = half * kYBox + (row >> 3) * 1024 + (row & 7) * 128;  // this row in a SW128 box
+    int it = 0, n_items = 0;
+    int4 meta = make_int4(0, 0, 0, 0);  // leader: the item's {row0, col0}
+    // records two items ahead and the next item's first segment, so that no
+    // dependent global load sits between two items
+    int64_t item = blockIdx.x;
+    int4 r1 = rec_at(item), r2 = rec_at(item + gridDim.x);
+    int4 g1 = first_seg(r1, p.seg_start, p.seg_len, p.seg_slot, p.n_segs);
+    for (; item < total; item += gridDim.x, ++n_items) {
+      const int4 rec = r1, seg0 = g1;
+      r1 = r2;
+      g1 = first_seg(r1, p.seg_start, p.seg_len, p.seg_slot, p.n_segs);
+      r2 = rec_at(item + 2 * int64_t(gridDim.x));
+      const int k = sub_items(rec, p.n_segs);
+      const int64_t row0 = int64_t(rec.x) * kTile;
+      const int ob = n_items & 1;
       const uint32_t so = s_out0 + ob * C::kYBytes;
-      if (work) {
-        for (int q = 0; q < NT / 32; ++q) {
-          float v[32];
-          {
-            float lo[16], hi[16];
-            tmem_ld16(tmem + (uint32_t(quad * 32) << 16) + a * NT + q * 32, lo);
-            tmem_ld16(tmem + (uint32_t(quad * 32) << 16) + a * NT + q * 32 + 16, hi);
+      // (B) the leader has seen the store that last read out[ob] finish (end of the previous item)
+      named_barrier_sync(1, kEpi);
+      for (int j = 0; j < k; ++j, ++it) {
+        const int s = it % ST;
+        const uint32_t ph = (it / ST) & 1;
+        const int a = it & 1;
+        const uint32_t aph = (it >> 1) & 1;
+        const SubRows sr = rows_of(rec, j, seg0, row0, p.n_tokens, p.seg_start, p.seg_len, p.seg_slot, p.n_segs,
+                                   p.n_slots, p.status, leader && (item % per_tile) == 0);
+        const bool in_seg = row >= sr.lo && row < sr.hi;
+        if (j > 0 && leader) mbar_arrive(bar(EMPTY + s));  // nothing here reads a later sub-item's stage
+        bool ok = !aborted(s_abort);
+        if (ok && !(mbar_wait(bar(ACC_FULL + a), aph) && (j > 0 || mbar_wait(bar(FULL + s), ph)))) {
+          fail();
+          ok = false;
+        }
+        const bool work = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld is collective
+        tc_fence_after();
+        if (work) {
+          uint32_t acc[64];
+          tmem_ld64(taddr + a * NT, acc);
+          if (j == 0 || in_seg) {
+            // sub-item 0 copies the y tile (its segment's rows with the delta);
+            // later sub-items add their segment's rows to the output tile
+            const uint32_t src = (j == 0 ? s_stage0 + s * C::kStageBytes : so) - base;
+            uint4 yv[8];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) { v[i] = lo[i]; v[16 + i] = hi[i]; }
+            for (int c = 0; c < 8; ++c)
+              yv[c] = *reinterpret_cast<const uint4*>(gbase + src + rbase + ((c ^ (row & 7)) << 4));
+            if (in_seg) {
+#pragma unroll
+              for (int c = 0; c < 8; ++c) {
+                uint32_t* w = reinterpret_cast<uint32_t*>(&yv[c]);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  // y + round(delta), rounded: the reference's two rounding points
+                  const float2 yf = Pack2<T>::unpack(w[i]);
+                  const float2 d = Pack2<T>::unpack(Pack2<T>::pack(__uint_as_float(acc[c * 8 + 2 * i]),
+                                                                   __uint_as_float(acc[c * 8 + 2 * i + 1])));
+                  w[i] = Pack2<T>::pack(yf.x + d.x, yf.y + d.y);
+                }
+              }
+            }
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              *reinterpret_cast<uint4*>(gbase + (so - base) + rbase + ((c ^ (row & 7)) << 4)) = yv[c];
           }
-          const uint32_t roff = (q >> 1) * kYBox + (row >> 3) * 1024 + (row & 7) * 128;
-#pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            const int chunk = (q & 1) * 4 + c4;
-            const uint32_t o = roff + ((chunk ^ (row & 7)) << 4);
-            uint4 raw16 = *reinterpret_cast<const uint4*>(gbase + (sy - base) + o);
-            T* e = reinterpret_cast<T*>(&raw16);
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              e[i] = DT<T>::from_f(DT<T>::to_f(e[i]) + round_through<T>(v[c4 * 8 + i]));
-            *reinterpret_cast<uint4*>(gbase + (so - base) + o) = raw16;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(ACC_EMPTY + a));  // this warp's TMEM reads are done
+        if (j == 0) {
+          // (C) every warp has read its rows of the y stage
+          named_barrier_sync(1, kEpi);
+          if (leader) {
+            meta = s_meta[s];             // read before the stage (and its metadata) is handed back
+            mbar_arrive(bar(EMPTY + s));  // the input stage may be refilled now
           }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(ACC_EMPTY + a));  // this warp's TMEM reads are done
       fence_proxy_async_smem();
-      // (C) every warp has read its rows of the y stage and written out[ob]
-      named_barrier_sync(1, 128);
+      // (D) every warp has written its rows of out[ob]
+      named_barrier_sync(1, kEpi);
       if (leader) {
-        const int4 meta = s_meta[s];  // read before the stage (and its metadata) is handed back
-        mbar_arrive(bar(EMPTY + s));  // the input stage may be refilled now
         if (!aborted(s_abort)) {
-          for (int j = 0; j < NT / 64; ++j) tma_store_2d(&p.y_map, so + j * kYBox, meta.y + j * 64, meta.x);
+          for (int b = 0; b < NT / 64; ++b) tma_store_2d(&p.y_map, so + b * kYBox, meta.y + b * 64, meta.x);
           tma_store_commit();
         }
         tma_store_wait_read_le1();  // the store that read the other output buffer has finished
@@ -484,7 +607,7 @@ int launch_expand(const ExpandPersistParams& p, cudaStream_t stream) {
   const int sms = sm_count();
   const int grid = int(total < sms ? total : sms);
   if (grid == 0) return LF_OK;
-  kern<<<grid, 192, C::kSmem, stream>>>(p);
+  kern<<<grid, kExpandThreads, C::kSmem, stream>>>(p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "launch lora_expand_persist");
   count_launch();

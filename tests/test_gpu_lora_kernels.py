@@ -375,6 +375,35 @@ def test_tc_persistent_shrink_with_multi_segment_tiles(cuda, R):
             assert (got - ref).abs().max().item() <= 2e-2 * max(ref.abs().max().item(), 1e-6)
 
 
+@pytest.mark.parametrize("R", [8, 16, 32, 64])
+def test_tc_persistent_packed_segments_equal_per_tile(cuda, R):
+    """Packed rows (no padding, segments starting anywhere, several per tile):
+    the persistent expand runs one sub-item per segment of a tile; the whole
+    delta equals the one-tile-per-CTA kernels' bit for bit and the oracle's
+    within tolerance."""
+    dtype = torch.bfloat16
+    H, n_slots = 512, 11
+    g = torch.Generator().manual_seed(500 + R)
+    lengths = torch.randint(1, 300, (24,), generator=g).tolist()
+    lengths[3] = 1
+    lengths[4] = 2
+    slots = torch.randint(0, n_slots, (24,), generator=g).tolist()
+    starts = [sum(lengths[:i]) for i in range(len(lengths))]
+    T = sum(lengths)
+    segs = list(zip(starts, lengths, slots))
+    fc, a_of, b_of = make_cache(n_slots, 3, H, R, dtype, cuda, seed=600 + R)
+    x = torch.randn(T, H, generator=g).to(dtype).to(cuda)
+    y = torch.randn(T, 3 * H, generator=g).to(dtype).to(cuda)
+    st = SegmentTable(starts, lengths, slots, T, cuda)
+    assert st.n_multi > 0
+    nat.set_option(nat.LF_OPT_SHRINK_CLUSTER, 1)
+    persistent = run_apply(x, y, fc, segs, [0, 1, 2], [0, H, 2 * H])
+    per_tile = run_per_tile(run_apply, x, y, fc, segs, [0, 1, 2], [0, H, 2 * H])
+    assert torch.equal(persistent, per_tile)
+    ref = segmented_apply(x.cpu(), y.cpu(), a_of, b_of, segs, col_offsets=[0, H, 2 * H], modules=[0, 1, 2])
+    check(persistent.cpu(), ref, y.cpu(), dtype)
+
+
 def test_tc_persistent_expand_many_items_per_cta(cuda):
     """bge-m3 q/k/v shape: 256 tiles x 3 modules x 8 column blocks = 6,144 work
     items over at most 148 CTAs, so every CTA cycles its stage ring many times;
