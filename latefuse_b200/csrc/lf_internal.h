@@ -89,6 +89,19 @@ struct alignas(64) ShrinkPersistParams {
   int32_t* status;
 };
 
+struct NormParams {
+  const void* a;
+  const void* b;       // may be null
+  int64_t lda, ldb;
+  const void* gamma;
+  const void* beta;
+  float eps;
+  int64_t n_rows;
+  int32_t hidden;
+  void* out;
+  int64_t ldo;
+};
+
 struct SimtParams {
   const void* x;
   int64_t ldx;

@@ -1,0 +1,223 @@
+// Encoder elementwise kernels: residual add + LayerNorm, and the exact GELU.
+//
+// add + LayerNorm (the encoder's "LayerNorm(sublayer_out + residual)",
+// src/latefuse/model/encoder.py:137,141, and the embeddings' LayerNorm at :275
+// with no residual):
+//     s   = round_T(a + b)                       the add materialises in T first
+//     out = round_T((s - mean) * rsqrt(var + eps) * gamma + beta)
+// mean and biased variance in f32 over the row (two passes over registers).
+// One warp per row: lane l holds elements [256 c + 8 l, 256 c + 8 l + 8) of
+// chunk c, read and written as 16-byte vectors, so a row is one pass over HBM.
+//
+// GELU (ACT2FN["gelu"], src/latefuse/model/encoder.py:122,139):
+//     out = round_T(x * 0.5 * (1 + erf(x / sqrt(2))))       in f32
+#include "lf_common.cuh"
+#include "lf_internal.h"
+
+namespace lf {
+
+namespace {
+
+// 8 consecutive elements of T as floats, and back (16-byte vectors for 2-byte T).
+template <typename T>
+struct Vec8 {
+  static __device__ __forceinline__ void load(const T* p, float (&v)[8]) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = Pack2<T>::unpack(w[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+  static __device__ __forceinline__ void store(T* p, const float (&v)[8]) {
+    uint4 raw;
+    raw.x = Pack2<T>::pack(v[0], v[1]);
+    raw.y = Pack2<T>::pack(v[2], v[3]);
+    raw.z = Pack2<T>::pack(v[4], v[5]);
+    raw.w = Pack2<T>::pack(v[6], v[7]);
+    *reinterpret_cast<uint4*>(p) = raw;
+  }
+};
+
+template <>
+struct Vec8<float> {
+  static __device__ __forceinline__ void load(const float* p, float (&v)[8]) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+  static __device__ __forceinline__ void store(float* p, const float (&v)[8]) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+constexpr int kNormWarps = 8;
+
+template <typename T, int NC>
+__global__ void __launch_bounds__(32 * kNormWarps)
+add_layernorm_kernel(const NormParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = int64_t(blockIdx.x) * kNormWarps + (threadIdx.x >> 5);
+  if (row >= p.n_rows) return;
+  const T* a = reinterpret_cast<const T*>(p.a) + row * p.lda;
+  const T* b = p.b != nullptr ? reinterpret_cast<const T*>(p.b) + row * p.ldb : nullptr;
+  const T* gamma = reinterpret_cast<const T*>(p.gamma);
+  const T* beta = reinterpret_cast<const T*>(p.beta);
+  T* out = reinterpret_cast<T*>(p.out) + row * p.ldo;
+  const int H = p.hidden;
+
+  float v[NC][8];
+  float sum = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int col = c * 256 + lane * 8;
+    if (col < H) {
+      Vec8<T>::load(a + col, v[c]);
+      if (b != nullptr) {
+        float w[8];
+        Vec8<T>::load(b + col, w);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[c][i] = round_through<T>(v[c][i] + w[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sum += v[c][i];
+    }
+  }
+  const float mean = warp_sum(sum) / float(H);
+  float sq = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    if (c * 256 + lane * 8 < H) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float d = v[c][i] - mean;
+        sq += d * d;
+      }
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(sq) / float(H) + p.eps);
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int col = c * 256 + lane * 8;
+    if (col < H) {
+      float g[8], bt[8], o[8];
+      Vec8<T>::load(gamma + col, g);
+      Vec8<T>::load(beta + col, bt);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = (v[c][i] - mean) * rstd * g[i] + bt[i];
+      Vec8<T>::store(out + col, o);
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) gelu_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t n8) {
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += stride) {
+    float v[8];
+    Vec8<T>::load(x + i * 8, v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = v[k] * 0.5f * (1.0f + erff(v[k] * 0.70710678118654752440f));
+    Vec8<T>::store(out + i * 8, v);
+  }
+}
+
+template <typename T>
+int launch_norm(const NormParams& p, cudaStream_t s) {
+  const int nc = (p.hidden + 255) / 256;
+  const unsigned blocks = unsigned((p.n_rows + kNormWarps - 1) / kNormWarps);
+  const dim3 grid{blocks}, block{32 * kNormWarps};
+  switch (nc) {
+#define LF_NORM_CASE(N) \
+  case N: add_layernorm_kernel<T, N><<<grid, block, 0, s>>>(p); break;
+    LF_NORM_CASE(1) LF_NORM_CASE(2) LF_NORM_CASE(3) LF_NORM_CASE(4) LF_NORM_CASE(5) LF_NORM_CASE(6)
+    LF_NORM_CASE(7) LF_NORM_CASE(8) LF_NORM_CASE(9) LF_NORM_CASE(10) LF_NORM_CASE(11) LF_NORM_CASE(12)
+    LF_NORM_CASE(13) LF_NORM_CASE(14) LF_NORM_CASE(15) LF_NORM_CASE(16)
+#undef LF_NORM_CASE
+    default: return set_error(LF_ERR_UNSUPPORTED, "lf_add_layernorm: hidden %d above 4096", p.hidden);
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, "launch add_layernorm");
+  count_launch();
+  return LF_OK;
+}
+
+template <typename T>
+int launch_gelu(const void* x, void* out, int64_t n, cudaStream_t s) {
+  const int64_t n8 = n / 8;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int64_t blocks = (n8 + 255) / 256;
+  if (blocks > int64_t(sms) * 8) blocks = int64_t(sms) * 8;
+  if (blocks == 0) return LF_OK;
+  gelu_kernel<T><<<unsigned(blocks), 256, 0, s>>>(static_cast<const T*>(x), static_cast<T*>(out), n8);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, "launch gelu");
+  count_launch();
+  return LF_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+}  // namespace lf
+
+using namespace lf;
+
+extern "C" int lf_add_layernorm(void* stream, int dtype, const void* a, int64_t lda, const void* b, int64_t ldb,
+                                const void* gamma, const void* beta, float eps, int64_t n_rows, int hidden,
+                                void* out, int64_t ldo) {
+  if (dtype != LF_DTYPE_BF16 && dtype != LF_DTYPE_F16 && dtype != LF_DTYPE_F32)
+    return set_error(LF_ERR_INVALID, "lf_add_layernorm: unknown dtype %d", dtype);
+  if (a == nullptr || gamma == nullptr || beta == nullptr || out == nullptr)
+    return set_error(LF_ERR_INVALID, "lf_add_layernorm: null a, gamma, beta or out");
+  if (n_rows < 0 || hidden <= 0 || hidden % 8 != 0)
+    return set_error(LF_ERR_INVALID, "lf_add_layernorm: hidden %d must be a positive multiple of 8", hidden);
+  if (hidden > 4096) return set_error(LF_ERR_UNSUPPORTED, "lf_add_layernorm: hidden %d above 4096", hidden);
+  if (lda < hidden || ldo < hidden || (b != nullptr && ldb < hidden))
+    return set_error(LF_ERR_INVALID, "lf_add_layernorm: a row stride is below hidden %d", hidden);
+  const int es = dtype == LF_DTYPE_F32 ? 4 : 2;
+  if (!aligned16(a) || !aligned16(out) || !aligned16(gamma) || !aligned16(beta) || (b != nullptr && !aligned16(b)) ||
+      (lda * es) % 16 != 0 || (ldo * es) % 16 != 0 || (b != nullptr && (ldb * es) % 16 != 0))
+    return set_error(LF_ERR_INVALID, "lf_add_layernorm: pointers and row strides must be 16-byte aligned");
+  if (n_rows == 0) return LF_OK;
+  NormParams p;
+  p.a = a;
+  p.b = b;
+  p.lda = lda;
+  p.ldb = ldb;
+  p.gamma = gamma;
+  p.beta = beta;
+  p.eps = eps;
+  p.n_rows = n_rows;
+  p.hidden = hidden;
+  p.out = out;
+  p.ldo = ldo;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == LF_DTYPE_BF16) return launch_norm<__nv_bfloat16>(p, s);
+  if (dtype == LF_DTYPE_F16) return launch_norm<__half>(p, s);
+  return launch_norm<float>(p, s);
+}
+
+extern "C" int lf_gelu(void* stream, int dtype, const void* x, void* out, int64_t n) {
+  if (dtype != LF_DTYPE_BF16 && dtype != LF_DTYPE_F16 && dtype != LF_DTYPE_F32)
+    return set_error(LF_ERR_INVALID, "lf_gelu: unknown dtype %d", dtype);
+  if (n < 0 || n % 8 != 0) return set_error(LF_ERR_INVALID, "lf_gelu: n %lld must be a multiple of 8", (long long)n);
+  if (n > 0 && (x == nullptr || out == nullptr)) return set_error(LF_ERR_INVALID, "lf_gelu: null x or out");
+  if (!aligned16(x) || !aligned16(out)) return set_error(LF_ERR_INVALID, "lf_gelu: x and out must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == LF_DTYPE_BF16) return launch_gelu<__nv_bfloat16>(x, out, n, s);
+  if (dtype == LF_DTYPE_F16) return launch_gelu<__half>(x, out, n, s);
+  return launch_gelu<float>(x, out, n, s);
+}

@@ -1,0 +1,53 @@
+"""The encoder's elementwise ops on the native kernels.
+
+``add_layernorm`` is ``nn.LayerNorm(sublayer_out + residual)`` in one pass over
+HBM (``src/latefuse/model/encoder.py:137,141``; with no residual, the embeddings'
+LayerNorm at ``:275``) and ``gelu`` is the exact erf GELU of the FFN
+(``:122,139``), both with torch's rounding points (see ``lf_add_layernorm`` and
+``lf_gelu`` in ``include/latefuse_b200.h``).
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from latefuse_b200 import _native as nat
+
+
+def _rows(t: Tensor) -> tuple[Tensor, int]:
+    t2 = t.reshape(-1, t.shape[-1])
+    if t2.stride(-1) != 1:
+        t2 = t2.contiguous()
+    return t2, t2.stride(0)
+
+
+def add_layernorm(a: Tensor, b: Tensor | None, weight: Tensor, bias: Tensor, eps: float,
+                  out: Tensor | None = None) -> Tensor:
+    """``layer_norm(a + b)`` (``b`` may be None) over the last dimension."""
+    dev = nat.require_cuda(a, b, weight, bias, out)
+    H = a.shape[-1]
+    a2, lda = _rows(a)
+    b2, ldb = _rows(b) if b is not None else (None, 0)
+    if out is None:
+        out = torch.empty(a.shape, dtype=a.dtype, device=a.device)
+    o2, ldo = _rows(out)
+    w = weight if weight.dtype == a.dtype else weight.to(a.dtype)
+    bb = bias if bias.dtype == a.dtype else bias.to(a.dtype)
+    rc = nat.lib().lf_add_layernorm(nat.stream_ptr(dev), nat.dtype_code(a.dtype), a2.data_ptr(), lda,
+                                    nat.ptr(b2), ldb, w.contiguous().data_ptr(), bb.contiguous().data_ptr(),
+                                    float(eps), a2.shape[0], H, o2.data_ptr(), ldo)
+    nat.check(rc, "lf_add_layernorm")
+    return out
+
+
+def gelu(x: Tensor, out: Tensor | None = None) -> Tensor:
+    """Exact (erf) GELU of a contiguous tensor."""
+    dev = nat.require_cuda(x, out)
+    if not x.is_contiguous():
+        x = x.contiguous()
+    if out is None:
+        out = torch.empty_like(x)
+    rc = nat.lib().lf_gelu(nat.stream_ptr(dev), nat.dtype_code(x.dtype), x.data_ptr(), out.data_ptr(), x.numel())
+    nat.check(rc, "lf_gelu")
+    return out

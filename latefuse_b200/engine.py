@@ -32,6 +32,7 @@ from latefuse_b200.batch import BatchedLRWeights, BatchLora, LayerwiseBatchedWei
 from latefuse_b200.config import LoraServingConfig
 from latefuse_b200.head import LRHeadOps, pool_tokens, validate_pooling
 from latefuse_b200.lora import FactorCache, SegmentTable, lora_apply, per_row_cache, workspace_bytes
+from latefuse_b200.encoder_ops import add_layernorm, gelu
 from latefuse_b200.packing import PackedBatch, pack_rows
 
 # Per-layer module paths (relative to "encoder.layer.{i}.") for each logical target.
@@ -314,6 +315,8 @@ class EncoderWithLora(nn.Module):
         self.pooler_w = nn.Parameter(torch.empty(H, H))
         self.pooler_b = nn.Parameter(torch.empty(H))
         self.act = ACT2FN[serving_config.hidden_act]
+        #: the FFN activation is the exact (erf) GELU: run it on the native kernel
+        self._native_gelu = serving_config.hidden_act == "gelu"
         self._runner = _DeltaRunner(serving_config)
         #: when a list, every LoRA delta op appends (start, end) CUDA events recorded
         #: around it on the current stream (used by the benchmark's roofline timing)
@@ -448,8 +451,8 @@ class EncoderWithLora(nn.Module):
         if token_type_ids is None:
             token_type_ids = torch.zeros(B, S, dtype=torch.long, device=dev)
         x = self.word_embeddings(input_ids) + self.token_type_embeddings(token_type_ids)
-        x = x + self.position_embeddings(self.position_ids(input_ids))
-        h = F.layer_norm(x, (H,), self.emb_ln.weight, self.emb_ln.bias, self.eps).view(T, H)
+        h = add_layernorm(x, self.position_embeddings(self.position_ids(input_ids)), self.emb_ln.weight,
+                          self.emb_ln.bias, self.eps).view(T, H)
 
         attn_mask = None
         if attention_mask is not None:
@@ -488,11 +491,17 @@ class EncoderWithLora(nn.Module):
                 else:
                     cache = _DeltaRunner.layerwise_cache(lora_weights[l], "dense")
                     lora_apply(ctx, ao, cache, segs, [0], [0], ws, status)
-            h1 = F.layer_norm(ao + h, (H,), layer.ln1.weight, layer.ln1.bias, self.eps)
-            mid = self.act(F.linear(h1, layer.wi, layer.bi))
-            o = F.linear(mid, layer.wo2, layer.bo2)
-            h = F.layer_norm(o + h1, (H,), layer.ln2.weight, layer.ln2.bias, self.eps)
+            h1, h = self._ffn(layer, ao, h)
         return h.view(B, S, H)
+
+    def _ffn(self, layer: _Layer, ao: Tensor, h: Tensor) -> tuple[Tensor, Tensor]:
+        """``h1 = LN1(ao + h)``, ``LN2(W2 act(W1 h1) + h1)``, on the native add+LayerNorm
+        and GELU kernels."""
+        h1 = add_layernorm(ao, h, layer.ln1.weight, layer.ln1.bias, self.eps)
+        mid = F.linear(h1, layer.wi, layer.bi)
+        mid = gelu(mid, out=mid) if self._native_gelu else self.act(mid)
+        o = F.linear(mid, layer.wo2, layer.bo2)
+        return h1, add_layernorm(o, h1, layer.ln2.weight, layer.ln2.bias, self.eps, out=o)
 
     # -- padding-free forward ------------------------------------------------
     @property
@@ -520,8 +529,8 @@ class EncoderWithLora(nn.Module):
         T = pb.n_tokens
         H, nh, hd = self.config.hidden_size, self.num_heads, self.head_dim
         x = self.word_embeddings(pb.ids) + self.token_type_embeddings(pb.token_types)
-        x = x + self.position_embeddings(pb.positions)
-        h = F.layer_norm(x, (H,), self.emb_ln.weight, self.emb_ln.bias, self.eps)
+        h = add_layernorm(x, self.position_embeddings(pb.positions), self.emb_ln.weight, self.emb_ln.bias,
+                          self.eps)
 
         do_lora = apply_lora and store is not None and (self._qkv_targets or self._dense_target)
         if do_lora:
@@ -547,10 +556,7 @@ class EncoderWithLora(nn.Module):
                 lora_apply(ctx, ao, store.factor_cache(l), segs, dense_idx, [0], ws, status)
                 if ev is not None:
                     ev[1].record()
-            h1 = F.layer_norm(ao + h, (H,), layer.ln1.weight, layer.ln1.bias, self.eps)
-            mid = self.act(F.linear(h1, layer.wi, layer.bi))
-            o = F.linear(mid, layer.wo2, layer.bo2)
-            h = F.layer_norm(o + h1, (H,), layer.ln2.weight, layer.ln2.bias, self.eps)
+            h1, h = self._ffn(layer, ao, h)
         return h
 
     def encode_pooled_packed(self, pb: PackedBatch, store, pooling: str = "auto",

@@ -1,0 +1,72 @@
+"""The encoder's native elementwise kernels against torch's own ops on the same
+GPU: residual add + LayerNorm (f32 1e-5; bf16/f16 within one or two output
+ulps, the only difference being the order of the f32 row sums) and the exact
+GELU."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from latefuse_b200 import _native as nat
+from latefuse_b200.encoder_ops import add_layernorm, gelu
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: (1e-5, 1e-5), torch.bfloat16: (2e-2, 1.6e-2), torch.float16: (4e-3, 2e-3)}
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("H", [64, 768, 1024, 2560, 4096])
+@pytest.mark.parametrize("residual", [True, False])
+def test_add_layernorm_matches_torch(cuda, dtype, H, residual):
+    g = torch.Generator(device=cuda).manual_seed(H)
+    rows = 1000
+    a = (torch.randn(rows, H, device=cuda, generator=g) * 3 + 1).to(dtype)
+    b = torch.randn(rows, H, device=cuda, generator=g).to(dtype) if residual else None
+    w = (1 + 0.1 * torch.randn(H, device=cuda, generator=g)).to(dtype)
+    bias = (0.1 * torch.randn(H, device=cuda, generator=g)).to(dtype)
+    ours = add_layernorm(a, b, w, bias, 1e-5)
+    ref = F.layer_norm(a + b if residual else a, (H,), w, bias, 1e-5)
+    atol, rtol = TOL[dtype]
+    torch.testing.assert_close(ours, ref, atol=atol, rtol=rtol)
+    if dtype != torch.float32:  # nearly every element is bit-identical
+        assert (ours != ref).float().mean().item() < 0.02
+
+
+def test_add_layernorm_in_place_and_strided(cuda):
+    dtype, H = torch.bfloat16, 1024
+    base = torch.randn(300, 2 * H, device=cuda).to(dtype)
+    a = base[:, :H]  # row stride 2H
+    b = torch.randn(300, H, device=cuda).to(dtype)
+    w = torch.ones(H, device=cuda, dtype=dtype)
+    z = torch.zeros(H, device=cuda, dtype=dtype)
+    ref = F.layer_norm(a + b, (H,), w, z, 1e-12)
+    out = b.clone()
+    add_layernorm(a, out, w, z, 1e-12, out=out)  # out aliases the residual
+    torch.testing.assert_close(out, ref, atol=2e-2, rtol=1.6e-2)
+
+
+def test_add_layernorm_rejects_bad_shapes(cuda):
+    a = torch.randn(4, 12, device=cuda)
+    with pytest.raises(nat.NativeLibraryError, match="multiple of 8"):
+        add_layernorm(a, None, torch.ones(12, device=cuda), torch.zeros(12, device=cuda), 1e-5)
+    a = torch.randn(4, 8192, device=cuda)
+    with pytest.raises(nat.NativeLibraryError, match="4096"):
+        add_layernorm(a, None, torch.ones(8192, device=cuda), torch.zeros(8192, device=cuda), 1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_gelu_matches_torch(cuda, dtype):
+    x = (torch.randn(16401, 4096, device=cuda) * 4).to(dtype)
+    ours = gelu(x)
+    ref = F.gelu(x)
+    if dtype == torch.float32:
+        torch.testing.assert_close(ours, ref, atol=1e-6, rtol=1e-6)
+    else:
+        torch.testing.assert_close(ours, ref, atol=0, rtol=8e-3)
+        assert (ours != ref).float().mean().item() < 1e-3
+    y = x.clone()
+    gelu(y, out=y)
+    assert torch.equal(y, ours)
