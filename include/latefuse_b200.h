@@ -298,6 +298,22 @@ int lf_add_layernorm(void* stream, int dtype, const void* a, int64_t lda, const 
  * n % 8 == 0; x and out 16-byte aligned; out may alias x. */
 int lf_gelu(void* stream, int dtype, const void* x, void* out, int64_t n);
 
+/* Self-attention of packed sequences (no padding): for every sequence, head h
+ * and query row i,  out[i][h] = softmax(scale * q_i . k_j over the sequence's
+ * keys j) @ v.  Replaces the encoder's masked attention
+ * (src/latefuse/model/encoder.py:82-98: scores, additive padding mask, f32
+ * softmax, probs @ v) on a padding-free batch.  q, k and v of token t, head h
+ * are the 64 elements at columns q_col + 64 h (k_col, v_col) of row t of qkv
+ * (row stride ld_qkv elements; the fused projection output).  `items` is a
+ * device int32 array of n_items records {row_start, len, q_tile, 0}, one per
+ * (sequence, 128-query tile), 16-byte aligned; ordering them longest sequence
+ * first balances the work.  head_dim must be 64; dtype bf16 or f16; column
+ * offsets multiples of 64.  out row t, head h at columns [64 h, 64 h + 64). */
+int lf_attention_varlen(void* stream, int dtype, const void* qkv, int64_t ld_qkv, int64_t n_tokens,
+                        int64_t q_col, int64_t k_col, int64_t v_col, int n_heads, int head_dim,
+                        const int32_t* items, int n_items, float scale, void* out, int64_t ld_out,
+                        int32_t* status);
+
 #ifdef __cplusplus
 }
 #endif

@@ -89,6 +89,19 @@ struct alignas(64) ShrinkPersistParams {
   int32_t* status;
 };
 
+// Packed varlen attention, head_dim 64 (see lf_attention.cu).
+struct alignas(64) AttnParams {
+  CUtensorMap qkv_map;               // 2D {ld_qkv, n_tokens}, box {64, 128}, SW128
+  const int4* items;                 // {row_start, len, q_tile, 0} per (sequence, 128-query tile)
+  int32_t n_items;
+  int32_t n_heads;
+  int32_t q_col, k_col, v_col;       // column of head 0's q / k / v in a qkv row
+  void* out;                         // (n_tokens, ld_out): head h at columns [64 h, 64 h + 64)
+  int64_t ldo;
+  float scale_log2;                  // softmax scale * log2(e)
+  int32_t* status;
+};
+
 struct NormParams {
   const void* a;
   const void* b;       // may be null

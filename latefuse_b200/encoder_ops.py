@@ -2,9 +2,10 @@
 
 ``add_layernorm`` is ``nn.LayerNorm(sublayer_out + residual)`` in one pass over
 HBM (``src/latefuse/model/encoder.py:137,141``; with no residual, the embeddings'
-LayerNorm at ``:275``) and ``gelu`` is the exact erf GELU of the FFN
-(``:122,139``), both with torch's rounding points (see ``lf_add_layernorm`` and
-``lf_gelu`` in ``include/latefuse_b200.h``).
+LayerNorm at ``:275``), ``gelu`` is the exact erf GELU of the FFN (``:122,139``),
+both with torch's rounding points, and ``attention_varlen`` is the encoder's
+masked self-attention (``:82-98``) on a padding-free batch (see the
+``lf_*`` declarations in ``include/latefuse_b200.h``).
 """
 
 from __future__ import annotations
@@ -50,4 +51,24 @@ def gelu(x: Tensor, out: Tensor | None = None) -> Tensor:
         out = torch.empty_like(x)
     rc = nat.lib().lf_gelu(nat.stream_ptr(dev), nat.dtype_code(x.dtype), x.data_ptr(), out.data_ptr(), x.numel())
     nat.check(rc, "lf_gelu")
+    return out
+
+
+def attention_varlen(qkv: Tensor, n_heads: int, items: Tensor, scale: float, out: Tensor | None = None,
+                     status: Tensor | None = None) -> Tensor:
+    """Self-attention of packed sequences, head_dim 64, read straight from the fused
+    ``(T, 3H)`` projection output (q, k, v at columns 0, H, 2H); ``items`` is the
+    ``(n, 4)`` device int32 work list of :class:`~latefuse_b200.packing.PackedBatch`.
+    Returns ``(T, H)``."""
+    dev = nat.require_cuda(qkv, items, out, status)
+    T, W = qkv.shape
+    H = W // 3
+    if qkv.stride(-1) != 1:
+        raise ValueError("qkv rows must be contiguous")
+    if out is None:
+        out = torch.empty(T, H, dtype=qkv.dtype, device=qkv.device)
+    rc = nat.lib().lf_attention_varlen(nat.stream_ptr(dev), nat.dtype_code(qkv.dtype), qkv.data_ptr(), qkv.stride(0),
+                                       T, 0, H, 2 * H, n_heads, H // n_heads, items.data_ptr(), items.shape[0],
+                                       float(scale), out.data_ptr(), out.stride(0), nat.ptr(status))
+    nat.check(rc, "lf_attention_varlen")
     return out

@@ -32,7 +32,7 @@ from latefuse_b200.batch import BatchedLRWeights, BatchLora, LayerwiseBatchedWei
 from latefuse_b200.config import LoraServingConfig
 from latefuse_b200.head import LRHeadOps, pool_tokens, validate_pooling
 from latefuse_b200.lora import FactorCache, SegmentTable, lora_apply, per_row_cache, workspace_bytes
-from latefuse_b200.encoder_ops import add_layernorm, gelu
+from latefuse_b200.encoder_ops import add_layernorm, attention_varlen, gelu
 from latefuse_b200.packing import PackedBatch, pack_rows
 
 # Per-layer module paths (relative to "encoder.layer.{i}.") for each logical target.
@@ -522,7 +522,8 @@ class EncoderWithLora(nn.Module):
         """Final hidden states of the real tokens, ``(n_tokens, H)`` in packed order.
 
         Same per-token arithmetic as :meth:`encode`; attention runs per sequence
-        over ``cu_seqlens`` (FlashAttention varlen), so no padded key exists.
+        (the tcgen05 kernel ``lf_attention_varlen`` for head_dim 64, FlashAttention
+        varlen otherwise), so no padded key exists.
         ``store`` is the :class:`~latefuse_b200.store.AdapterStore` whose slots
         ``pb.segments`` names.
         """
@@ -548,8 +549,11 @@ class EncoderWithLora(nn.Module):
                 lora_apply(h, qkv, store.factor_cache(l), segs, qkv_idx, qkv_offs, ws, status)
                 if ev is not None:
                     ev[1].record()
-            q, k, v = qkv.view(T, 3, nh, hd).unbind(1)
-            ctx = varlen_attention(q, k, v, pb.cu_seqlens, pb.max_len).view(T, H)
+            if hd == 64:
+                ctx = attention_varlen(qkv, nh, pb.attn_items, hd ** -0.5, status=self._runner.status)
+            else:  # head sizes the tcgen05 kernel does not tile
+                q, k, v = qkv.view(T, 3, nh, hd).unbind(1)
+                ctx = varlen_attention(q, k, v, pb.cu_seqlens, pb.max_len).view(T, H)
             ao = F.linear(ctx, layer.wo, layer.bo)
             if do_lora and self._dense_target:
                 ev = self._event_pair("dense")

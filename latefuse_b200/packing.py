@@ -12,9 +12,9 @@ the same results on every real token.
 
 Rows are laid out sorted by adapter slot (stable), so all rows of one tenant
 are adjacent and the LoRA delta sees one segment per tenant run rather than one
-per row.  Everything the device needs (token ids, position ids, token types,
-``cu_seqlens``, the first token of each row, the row of each token, row
-lengths) goes over in one pinned host-to-device copy.
+per row.  Everything the device needs (the attention work list, token ids,
+position ids, token types, ``cu_seqlens``, the first token of each row, the row
+of each token, row lengths) goes over in one pinned host-to-device copy.
 """
 
 from __future__ import annotations
@@ -50,7 +50,26 @@ class PackedBatch:
     row_of_token: Tensor        # (n_tokens,) input row of each packed token
     row_lengths: Tensor         # (n_rows,) per input row
     segments: SegmentTable      # LoRA segments: runs of rows with one slot
+    attn_items: Tensor          # (n_attn_items, 4) {row_start, len, q_tile, 0}, longest sequences first
     host_bytes: int             # bytes copied host -> device for this batch
+
+
+def attention_items(starts, lengths) -> np.ndarray:
+    """The attention work list of packed sequences: ``(n, 4)`` int64 records
+    ``{row_start, len, q_tile, 0}``, one per (sequence, 128-query tile), the
+    sequences with more key tiles first so that the persistent kernel's
+    round-robin over CTAs balances."""
+    starts = np.asarray(starts, dtype=np.int64)
+    lengths = np.asarray(lengths, dtype=np.int64)
+    n_qt = (lengths + 127) // 128
+    seq_order = np.argsort(-n_qt, kind="stable")
+    items = np.zeros((int(n_qt.sum()), 4), dtype=np.int64)
+    k = 0
+    for i in seq_order:
+        for t in range(int(n_qt[i])):
+            items[k] = (starts[i], lengths[i], t, 0)
+            k += 1
+    return items
 
 
 def pack_rows(input_ids: Tensor, lengths: list[int], slots: list[int], positions: Tensor,
@@ -78,10 +97,14 @@ def pack_rows(input_ids: Tensor, lengths: list[int], slots: list[int], positions
     first = np.empty(B, dtype=np.int64)
     first[order] = cu[:-1]
 
-    n_parts = 3 * T + (B + 1) + B + T + B
+    items = attention_items(cu[:-1], olens)
+    n_items = items.shape[0]
+
+    n_parts = 4 * n_items + 3 * T + (B + 1) + B + T + B
     buf = torch.empty(n_parts, dtype=torch.int32, pin_memory=device.type == "cuda")
     a = buf.numpy()
-    o = 0
+    a[:4 * n_items] = items.reshape(-1)
+    o = 4 * n_items
     a[o:o + T] = input_ids.reshape(-1).numpy()[sel]
     o += T
     a[o:o + T] = positions.reshape(-1).numpy()[sel]
@@ -96,7 +119,7 @@ def pack_rows(input_ids: Tensor, lengths: list[int], slots: list[int], positions
     o += T
     a[o:o + B] = lens
     dev_buf = buf.to(device, non_blocking=True) if device.type == "cuda" else buf.clone()
-    views, o = [], 0
+    views, o = [dev_buf[:4 * n_items].view(n_items, 4)], 4 * n_items
     for n in (T, T, T, B + 1, B, T, B):
         views.append(dev_buf[o:o + n])
         o += n
@@ -112,6 +135,6 @@ def pack_rows(input_ids: Tensor, lengths: list[int], slots: list[int], positions
             seg_slots.append(int(slots[b]))
     segs = SegmentTable(starts, seg_lens, seg_slots, T, device)
     return PackedBatch(n_rows=B, n_tokens=T, max_len=int(lens.max()), lengths=[int(n) for n in lens],
-                       order=order, slots=list(slots), ids=views[0], positions=views[1], token_types=views[2],
-                       cu_seqlens=views[3], first_token=views[4], row_of_token=views[5], row_lengths=views[6],
-                       segments=segs, host_bytes=n_parts * 4 + segs.host.numel() * 4)
+                       order=order, slots=list(slots), ids=views[1], positions=views[2], token_types=views[3],
+                       cu_seqlens=views[4], first_token=views[5], row_of_token=views[6], row_lengths=views[7],
+                       segments=segs, attn_items=views[0], host_bytes=n_parts * 4 + segs.host.numel() * 4)

@@ -89,8 +89,19 @@ def test_pack_rows_layout():
     assert segs.n_segs == 2 and segs.slots == [3, 5]
     starts, seg_lens = segs.host[4 * segs.n_tiles:].view(3, -1)[:2].tolist()
     assert starts == [0, 3] and seg_lens == [3, 10]
+    # attention work list: one record per (sequence, 128-query tile)
+    assert pb.attn_items.tolist() == [[0, 2, 0, 0], [2, 1, 0, 0], [3, 6, 0, 0], [9, 4, 0, 0]]
     with pytest.raises(ValueError):
         pack_rows(ids, [6, 0, 4, 1], slots, pos, None, torch.device("cpu"))
+
+
+def test_attention_items_order_and_tiles():
+    from latefuse_b200.packing import attention_items
+
+    items = attention_items([0, 5, 305], [5, 300, 129]).tolist()
+    # the 300-token sequence (3 query tiles) first, then the 129-token one (2), then the short one
+    assert items == [[5, 300, 0, 0], [5, 300, 1, 0], [5, 300, 2, 0], [305, 129, 0, 0], [305, 129, 1, 0],
+                     [0, 5, 0, 0]]
 
 
 def test_store_shapes_and_accounting():
