@@ -166,10 +166,11 @@ static int shrink_impl(cudaStream_t stream, int dtype, const void* x, int64_t ld
     p.status = status;
     return run_shrink_simt(dtype, p, stream);
   }
-  // tcgen05 path.  Tiles with one segment go to the persistent kernel (all
-  // modules in one pass over x); the rest to the per-tile cluster kernel.
+  // tcgen05 path: the persistent kernel (all modules in one pass over x) when
+  // there are tile records, else the per-tile cluster kernel.
   const int rp = rank < 16 ? 16 : rank;
-  if (tiles != nullptr && g_persistent.load() && n_tiles - n_multi > 0) {
+  (void)n_multi;
+  if (tiles != nullptr && g_persistent.load() && n_tiles > 0) {
     ShrinkPersistParams q;
     memset(&q, 0, sizeof(q));
     {
@@ -192,8 +193,7 @@ static int shrink_impl(cudaStream_t stream, int dtype, const void* x, int64_t ld
     q.hidden = hidden;
     q.n_modules = n_modules;
     q.n_slots = n_slots;
-    q.n_tiles = n_tiles - n_multi;
-    q.acc_cols = uint32_t(n_modules * rp);
+    q.n_tiles = n_tiles;
     q.tiles = tiles;
     q.seg_start = seg_start;
     q.seg_len = seg_len;
@@ -201,11 +201,7 @@ static int shrink_impl(cudaStream_t stream, int dtype, const void* x, int64_t ld
     q.n_segs = n_segs;
     q.u = u;
     q.status = status;
-    int rc = run_shrink_persist(dtype, q, rank, stream);
-    if (rc) return rc;
-    if (n_multi == 0) return LF_OK;
-    tiles += 4 * (n_tiles - n_multi);  // the per-tile kernel takes the rest
-    n_tiles = n_multi;
+    return run_shrink_persist(dtype, q, rank, stream);
   }
   // per-tile cluster kernel; modules in groups whose fp32 partials fit on chip
   const int group = rp * n_modules <= 64 ? n_modules : (64 / rp > 0 ? 64 / rp : 1);
@@ -260,7 +256,7 @@ static int expand_impl(cudaStream_t stream, int dtype, const void* u, void* y, i
                        int64_t b_module_stride, int n_slots, int n_modules, const int32_t* modules,
                        const int64_t* y_col_offsets, const int32_t* seg_start, const int32_t* seg_len,
                        const int32_t* seg_slot, int n_segs, const int32_t* tiles, int n_tiles, int n_multi,
-                       int accumulate, int32_t* status) {
+                       int accumulate, bool after_shrink, int32_t* status) {
   const int es = elem_size(dtype);
   int64_t y_cols = 0;
   bool offs_aligned = true;
@@ -364,7 +360,7 @@ static int expand_impl(cudaStream_t stream, int dtype, const void* u, void* y, i
     q.seg_slot = seg_slot;
     q.n_segs = n_segs;
     q.status = status;
-    return run_expand_persist(dtype, q, rank, 128, stream);
+    return run_expand_persist(dtype, q, rank, 128, after_shrink, stream);
   }
   p.tiles = tiles;
   p.n_tiles = n_tiles;
@@ -440,7 +436,7 @@ int lf_lora_expand(void* stream, int dtype, const void* u, void* y, int64_t ldy,
   if (n_tokens == 0) return LF_OK;
   return expand_impl(static_cast<cudaStream_t>(stream), dtype, u, y, ldy, n_tokens, hidden, rank, cache_b,
                      b_slot_stride, b_module_stride, n_slots, n_modules, modules, y_col_offsets, seg_start, seg_len,
-                     seg_slot, n_segs, tiles, n_tiles, n_multi, accumulate, status);
+                     seg_slot, n_segs, tiles, n_tiles, n_multi, accumulate, false, status);
 }
 
 int lf_lora_apply(void* stream, int dtype, const void* x, int64_t ldx, void* y, int64_t ldy, int64_t n_tokens,
@@ -467,7 +463,7 @@ int lf_lora_apply(void* stream, int dtype, const void* x, int64_t ldx, void* y, 
   if (rc) return rc;
   return expand_impl(s, dtype, workspace, y, ldy, n_tokens, hidden, rank, cache_b, b_slot_stride, b_module_stride,
                      n_slots, n_modules, modules, y_col_offsets, seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles,
-                     n_multi, 1, status);
+                     n_multi, 1, true, status);
 }
 
 }  // extern "C"

@@ -70,7 +70,7 @@ struct alignas(64) ExpandPersistParams {
   int32_t* status;
 };
 
-// Persistent shrink over single-segment tiles (see lf_lora_persist.cu).
+// Persistent shrink over the tile records (see lf_lora_persist.cu).
 struct alignas(64) ShrinkPersistParams {
   CUtensorMap x_map;                 // 2D {hidden, n_tokens}, box {64, 128}, SW128
   CUtensorMap a_map[kMaxModules];    // 3D {rank, hidden, n_slots}, box {rank, 64, 1}
@@ -78,9 +78,10 @@ struct alignas(64) ShrinkPersistParams {
   int32_t hidden;
   int32_t n_modules;
   int32_t n_slots;
-  int32_t n_tiles;                   // single-segment tile records
-  uint32_t acc_cols;                 // TMEM columns of one accumulator (n_modules * rank, padded)
-  const int32_t* tiles;              // records {tile, first segment, 1, slot}
+  int32_t n_tiles;                   // tile records
+  int32_t kmax;                      // segments multiplied per pass over a tile's x
+  uint32_t acc_cols;                 // TMEM columns of one accumulator set (kmax * n_modules * rank, padded)
+  const int32_t* tiles;              // records {tile, first segment, segment count, first slot}
   const int32_t* seg_start;
   const int32_t* seg_len;
   const int32_t* seg_slot;
@@ -151,7 +152,10 @@ size_t shrink_tc_smem(int dtype, int rank, int kchunk, int n_mod);
 uint32_t shrink_tc_tmem_cols(int rank, int n_mod);
 CUtensorMapSwizzle a_tma_swizzle(int rank);
 
-int run_expand_persist(int dtype, const ExpandPersistParams& p, int rank, int nt, cudaStream_t s);
+// after_shrink: launched right behind the persistent shrink that writes u, as
+// its programmatic dependent (the expand starts early and waits for u).
+int run_expand_persist(int dtype, const ExpandPersistParams& p, int rank, int nt, bool after_shrink,
+                       cudaStream_t s);
 int run_shrink_persist(int dtype, const ShrinkPersistParams& p, int rank, cudaStream_t s);
 
 // CUDA-core path

@@ -9,11 +9,11 @@
 //               MMAs are already in flight: 4 warps in the shrink, 8 in the
 //               expand (two per quadrant, 64 columns each).
 //
-// Shrink  (item = 128-token tile holding one segment):  u[m][t] =
-//         round(x[t] . A(slot, m)) for every module, the hidden dimension
-//         streamed in 64-wide K blocks; the epilogue writes u (0 for tile rows
-//         outside the segment).  Tiles with several segments use the
-//         one-tile-per-CTA kernel in lf_lora_tc.cu.
+// Shrink  (item = 128-token tile):  u[m][t] = round(x[t] . A(slot(t), m)) for
+//         every module, the hidden dimension streamed in 64-wide K blocks; the
+//         epilogue writes u (0 for tile rows outside every segment).  A tile
+//         with several segments multiplies each x K-block by every segment's
+//         A (up to kmax at once, more in further passes).
 // Expand  (item = tile x module x 128 columns):  y += round(u . B(slot, m)); the
 //         y tile, the B factor tile and the u tile (canonical K-major layout,
 //         straight from the shrink output) arrive by TMA; the epilogue adds in
@@ -204,6 +204,22 @@ lora_expand_persist_kernel(const __grid_constant__ ExpandPersistParams p) {
     if (lane == 0) {
       int it = 0;
       bool stop = false;
+      // When launched as a programmatic dependent of the shrink, u may not be
+      // written yet: the first ST stages get their y and B loads at once and
+      // their u loads after griddepcontrol.wait (which returns at once when
+      // there is nothing to wait for).
+      bool dep_done = false;
+      int n_pend = 0;
+      int4 pend[ST];  // {stage, u row, 0, 0}
+      auto flush = [&]() {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        for (int q = 0; q < n_pend; ++q) {
+          const uint32_t su = s_stage0 + pend[q].x * C::kStageBytes + C::kYBytes + C::kBBytes;
+          tma_load_2d(su, &p.u_map, bar(FULL + pend[q].x), 0, pend[q].y);
+        }
+        n_pend = 0;
+        dep_done = true;
+      };
       int64_t item = blockIdx.x;
       int4 rnext = rec_at(item);
       for (; item < total && !stop; item += gridDim.x) {
@@ -233,9 +249,16 @@ lora_expand_persist_kernel(const __grid_constant__ ExpandPersistParams p) {
           }
           for (int b = 0; b < C::kNBox; ++b)
             tma_load_3d(sb + b * C::kBBox, &p.b_map[m], bar(FULL + s), cb * NT + b * 64, 0, slot);
-          tma_load_2d(su, &p.u_map, bar(FULL + s), 0, int32_t(int64_t(m) * p.n_tokens + row0));
+          const int32_t urow = int32_t(int64_t(m) * p.n_tokens + row0);
+          if (dep_done) {
+            tma_load_2d(su, &p.u_map, bar(FULL + s), 0, urow);
+          } else {
+            pend[n_pend++] = make_int4(s, urow, 0, 0);
+            if (n_pend == ST) flush();  // every stage is waiting for its u
+          }
         }
       }
+      if (!dep_done) flush();
       if (aborted(s_abort)) {  // loads nobody consumed must land before the CTA exits (bounded)
         for (int q = (it > ST ? it - ST : 0); q < it; ++q) mbar_wait(bar(FULL + q % ST), (q / ST) & 1);
       }
@@ -396,6 +419,11 @@ lora_expand_persist_kernel(const __grid_constant__ ExpandPersistParams p) {
 }
 
 // ------------------------------------------------------------------ shrink
+// One item per tile record.  A record with k segments takes ceil(k / kmax)
+// passes over the tile's x; a pass multiplies each x K-block by the A factors
+// of up to kmax segments at once (one TMEM accumulator set per segment), and
+// its epilogue writes the rows that pass owns: each row gets the product with
+// its own segment's A, rows in no segment get 0.
 template <typename T, int R>
 __global__ void __launch_bounds__(192, 1)
 lora_shrink_persist_kernel(const __grid_constant__ ShrinkPersistParams p, int stages, int stage_bytes) {
@@ -407,9 +435,13 @@ lora_shrink_persist_kernel(const __grid_constant__ ShrinkPersistParams p, int st
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
 
+  // the expand that follows may be scheduled on SMs this grid leaves free
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ST = stages;
   const int n_mod = p.n_modules;
+  const int KM = p.kmax;
   const int nkb = p.hidden / 64;
   const uint32_t s_stage0 = base;
   const uint32_t s_zero = base + ST * stage_bytes;  // 1 KB of zeros (rank 8 only)
@@ -419,9 +451,11 @@ lora_shrink_persist_kernel(const __grid_constant__ ShrinkPersistParams p, int st
   const int FULL = 0, EMPTY = ST, ACC_FULL = 2 * ST, ACC_EMPTY = 2 * ST + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(&bars[2 * ST + 4]);
   int32_t* s_abort = reinterpret_cast<int32_t*>(tmem_slot + 1);
-  const uint32_t acc_cols = p.acc_cols;
+  const uint32_t acc_cols = p.acc_cols;  // one accumulator set: kmax * n_mod * RP columns
   uint32_t alloc_cols = 32;
   while (alloc_cols < 2 * acc_cols) alloc_cols <<= 1;
+  const int4* recs = reinterpret_cast<const int4*>(p.tiles);
+  auto rec_at = [&](int i) { return i < p.n_tiles ? __ldg(recs + i) : int4{}; };
 
   if (tid == 0) {
     for (int i = 0; i < ST; ++i) {
@@ -458,29 +492,36 @@ lora_shrink_persist_kernel(const __grid_constant__ ShrinkPersistParams p, int st
     if (lane == 0) {
       int kk = 0;
       int ti = blockIdx.x;
-      int4 rec = ti < p.n_tiles ? __ldg(reinterpret_cast<const int4*>(p.tiles) + ti) : int4{};
+      int4 rnext = rec_at(ti);
       bool stop = false;
       for (; ti < p.n_tiles && !stop; ti += gridDim.x) {
-        const int4 cur = rec;
-        if (ti + int(gridDim.x) < p.n_tiles) rec = __ldg(reinterpret_cast<const int4*>(p.tiles) + ti + gridDim.x);
+        const int4 cur = rnext;
+        rnext = rec_at(ti + gridDim.x);
         const int32_t row0 = cur.x * kTile;
-        for (int kb = 0; kb < nkb; ++kb, ++kk) {
-          const int s = kk % ST;
-          const uint32_t ph = (kk / ST) & 1;
-          if (aborted(s_abort) || !mbar_wait(bar(EMPTY + s), ph ^ 1)) {
-            if (!aborted(s_abort)) fail();
-            stop = true;
-            break;
+        const int k = sub_items(cur, p.n_segs);
+        for (int j0 = 0; j0 < k && !stop; j0 += KM) {
+          const int kp = min(KM, k - j0);
+          for (int kb = 0; kb < nkb; ++kb, ++kk) {
+            const int s = kk % ST;
+            const uint32_t ph = (kk / ST) & 1;
+            if (aborted(s_abort) || !mbar_wait(bar(EMPTY + s), ph ^ 1)) {
+              if (!aborted(s_abort)) fail();
+              stop = true;
+              break;
+            }
+            const uint32_t st = s_stage0 + s * stage_bytes;
+            mbar_arrive_expect_tx(bar(FULL + s), kYBox + kp * n_mod * kABox);
+            tma_load_2d(st, &p.x_map, bar(FULL + s), kb * 64, row0);
+            for (int jj = 0; jj < kp; ++jj) {
+              const int32_t slot = sub_slot(cur, j0 + jj, p.seg_slot, p.n_segs);
+              for (int m = 0; m < n_mod; ++m)
+                tma_load_3d(st + kYBox + (jj * n_mod + m) * kABox, &p.a_map[m], bar(FULL + s), 0, kb * 64, slot);
+            }
           }
-          const uint32_t st = s_stage0 + s * stage_bytes;
-          mbar_arrive_expect_tx(bar(FULL + s), kYBox + n_mod * kABox);
-          tma_load_2d(st, &p.x_map, bar(FULL + s), kb * 64, row0);
-          for (int m = 0; m < n_mod; ++m)
-            tma_load_3d(st + kYBox + m * kABox, &p.a_map[m], bar(FULL + s), 0, kb * 64, cur.w);
         }
       }
       if (aborted(s_abort)) {
-        for (int k = (kk > ST ? kk - ST : 0); k < kk; ++k) mbar_wait(bar(FULL + k % ST), (k / ST) & 1);
+        for (int q = (kk > ST ? kk - ST : 0); q < kk; ++q) mbar_wait(bar(FULL + q % ST), (q / ST) & 1);
       }
     }
   } else if (warp == 1) {
@@ -489,33 +530,42 @@ lora_shrink_persist_kernel(const __grid_constant__ ShrinkPersistParams p, int st
       constexpr uint32_t idesc = umma_idesc_f16(DT<T>::umma_fmt, kTile, RP, /*a_mn=*/0, /*b_mn=*/1);
       int kk = 0, it = 0;
       bool stop = false;
-      for (int ti = blockIdx.x; ti < p.n_tiles && !stop; ti += gridDim.x, ++it) {
-        const int a = it & 1;
-        const uint32_t aph = (it >> 1) & 1;
-        if (aborted(s_abort) || !mbar_wait(bar(ACC_EMPTY + a), aph ^ 1)) {
-          if (!aborted(s_abort)) fail();
-          break;
-        }
-        for (int kb = 0; kb < nkb; ++kb, ++kk) {
-          const int s = kk % ST;
-          const uint32_t ph = (kk / ST) & 1;
-          if (!mbar_wait(bar(FULL + s), ph)) { fail(); stop = true; break; }
-          tc_fence_after();
-          const uint32_t st = s_stage0 + s * stage_bytes;
-          for (int m = 0; m < n_mod; ++m) {
-            const uint32_t ab = st + kYBox + m * kABox;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint64_t ad = smem_desc(st + k * 32, 16, 1024, 2);
-              const uint32_t bstart = ab + k * 16 * A::kRowBytes;
-              const uint64_t bd = (R == 8) ? smem_desc(bstart, 128, s_zero + k * 256 - bstart, 0)
-                                           : smem_desc(bstart, A::kSbo, A::kSbo, A::kLayout);
-              umma_f16(tmem + a * acc_cols + m * RP, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
-            }
+      int ti = blockIdx.x;
+      int4 rnext = rec_at(ti);
+      for (; ti < p.n_tiles && !stop; ti += gridDim.x) {
+        const int4 rec = rnext;
+        rnext = rec_at(ti + gridDim.x);
+        const int k = sub_items(rec, p.n_segs);
+        for (int j0 = 0; j0 < k && !stop; j0 += KM, ++it) {
+          const int kp = min(KM, k - j0);
+          const int a = it & 1;
+          const uint32_t aph = (it >> 1) & 1;
+          if (aborted(s_abort) || !mbar_wait(bar(ACC_EMPTY + a), aph ^ 1)) {
+            if (!aborted(s_abort)) fail();
+            stop = true;
+            break;
           }
-          umma_commit(bar(EMPTY + s));
+          for (int kb = 0; kb < nkb; ++kb, ++kk) {
+            const int s = kk % ST;
+            const uint32_t ph = (kk / ST) & 1;
+            if (!mbar_wait(bar(FULL + s), ph)) { fail(); stop = true; break; }
+            tc_fence_after();
+            const uint32_t st = s_stage0 + s * stage_bytes;
+            for (int jm = 0; jm < kp * n_mod; ++jm) {
+              const uint32_t ab = st + kYBox + jm * kABox;
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const uint64_t ad = smem_desc(st + q * 32, 16, 1024, 2);
+                const uint32_t bstart = ab + q * 16 * A::kRowBytes;
+                const uint64_t bd = (R == 8) ? smem_desc(bstart, 128, s_zero + q * 256 - bstart, 0)
+                                             : smem_desc(bstart, A::kSbo, A::kSbo, A::kLayout);
+                umma_f16(tmem + a * acc_cols + jm * RP, ad, bd, idesc, (kb | q) != 0 ? 1u : 0u);
+              }
+            }
+            umma_commit(bar(EMPTY + s));
+          }
+          if (!stop) umma_commit(bar(ACC_FULL + a));
         }
-        if (!stop) umma_commit(bar(ACC_FULL + a));
       }
       if (it > 0 && aborted(s_abort)) mbar_wait(bar(ACC_FULL + ((it - 1) & 1)), ((it - 1) >> 1) & 1);
     }
@@ -524,58 +574,70 @@ lora_shrink_persist_kernel(const __grid_constant__ ShrinkPersistParams p, int st
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     int it = 0;
-    for (int ti = blockIdx.x; ti < p.n_tiles; ti += gridDim.x, ++it) {
-      const int a = it & 1;
-      const uint32_t aph = (it >> 1) & 1;
-      // the tile's segment, read while the MMAs run
-      const int4 rec = __ldg(reinterpret_cast<const int4*>(p.tiles) + ti);
+    int ti = blockIdx.x;
+    int4 r1 = rec_at(ti), r2 = rec_at(ti + int(gridDim.x));
+    int4 g1 = first_seg(r1, p.seg_start, p.seg_len, p.seg_slot, p.n_segs);
+    for (; ti < p.n_tiles; ti += gridDim.x) {
+      // records two tiles ahead, the next tile's first segment one ahead
+      const int4 rec = r1, seg0 = g1;
+      r1 = r2;
+      g1 = first_seg(r1, p.seg_start, p.seg_len, p.seg_slot, p.n_segs);
+      r2 = rec_at(ti + 2 * int(gridDim.x));
       const int64_t row0 = int64_t(rec.x) * kTile;
-      int64_t lo = 0, hi = 0;
-      if (rec.y >= 0 && rec.y < p.n_segs) {
-        const int64_t s0 = __ldg(p.seg_start + rec.y), l0 = __ldg(p.seg_len + rec.y);
-        if (__ldg(p.seg_slot + rec.y) == rec.w && rec.w >= 0 && rec.w < p.n_slots) {
-          lo = max(s0, row0) - row0;
-          hi = min(min(s0 + l0, row0 + kTile), p.n_tokens) - row0;
-        } else if (row == 0 && quad == 0) {
-          set_status(p.status, (rec.w < 0 || rec.w >= p.n_slots) ? LF_STATUS_BAD_SLOT : LF_STATUS_BAD_SEGMENT);
-        }
-      } else if (row == 0 && quad == 0) {
-        set_status(p.status, LF_STATUS_BAD_SEGMENT);
-      }
-      bool ok = !aborted(s_abort);
-      if (ok && !mbar_wait(bar(ACC_FULL + a), aph)) {
-        fail();
-        ok = false;
-      }
-      const bool work = __all_sync(0xffffffffu, ok);
-      tc_fence_after();
       const int64_t t = row0 + row;
-      const bool mine = row >= lo && row < hi;
-      if (work) {
-        for (int m = 0; m < n_mod; ++m) {
-          T* dst = reinterpret_cast<T*>(p.u) + (int64_t(m) * p.n_tokens + t) * R;
+      const int k = sub_items(rec, p.n_segs);
+      int own_lo = 0;  // rows below were written by an earlier pass
+      for (int j0 = 0; j0 < k; j0 += KM, ++it) {
+        const int kp = min(KM, k - j0);
+        const int a = it & 1;
+        const uint32_t aph = (it >> 1) & 1;
+        int j_row = -1, hi_last = 0;
+        for (int jj = 0; jj < kp; ++jj) {
+          const SubRows sr = rows_of(rec, j0 + jj, seg0, row0, p.n_tokens, p.seg_start, p.seg_len, p.seg_slot,
+                                     p.n_segs, p.n_slots, p.status, row == 0 && quad == 0);
+          if (row >= sr.lo && row < sr.hi) j_row = jj;
+          if (sr.hi > hi_last) hi_last = sr.hi;
+        }
+        const int own_hi = (j0 + kp >= k) ? kTile : max(own_lo, hi_last);
+        const bool mine = row >= own_lo && row < own_hi && t < p.n_tokens;
+        own_lo = own_hi;
+        bool ok = !aborted(s_abort);
+        if (ok && !mbar_wait(bar(ACC_FULL + a), aph)) {
+          fail();
+          ok = false;
+        }
+        const bool work = __all_sync(0xffffffffu, ok);
+        tc_fence_after();
+        if (work) {
+          for (int m = 0; m < n_mod; ++m) {
+            T* dst = reinterpret_cast<T*>(p.u) + (int64_t(m) * p.n_tokens + t) * R;
+            for (int jj = 0; jj < kp; ++jj) {
 #pragma unroll
-          for (int c = 0; c < RP / 16; ++c) {
-            float v[16];
-            tmem_ld16(tmem + (uint32_t(quad * 32) << 16) + a * acc_cols + m * RP + c * 16, v);
-            if (t < p.n_tokens) {
+              for (int c = 0; c < RP / 16; ++c) {
+                float v[16];
+                tmem_ld16(tmem + (uint32_t(quad * 32) << 16) + a * acc_cols + (jj * n_mod + m) * RP + c * 16, v);
+                // a row in no segment of this pass writes zeros once (with jj == 0)
+                if (mine && (j_row == jj || (j_row < 0 && jj == 0))) {
 #pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                if (c * 16 + h * 8 < R) {
-                  uint4 pk;
-                  T* e = reinterpret_cast<T*>(&pk);
-#pragma unroll
-                  for (int i = 0; i < 8; ++i) e[i] = DT<T>::from_f(mine ? v[h * 8 + i] : 0.f);
-                  *reinterpret_cast<uint4*>(dst + c * 16 + h * 8) = pk;
+                  for (int h = 0; h < 2; ++h) {
+                    if (c * 16 + h * 8 < R) {
+                      uint4 pk;
+                      pk.x = Pack2<T>::pack(j_row < 0 ? 0.f : v[h * 8 + 0], j_row < 0 ? 0.f : v[h * 8 + 1]);
+                      pk.y = Pack2<T>::pack(j_row < 0 ? 0.f : v[h * 8 + 2], j_row < 0 ? 0.f : v[h * 8 + 3]);
+                      pk.z = Pack2<T>::pack(j_row < 0 ? 0.f : v[h * 8 + 4], j_row < 0 ? 0.f : v[h * 8 + 5]);
+                      pk.w = Pack2<T>::pack(j_row < 0 ? 0.f : v[h * 8 + 6], j_row < 0 ? 0.f : v[h * 8 + 7]);
+                      *reinterpret_cast<uint4*>(dst + c * 16 + h * 8) = pk;
+                    }
+                  }
                 }
               }
             }
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(ACC_EMPTY + a));
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(ACC_EMPTY + a));
     }
   }
 
@@ -598,7 +660,7 @@ int sm_count() {
 }
 
 template <typename T, int R, int NT>
-int launch_expand(const ExpandPersistParams& p, cudaStream_t stream) {
+int launch_expand(const ExpandPersistParams& p, bool after_shrink, cudaStream_t stream) {
   using C = ExpandCfg<R, NT>;
   auto kern = lora_expand_persist_kernel<T, R, NT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(C::kSmem));
@@ -607,20 +669,41 @@ int launch_expand(const ExpandPersistParams& p, cudaStream_t stream) {
   const int sms = sm_count();
   const int grid = int(total < sms ? total : sms);
   if (grid == 0) return LF_OK;
-  kern<<<grid, kExpandThreads, C::kSmem, stream>>>(p);
-  e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(kExpandThreads);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  if (after_shrink) {  // may start while the shrink that writes u still runs
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  e = cudaLaunchKernelEx(&cfg, kern, p);
   if (e != cudaSuccess) return cuda_error(e, "launch lora_expand_persist");
   count_launch();
   return LF_OK;
 }
 
 template <typename T, int R>
-int launch_shrink(const ShrinkPersistParams& p, cudaStream_t stream) {
-  const int stage_bytes = kYBox + p.n_modules * 64 * R * 2;  // multiple of 1024
-  const int fixed = 1024 + 1024 + 1024;                      // alignment, zeros, barriers
+int launch_shrink(ShrinkPersistParams p, cudaStream_t stream) {
+  constexpr int RP = R < 16 ? 16 : R;
+  const int fixed = 1024 + 1024 + 1024;  // alignment, zeros, barriers
+  // segments per pass: two accumulator sets must fit in TMEM's 512 columns,
+  // and the stage ring should keep at least 5 stages in flight
+  int kmax = 256 / (p.n_modules * RP);
+  if (kmax > 4) kmax = 4;
+  if (kmax < 1) return set_error(LF_ERR_UNSUPPORTED, "persistent shrink: %d modules of rank %d", p.n_modules, R);
+  auto stage_of = [&](int km) { return kYBox + km * p.n_modules * 64 * R * 2; };  // multiple of 1024
+  while (kmax > 1 && (kSmemBudget - fixed) / stage_of(kmax) < 5) --kmax;
+  const int stage_bytes = stage_of(kmax);
   int stages = (kSmemBudget - fixed) / stage_bytes;
   if (stages > 8) stages = 8;
   if (stages < 2) return set_error(LF_ERR_UNSUPPORTED, "persistent shrink: %d modules of rank %d do not fit", p.n_modules, R);
+  p.kmax = kmax;
+  p.acc_cols = uint32_t(kmax * p.n_modules * RP);
   const size_t smem = size_t(fixed) + size_t(stages) * stage_bytes;
   auto kern = lora_shrink_persist_kernel<T, R>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -636,12 +719,12 @@ int launch_shrink(const ShrinkPersistParams& p, cudaStream_t stream) {
 }
 
 template <typename T>
-int expand_rank(const ExpandPersistParams& p, int rank, cudaStream_t s) {
+int expand_rank(const ExpandPersistParams& p, int rank, bool after_shrink, cudaStream_t s) {
   switch (rank) {
-    case 8: return launch_expand<T, 8, 128>(p, s);
-    case 16: return launch_expand<T, 16, 128>(p, s);
-    case 32: return launch_expand<T, 32, 128>(p, s);
-    case 64: return launch_expand<T, 64, 128>(p, s);
+    case 8: return launch_expand<T, 8, 128>(p, after_shrink, s);
+    case 16: return launch_expand<T, 16, 128>(p, after_shrink, s);
+    case 32: return launch_expand<T, 32, 128>(p, after_shrink, s);
+    case 64: return launch_expand<T, 64, 128>(p, after_shrink, s);
   }
   return set_error(LF_ERR_UNSUPPORTED, "persistent expand: rank %d", rank);
 }
@@ -659,10 +742,11 @@ int shrink_rank(const ShrinkPersistParams& p, int rank, cudaStream_t s) {
 
 }  // namespace
 
-int run_expand_persist(int dtype, const ExpandPersistParams& p, int rank, int nt, cudaStream_t s) {
+int run_expand_persist(int dtype, const ExpandPersistParams& p, int rank, int nt, bool after_shrink,
+                       cudaStream_t s) {
   if (nt != 128) return set_error(LF_ERR_UNSUPPORTED, "persistent expand: column tile %d", nt);
-  if (dtype == LF_DTYPE_BF16) return expand_rank<__nv_bfloat16>(p, rank, s);
-  return expand_rank<__half>(p, rank, s);
+  if (dtype == LF_DTYPE_BF16) return expand_rank<__nv_bfloat16>(p, rank, after_shrink, s);
+  return expand_rank<__half>(p, rank, after_shrink, s);
 }
 
 int run_shrink_persist(int dtype, const ShrinkPersistParams& p, int rank, cudaStream_t s) {

@@ -404,6 +404,58 @@ def test_tc_persistent_packed_segments_equal_per_tile(cuda, R):
     check(persistent.cpu(), ref, y.cpu(), dtype)
 
 
+@pytest.mark.parametrize("n_mod,R", [(1, 16), (3, 16), (3, 64), (2, 8)])
+def test_tc_persistent_many_short_segments_per_tile(cuda, n_mod, R):
+    """Tiles holding up to ~20 short segments with gaps between them: the
+    persistent shrink multiplies each x K-block by several segments' A at once
+    and needs several passes per tile; u (0 in the gaps) and the whole delta
+    equal the one-tile-per-CTA kernels' bit for bit."""
+    dtype = torch.bfloat16
+    H, n_slots = 256, 13
+    g = torch.Generator().manual_seed(700 + 10 * n_mod + R)
+    lengths = torch.randint(1, 20, (60,), generator=g).tolist()
+    gaps = torch.randint(0, 4, (60,), generator=g).tolist()
+    starts, t = [], 0
+    for n, gap in zip(lengths, gaps):
+        t += gap
+        starts.append(t)
+        t += n
+    T = t + 5
+    slots = torch.randint(0, n_slots, (60,), generator=g).tolist()
+    segs = list(zip(starts, lengths, slots))
+    fc, a_of, b_of = make_cache(n_slots, n_mod, H, R, dtype, cuda, seed=800 + R)
+    x = torch.randn(T, H, generator=g).to(dtype).to(cuda)
+    y = torch.randn(T, n_mod * H, generator=g).to(dtype).to(cuda)
+    mods, offs = list(range(n_mod)), [m * H for m in range(n_mod)]
+    st = SegmentTable(starts, lengths, slots, T, cuda)
+    assert st.n_multi > 0
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+
+    def shrink():
+        u = torch.full((n_mod, T, R), float("nan"), dtype=dtype, device=cuda)
+        lora_shrink(x, u, fc, st, mods, status)
+        torch.cuda.synchronize()
+        assert status.item() == 0, nat.decode_status(status.item())
+        return u
+
+    nat.set_option(nat.LF_OPT_SHRINK_CLUSTER, 1)
+    u_p = shrink()
+    u_t = run_per_tile(shrink)
+    covered = torch.zeros(T, dtype=torch.bool, device=cuda)
+    for s0, n in zip(starts, lengths):
+        covered[s0:s0 + n] = True
+    touched = torch.zeros(T, dtype=torch.bool, device=cuda)
+    for s0, n in zip(starts, lengths):
+        touched[s0 // 128 * 128: min(T, (s0 + n + 127) // 128 * 128)] = True
+    assert torch.equal(u_p[:, touched], u_t[:, touched])
+    assert (u_p[:, touched & ~covered] == 0).all()
+    persistent = run_apply(x, y, fc, segs, mods, offs)
+    per_tile = run_per_tile(run_apply, x, y, fc, segs, mods, offs)
+    assert torch.equal(persistent, per_tile)
+    ref = segmented_apply(x.cpu(), y.cpu(), a_of, b_of, segs, col_offsets=offs, modules=mods)
+    check(persistent.cpu(), ref, y.cpu(), dtype)
+
+
 def test_tc_persistent_expand_many_items_per_cta(cuda):
     """bge-m3 q/k/v shape: 256 tiles x 3 modules x 8 column blocks = 6,144 work
     items over at most 148 CTAs, so every CTA cycles its stage ring many times;
