@@ -527,7 +527,7 @@ lora_shrink_persist_kernel(const __grid_constant__ ShrinkPersistParams p, int st
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16(DT<T>::umma_fmt, kTile, RP, /*a_mn=*/0, /*b_mn=*/1);
+      constexpr uint32_t idesc16 = umma_idesc_f16(DT<T>::umma_fmt, kTile, RP, /*a_mn=*/0, /*b_mn=*/1);
       int kk = 0, it = 0;
       bool stop = false;
       int ti = blockIdx.x;
@@ -551,15 +551,28 @@ lora_shrink_persist_kernel(const __grid_constant__ ShrinkPersistParams p, int st
             if (!mbar_wait(bar(FULL + s), ph)) { fail(); stop = true; break; }
             tc_fence_after();
             const uint32_t st = s_stage0 + s * stage_bytes;
-            for (int jm = 0; jm < kp * n_mod; ++jm) {
-              const uint32_t ab = st + kYBox + jm * kABox;
+            if (R == 8) {
+              // 8 columns per box, padded to N=16 with a zero block: one MMA per box
+              for (int jm = 0; jm < kp * n_mod; ++jm) {
+                const uint32_t ab = st + kYBox + jm * kABox;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const uint64_t ad = smem_desc(st + q * 32, 16, 1024, 2);
+                  const uint32_t bstart = ab + q * 16 * A::kRowBytes;
+                  const uint64_t bd = smem_desc(bstart, 128, s_zero + q * 256 - bstart, 0);
+                  umma_f16(tmem + a * acc_cols + jm * RP, ad, bd, idesc16, (kb | q) != 0 ? 1u : 0u);
+                }
+              }
+            } else {
+              // the pass's A boxes lie kABox apart, one swizzle atom of R columns
+              // each: a single MMA with N = kp * n_mod * R reads them all as
+              // consecutive MN atoms (leading byte offset = kABox)
+              const uint32_t idesc = umma_idesc_f16(DT<T>::umma_fmt, kTile, uint32_t(kp * n_mod * R), 0, 1);
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
                 const uint64_t ad = smem_desc(st + q * 32, 16, 1024, 2);
-                const uint32_t bstart = ab + q * 16 * A::kRowBytes;
-                const uint64_t bd = (R == 8) ? smem_desc(bstart, 128, s_zero + q * 256 - bstart, 0)
-                                             : smem_desc(bstart, A::kSbo, A::kSbo, A::kLayout);
-                umma_f16(tmem + a * acc_cols + jm * RP, ad, bd, idesc, (kb | q) != 0 ? 1u : 0u);
+                const uint64_t bd = smem_desc(st + kYBox + q * 16 * A::kRowBytes, kABox, A::kSbo, A::kLayout);
+                umma_f16(tmem + a * acc_cols, ad, bd, idesc, (kb | q) != 0 ? 1u : 0u);
               }
             }
             umma_commit(bar(EMPTY + s));
@@ -691,8 +704,9 @@ template <typename T, int R>
 int launch_shrink(ShrinkPersistParams p, cudaStream_t stream) {
   constexpr int RP = R < 16 ? 16 : R;
   const int fixed = 1024 + 1024 + 1024;  // alignment, zeros, barriers
-  // segments per pass: two accumulator sets must fit in TMEM's 512 columns,
-  // and the stage ring should keep at least 5 stages in flight
+  // segments per pass: one MMA covers every segment and module of a pass
+  // (N = kmax * n_modules * RP <= 256, which also keeps two accumulator sets
+  // inside TMEM's 512 columns), and the ring keeps at least 5 stages
   int kmax = 256 / (p.n_modules * RP);
   if (kmax > 4) kmax = 4;
   if (kmax < 1) return set_error(LF_ERR_UNSUPPORTED, "persistent shrink: %d modules of rank %d", p.n_modules, R);
