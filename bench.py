@@ -42,6 +42,10 @@ if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
 
 METRIC = "sequences/sec at bge-m3 shape, 10k adapters; LoRA-kernel HBM GB/s vs peak"
+# DRAM bytes (read + write) of one LoRA op, averaged over the q/k/v op (182.85 MB) and the
+# dense op (70.34 MB) of the bge-m3 step at r=16, from one ncu capture of the same launch
+# shapes (profiles/lora_kernels_serve_traffic.md holds the command and the table).
+NCU_TRAFFIC_PER_OP_R16 = (182.85e6 + 70.34e6) / 2
 TARGETS = ["query", "key", "value", "dense"]
 FALLBACK_HBM_GBS = 6650.0
 
@@ -356,7 +360,10 @@ def run_ours(args):
             "peak": peak,
             "unit": "GB/s",
             "frac": achieved / peak,
-            "traffic": None,
+            "traffic": (NCU_TRAFFIC_PER_OP_R16 if packed is not None and args.rank == 16 and args.batch == 64
+                        and args.seq == 512 else None),
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per LoRA op (shrink + expand) "
+                              "of this workload; y writes still in L2 at kernel end are not counted",
             "kernel": "LoRA delta op = tcgen05 shrink + expand launches (per layer: q/k/v op, dense op)",
             "algorithmic_bytes_per_op": bytes_step / ops_step,
             "op_ms": lora_ms_step / ops_step,
