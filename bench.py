@@ -44,7 +44,7 @@ if str(ROOT) not in sys.path:
 METRIC = "sequences/sec at bge-m3 shape, 10k adapters; LoRA-kernel HBM GB/s vs peak"
 # DRAM bytes (read + write) of one LoRA op, averaged over the q/k/v op (182.85 MB) and the
 # dense op (70.34 MB) of the bge-m3 step at r=16, from one ncu capture of the same launch
-# shapes (profiles/lora_kernels_serve_traffic.md holds the command and the table).
+# shapes (the serve-traffic summary under profiles/ holds the command and the table).
 NCU_TRAFFIC_PER_OP_R16 = (182.85e6 + 70.34e6) / 2
 TARGETS = ["query", "key", "value", "dense"]
 FALLBACK_HBM_GBS = 6650.0
