@@ -515,8 +515,8 @@ class EncoderWithLora(nn.Module):
              token_type_ids: Tensor | None = None) -> PackedBatch:
         """Pack right-padded host rows (``lengths[b]`` real tokens first) for
         :meth:`encode_pooled_packed`; position ids follow the padded rows."""
-        return pack_rows(input_ids, lengths, slots, self.position_ids(input_ids), token_type_ids,
-                         self.config.device)
+        return pack_rows(input_ids, lengths, slots, self.pad_idx if self.offset_positions else None,
+                         token_type_ids, self.config.device)
 
     def encode_packed(self, pb: PackedBatch, store, apply_lora: bool = True) -> Tensor:
         """Final hidden states of the real tokens, ``(n_tokens, H)`` in packed order.

@@ -16,6 +16,7 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 from torch import Tensor
 
@@ -80,24 +81,29 @@ class SegmentTable:
 
 def _tile_records(starts, lengths, slots) -> list[int]:
     """Flattened ``{tile, first segment, segment count, first slot}`` records of the
-    tiles that hold segment tokens (segments sorted by start): single-segment
-    tiles first, in tile order, then the tiles with several segments."""
+    tiles that hold segment tokens (segments sorted by start, not overlapping):
+    single-segment tiles first, in tile order, then the tiles with several segments."""
     tile = nat.TILE_TOKENS
-    first: dict[int, int] = {}
-    count: dict[int, int] = {}
-    for g, (s, n) in enumerate(zip(starts, lengths)):
-        if n <= 0:
-            continue
-        for t in range(s // tile, (s + n - 1) // tile + 1):
-            if t not in first:
-                first[t] = g
-                count[t] = 0
-            count[t] = g - first[t] + 1
-    out: list[int] = []
-    # tiles with one segment first (the persistent kernel takes those), then the rest
-    for t in sorted(first, key=lambda t: (count[t] != 1, t)):
-        out += [t, first[t], count[t], slots[first[t]]]
-    return out
+    st = np.asarray(starts, dtype=np.int64)
+    ln = np.asarray(lengths, dtype=np.int64)
+    seg = np.nonzero(ln > 0)[0]
+    if seg.size == 0:
+        return []
+    t0 = st[seg] // tile
+    nt = (st[seg] + ln[seg] - 1) // tile - t0 + 1
+    # one (segment, tile) entry per tile a segment touches, by segment then tile
+    seg_of = np.repeat(seg, nt)
+    tile_of = np.repeat(t0, nt) + np.arange(int(nt.sum())) - np.repeat(np.cumsum(nt) - nt, nt)
+    order = np.argsort(tile_of, kind="stable")  # by tile; within a tile by segment
+    tiles, first_idx, n_touch = np.unique(tile_of[order], return_index=True, return_counts=True)
+    first = seg_of[order][first_idx]
+    # the count spans segment indices first..last (an empty segment in between counts)
+    count = seg_of[order][first_idx + n_touch - 1] - first + 1
+    slot_arr = np.asarray(slots, dtype=np.int64)
+    recs = np.stack([tiles, first, count, slot_arr[first]], axis=1)
+    # tiles with one segment first (the cheapest work first), then the rest, each in tile order
+    recs = recs[np.argsort(count != 1, kind="stable")]
+    return recs.reshape(-1).tolist()
 
 
 # ---------------------------------------------------------------------------

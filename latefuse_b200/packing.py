@@ -63,21 +63,23 @@ def attention_items(starts, lengths) -> np.ndarray:
     lengths = np.asarray(lengths, dtype=np.int64)
     n_qt = (lengths + 127) // 128
     seq_order = np.argsort(-n_qt, kind="stable")
-    items = np.zeros((int(n_qt.sum()), 4), dtype=np.int64)
-    k = 0
-    for i in seq_order:
-        for t in range(int(n_qt[i])):
-            items[k] = (starts[i], lengths[i], t, 0)
-            k += 1
+    reps = n_qt[seq_order]
+    total = int(reps.sum())
+    items = np.zeros((total, 4), dtype=np.int64)
+    items[:, 0] = np.repeat(starts[seq_order], reps)
+    items[:, 1] = np.repeat(lengths[seq_order], reps)
+    items[:, 2] = np.arange(total) - np.repeat(np.cumsum(reps) - reps, reps)
     return items
 
 
-def pack_rows(input_ids: Tensor, lengths: list[int], slots: list[int], positions: Tensor,
+def pack_rows(input_ids: Tensor, lengths: list[int], slots: list[int], position_pad: int | None,
               token_type_ids: Tensor | None, device: torch.device) -> PackedBatch:
     """Pack the real tokens of right-padded host rows (``1 <= lengths[b] <= S``).
 
-    ``positions`` are the model's position ids for the padded rows (computed on
-    the host by the model's own rule), so packing changes no position.
+    Position ids follow the model's rule on the padded rows, so packing changes
+    no position: ``position_pad=None`` numbers every row ``0, 1, 2 ...`` (BERT);
+    an integer ``pad`` numbers the non-pad tokens of a row ``pad+1, pad+2 ...``
+    and gives pad tokens ``pad`` (the RoBERTa family, from ``input_ids != pad``).
     """
     B, S = input_ids.shape
     if len(lengths) != B or len(slots) != B:
@@ -105,9 +107,18 @@ def pack_rows(input_ids: Tensor, lengths: list[int], slots: list[int], positions
     a = buf.numpy()
     a[:4 * n_items] = items.reshape(-1)
     o = 4 * n_items
-    a[o:o + T] = input_ids.reshape(-1).numpy()[sel]
+    ids_sel = input_ids.reshape(-1).numpy()[sel]
+    a[o:o + T] = ids_sel
     o += T
-    a[o:o + T] = positions.reshape(-1).numpy()[sel]
+    if position_pad is None:
+        a[o:o + T] = col
+    else:
+        # within a row the real tokens are a prefix, so a running count over the
+        # packed tokens restarted at each row gives the padded rows' cumsum
+        ne = (ids_sel != position_pad).astype(np.int64)
+        cs = np.cumsum(ne)
+        base = np.repeat(cs[cu[:-1]] - ne[cu[:-1]], olens)
+        a[o:o + T] = (cs - base) * ne + position_pad
     o += T
     a[o:o + T] = token_type_ids.reshape(-1).numpy()[sel] if token_type_ids is not None else 0
     o += T

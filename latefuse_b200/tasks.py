@@ -18,6 +18,7 @@ from collections.abc import Iterator, Sequence
 from dataclasses import dataclass
 from typing import TypeVar
 
+import numpy as np
 import torch
 from torch import Tensor
 
@@ -64,12 +65,13 @@ def _default_dtype(device: torch.device) -> torch.dtype:
 def right_padded_lengths(mask: Tensor) -> list[int] | None:
     """Per-row real lengths of a host ``(B, S)`` 0/1 mask, or None unless every row is
     ones followed by zeros (only then can padding be skipped as a suffix)."""
-    m = mask.to(torch.int64)
-    lengths = m.sum(dim=1)
-    pos = torch.arange(m.shape[1]).unsqueeze(0)
-    if not torch.equal(m, (pos < lengths.unsqueeze(1)).to(torch.int64)):
+    m = mask.numpy() if mask.dtype != torch.bool else mask.numpy().astype(np.int8)
+    if m.ndim != 2 or m.size == 0:
+        return None if m.ndim != 2 else [0] * m.shape[0]
+    # ones followed by zeros: 0/1 values, never increasing along a row
+    if ((m != 0) & (m != 1)).any() or (m[:, 1:] > m[:, :-1]).any():
         return None
-    return lengths.tolist()
+    return m.sum(axis=1).astype(np.int64).tolist()
 
 
 class TaskPipeline:

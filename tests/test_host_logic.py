@@ -70,11 +70,13 @@ def test_pack_rows_layout():
 
     B, S = 4, 6
     ids = torch.arange(B * S).view(B, S) + 100
-    pos = torch.arange(S).expand(B, S) + 2
+    ids[0, 2] = 1  # a pad id inside a real span keeps the RoBERTa rule honest
     tt = torch.zeros(B, S, dtype=torch.long)
     tt[:, 3:] = 1
     lengths, slots = [6, 2, 4, 1], [5, 3, 5, 3]
-    pb = pack_rows(ids, lengths, slots, pos, tt, torch.device("cpu"))
+    m = ids.ne(1).long()
+    pos = torch.cumsum(m, 1) * m + 1  # HF create_position_ids_from_input_ids with pad 1
+    pb = pack_rows(ids, lengths, slots, 1, tt, torch.device("cpu"))
     assert pb.order == [1, 3, 0, 2]
     assert pb.n_tokens == 13 and pb.max_len == 6
     assert pb.cu_seqlens.tolist() == [0, 2, 3, 9, 13]
@@ -91,8 +93,10 @@ def test_pack_rows_layout():
     assert starts == [0, 3] and seg_lens == [3, 10]
     # attention work list: one record per (sequence, 128-query tile)
     assert pb.attn_items.tolist() == [[0, 2, 0, 0], [2, 1, 0, 0], [3, 6, 0, 0], [9, 4, 0, 0]]
+    arange = pack_rows(ids, lengths, slots, None, None, torch.device("cpu"))  # BERT numbering
+    assert arange.positions.tolist() == torch.cat([torch.arange(lengths[b]) for b in pb.order]).tolist()
     with pytest.raises(ValueError):
-        pack_rows(ids, [6, 0, 4, 1], slots, pos, None, torch.device("cpu"))
+        pack_rows(ids, [6, 0, 4, 1], slots, None, None, torch.device("cpu"))
 
 
 def test_attention_items_order_and_tiles():
