@@ -67,7 +67,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   const int Q_FULL = 0, Q_EMPTY = 2, KV_FULL = 4, KV_EMPTY = 4 + kKvStages, S_FULL = 4 + 2 * kKvStages,
             S_EMPTY = S_FULL + 2, P_FULL = S_EMPTY + 2, P_EMPTY = P_FULL + 2, O_FULL = P_EMPTY + 2,
-            O_EMPTY = O_FULL + 1, DRAIN = O_EMPTY + 1, N_BARS = DRAIN + 1;
+            O_EMPTY = O_FULL + 2, DRAIN = O_EMPTY + 2, N_BARS = DRAIN + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(&bars[N_BARS]);
   int32_t* s_abort = reinterpret_cast<int32_t*>(tmem_slot + 1);
   float* s_max = reinterpret_cast<float*>(gbase + (sP + 4 * kTileBytes + 1024 - base));  // [2][2][128]
@@ -88,15 +88,17 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
       mbar_init(bar(KV_FULL + i), 1);
       mbar_init(bar(KV_EMPTY + i), 1);
     }
-    mbar_init(bar(O_FULL), 1);
-    mbar_init(bar(O_EMPTY), kSoftmaxWarps);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(O_FULL + i), 1);
+      mbar_init(bar(O_EMPTY + i), kSoftmaxWarps);
+    }
     mbar_init(bar(DRAIN), 1);
     *s_abort = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
     __syncwarp();
-    tmem_alloc(smem_u32(tmem_slot), 512);  // S0 [0,128) S1 [128,256) O [256,320)
+    tmem_alloc(smem_u32(tmem_slot), 512);  // S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384)
   }
   __syncthreads();
   tc_fence_after();
@@ -162,11 +164,12 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
       constexpr uint32_t idesc_o = umma_idesc_f16(DT<T>::umma_fmt, kRows, kHd, /*a_mn=*/0, /*b_mn=*/1);
       int u = 0, g = 0;
       bool stop = false;
-      // O += P_gp V_gp, the first of a unit overwriting O once the previous unit's O was read
+      // O_u += P_gp V_gp; the first of a unit overwrites O buffer u&1 once unit
+      // u-2's O was read from it
       auto pv = [&](int gp, bool first) -> bool {
         const int bp = gp & 1, sp = gp % kKvStages;
         if (!mbar_wait(bar(P_FULL + bp), (gp >> 1) & 1)) return false;
-        if (first && !mbar_wait(bar(O_EMPTY), (u & 1) ^ 1)) return false;
+        if (first && !mbar_wait(bar(O_EMPTY + (u & 1)), ((u >> 1) & 1) ^ 1)) return false;
         tc_fence_after();
         const uint32_t pb = sP + bp * 2 * kTileBytes;
         const uint32_t vb = sKV + sp * 2 * kTileBytes + kTileBytes;
@@ -174,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
         for (int t = 0; t < kRows / 16; ++t) {
           const uint64_t ad = smem_desc(pb + (t >> 2) * kTileBytes + (t & 3) * 32, 16, 1024, 2);
           const uint64_t bd = smem_desc(vb + t * 2048, kTileBytes, 1024, 2);
-          umma_f16(tmem + 256, ad, bd, idesc_o, (first && t == 0) ? 0u : 1u);
+          umma_f16(tmem + 256 + (u & 1) * kHd, ad, bd, idesc_o, (first && t == 0) ? 0u : 1u);
         }
         umma_commit(bar(P_EMPTY + bp));
         umma_commit(bar(KV_EMPTY + sp));
@@ -220,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
           stop = true;
           break;
         }
-        umma_commit(bar(O_FULL));
+        umma_commit(bar(O_FULL + (u & 1)));
       }
       if (aborted(s_abort)) {  // every issued MMA must finish before TMEM is released (bounded)
         umma_commit(bar(DRAIN));
@@ -237,6 +240,44 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
     const uint32_t pair_bar = 1 + quad;  // named barrier of this quadrant's two warps
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
     const uint32_t prow = (row >> 3) * 1024 + (row & 7) * 128;  // this row in a SW128 block
+    // O / l of a finished unit: the pair adds its two shares of the row sum,
+    // normalises and stores this half's 32 columns, and frees O buffer uu&1
+    auto epilogue = [&](const int4& eit, int eh, int uu, float el) {
+      s_lsum[half * 128 + row] = el;
+      named_barrier_sync(pair_bar, 64);
+      const float l_row = el + s_lsum[(half ^ 1) * 128 + row];
+      bool ok = !aborted(s_abort);
+      if (ok && !mbar_wait(bar(O_FULL + (uu & 1)), (uu >> 1) & 1)) {
+        fail();
+        ok = false;
+      }
+      if (__all_sync(0xffffffffu, ok)) {
+        tc_fence_after();
+        uint32_t ov[32];
+        tmem_ld32(tmem + lane_addr + 256 + (uu & 1) * kHd + half * 32, ov);
+        const int qr = eit.z * kRows + row;
+        if (qr < eit.y) {
+          const float inv = 1.f / l_row;
+          T* dst = reinterpret_cast<T*>(p.out) + int64_t(eit.x + qr) * p.ldo + eh * kHd + half * 32;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint4 w;
+            w.x = Pack2<T>::pack(__uint_as_float(ov[8 * c + 0]) * inv, __uint_as_float(ov[8 * c + 1]) * inv);
+            w.y = Pack2<T>::pack(__uint_as_float(ov[8 * c + 2]) * inv, __uint_as_float(ov[8 * c + 3]) * inv);
+            w.z = Pack2<T>::pack(__uint_as_float(ov[8 * c + 4]) * inv, __uint_as_float(ov[8 * c + 5]) * inv);
+            w.w = Pack2<T>::pack(__uint_as_float(ov[8 * c + 6]) * inv, __uint_as_float(ov[8 * c + 7]) * inv);
+            reinterpret_cast<uint4*>(dst)[c] = w;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(O_EMPTY + (uu & 1)));
+    };
+    bool have_pending = false;
+    int4 pend_it = make_int4(0, 1, 0, 0);
+    int pend_h = 0, pend_u = 0;
+    float pend_l = 0.f;
     int u = 0, g = 0;
     int4 nxt = unit_item(blockIdx.x);
     for (int64_t unit = blockIdx.x; unit < n_units; unit += gridDim.x, ++u) {
@@ -244,7 +285,6 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
       nxt = unit_item(unit + gridDim.x);
       const int h = int(unit % p.n_heads);
       const int n_kv = (it.y + kRows - 1) / kRows;
-      const int qrow = it.z * kRows + row;  // row within the sequence
       float m = -INFINITY, l = 0.f;         // l: this half's share of the row sum
       for (int j = 0; j < n_kv; ++j, ++g) {
         const int b = g & 1;
@@ -323,48 +363,29 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
           if (__all_sync(0xffffffffu, ok2)) {
             tc_fence_after();
             uint32_t ov[32];
-            tmem_ld32(tmem + lane_addr + 256 + half * 32, ov);
+            tmem_ld32(tmem + lane_addr + 256 + (u & 1) * kHd + half * 32, ov);
 #pragma unroll
             for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
-            tmem_st32(tmem + lane_addr + 256 + half * 32, ov);
+            tmem_st32(tmem + lane_addr + 256 + (u & 1) * kHd + half * 32, ov);
           }
         }
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(P_FULL + b));
-      }
-      // O / l for this unit: the pair adds its two shares of the row sum
-      s_lsum[half * 128 + row] = l;
-      named_barrier_sync(pair_bar, 64);
-      const float l_row = l + s_lsum[(half ^ 1) * 128 + row];
-      bool ok = !aborted(s_abort);
-      if (ok && !mbar_wait(bar(O_FULL), u & 1)) {
-        fail();
-        ok = false;
-      }
-      if (__all_sync(0xffffffffu, ok)) {
-        tc_fence_after();
-        uint32_t ov[32];
-        tmem_ld32(tmem + lane_addr + 256 + half * 32, ov);
-        if (qrow < it.y) {
-          const float inv = 1.f / l_row;
-          T* dst = reinterpret_cast<T*>(p.out) + int64_t(it.x + qrow) * p.ldo + h * kHd + half * 32;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint4 w;
-            w.x = Pack2<T>::pack(__uint_as_float(ov[8 * c + 0]) * inv, __uint_as_float(ov[8 * c + 1]) * inv);
-            w.y = Pack2<T>::pack(__uint_as_float(ov[8 * c + 2]) * inv, __uint_as_float(ov[8 * c + 3]) * inv);
-            w.z = Pack2<T>::pack(__uint_as_float(ov[8 * c + 4]) * inv, __uint_as_float(ov[8 * c + 5]) * inv);
-            w.w = Pack2<T>::pack(__uint_as_float(ov[8 * c + 6]) * inv, __uint_as_float(ov[8 * c + 7]) * inv);
-            reinterpret_cast<uint4*>(dst)[c] = w;
-          }
+        // the previous unit's output, now that its last O += P V has long finished
+        if (j == 0 && have_pending) {
+          epilogue(pend_it, pend_h, pend_u, pend_l);
+          have_pending = false;
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(O_EMPTY));
+      pend_it = it;
+      pend_h = h;
+      pend_u = u;
+      pend_l = l;
+      have_pending = true;
     }
+    if (have_pending) epilogue(pend_it, pend_h, pend_u, pend_l);
   }
 
   __syncthreads();
