@@ -159,17 +159,20 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // One flat sequence over the CTA's tiles: S of a tile is issued before the
+    // previous tile's O += P V, across unit boundaries too, so the next unit's
+    // first scores are ready when the softmax warps finish the last tile.
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_f16(DT<T>::umma_fmt, kRows, kRows, /*a_mn=*/0, /*b_mn=*/0);
       constexpr uint32_t idesc_o = umma_idesc_f16(DT<T>::umma_fmt, kRows, kHd, /*a_mn=*/0, /*b_mn=*/1);
       int u = 0, g = 0;
       bool stop = false;
-      // O_u += P_gp V_gp; the first of a unit overwrites O buffer u&1 once unit
-      // u-2's O was read from it
-      auto pv = [&](int gp, bool first) -> bool {
+      // O_uu += P_gp V_gp; the first of a unit overwrites O buffer uu&1 once unit
+      // uu-2's O was read from it; the last of a unit publishes O
+      auto pv = [&](int gp, bool first, bool last, int uu) -> bool {
         const int bp = gp & 1, sp = gp % kKvStages;
         if (!mbar_wait(bar(P_FULL + bp), (gp >> 1) & 1)) return false;
-        if (first && !mbar_wait(bar(O_EMPTY + (u & 1)), ((u >> 1) & 1) ^ 1)) return false;
+        if (first && !mbar_wait(bar(O_EMPTY + (uu & 1)), ((uu >> 1) & 1) ^ 1)) return false;
         tc_fence_after();
         const uint32_t pb = sP + bp * 2 * kTileBytes;
         const uint32_t vb = sKV + sp * 2 * kTileBytes + kTileBytes;
@@ -177,12 +180,15 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
         for (int t = 0; t < kRows / 16; ++t) {
           const uint64_t ad = smem_desc(pb + (t >> 2) * kTileBytes + (t & 3) * 32, 16, 1024, 2);
           const uint64_t bd = smem_desc(vb + t * 2048, kTileBytes, 1024, 2);
-          umma_f16(tmem + 256 + (u & 1) * kHd, ad, bd, idesc_o, (first && t == 0) ? 0u : 1u);
+          umma_f16(tmem + 256 + (uu & 1) * kHd, ad, bd, idesc_o, (first && t == 0) ? 0u : 1u);
         }
         umma_commit(bar(P_EMPTY + bp));
         umma_commit(bar(KV_EMPTY + sp));
+        if (last) umma_commit(bar(O_FULL + (uu & 1)));
         return true;
       };
+      bool have_prev = false, prev_first = false, prev_last = false;
+      int prev_g = 0, prev_u = 0;
       int4 nxt = unit_item(blockIdx.x);
       for (int64_t unit = blockIdx.x; unit < n_units && !stop; unit += gridDim.x, ++u) {
         const int4 it = nxt;
@@ -194,7 +200,6 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
           stop = true;
           break;
         }
-        const int g0 = g;
         for (int j = 0; j < n_kv; ++j, ++g) {
           const int s = g % kKvStages, b = g & 1;
           if (aborted(s_abort) || !mbar_wait(bar(KV_FULL + s), (g / kKvStages) & 1) ||
@@ -211,20 +216,19 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
                      idesc_s, t > 0 ? 1u : 0u);
           umma_commit(bar(S_FULL + b));
           if (j == n_kv - 1) umma_commit(bar(Q_EMPTY + qb));
-          if (j >= 1 && !pv(g - 1, j - 1 == 0)) {
+          if (have_prev && !pv(prev_g, prev_first, prev_last, prev_u)) {
             fail();
             stop = true;
             break;
           }
+          have_prev = true;
+          prev_g = g;
+          prev_first = j == 0;
+          prev_last = j == n_kv - 1;
+          prev_u = u;
         }
-        if (stop) break;
-        if (!pv(g0 + n_kv - 1, n_kv == 1)) {
-          fail();
-          stop = true;
-          break;
-        }
-        umma_commit(bar(O_FULL + (u & 1)));
       }
+      if (!stop && have_prev && !pv(prev_g, prev_first, prev_last, prev_u)) fail();
       if (aborted(s_abort)) {  // every issued MMA must finish before TMEM is released (bounded)
         umma_commit(bar(DRAIN));
         mbar_wait(bar(DRAIN), 0);
@@ -300,15 +304,19 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
         float mx = -INFINITY;
         if (work) {
           tmem_ld64(tmem + lane_addr + b * kRows + half * 64, sv);
-          float raw_max = -INFINITY;
+          float mxs[8];  // eight independent chains instead of one 64-long one
+#pragma unroll
+          for (int q = 0; q < 8; ++q) mxs[q] = -INFINITY;
           if (nvalid >= 64) {  // warp-uniform: a full half tile needs no mask
 #pragma unroll
-            for (int c = 0; c < 64; ++c) raw_max = fmaxf(raw_max, __uint_as_float(sv[c]));
+            for (int c = 0; c < 64; ++c) mxs[c & 7] = fmaxf(mxs[c & 7], __uint_as_float(sv[c]));
           } else {
 #pragma unroll
             for (int c = 0; c < 64; ++c)
-              if (c < nvalid) raw_max = fmaxf(raw_max, __uint_as_float(sv[c]));
+              if (c < nvalid) mxs[c & 7] = fmaxf(mxs[c & 7], __uint_as_float(sv[c]));
           }
+          const float raw_max = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
+                                      fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
           mx = raw_max * p.scale_log2;  // the scale is positive: max commutes with it
         }
         tc_fence_before();
@@ -327,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
           fail();
           ok = false;
         }
-        float sum = 0.f;
+        float sums[4] = {0.f, 0.f, 0.f, 0.f};  // independent chains
         if (__all_sync(0xffffffffu, ok)) {
           const uint32_t pb = sP + b * 2 * kTileBytes + half * kTileBytes - base;
           const float sl2 = p.scale_log2, neg_m = -m_new;
@@ -344,14 +352,14 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
                 p0 = c < nvalid ? p0 : 0.f;
                 p1 = c + 1 < nvalid ? p1 : 0.f;
               }
-              sum += p0 + p1;
+              sums[i] += p0 + p1;
               w[i] = Pack2<T>::pack(p0, p1);
             }
             *reinterpret_cast<uint4*>(gbase + pb + prow + ((c8 ^ (row & 7)) << 4)) =
                 make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
-        l = l * alpha + sum;
+        l = l * alpha + ((sums[0] + sums[1]) + (sums[2] + sums[3]));
         m = m_new;
         // the max moved: rescale this half's O columns once the previous O += P V has finished
         if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
