@@ -45,11 +45,13 @@ def _read_state_dict(path: str, device) -> dict:
 
 
 def load_peft_adapter(store: AdapterStore, adapter_id: str, path: str, *, adapter_name: str = "default",
-                      lora_alpha: float | None = None, strict: bool = True) -> None:
+                      lora_alpha: float | None = None, strict: bool = True, pad_rank: bool = False) -> None:
     """Load a PEFT adapter directory into ``store`` under ``adapter_id``.
 
     Checks ``adapter_config.json`` against the serving config (rank, target
-    modules) and folds ``lora_alpha / r`` into B, as the reference does.
+    modules) and folds ``lora_alpha / r`` into B, as the reference does.  With
+    ``pad_rank`` an adapter trained at a lower rank than the store's is accepted
+    and zero-padded into its slot (mixed-rank serving; same delta).
 
     Raises:
         ValueError:        on a config mismatch under ``strict``.
@@ -64,20 +66,21 @@ def load_peft_adapter(store: AdapterStore, adapter_id: str, path: str, *, adapte
         with open(peft_config_path) as fh:
             peft_config = json.load(fh)
     if peft_config:
-        _check_compatible(peft_config, cfg, adapter_id, strict)
+        _check_compatible(peft_config, cfg, adapter_id, strict, pad_rank)
     if lora_alpha is None:
         lora_alpha = peft_config.get("lora_alpha")
     model_type = cfg.hf_config.model_type
     state_dict = _read_state_dict(path, "cpu" if cfg.device.type != "cuda" else cfg.device)
-    store.load_from_state_dict(adapter_id, state_dict, peft_key_fn(model_type, adapter_name), lora_alpha=lora_alpha)
+    store.load_from_state_dict(adapter_id, state_dict, peft_key_fn(model_type, adapter_name), lora_alpha=lora_alpha,
+                               pad_rank=pad_rank or not strict)
 
 
-def _check_compatible(peft_config: dict, cfg, adapter_id: str, strict: bool) -> None:
+def _check_compatible(peft_config: dict, cfg, adapter_id: str, strict: bool, pad_rank: bool = False) -> None:
     import warnings
 
     problems = []
     rank = peft_config.get("r")
-    if rank is not None and rank != cfg.lora_rank:
+    if rank is not None and rank != cfg.lora_rank and not (pad_rank and rank < cfg.lora_rank):
         problems.append(
             f"adapter was trained at rank {rank} but this pipeline serves rank {cfg.lora_rank}. One pipeline "
             "serves one rank; build a second pipeline for the other."

@@ -66,15 +66,29 @@ class LoraWeight:
         """Load from column-major tensors (as stored in adapter files).
 
         Args:
-            a_by_module: module -> (num_layers, lora_rank, hidden_size)
-            b_by_module: module -> (num_layers, hidden_size, lora_rank)
+            a_by_module: module -> (num_layers, rank, hidden_size)
+            b_by_module: module -> (num_layers, hidden_size, rank)
             scale:       alpha / rank, folded into B (same arithmetic as the
                          reference: cast to the model dtype, transpose, multiply).
+
+        A rank below the slot's is zero-padded: A's extra columns and B's extra
+        rows are zero, so ``B A x`` is unchanged (exactly) and nothing of a
+        previous occupant of the slot survives.
         """
         for m, a in a_by_module.items():
-            self.wa[m].copy_(a.to(self.wa[m].device, self.wa[m].dtype).transpose(1, 2))
+            r = a.shape[1]
+            if r == self.wa[m].shape[2]:
+                self.wa[m].copy_(a.to(self.wa[m].device, self.wa[m].dtype).transpose(1, 2))
+            else:
+                self.wa[m].zero_()
+                self.wa[m][:, :, :r].copy_(a.to(self.wa[m].device, self.wa[m].dtype).transpose(1, 2))
         for m, b in b_by_module.items():
-            self.wb[m].copy_(b.to(self.wb[m].device, self.wb[m].dtype).transpose(1, 2))
+            r = b.shape[2]
+            if r == self.wb[m].shape[1]:
+                self.wb[m].copy_(b.to(self.wb[m].device, self.wb[m].dtype).transpose(1, 2))
+            else:
+                self.wb[m].zero_()
+                self.wb[m][:, :r, :].copy_(b.to(self.wb[m].device, self.wb[m].dtype).transpose(1, 2))
             if scale != 1.0:
                 self.wb[m].mul_(scale)
 
@@ -178,14 +192,15 @@ class AdapterStore:
         self.load_from_state_dict(adapter_id, state_dict, key_fn, lora_alpha=lora_alpha)
 
     def load_from_state_dict(self, adapter_id: str, state_dict: dict, key_fn: KeyResolverFn,
-                             lora_alpha: float | None = None) -> None:
+                             lora_alpha: float | None = None, pad_rank: bool = False) -> None:
         """Cache an adapter from an already-loaded state dict.
 
         ``alpha / rank`` is folded into B at load time, as in the reference
-        (``src/latefuse/weights/store.py:104-145``).
+        (``src/latefuse/weights/store.py:104-145``).  With ``pad_rank`` an adapter
+        of a lower rank ``r`` is zero-padded into the slot (mixed-rank serving:
+        the delta ``(alpha / r) B A x`` is exactly that of the rank-``r`` adapter).
         """
         cfg = self._config
-        scale = 1.0 if lora_alpha is None else lora_alpha / cfg.lora_rank
         a_by_module: dict[str, Tensor] = {}
         b_by_module: dict[str, Tensor] = {}
         for module in cfg.target_modules:
@@ -203,6 +218,16 @@ class AdapterStore:
                 b_tensors.append(state_dict[key_b])
             a_by_module[module] = torch.stack(a_tensors)
             b_by_module[module] = torch.stack(b_tensors)
+        ranks = {a.shape[1] for a in a_by_module.values()} | {b.shape[2] for b in b_by_module.values()}
+        if len(ranks) != 1:
+            raise ValueError(f"adapter '{adapter_id}' mixes ranks {sorted(ranks)} across its modules")
+        rank = ranks.pop()
+        if rank > cfg.lora_rank or (rank < cfg.lora_rank and not pad_rank):
+            raise ValueError(
+                f"adapter '{adapter_id}' has rank {rank} but this store serves rank {cfg.lora_rank}"
+                + ("" if rank > cfg.lora_rank else "; pass pad_rank=True to zero-pad it into a slot")
+            )
+        scale = 1.0 if lora_alpha is None else lora_alpha / rank
         slot, weight = self._claim(adapter_id)
         weight.copy_from_tensors(a_by_module, b_by_module, scale=scale)
         self._commit(adapter_id, slot, weight)

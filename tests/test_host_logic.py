@@ -264,6 +264,63 @@ def test_peft_loader_rejects_mismatch(tmp_path, conf, match):
         lf.load_peft_adapter(lf.AdapterStore(cfg()), "t", str(d))
 
 
+def _peft_dir(tmp_path, c, rank, alpha, seed):
+    """A PEFT adapter directory for the tiny config at ``rank`` (A (r,H), B (H,r) per layer)."""
+    g = torch.Generator().manual_seed(seed)
+    sd = {}
+    for i in range(c.num_layers):
+        for m in c.target_modules:
+            ka, kb = lf.peft_key_fn("bert")(i, m)
+            sd[ka] = torch.randn(rank, c.hidden_size, generator=g)
+            sd[kb] = torch.randn(c.hidden_size, rank, generator=g)
+    d = tmp_path / f"adapter_r{rank}_{seed}"
+    d.mkdir()
+    (d / "adapter_config.json").write_text(json.dumps({"r": rank, "lora_alpha": alpha,
+                                                        "target_modules": list(c.target_modules)}))
+    torch.save(sd, d / "adapter_model.bin")
+    return d, sd
+
+
+def test_mixed_rank_padding_preserves_the_delta(tmp_path):
+    """A rank-2 adapter zero-padded into a rank-4 store gives exactly the delta
+    (alpha / 2) B A x of the rank-2 adapter, in f32."""
+    c = cfg(rank=4)
+    store = lf.AdapterStore(c)
+    d, sd = _peft_dir(tmp_path, c, rank=2, alpha=6, seed=5)
+    with pytest.raises(ValueError, match="rank"):
+        lf.load_peft_adapter(store, "low", str(d))  # the reference's default: one rank per pipeline
+    lf.load_peft_adapter(store, "low", str(d), pad_rank=True)
+    w = store.get("low")
+    x = torch.randn(7, c.hidden_size, generator=torch.Generator().manual_seed(1))
+    for i in range(c.num_layers):
+        for m in c.target_modules:
+            ka, kb = lf.peft_key_fn("bert")(i, m)
+            want = (x @ sd[ka].T) @ sd[kb].T * (6 / 2)
+            got = (x @ w.wa[m][i]) @ w.wb[m][i]
+            torch.testing.assert_close(got, want, atol=1e-5, rtol=1e-5)
+            assert (w.wa[m][i][:, 2:] == 0).all() and (w.wb[m][i][2:] == 0).all()
+
+
+def test_mixed_rank_no_stale_weights_in_a_reused_slot(tmp_path):
+    """A padded adapter loaded into the slot a full-rank adapter left behind
+    carries none of its columns."""
+    c = cfg(rank=4)
+    store = lf.AdapterStore(c)
+    d4, _ = _peft_dir(tmp_path, c, rank=4, alpha=4, seed=1)
+    d2, _ = _peft_dir(tmp_path, c, rank=2, alpha=2, seed=2)
+    lf.load_peft_adapter(store, "full", str(d4))
+    slot = store.slot_of("full")
+    store.evict("full")
+    lf.load_peft_adapter(store, "low", str(d2), pad_rank=True)
+    assert store.slot_of("low") == slot
+    w = store.get("low")
+    for m in c.target_modules:
+        assert (w.wa[m][:, :, 2:] == 0).all() and (w.wb[m][:, 2:, :] == 0).all()
+    d8, _ = _peft_dir(tmp_path, c, rank=8, alpha=8, seed=3)
+    with pytest.raises(ValueError, match="rank"):
+        lf.load_peft_adapter(store, "high", str(d8), pad_rank=True)  # cannot shrink a rank
+
+
 # ------------------------------------------------------------------- misc ---
 def test_pooling_validation():
     assert lf.validate_pooling("mean") == "mean"
