@@ -5,22 +5,31 @@
 // batch whose padding has been removed: every sequence attends to itself only.
 //
 // Work unit = (query tile of 128 rows of one sequence, head).  One persistent
-// CTA per SM loops over units with four roles:
-//   warp 0      producer: Q tile (double-buffered) and the sequence's K/V tiles
-//               (128 keys each, a 3-stage ring) by TMA straight from the fused
-//               QKV activation buffer (SW128, 128-byte rows of 64 head dims);
-//   warp 1      MMA issuer: S_j = Q K_j^T (M=128, N=128, K=64) into one of two
-//               TMEM S buffers, then O += P_j V_j (M=128, N=64, K=128) into the
-//               TMEM O accumulator, S_{j+1} issued before O += P_j V_j so the
-//               tensor core works while the softmax warps do;
-//   warps 2-9   softmax, two warps per TMEM lane quadrant (a query row's 128
-//               key columns split 64/64, the pair exchanging row maxima through
-//               shared memory): online softmax in the log2 domain with the
-//               running max raised only when a tile's max exceeds it by more
-//               than 2^8 (the final division keeps the result exact), P rounded
-//               to the model dtype into shared memory (the canonical K-major
-//               SW128 layout the MMA reads), O rescaled in TMEM when the max
-//               moves, and at the end O / l rounded and stored.
+// CTA per SM takes every gridDim-th unit and splits them over two softmax
+// groups that run in ping-pong, so that one group's exponentials overlap the
+// other group's row-max phase and the tensor core works for both:
+//   warp 0      producer: each group's Q tile, and the K and V tiles of the
+//               units' sequences (128 keys each; K in a 3-stage ring, freed once
+//               S is computed; V in a 4-stage ring, freed once O += P V is), by
+//               TMA straight from the fused QKV activation buffer (SW128, 128-
+//               byte rows of 64 head dims), in the order the MMA warp uses them;
+//   warp 1      MMA issuer, alternating between the groups: for a group's next
+//               tile S = Q K^T (M=128, N=128, K=64) into one of three TMEM S
+//               buffers the groups share round-robin (so the next S is computed
+//               while the group's softmax still reads the current one), then
+//               O += P V (M=128, N=64, K=128) for its previous tile into the
+//               group's TMEM O accumulator;
+//   warps 2-5,  softmax groups 0 and 1, one thread per query row (its TMEM
+//   6-9         lane): online softmax in the log2 domain with the running max
+//               raised only when a tile's max exceeds it by more than 2^8 (the
+//               final division keeps the result exact), P rounded to the model
+//               dtype into the group's shared-memory P tile (the MMA's K-major
+//               SW128 layout), O rescaled in TMEM when the max moves, and after
+//               a unit's last tile O / l rounded and stored.  The softmax loops
+//               run 64 columns per iteration without unrolling the iterations:
+//               the smaller loop body measured faster than the unrolled one
+//               (instruction-fetch stalls), and the paired f32x2 FMA / add and
+//               three-input max cut the instruction count per score.
 // Keys past the sequence end (the next sequence's rows, or TMA zero fill past
 // the buffer) are masked; query rows past it are computed and not stored.
 // Every wait is bounded: a timeout sets LF_STATUS_TIMEOUT and the roles unwind.
@@ -34,10 +43,16 @@ namespace {
 constexpr int kRows = 128;                   // query / key tile rows
 constexpr int kHd = 64;                      // head dim: one 128-byte swizzle atom
 constexpr int kTileBytes = kRows * kHd * 2;  // 16 KB
-constexpr int kKvStages = 3;
-constexpr int kSoftmaxWarps = 8;
+constexpr int kKStages = 3;
+constexpr int kVStages = 4;
+constexpr int kGroups = 2;
+constexpr int kSBufs = 3;                    // TMEM S buffers shared by the groups
+constexpr int kOCol = kSBufs * kRows;        // group g's O at TMEM column kOCol + 64 g
+constexpr int kSoftmaxWarps = 4 * kGroups;
 constexpr int kThreads = 64 + 32 * kSoftmaxWarps;
-constexpr int kSmemBytes = 1024 + 2 * kTileBytes + kKvStages * 2 * kTileBytes + 2 * 2 * kTileBytes + 1024 + 3072;
+// Q per group, K and V rings, P per group, barriers
+constexpr int kSmemBytes =
+    1024 + kGroups * kTileBytes + (kKStages + kVStages) * kTileBytes + kGroups * 2 * kTileBytes + 1024;
 constexpr float kMaxSlack = 8.f;             // log2 units the running max may lag a tile's max
 
 __device__ __forceinline__ bool aborted(const int32_t* flag) {
@@ -52,6 +67,42 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// max(a, b, c) in one instruction.
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Two lanes of a * b + c (each rounded once, as fmaf) in one paired instruction.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 pa, pb, pc, pd;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+      "mov.b64 pc, {%6, %7};\n\tfma.rn.f32x2 pd, pa, pb, pc;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+// Two lanes of a + b in one paired instruction.
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 pa, pb, pd;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+      "add.rn.f32x2 pd, pa, pb;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// A group's walk over its units and their key tiles.
+struct Cursor {
+  int64_t unit;  // global unit index, or >= n_units when done
+  int4 it;       // {row_start, len, q_tile, 0}
+  int j, n_kv;   // key tile within the unit
+  int u;         // units this group has started (for buffer parities)
+  int t;         // tiles this group has started
+};
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -60,37 +111,43 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
   uint8_t* gbase = smem_raw + (base - raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-  const uint32_t sQ = base;                                   // 2 x 16 KB
-  const uint32_t sKV = sQ + 2 * kTileBytes;                   // stages x (K 16 KB | V 16 KB)
-  const uint32_t sP = sKV + kKvStages * 2 * kTileBytes;       // 2 x 32 KB (two 64-key SW128 blocks)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + (sP + 4 * kTileBytes - base));
+  const uint32_t sQ = base;                              // kGroups x 16 KB
+  const uint32_t sK = sQ + kGroups * kTileBytes;         // kKStages x 16 KB
+  const uint32_t sV = sK + kKStages * kTileBytes;        // kVStages x 16 KB
+  const uint32_t sP = sV + kVStages * kTileBytes;        // kGroups x 32 KB (two 64-key SW128 blocks)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + (sP + kGroups * 2 * kTileBytes - base));
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  const int Q_FULL = 0, Q_EMPTY = 2, KV_FULL = 4, KV_EMPTY = 4 + kKvStages, S_FULL = 4 + 2 * kKvStages,
-            S_EMPTY = S_FULL + 2, P_FULL = S_EMPTY + 2, P_EMPTY = P_FULL + 2, O_FULL = P_EMPTY + 2,
-            O_EMPTY = O_FULL + 2, DRAIN = O_EMPTY + 2, N_BARS = DRAIN + 1;
+  // per-group barriers at index (kind * kGroups + group)
+  const int Q_FULL = 0, Q_EMPTY = 1, P_FULL = 2, P_EMPTY = 3, O_FULL = 4, O_EMPTY = 5;
+  auto gbar = [&](int kind, int grp) { return bar(kind * kGroups + grp); };
+  const int S_FULL = 6 * kGroups, S_EMPTY = S_FULL + kSBufs, K_FULL = S_EMPTY + kSBufs,
+            K_EMPTY = K_FULL + kKStages, V_FULL = K_EMPTY + kKStages, V_EMPTY = V_FULL + kVStages,
+            DRAIN = V_EMPTY + kVStages, N_BARS = DRAIN + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(&bars[N_BARS]);
   int32_t* s_abort = reinterpret_cast<int32_t*>(tmem_slot + 1);
-  float* s_max = reinterpret_cast<float*>(gbase + (sP + 4 * kTileBytes + 1024 - base));  // [2][2][128]
-  float* s_lsum = s_max + 512;                                                          // [2][128]
 
   const int64_t n_units = int64_t(p.n_items) * p.n_heads;
 
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(bar(Q_FULL + i), 1);
-      mbar_init(bar(Q_EMPTY + i), 1);
+    for (int grp = 0; grp < kGroups; ++grp) {
+      mbar_init(gbar(Q_FULL, grp), 1);
+      mbar_init(gbar(Q_EMPTY, grp), 1);
+      mbar_init(gbar(P_FULL, grp), 4);
+      mbar_init(gbar(P_EMPTY, grp), 1);
+      mbar_init(gbar(O_FULL, grp), 1);
+      mbar_init(gbar(O_EMPTY, grp), 4);
+    }
+    for (int i = 0; i < kSBufs; ++i) {
       mbar_init(bar(S_FULL + i), 1);
-      mbar_init(bar(S_EMPTY + i), kSoftmaxWarps);
-      mbar_init(bar(P_FULL + i), kSoftmaxWarps);
-      mbar_init(bar(P_EMPTY + i), 1);
+      mbar_init(bar(S_EMPTY + i), 4);
     }
-    for (int i = 0; i < kKvStages; ++i) {
-      mbar_init(bar(KV_FULL + i), 1);
-      mbar_init(bar(KV_EMPTY + i), 1);
+    for (int i = 0; i < kKStages; ++i) {
+      mbar_init(bar(K_FULL + i), 1);
+      mbar_init(bar(K_EMPTY + i), 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(bar(O_FULL + i), 1);
-      mbar_init(bar(O_EMPTY + i), kSoftmaxWarps);
+    for (int i = 0; i < kVStages; ++i) {
+      mbar_init(bar(V_FULL + i), 1);
+      mbar_init(bar(V_EMPTY + i), 1);
     }
     mbar_init(bar(DRAIN), 1);
     *s_abort = 0;
@@ -98,7 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
   }
   if (warp == 1) {
     __syncwarp();
-    tmem_alloc(smem_u32(tmem_slot), 512);  // S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384)
+    tmem_alloc(smem_u32(tmem_slot), 512);  // S buffers at 0, 128, 256; group g's O at 384 + 64 g
   }
   __syncthreads();
   tc_fence_after();
@@ -110,290 +167,315 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
   };
   // {row_start, len, q_tile, 0}; a zero length is read as 1 so that every role
   // walks the same tiles (nothing of such an item is stored)
-  auto unit_item = [&](int64_t unit) {
-    if (unit >= n_units) return make_int4(0, 1, 0, 0);
+  auto item_of = [&](int64_t unit) {
     int4 it = __ldg(p.items + unit / p.n_heads);
     it.y = max(it.y, 1);
     return it;
   };
+  // group grp takes the CTA's units 2k + grp
+  auto start = [&](Cursor& c, int grp) {
+    c.unit = blockIdx.x + int64_t(grp) * gridDim.x;
+    c.u = 0;
+    c.t = 0;
+    c.j = 0;
+    if (c.unit < n_units) {
+      c.it = item_of(c.unit);
+      c.n_kv = (c.it.y + kRows - 1) / kRows;
+    }
+  };
+  auto advance = [&](Cursor& c) {
+    ++c.t;
+    if (++c.j < c.n_kv) return;
+    c.unit += int64_t(kGroups) * gridDim.x;
+    ++c.u;
+    c.j = 0;
+    if (c.unit < n_units) {
+      c.it = item_of(c.unit);
+      c.n_kv = (c.it.y + kRows - 1) / kRows;
+    }
+  };
+  auto live = [&](const Cursor& c) { return c.unit < n_units; };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      int u = 0, g = 0, nq = 0;
+      Cursor c[kGroups];
+      for (int grp = 0; grp < kGroups; ++grp) start(c[grp], grp);
+      int kc = 0, nq[kGroups] = {0, 0};
       bool stop = false;
-      int4 nxt = unit_item(blockIdx.x);
-      for (int64_t unit = blockIdx.x; unit < n_units && !stop; unit += gridDim.x, ++u) {
-        const int4 it = nxt;
-        nxt = unit_item(unit + gridDim.x);  // the next unit's item loads while this one issues
-        const int h = int(unit % p.n_heads);
-        const int n_kv = (it.y + kRows - 1) / kRows;
-        const int qb = u & 1;
-        if (aborted(s_abort) || !mbar_wait(bar(Q_EMPTY + qb), ((u >> 1) & 1) ^ 1)) {
-          if (!aborted(s_abort)) fail();
-          stop = true;
-          break;
-        }
-        mbar_arrive_expect_tx(bar(Q_FULL + qb), kTileBytes);
-        tma_load_2d(sQ + qb * kTileBytes, &p.qkv_map, bar(Q_FULL + qb), p.q_col + h * kHd,
-                    it.x + it.z * kRows);
-        ++nq;
-        for (int j = 0; j < n_kv; ++j, ++g) {
-          const int s = g % kKvStages;
-          if (aborted(s_abort) || !mbar_wait(bar(KV_EMPTY + s), ((g / kKvStages) & 1) ^ 1)) {
+      while (!stop && (live(c[0]) || live(c[1]))) {
+        for (int grp = 0; grp < kGroups && !stop; ++grp) {
+          Cursor& cg = c[grp];
+          if (!live(cg)) continue;
+          const int h = int(cg.unit % p.n_heads);
+          if (cg.j == 0) {  // the unit's Q tile, once the group's previous unit has no S left to issue
+            if (aborted(s_abort) || !mbar_wait(gbar(Q_EMPTY, grp), (cg.u & 1) ^ 1)) {
+              if (!aborted(s_abort)) fail();
+              stop = true;
+              break;
+            }
+            mbar_arrive_expect_tx(gbar(Q_FULL, grp), kTileBytes);
+            tma_load_2d(sQ + grp * kTileBytes, &p.qkv_map, gbar(Q_FULL, grp), p.q_col + h * kHd,
+                        cg.it.x + cg.it.z * kRows);
+            ++nq[grp];
+          }
+          const int sk = kc % kKStages, sv = kc % kVStages;
+          if (aborted(s_abort) || !mbar_wait(bar(K_EMPTY + sk), ((kc / kKStages) & 1) ^ 1) ||
+              !mbar_wait(bar(V_EMPTY + sv), ((kc / kVStages) & 1) ^ 1)) {
             if (!aborted(s_abort)) fail();
             stop = true;
             break;
           }
-          const uint32_t sk = sKV + s * 2 * kTileBytes;
-          mbar_arrive_expect_tx(bar(KV_FULL + s), 2 * kTileBytes);
-          tma_load_2d(sk, &p.qkv_map, bar(KV_FULL + s), p.k_col + h * kHd, it.x + j * kRows);
-          tma_load_2d(sk + kTileBytes, &p.qkv_map, bar(KV_FULL + s), p.v_col + h * kHd, it.x + j * kRows);
+          const int32_t krow = cg.it.x + cg.j * kRows;
+          mbar_arrive_expect_tx(bar(K_FULL + sk), kTileBytes);
+          tma_load_2d(sK + sk * kTileBytes, &p.qkv_map, bar(K_FULL + sk), p.k_col + h * kHd, krow);
+          mbar_arrive_expect_tx(bar(V_FULL + sv), kTileBytes);
+          tma_load_2d(sV + sv * kTileBytes, &p.qkv_map, bar(V_FULL + sv), p.v_col + h * kHd, krow);
+          ++kc;
+          advance(cg);
         }
       }
       if (aborted(s_abort)) {  // loads nobody consumed must land before the CTA exits (bounded)
-        for (int q = (g > kKvStages ? g - kKvStages : 0); q < g; ++q)
-          mbar_wait(bar(KV_FULL + q % kKvStages), (q / kKvStages) & 1);
-        for (int q = (nq > 2 ? nq - 2 : 0); q < nq; ++q) mbar_wait(bar(Q_FULL + (q & 1)), (q >> 1) & 1);
+        for (int q = (kc > kKStages ? kc - kKStages : 0); q < kc; ++q)
+          mbar_wait(bar(K_FULL + q % kKStages), (q / kKStages) & 1);
+        for (int q = (kc > kVStages ? kc - kVStages : 0); q < kc; ++q)
+          mbar_wait(bar(V_FULL + q % kVStages), (q / kVStages) & 1);
+        for (int grp = 0; grp < kGroups; ++grp)  // only a group's latest Q can be unconsumed
+          if (nq[grp] > 0) mbar_wait(gbar(Q_FULL, grp), (nq[grp] - 1) & 1);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    // One flat sequence over the CTA's tiles: S of a tile is issued before the
-    // previous tile's O += P V, across unit boundaries too, so the next unit's
-    // first scores are ready when the softmax warps finish the last tile.
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_f16(DT<T>::umma_fmt, kRows, kRows, /*a_mn=*/0, /*b_mn=*/0);
       constexpr uint32_t idesc_o = umma_idesc_f16(DT<T>::umma_fmt, kRows, kHd, /*a_mn=*/0, /*b_mn=*/1);
-      int u = 0, g = 0;
+      struct Prev { bool valid, first, last; int t, u, kv; };
+      Cursor c[kGroups];
+      Prev prev[kGroups];
+      for (int grp = 0; grp < kGroups; ++grp) {
+        start(c[grp], grp);
+        prev[grp].valid = false;
+      }
+      int kc = 0;
       bool stop = false;
-      // O_uu += P_gp V_gp; the first of a unit overwrites O buffer uu&1 once unit
-      // uu-2's O was read from it; the last of a unit publishes O
-      auto pv = [&](int gp, bool first, bool last, int uu) -> bool {
-        const int bp = gp & 1, sp = gp % kKvStages;
-        if (!mbar_wait(bar(P_FULL + bp), (gp >> 1) & 1)) return false;
-        if (first && !mbar_wait(bar(O_EMPTY + (uu & 1)), ((uu >> 1) & 1) ^ 1)) return false;
+      // O_grp += P V for the group's previous tile
+      auto pv = [&](int grp, const Prev& e) -> bool {
+        const int sv = e.kv % kVStages;
+        if (!mbar_wait(gbar(P_FULL, grp), e.t & 1)) return false;
+        if (!mbar_wait(bar(V_FULL + sv), (e.kv / kVStages) & 1)) return false;
+        if (e.first && !mbar_wait(gbar(O_EMPTY, grp), (e.u & 1) ^ 1)) return false;
         tc_fence_after();
-        const uint32_t pb = sP + bp * 2 * kTileBytes;
-        const uint32_t vb = sKV + sp * 2 * kTileBytes + kTileBytes;
+        const uint32_t pb = sP + grp * 2 * kTileBytes;
+        const uint32_t vb = sV + sv * kTileBytes;
 #pragma unroll
         for (int t = 0; t < kRows / 16; ++t) {
           const uint64_t ad = smem_desc(pb + (t >> 2) * kTileBytes + (t & 3) * 32, 16, 1024, 2);
           const uint64_t bd = smem_desc(vb + t * 2048, kTileBytes, 1024, 2);
-          umma_f16(tmem + 256 + (uu & 1) * kHd, ad, bd, idesc_o, (first && t == 0) ? 0u : 1u);
+          umma_f16(tmem + kOCol + kHd * grp, ad, bd, idesc_o, (e.first && t == 0) ? 0u : 1u);
         }
-        umma_commit(bar(P_EMPTY + bp));
-        umma_commit(bar(KV_EMPTY + sp));
-        if (last) umma_commit(bar(O_FULL + (uu & 1)));
+        umma_commit(gbar(P_EMPTY, grp));
+        umma_commit(bar(V_EMPTY + sv));
+        if (e.last) umma_commit(gbar(O_FULL, grp));
         return true;
       };
-      bool have_prev = false, prev_first = false, prev_last = false;
-      int prev_g = 0, prev_u = 0;
-      int4 nxt = unit_item(blockIdx.x);
-      for (int64_t unit = blockIdx.x; unit < n_units && !stop; unit += gridDim.x, ++u) {
-        const int4 it = nxt;
-        nxt = unit_item(unit + gridDim.x);
-        const int n_kv = (it.y + kRows - 1) / kRows;
-        const int qb = u & 1;
-        if (aborted(s_abort) || !mbar_wait(bar(Q_FULL + qb), (u >> 1) & 1)) {
-          if (!aborted(s_abort)) fail();
-          stop = true;
-          break;
-        }
-        for (int j = 0; j < n_kv; ++j, ++g) {
-          const int s = g % kKvStages, b = g & 1;
-          if (aborted(s_abort) || !mbar_wait(bar(KV_FULL + s), (g / kKvStages) & 1) ||
-              !mbar_wait(bar(S_EMPTY + b), ((g >> 1) & 1) ^ 1)) {
-            if (!aborted(s_abort)) fail();
-            stop = true;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t qa = sQ + qb * kTileBytes, kb = sKV + s * 2 * kTileBytes;
+      // S for tile kc goes to buffer kc % kSBufs once that buffer's previous
+      // tile (kc - kSBufs, of either group) has been read
+      while (!stop && (live(c[0]) || live(c[1]) || prev[0].valid || prev[1].valid)) {
+        for (int grp = 0; grp < kGroups && !stop; ++grp) {
+          Cursor& cg = c[grp];
+          Prev cur{false, false, false, 0, 0, 0};
+          if (live(cg)) {
+            const int sk = kc % kKStages, sb = kc % kSBufs;
+            if (aborted(s_abort) || (cg.j == 0 && !mbar_wait(gbar(Q_FULL, grp), cg.u & 1)) ||
+                !mbar_wait(bar(K_FULL + sk), (kc / kKStages) & 1) ||
+                !mbar_wait(bar(S_EMPTY + sb), ((kc / kSBufs) & 1) ^ 1)) {
+              if (!aborted(s_abort)) fail();
+              stop = true;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t qa = sQ + grp * kTileBytes, kb = sK + sk * kTileBytes;
 #pragma unroll
-          for (int t = 0; t < kHd / 16; ++t)
-            umma_f16(tmem + b * kRows, smem_desc(qa + t * 32, 16, 1024, 2), smem_desc(kb + t * 32, 16, 1024, 2),
-                     idesc_s, t > 0 ? 1u : 0u);
-          umma_commit(bar(S_FULL + b));
-          if (j == n_kv - 1) umma_commit(bar(Q_EMPTY + qb));
-          if (have_prev && !pv(prev_g, prev_first, prev_last, prev_u)) {
+            for (int t = 0; t < kHd / 16; ++t)
+              umma_f16(tmem + kRows * sb, smem_desc(qa + t * 32, 16, 1024, 2), smem_desc(kb + t * 32, 16, 1024, 2),
+                       idesc_s, t > 0 ? 1u : 0u);
+            umma_commit(bar(S_FULL + sb));
+            umma_commit(bar(K_EMPTY + sk));
+            if (cg.j == cg.n_kv - 1) umma_commit(gbar(Q_EMPTY, grp));
+            cur = Prev{true, cg.j == 0, cg.j == cg.n_kv - 1, cg.t, cg.u, kc};
+            ++kc;
+            advance(cg);
+          }
+          if (prev[grp].valid && !pv(grp, prev[grp])) {
             fail();
             stop = true;
             break;
           }
-          have_prev = true;
-          prev_g = g;
-          prev_first = j == 0;
-          prev_last = j == n_kv - 1;
-          prev_u = u;
+          prev[grp] = cur;
         }
       }
-      if (!stop && have_prev && !pv(prev_g, prev_first, prev_last, prev_u)) fail();
       if (aborted(s_abort)) {  // every issued MMA must finish before TMEM is released (bounded)
         umma_commit(bar(DRAIN));
         mbar_wait(bar(DRAIN), 0);
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax + output (warps 2..9)
-    // Both warps of a quadrant take every tile and every pair barrier, whatever
-    // happens, so that neither can be left waiting at bar.sync.
+    // ------------------------------------------------------------ softmax groups (warps 2..9)
+    const int grp = (warp - 2) >> 2;
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;  // key columns [64 half, +64) of S, O columns [32 half, +32)
     const int row = quad * 32 + lane;
-    const uint32_t pair_bar = 1 + quad;  // named barrier of this quadrant's two warps
-    const uint32_t lane_addr = uint32_t(quad * 32) << 16;
+    const uint32_t lane_addr = tmem + (uint32_t(quad * 32) << 16);
+    const uint32_t o_addr = lane_addr + kOCol + kHd * grp;  // this row of the group's O
     const uint32_t prow = (row >> 3) * 1024 + (row & 7) * 128;  // this row in a SW128 block
-    // O / l of a finished unit: the pair adds its two shares of the row sum,
-    // normalises and stores this half's 32 columns, and frees O buffer uu&1
-    auto epilogue = [&](const int4& eit, int eh, int uu, float el) {
-      s_lsum[half * 128 + row] = el;
-      named_barrier_sync(pair_bar, 64);
-      const float l_row = el + s_lsum[(half ^ 1) * 128 + row];
+    const uint32_t pb = sP + grp * 2 * kTileBytes - base;
+    const float2 sl2 = make_float2(p.scale_log2, p.scale_log2);
+    // The MMA warp issues the groups' S tiles round-robin (group 0 first), so
+    // this group's n-th tile is global tile n + min(n + grp, tiles of the other group).
+    int other_tiles = 0;
+    {
+      Cursor o;
+      start(o, grp ^ 1);
+      while (live(o)) {
+        other_tiles += o.n_kv;
+        o.t += o.n_kv - 1;
+        o.j = o.n_kv - 1;
+        advance(o);
+      }
+    }
+    Cursor c;
+    start(c, grp);
+    float m = -INFINITY, l = 0.f;
+    while (live(c)) {
+      const int t = c.t, j = c.j;
+      const int kc = t + min(t + grp, other_tiles);
+      const int sb = kc % kSBufs;
+      const uint32_t s_addr = lane_addr + kRows * sb;
+      const int4 it = c.it;
+      const int64_t unit = c.unit;
+      const int uu = c.u;
+      const bool last = j == c.n_kv - 1;
+      const int nvalid = min(kRows, it.y - j * kRows);
       bool ok = !aborted(s_abort);
-      if (ok && !mbar_wait(bar(O_FULL + (uu & 1)), (uu >> 1) & 1)) {
+      if (ok && !mbar_wait(bar(S_FULL + sb), (kc / kSBufs) & 1)) {
         fail();
         ok = false;
       }
-      if (__all_sync(0xffffffffu, ok)) {
-        tc_fence_after();
-        uint32_t ov[32];
-        tmem_ld32(tmem + lane_addr + 256 + (uu & 1) * kHd + half * 32, ov);
-        const int qr = eit.z * kRows + row;
-        if (qr < eit.y) {
-          const float inv = 1.f / l_row;
-          T* dst = reinterpret_cast<T*>(p.out) + int64_t(eit.x + qr) * p.ldo + eh * kHd + half * 32;
+      const bool work = __all_sync(0xffffffffu, ok);
+      tc_fence_after();
+      // pass 1: the row max over the valid keys, 64 columns at a time
+      float mx = -INFINITY;
+      if (work) {
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t sv[64];
+          tmem_ld64(s_addr + hh * 64, sv);
+          if (nvalid < hh * 64 + 64) {  // warp-uniform: keys past the end do not count
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint4 w;
-            w.x = Pack2<T>::pack(__uint_as_float(ov[8 * c + 0]) * inv, __uint_as_float(ov[8 * c + 1]) * inv);
-            w.y = Pack2<T>::pack(__uint_as_float(ov[8 * c + 2]) * inv, __uint_as_float(ov[8 * c + 3]) * inv);
-            w.z = Pack2<T>::pack(__uint_as_float(ov[8 * c + 4]) * inv, __uint_as_float(ov[8 * c + 5]) * inv);
-            w.w = Pack2<T>::pack(__uint_as_float(ov[8 * c + 6]) * inv, __uint_as_float(ov[8 * c + 7]) * inv);
-            reinterpret_cast<uint4*>(dst)[c] = w;
+            for (int q = 0; q < 64; ++q)
+              if (hh * 64 + q >= nvalid) sv[q] = __float_as_uint(-INFINITY);
           }
+          float mxs[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+          for (int q = 0; q < 64; q += 8) {
+            mxs[(q >> 3) & 3] = max3(mxs[(q >> 3) & 3], __uint_as_float(sv[q]), __uint_as_float(sv[q + 1]));
+            mxs[(q >> 3) & 3] = max3(mxs[(q >> 3) & 3], __uint_as_float(sv[q + 2]), __uint_as_float(sv[q + 3]));
+            mxs[((q >> 3) + 2) & 3] =
+                max3(mxs[((q >> 3) + 2) & 3], __uint_as_float(sv[q + 4]), __uint_as_float(sv[q + 5]));
+            mxs[((q >> 3) + 2) & 3] =
+                max3(mxs[((q >> 3) + 2) & 3], __uint_as_float(sv[q + 6]), __uint_as_float(sv[q + 7]));
+          }
+          mx = max3(mx, fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3]));
         }
+        mx *= sl2.x;  // the scale is positive: max commutes with it
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(O_EMPTY + (uu & 1)));
-    };
-    bool have_pending = false;
-    int4 pend_it = make_int4(0, 1, 0, 0);
-    int pend_h = 0, pend_u = 0;
-    float pend_l = 0.f;
-    int u = 0, g = 0;
-    int4 nxt = unit_item(blockIdx.x);
-    for (int64_t unit = blockIdx.x; unit < n_units; unit += gridDim.x, ++u) {
-      const int4 it = nxt;
-      nxt = unit_item(unit + gridDim.x);
-      const int h = int(unit % p.n_heads);
-      const int n_kv = (it.y + kRows - 1) / kRows;
-      float m = -INFINITY, l = 0.f;         // l: this half's share of the row sum
-      for (int j = 0; j < n_kv; ++j, ++g) {
-        const int b = g & 1;
-        bool ok = !aborted(s_abort);
-        if (ok && !mbar_wait(bar(S_FULL + b), (g >> 1) & 1)) {
-          fail();
-          ok = false;
-        }
-        const bool work = __all_sync(0xffffffffu, ok);
+      const float m_new = (j == 0 || mx > m + kMaxSlack) ? mx : m;
+      const float alpha = (j == 0) ? 1.f : ex2(m - m_new);
+      // the previous tile's O += P V has finished: P may be overwritten, O rescaled
+      ok = work && !aborted(s_abort);
+      if (ok && !mbar_wait(gbar(P_EMPTY, grp), (t & 1) ^ 1)) {
+        fail();
+        ok = false;
+      }
+      const bool go = __all_sync(0xffffffffu, ok);
+      if (go && j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
         tc_fence_after();
-        const int nvalid = min(kRows, it.y - j * kRows) - half * 64;  // valid keys in this half
-        uint32_t sv[64];
-        float mx = -INFINITY;
-        if (work) {
-          tmem_ld64(tmem + lane_addr + b * kRows + half * 64, sv);
-          float mxs[8];  // eight independent chains instead of one 64-long one
+        uint32_t ov[64];
+        tmem_ld64(o_addr, ov);
 #pragma unroll
-          for (int q = 0; q < 8; ++q) mxs[q] = -INFINITY;
-          if (nvalid >= 64) {  // warp-uniform: a full half tile needs no mask
+        for (int q = 0; q < 64; ++q) ov[q] = __float_as_uint(__uint_as_float(ov[q]) * alpha);
+        tmem_st64(o_addr, ov);
+      }
+      // pass 2: p = 2^(s - max), rounded to T into the group's SW128 K-major P tile
+      float2 sums[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      if (go) {
+        const float2 neg_m = make_float2(-m_new, -m_new);
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t sv[64];
+          tmem_ld64(s_addr + hh * 64, sv);
+          if (nvalid < hh * 64 + 64) {  // warp-uniform: keys past the end score -inf, so p = 0
 #pragma unroll
-            for (int c = 0; c < 64; ++c) mxs[c & 7] = fmaxf(mxs[c & 7], __uint_as_float(sv[c]));
-          } else {
-#pragma unroll
-            for (int c = 0; c < 64; ++c)
-              if (c < nvalid) mxs[c & 7] = fmaxf(mxs[c & 7], __uint_as_float(sv[c]));
+            for (int q = 0; q < 64; ++q)
+              if (hh * 64 + q >= nvalid) sv[q] = __float_as_uint(-INFINITY);
           }
-          const float raw_max = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
-                                      fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
-          mx = raw_max * p.scale_log2;  // the scale is positive: max commutes with it
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(S_EMPTY + b));  // this half of S_j is in registers
-        // the row max over both halves
-        float* smx = s_max + (g & 1) * 256;
-        smx[half * 128 + row] = mx;
-        named_barrier_sync(pair_bar, 64);
-        mx = fmaxf(mx, smx[(half ^ 1) * 128 + row]);
-        const float m_new = (j == 0 || mx > m + kMaxSlack) ? mx : m;
-        const float alpha = (j == 0) ? 1.f : ex2(m - m_new);
-        // P_j goes into buffer b once the MMA that read it two tiles ago has finished
-        ok = work && !aborted(s_abort);
-        if (ok && !mbar_wait(bar(P_EMPTY + b), ((g >> 1) & 1) ^ 1)) {
-          fail();
-          ok = false;
-        }
-        float sums[4] = {0.f, 0.f, 0.f, 0.f};  // independent chains
-        if (__all_sync(0xffffffffu, ok)) {
-          const uint32_t pb = sP + b * 2 * kTileBytes + half * kTileBytes - base;
-          const float sl2 = p.scale_log2, neg_m = -m_new;
-          const bool full = nvalid >= 64;  // warp-uniform
 #pragma unroll
           for (int c8 = 0; c8 < 8; ++c8) {  // 16-byte chunks = 8 keys
             uint32_t w[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              const int c = c8 * 8 + 2 * i;
-              float p0 = ex2(fmaf(__uint_as_float(sv[c]), sl2, neg_m));
-              float p1 = ex2(fmaf(__uint_as_float(sv[c + 1]), sl2, neg_m));
-              if (!full) {
-                p0 = c < nvalid ? p0 : 0.f;
-                p1 = c + 1 < nvalid ? p1 : 0.f;
-              }
-              sums[i] += p0 + p1;
-              w[i] = Pack2<T>::pack(p0, p1);
+              const int col = c8 * 8 + 2 * i;
+              const float2 x = fma2(make_float2(__uint_as_float(sv[col]), __uint_as_float(sv[col + 1])), sl2, neg_m);
+              const float2 pr = make_float2(ex2(x.x), ex2(x.y));
+              sums[i & 1] = add2(sums[i & 1], pr);
+              w[i] = Pack2<T>::pack(pr.x, pr.y);
             }
-            *reinterpret_cast<uint4*>(gbase + pb + prow + ((c8 ^ (row & 7)) << 4)) =
+            *reinterpret_cast<uint4*>(gbase + pb + hh * kTileBytes + prow + ((c8 ^ (row & 7)) << 4)) =
                 make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
-        l = l * alpha + ((sums[0] + sums[1]) + (sums[2] + sums[3]));
-        m = m_new;
-        // the max moved: rescale this half's O columns once the previous O += P V has finished
-        if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
-          bool ok2 = !aborted(s_abort);
-          if (ok2 && !mbar_wait(bar(P_EMPTY + ((g - 1) & 1)), ((g - 1) >> 1) & 1)) {
-            fail();
-            ok2 = false;
-          }
-          if (__all_sync(0xffffffffu, ok2)) {
-            tc_fence_after();
-            uint32_t ov[32];
-            tmem_ld32(tmem + lane_addr + 256 + (u & 1) * kHd + half * 32, ov);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(S_EMPTY + sb));  // S has been read: the buffer may take the next S
+      const float sum = (sums[0].x + sums[0].y) + (sums[1].x + sums[1].y);
+      l = (j == 0) ? sum : l * alpha + sum;
+      m = m_new;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(gbar(P_FULL, grp));
+      advance(c);
+      if (last) {
+        // the unit's output: O / l, once its last O += P V has finished
+        ok = !aborted(s_abort);
+        if (ok && !mbar_wait(gbar(O_FULL, grp), uu & 1)) {
+          fail();
+          ok = false;
+        }
+        if (__all_sync(0xffffffffu, ok)) {
+          tc_fence_after();
+          uint32_t ov[64];
+          tmem_ld64(o_addr, ov);
+          const int qr = it.z * kRows + row;
+          if (qr < it.y) {
+            const float inv = 1.f / l;
+            T* dst = reinterpret_cast<T*>(p.out) + int64_t(it.x + qr) * p.ldo + int(unit % p.n_heads) * kHd;
 #pragma unroll
-            for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
-            tmem_st32(tmem + lane_addr + 256 + (u & 1) * kHd + half * 32, ov);
+            for (int q = 0; q < 8; ++q) {
+              uint4 w;
+              w.x = Pack2<T>::pack(__uint_as_float(ov[8 * q + 0]) * inv, __uint_as_float(ov[8 * q + 1]) * inv);
+              w.y = Pack2<T>::pack(__uint_as_float(ov[8 * q + 2]) * inv, __uint_as_float(ov[8 * q + 3]) * inv);
+              w.z = Pack2<T>::pack(__uint_as_float(ov[8 * q + 4]) * inv, __uint_as_float(ov[8 * q + 5]) * inv);
+              w.w = Pack2<T>::pack(__uint_as_float(ov[8 * q + 6]) * inv, __uint_as_float(ov[8 * q + 7]) * inv);
+              reinterpret_cast<uint4*>(dst)[q] = w;
+            }
           }
         }
-        fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(P_FULL + b));
-        // the previous unit's output, now that its last O += P V has long finished
-        if (j == 0 && have_pending) {
-          epilogue(pend_it, pend_h, pend_u, pend_l);
-          have_pending = false;
-        }
+        if (lane == 0) mbar_arrive(gbar(O_EMPTY, grp));
       }
-      pend_it = it;
-      pend_h = h;
-      pend_u = u;
-      pend_l = l;
-      have_pending = true;
     }
-    if (have_pending) epilogue(pend_it, pend_h, pend_u, pend_l);
   }
 
   __syncthreads();
