@@ -209,6 +209,34 @@ int lf_lora_apply_noalloc(void* stream, int dtype,
                           int n_segs, const int32_t* tiles, int n_tiles, int n_multi,
                           int32_t* status);
 
+/* The delta written into a fresh output for a GEMM to accumulate onto:
+ *     y[t, off_m + n] = round(round(r[t, off_m + n] + bias[off_m + n]) + delta)
+ * for every token of every tile the records name (r and bias may each be NULL,
+ * read as 0; rows of a record's tile in no segment get round(r + bias)).  A
+ * caller then adds the projection with a beta = 1 GEMM (y += x W^T), so the
+ * projection output is written once and never re-read for the delta, and a
+ * residual r that a LayerNorm would add is already in y.  Same shrink, factor
+ * layout and segment rules as lf_lora_apply; it needs tile records whose tiles
+ * cover every token (segments covering [0, n_tokens)), bf16 or f16, rank 8, 16,
+ * 32 or 64, hidden a multiple of 128, and 16-byte aligned buffers and strides
+ * (LF_ERR_UNSUPPORTED otherwise); r must not alias y.  It fuses, per layer, the
+ * reference's projection bias, `output + owner.lora_ops.output`
+ * (src/latefuse/model/hf_wrapper.py:217; src/latefuse/model/encoder.py:80) and,
+ * with r, the residual add before LayerNorm (src/latefuse/model/encoder.py:137). */
+int lf_lora_apply_into(void* stream, int dtype,
+                       const void* x, int64_t ldx,
+                       const void* r, int64_t ldr,
+                       const void* bias,
+                       void* y, int64_t ldy,
+                       int64_t n_tokens, int hidden, int rank,
+                       const void* cache_a, int64_t a_slot_stride, int64_t a_module_stride,
+                       const void* cache_b, int64_t b_slot_stride, int64_t b_module_stride,
+                       int n_slots, int n_modules, const int32_t* modules,
+                       const int64_t* y_col_offsets,
+                       const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot,
+                       int n_segs, const int32_t* tiles, int n_tiles, int n_multi,
+                       void* workspace, size_t workspace_bytes, int32_t* status);
+
 /* ------------------------------------------------------------------------ */
 /* Adapter cache                                                            */
 /* ------------------------------------------------------------------------ */

@@ -54,6 +54,11 @@ SIGNATURES: dict[str, tuple] = {
         c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int,
         POINTER(c_int32), POINTER(c_int64), c_void_p, c_void_p, c_void_p, c_int,
         c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "lf_lora_apply_into": (c_int, [
+        c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int,
+        c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int,
+        POINTER(c_int32), POINTER(c_int64), c_void_p, c_void_p, c_void_p, c_int,
+        c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "lf_lora_apply_noalloc": (c_int, [
         c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_int,
         c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int,

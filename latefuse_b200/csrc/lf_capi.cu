@@ -256,7 +256,8 @@ static int expand_impl(cudaStream_t stream, int dtype, const void* u, void* y, i
                        int64_t b_module_stride, int n_slots, int n_modules, const int32_t* modules,
                        const int64_t* y_col_offsets, const int32_t* seg_start, const int32_t* seg_len,
                        const int32_t* seg_slot, int n_segs, const int32_t* tiles, int n_tiles, int n_multi,
-                       int accumulate, bool after_shrink, int32_t* status) {
+                       int accumulate, bool after_shrink, int32_t* status, const void* into_r = nullptr,
+                       int64_t ldr = 0, const void* into_bias = nullptr, bool into = false) {
   const int es = elem_size(dtype);
   int64_t y_cols = 0;
   bool offs_aligned = true;
@@ -266,6 +267,23 @@ static int expand_impl(cudaStream_t stream, int dtype, const void* u, void* y, i
     if (y_col_offsets[m] % 8 != 0) offs_aligned = false;
   }
   if (ldy < y_cols) return set_error(LF_ERR_INVALID, "lf_lora_expand: ldy %lld < output columns %lld", (long long)ldy, (long long)y_cols);
+  if (into) {
+    // into mode runs on the persistent tcgen05 expand only
+    const bool ok = !option_force_simt() && g_persistent.load() && dtype != LF_DTYPE_F32 && tc_rank(rank) &&
+                    hidden % 128 == 0 && offs_aligned && tiles != nullptr && n_tiles > 0 && aligned16(y) &&
+                    aligned16(cache_b) && aligned16(u) && (ldy * es) % 16 == 0 &&
+                    (b_slot_stride * es) % 16 == 0 && (b_module_stride * es) % 16 == 0 &&
+                    (n_slots == 1 || b_slot_stride >= int64_t(hidden) * rank) &&
+                    (into_r == nullptr || (aligned16(into_r) && (ldr * es) % 16 == 0)) &&
+                    (into_bias == nullptr || aligned16(into_bias));
+    if (!ok)
+      return set_error(LF_ERR_UNSUPPORTED,
+                       "lf_lora_apply_into: needs bf16/f16, rank 8/16/32/64, hidden %% 128 == 0, tile records, "
+                       "16-byte aligned buffers and strides, and the persistent tcgen05 path");
+    if (into_r != nullptr && ldr < y_cols)
+      return set_error(LF_ERR_INVALID, "lf_lora_apply_into: ldr %lld < output columns %lld", (long long)ldr,
+                       (long long)y_cols);
+  }
   const bool tc = !option_force_simt() && dtype != LF_DTYPE_F32 && tc_rank(rank) && hidden % 64 == 0 &&
                   offs_aligned && aligned16(y) && aligned16(cache_b) && aligned16(u) && (ldy * es) % 16 == 0 &&
                   (hidden * es) % 16 == 0 && (b_slot_stride * es) % 16 == 0 && (b_module_stride * es) % 16 == 0 &&
@@ -338,6 +356,19 @@ static int expand_impl(cudaStream_t stream, int dtype, const void* u, void* y, i
     ExpandPersistParams q;
     memset(&q, 0, sizeof(q));
     q.y_map = p.y_map;
+    if (into) {
+      q.into = 1;
+      q.bias = into_bias;
+      if (into_r != nullptr) {
+        cuuint64_t dims[2] = {cuuint64_t(y_cols), cuuint64_t(n_tokens)};
+        cuuint64_t strides[1] = {cuuint64_t(ldr) * es};
+        cuuint32_t box[2] = {64, 128};
+        int rc = encode(&q.r_map, dtype, 2, const_cast<void*>(into_r), dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                        "r");
+        if (rc) return rc;
+        q.has_r = 1;
+      }
+    }
     for (int m = 0; m < n_modules; ++m) {
       q.b_map[m] = p.b_map[m];
       q.y_col_off[m] = p.y_col_off[m];
@@ -464,6 +495,38 @@ int lf_lora_apply(void* stream, int dtype, const void* x, int64_t ldx, void* y, 
   return expand_impl(s, dtype, workspace, y, ldy, n_tokens, hidden, rank, cache_b, b_slot_stride, b_module_stride,
                      n_slots, n_modules, modules, y_col_offsets, seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles,
                      n_multi, 1, true, status);
+}
+
+int lf_lora_apply_into(void* stream, int dtype, const void* x, int64_t ldx, const void* r, int64_t ldr,
+                       const void* bias, void* y, int64_t ldy, int64_t n_tokens, int hidden, int rank,
+                       const void* cache_a, int64_t a_slot_stride, int64_t a_module_stride, const void* cache_b,
+                       int64_t b_slot_stride, int64_t b_module_stride, int n_slots, int n_modules,
+                       const int32_t* modules, const int64_t* y_col_offsets, const int32_t* seg_start,
+                       const int32_t* seg_len, const int32_t* seg_slot, int n_segs, const int32_t* tiles,
+                       int n_tiles, int n_multi, void* workspace, size_t workspace_bytes, int32_t* status) {
+  int rc = check_common("lf_lora_apply_into", dtype, n_tokens, hidden, rank, n_slots, n_modules, modules, seg_start,
+                        seg_len, seg_slot, n_segs);
+  if (rc) return rc;
+  if ((rc = check_tiles("lf_lora_apply_into", tiles, n_tiles, n_multi, n_tokens))) return rc;
+  if (x == nullptr || y == nullptr || cache_a == nullptr || cache_b == nullptr || y_col_offsets == nullptr)
+    return set_error(LF_ERR_INVALID, "lf_lora_apply_into: NULL buffer");
+  if (ldx < hidden) return set_error(LF_ERR_INVALID, "lf_lora_apply_into: ldx < hidden");
+  if (r != nullptr && r == y) return set_error(LF_ERR_INVALID, "lf_lora_apply_into: r and y must not alias");
+  if (n_tokens == 0) return LF_OK;
+  if (tiles == nullptr || n_tiles == 0)
+    return set_error(LF_ERR_UNSUPPORTED, "lf_lora_apply_into: tile records are required");
+  const size_t need = lf_lora_workspace_bytes(dtype, n_tokens, rank, n_modules);
+  if (workspace == nullptr || workspace_bytes < need)
+    return set_error(LF_ERR_WORKSPACE, "lf_lora_apply_into: workspace of %zu bytes needed, %zu given", need,
+                     workspace_bytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  rc = shrink_impl(s, dtype, x, ldx, n_tokens, hidden, rank, cache_a, a_slot_stride, a_module_stride, n_slots,
+                   n_modules, modules, seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles, n_multi, workspace,
+                   status);
+  if (rc) return rc;
+  return expand_impl(s, dtype, workspace, y, ldy, n_tokens, hidden, rank, cache_b, b_slot_stride, b_module_stride,
+                     n_slots, n_modules, modules, y_col_offsets, seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles,
+                     n_multi, 1, true, status, r, ldr, bias, true);
 }
 
 }  // extern "C"

@@ -54,6 +54,7 @@ struct alignas(64) ExpandTcParams {
 // Persistent expand over single-segment tiles (see lf_lora_persist.cu).
 struct alignas(64) ExpandPersistParams {
   CUtensorMap y_map;                 // 2D {y_cols, n_tokens}, box {64, 128}, SW128
+  CUtensorMap r_map;                 // into mode with a residual: like y_map, over r
   CUtensorMap b_map[kMaxModules];    // 3D {hidden, rank, n_slots}, box {64, rank, 1}, SW128
   CUtensorMap u_map;                 // 2D {rank, n_modules * n_tokens}, box {rank, 128}, swizzle by rank
   int64_t n_tokens;
@@ -68,6 +69,11 @@ struct alignas(64) ExpandPersistParams {
   const int32_t* seg_slot;
   int32_t n_segs;
   int32_t* status;
+  // into mode: y = round(round(r + bias) + delta) written to every row of every
+  // record's tiles (r and bias each optional), instead of y += delta in place
+  int32_t into;
+  int32_t has_r;
+  const void* bias;                  // y_cols entries, or null
 };
 
 // Persistent shrink over the tile records (see lf_lora_persist.cu).

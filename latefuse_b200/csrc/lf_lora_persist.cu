@@ -241,9 +241,13 @@ lora_expand_persist_kernel(const __grid_constant__ ExpandPersistParams p) {
           const int32_t slot = sub_slot(cur, j, p.seg_slot, p.n_segs);
           if (j == 0) {
             s_meta[s] = make_int4(row0, col0, 0, 0);
-            mbar_arrive_expect_tx(bar(FULL + s), C::kStageBytes);
-            for (int b = 0; b < C::kNBox; ++b)
-              tma_load_2d(sy + b * kYBox, &p.y_map, bar(FULL + s), col0 + b * 64, row0);
+            if (!p.into || p.has_r) {  // the tile's y (in place) or r (into mode)
+              mbar_arrive_expect_tx(bar(FULL + s), C::kStageBytes);
+              const CUtensorMap* src = p.into ? &p.r_map : &p.y_map;
+              for (int b = 0; b < C::kNBox; ++b) tma_load_2d(sy + b * kYBox, src, bar(FULL + s), col0 + b * 64, row0);
+            } else {
+              mbar_arrive_expect_tx(bar(FULL + s), C::kBBytes + C::kUBytes);
+            }
           } else {
             mbar_arrive_expect_tx(bar(FULL + s), C::kBBytes + C::kUBytes);
           }
@@ -359,12 +363,35 @@ lora_expand_persist_kernel(const __grid_constant__ ExpandPersistParams p) {
           tmem_ld64(taddr + a * NT, acc);
           if (j == 0 || in_seg) {
             // sub-item 0 copies the y tile (its segment's rows with the delta);
-            // later sub-items add their segment's rows to the output tile
+            // later sub-items add their segment's rows to the output tile.  In
+            // into mode sub-item 0 starts from round(r + bias) instead of y.
             const uint32_t src = (j == 0 ? s_stage0 + s * C::kStageBytes : so) - base;
             uint4 yv[8];
+            if (j > 0 || !p.into || p.has_r) {
 #pragma unroll
-            for (int c = 0; c < 8; ++c)
-              yv[c] = *reinterpret_cast<const uint4*>(gbase + src + rbase + ((c ^ (row & 7)) << 4));
+              for (int c = 0; c < 8; ++c)
+                yv[c] = *reinterpret_cast<const uint4*>(gbase + src + rbase + ((c ^ (row & 7)) << 4));
+            } else {
+#pragma unroll
+              for (int c = 0; c < 8; ++c) yv[c] = make_uint4(0, 0, 0, 0);
+            }
+            if (j == 0 && p.into && p.bias != nullptr) {
+              const int rem = int(item % per_tile);
+              const int64_t col = p.y_col_off[rem / ncb] + (rem % ncb) * NT + half * 64;
+              const uint4* bv = reinterpret_cast<const uint4*>(static_cast<const T*>(p.bias) + col);
+#pragma unroll
+              for (int c = 0; c < 8; ++c) {
+                const uint4 braw = __ldg(bv + c);
+                const uint32_t bw[4] = {braw.x, braw.y, braw.z, braw.w};
+                uint32_t* w = reinterpret_cast<uint32_t*>(&yv[c]);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const float2 yf = Pack2<T>::unpack(w[i]);
+                  const float2 bf = Pack2<T>::unpack(bw[i]);
+                  w[i] = Pack2<T>::pack(yf.x + bf.x, yf.y + bf.y);
+                }
+              }
+            }
             if (in_seg) {
 #pragma unroll
               for (int c = 0; c < 8; ++c) {

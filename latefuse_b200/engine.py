@@ -31,7 +31,8 @@ from torch.utils.hooks import RemovableHandle
 from latefuse_b200.batch import BatchedLRWeights, BatchLora, LayerwiseBatchedWeights
 from latefuse_b200.config import LoraServingConfig
 from latefuse_b200.head import LRHeadOps, pool_tokens, validate_pooling
-from latefuse_b200.lora import FactorCache, SegmentTable, lora_apply, per_row_cache, workspace_bytes
+from latefuse_b200.lora import (FactorCache, SegmentTable, lora_apply, lora_apply_into, per_row_cache,
+                                 workspace_bytes)
 from latefuse_b200.encoder_ops import add_layernorm, attention_varlen, gelu
 from latefuse_b200.packing import PackedBatch, pack_rows
 
@@ -495,13 +496,23 @@ class EncoderWithLora(nn.Module):
         return h.view(B, S, H)
 
     def _ffn(self, layer: _Layer, ao: Tensor, h: Tensor) -> tuple[Tensor, Tensor]:
-        """``h1 = LN1(ao + h)``, ``LN2(W2 act(W1 h1) + h1)``, on the native add+LayerNorm
-        and GELU kernels."""
+        """``h1 = LN1(ao + h)`` (``LN1(ao)`` when ``h`` is None: the residual is already
+        in ``ao``), ``LN2(W2 act(W1 h1) + h1)``, on the native add+LayerNorm and GELU
+        kernels."""
         h1 = add_layernorm(ao, h, layer.ln1.weight, layer.ln1.bias, self.eps)
         mid = F.linear(h1, layer.wi, layer.bi)
         mid = gelu(mid, out=mid) if self._native_gelu else self.act(mid)
         o = F.linear(mid, layer.wo2, layer.bo2)
         return h1, add_layernorm(o, h1, layer.ln2.weight, layer.ln2.bias, self.eps, out=o)
+
+    def _fused_dense_ok(self, dtype: torch.dtype, rank: int) -> bool:
+        """Whether the packed forward writes the attention-output delta (with bias and
+        residual) first and lets the projection GEMM accumulate onto it
+        (``lora_apply_into``).  Not done for q/k/v: there the in-place delta right
+        after the GEMM re-reads an output the L2 still holds, which measured faster
+        than writing the delta to a fresh buffer for the GEMM to read."""
+        return bool(self._dense_target) and dtype in (torch.bfloat16, torch.float16) and \
+            self.config.hidden_size % 128 == 0 and rank in (8, 16, 32, 64)
 
     # -- padding-free forward ------------------------------------------------
     @property
@@ -541,6 +552,9 @@ class EncoderWithLora(nn.Module):
             status = self._runner.status
             qkv_offs = [j * H for _, j in self._qkv_targets]
             segs = pb.segments
+            fuse_dense = self._fused_dense_ok(h.dtype, store.factor_cache(0).rank)
+        else:
+            fuse_dense = False
 
         for l, layer in enumerate(self.layers):
             qkv = F.linear(h, layer.wqkv, layer.bqkv)  # (T, 3H)
@@ -554,13 +568,26 @@ class EncoderWithLora(nn.Module):
             else:  # head sizes the tcgen05 kernel does not tile
                 q, k, v = qkv.view(T, 3, nh, hd).unbind(1)
                 ctx = varlen_attention(q, k, v, pb.cu_seqlens, pb.max_len).view(T, H)
-            ao = F.linear(ctx, layer.wo, layer.bo)
-            if do_lora and self._dense_target:
+            if fuse_dense:
+                # The delta, bias and residual go first, into a fresh output that
+                # the projection GEMM accumulates onto (beta = 1); the LayerNorm
+                # then reads one tensor instead of two.
                 ev = self._event_pair("dense")
-                lora_apply(ctx, ao, store.factor_cache(l), segs, dense_idx, [0], ws, status)
+                ao = torch.empty(T, H, dtype=h.dtype, device=h.device)
+                lora_apply_into(ctx, ao, store.factor_cache(l), segs, dense_idx, [0], ws, status,
+                                residual=h, bias=layer.bo)
                 if ev is not None:
                     ev[1].record()
-            h1, h = self._ffn(layer, ao, h)
+                ao.addmm_(ctx, layer.wo.t())
+                h1, h = self._ffn(layer, ao, None)
+            else:
+                ao = F.linear(ctx, layer.wo, layer.bo)
+                if do_lora and self._dense_target:
+                    ev = self._event_pair("dense")
+                    lora_apply(ctx, ao, store.factor_cache(l), segs, dense_idx, [0], ws, status)
+                    if ev is not None:
+                        ev[1].record()
+                h1, h = self._ffn(layer, ao, h)
         return h
 
     def encode_pooled_packed(self, pb: PackedBatch, store, pooling: str = "auto",

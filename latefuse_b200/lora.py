@@ -186,6 +186,44 @@ def lora_apply(x: Tensor, y: Tensor, cache: FactorCache, segs: SegmentTable, mod
     nat.check(rc, "lf_lora_apply")
 
 
+def lora_apply_into(x: Tensor, y: Tensor, cache: FactorCache, segs: SegmentTable, modules, y_col_offsets,
+                    workspace: Tensor, status: Tensor | None = None, residual: Tensor | None = None,
+                    bias: Tensor | None = None) -> None:
+    """``y[:, off_m : off_m + H] = round(round(residual + bias) + B(A x))`` for each op
+    module (``residual``/``bias`` optional), written for every token, so that a
+    ``y.addmm_(x, W.t())`` afterwards gives the biased projection plus delta (plus
+    residual) with the projection output written once.  The segments must cover
+    every token and carry tile records (a packed batch's table does); the op
+    modules must cover every column of ``y`` the caller reads.
+    """
+    dev = nat.require_cuda(x, y, workspace, segs.table, residual, bias)
+    if not segs.use_records or segs.real_tokens != x.reshape(-1, x.shape[-1]).shape[0]:
+        raise ValueError("lora_apply_into needs tile records and segments covering every token")
+    x2, ldx = _rows(x)
+    y2 = y.reshape(-1, y.shape[-1])
+    if y2.data_ptr() != y.data_ptr() or y2.stride(-1) != 1:
+        raise ValueError("y must be viewable as rows without a copy")
+    r2, ldr = (None, 0)
+    if residual is not None:
+        r2 = residual.reshape(-1, residual.shape[-1])
+        if r2.stride(-1) != 1:
+            raise ValueError("residual rows must be contiguous")
+        ldr = r2.stride(0)
+    b = None if bias is None else (bias if bias.dtype == y.dtype else bias.to(y.dtype)).contiguous()
+    n = len(modules)
+    rc = nat.lib().lf_lora_apply_into(
+        nat.stream_ptr(dev), nat.dtype_code(x.dtype),
+        x2.data_ptr(), ldx, nat.ptr(r2), ldr, nat.ptr(b), y2.data_ptr(), y2.stride(0), x2.shape[0],
+        cache.hidden, cache.rank,
+        cache.a_ptr, cache.a_slot_stride, cache.a_module_stride,
+        cache.b_ptr, cache.b_slot_stride, cache.b_module_stride,
+        cache.n_slots, n, nat.i32_array(modules), nat.i64_array(y_col_offsets),
+        *_seg_args(segs),
+        workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+        nat.ptr(status))
+    nat.check(rc, "lf_lora_apply_into")
+
+
 def lora_shrink(x: Tensor, u: Tensor, cache: FactorCache, segs: SegmentTable, modules,
                 status: Tensor | None = None) -> None:
     """``u[m, t] = A_m(slot(t))^T x[t]`` rounded to the dtype; ``u`` is ``(n_mod, T, R)``."""
