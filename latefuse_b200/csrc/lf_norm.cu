@@ -11,6 +11,15 @@
 //
 // GELU (ACT2FN["gelu"], src/latefuse/model/encoder.py:122,139):
 //     out = round_T(x * 0.5 * (1 + erf(x / sqrt(2))))       in f32
+// For bf16 and f16 the input has only 65,536 values, so the function is a
+// table: each device computes it once (every input bit pattern through the f32
+// formula above, then rounded), and the kernel copies the 128 KB table into
+// shared memory and looks every element up.  The results are the formula's,
+// bit for bit, and the kernel runs at the speed of its HBM traffic instead of
+// the erf arithmetic.
+#include <mutex>
+#include <type_traits>
+
 #include "lf_common.cuh"
 #include "lf_internal.h"
 
@@ -119,6 +128,47 @@ add_layernorm_kernel(const NormParams p) {
   }
 }
 
+__device__ __forceinline__ float gelu_f32(float v) { return v * 0.5f * (1.0f + erff(v * 0.70710678118654752440f)); }
+
+// One table per 2-byte dtype and device: entry i is GELU of the value whose bits are i.
+__device__ uint16_t g_gelu_table[2][65536];
+
+template <typename T>
+__global__ void __launch_bounds__(256) gelu_table_init_kernel(int which) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= 65536) return;
+  const uint16_t bits = uint16_t(i);
+  const T v = *reinterpret_cast<const T*>(&bits);
+  const T r = DT<T>::from_f(gelu_f32(DT<T>::to_f(v)));
+  g_gelu_table[which][i] = *reinterpret_cast<const uint16_t*>(&r);
+}
+
+constexpr int kLutThreads = 1024;
+
+// x and out as 16-byte vectors of 8 elements; the table goes to shared memory first.
+__global__ void __launch_bounds__(kLutThreads, 1)
+gelu_lut_kernel(const uint4* __restrict__ x, uint4* __restrict__ out, int64_t n8, int which) {
+  extern __shared__ uint4 s_tab4[];
+  const uint4* tab = reinterpret_cast<const uint4*>(g_gelu_table[which]);
+  for (int i = threadIdx.x; i < 65536 / 8; i += kLutThreads) s_tab4[i] = tab[i];
+  __syncthreads();
+  const uint16_t* s_tab = reinterpret_cast<const uint16_t*>(s_tab4);
+  auto map = [&](uint32_t w) {
+    return uint32_t(s_tab[w & 0xffffu]) | (uint32_t(s_tab[w >> 16]) << 16);
+  };
+  const int64_t stride = int64_t(gridDim.x) * kLutThreads;
+  int64_t i = int64_t(blockIdx.x) * kLutThreads + threadIdx.x;
+  for (; i + stride < n8; i += 2 * stride) {  // two vectors in flight per thread
+    const uint4 a = x[i], b = x[i + stride];
+    out[i] = make_uint4(map(a.x), map(a.y), map(a.z), map(a.w));
+    out[i + stride] = make_uint4(map(b.x), map(b.y), map(b.z), map(b.w));
+  }
+  if (i < n8) {
+    const uint4 a = x[i];
+    out[i] = make_uint4(map(a.x), map(a.y), map(a.z), map(a.w));
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) gelu_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t n8) {
   const int64_t stride = int64_t(gridDim.x) * blockDim.x;
@@ -126,7 +176,7 @@ __global__ void __launch_bounds__(256) gelu_kernel(const T* __restrict__ x, T* _
     float v[8];
     Vec8<T>::load(x + i * 8, v);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] = v[k] * 0.5f * (1.0f + erff(v[k] * 0.70710678118654752440f));
+    for (int k = 0; k < 8; ++k) v[k] = gelu_f32(v[k]);
     Vec8<T>::store(out + i * 8, v);
   }
 }
@@ -151,12 +201,57 @@ int launch_norm(const NormParams& p, cudaStream_t s) {
   return LF_OK;
 }
 
+constexpr int kMaxDevices = 64;
+std::mutex g_table_mu;
+bool g_table_ready[kMaxDevices][2];
+
+// The device's table for this dtype, built on first use (on `s`, then waited for).
+template <typename T>
+int ensure_gelu_table(int dev, int which, cudaStream_t s) {
+  if (dev < 0 || dev >= kMaxDevices) return set_error(LF_ERR_UNSUPPORTED, "lf_gelu: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_table_mu);
+  if (g_table_ready[dev][which]) return LF_OK;
+  gelu_table_init_kernel<T><<<65536 / 256, 256, 0, s>>>(which);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, "launch gelu table");
+  count_launch();
+  e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_error(e, "gelu table");
+  e = cudaFuncSetAttribute(gelu_lut_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 65536 * 2);
+  if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gelu_lut)");
+  g_table_ready[dev][which] = true;
+  return LF_OK;
+}
+
 template <typename T>
 int launch_gelu(const void* x, void* out, int64_t n, cudaStream_t s) {
   const int64_t n8 = n / 8;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(s, &cap);
+  const int which = std::is_same<T, __half>::value ? 1 : 0;
+  bool ready = false;
+  if (sizeof(T) == 2 && dev >= 0 && dev < kMaxDevices) {
+    std::lock_guard<std::mutex> lock(g_table_mu);
+    ready = g_table_ready[dev][which];
+  }
+  // the table is built (and waited for) outside a stream capture; a captured
+  // call before that computes the formula directly, with the same results
+  if (sizeof(T) == 2 && (ready || cap == cudaStreamCaptureStatusNone)) {
+    if (n8 == 0) return LF_OK;
+    int rc = ensure_gelu_table<T>(dev, which, s);
+    if (rc) return rc;
+    int64_t blocks = (n8 + kLutThreads - 1) / kLutThreads;
+    if (blocks > sms) blocks = sms;
+    gelu_lut_kernel<<<unsigned(blocks), kLutThreads, 65536 * 2, s>>>(static_cast<const uint4*>(x),
+                                                                      static_cast<uint4*>(out), n8, which);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_error(e, "launch gelu_lut");
+    count_launch();
+    return LF_OK;
+  }
   int64_t blocks = (n8 + 255) / 256;
   if (blocks > int64_t(sms) * 8) blocks = int64_t(sms) * 8;
   if (blocks == 0) return LF_OK;

@@ -70,3 +70,33 @@ def test_gelu_matches_torch(cuda, dtype):
     y = x.clone()
     gelu(y, out=y)
     assert torch.equal(y, ours)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_gelu_every_2byte_input_matches_the_f32_formula(cuda, dtype):
+    """The table path covers every bit pattern: each must equal the f32 formula rounded once."""
+    bits = torch.arange(-32768, 32768, dtype=torch.int32, device=cuda).to(torch.int16)
+    x = bits.view(dtype)
+    ours = gelu(x)
+    xf = x.float()
+    ref = (xf * 0.5 * (1.0 + torch.erf(xf * 0.70710678118654752440))).to(dtype)
+    nan = torch.isnan(ref)
+    assert torch.equal(torch.isnan(ours), nan)
+    assert torch.equal(ours.view(torch.int16)[~nan], ref.view(torch.int16)[~nan])
+    # odd lengths and offsets of whole 16-byte vectors
+    for n in (8, 8 * 1023, 8 * 1025 + 8):
+        torch.testing.assert_close(gelu(x[:n].clone()), ours[:n], atol=0, rtol=0, equal_nan=True)
+
+
+def test_gelu_under_stream_capture(cuda):
+    x = (torch.randn(4096, 1024, device=cuda) * 3).to(torch.bfloat16)
+    ref = gelu(x)
+    out = torch.empty_like(x)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            gelu(x, out=out)
+        g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
