@@ -63,6 +63,32 @@ struct Vec8<float> {
   }
 };
 
+// 8 consecutive elements of T kept as raw bytes (one or two 16-byte words)
+// until they are needed: half the registers of 8 floats for 2-byte T.
+template <typename T>
+struct Raw8 {
+  uint4 w[sizeof(T) / 2];
+  __device__ __forceinline__ void load(const T* p) {
+#pragma unroll
+    for (int i = 0; i < int(sizeof(T) / 2); ++i) w[i] = reinterpret_cast<const uint4*>(p)[i];
+  }
+  __device__ __forceinline__ void unpack(float (&v)[8]) const {
+    if constexpr (sizeof(T) == 2) {
+      const uint32_t u[4] = {w[0].x, w[0].y, w[0].z, w[0].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = Pack2<T>::unpack(u[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+    } else {
+      const uint32_t u[8] = {w[0].x, w[0].y, w[0].z, w[0].w, w[1].x, w[1].y, w[1].z, w[1].w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(u[i]);
+    }
+  }
+};
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -71,29 +97,54 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 constexpr int kNormWarps = 8;
 
-template <typename T, int NC>
+template <typename T, int NC, bool HAS_B>
 __global__ void __launch_bounds__(32 * kNormWarps)
-add_layernorm_kernel(const NormParams p) {
+add_layernorm_kernel(const NormParams p, int full) {
   const int lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * kNormWarps + (threadIdx.x >> 5);
   if (row >= p.n_rows) return;
   const T* a = reinterpret_cast<const T*>(p.a) + row * p.lda;
-  const T* b = p.b != nullptr ? reinterpret_cast<const T*>(p.b) + row * p.ldb : nullptr;
+  const T* b = HAS_B ? reinterpret_cast<const T*>(p.b) + row * p.ldb : nullptr;
   const T* gamma = reinterpret_cast<const T*>(p.gamma);
   const T* beta = reinterpret_cast<const T*>(p.beta);
   T* out = reinterpret_cast<T*>(p.out) + row * p.ldo;
   const int H = p.hidden;
 
+  // every load of the row (and gamma / beta) is issued before any arithmetic
+  Raw8<T> ra[NC], rb[NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int col = c * 256 + lane * 8;
+    if (full || col < H) {
+      ra[c].load(a + col);
+      if (HAS_B) rb[c].load(b + col);
+    }
+  }
+  // gamma and beta too, so that their latency overlaps the reductions instead
+  // of following them (rows up to 2048 wide; wider rows load them at the end,
+  // where the registers are free)
+  constexpr bool kEarly = NC <= 8;
+  Raw8<T> g[kEarly ? NC : 1], bt[kEarly ? NC : 1];
+  if constexpr (kEarly) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int col = c * 256 + lane * 8;
+      if (full || col < H) {
+        g[c].load(gamma + col);
+        bt[c].load(beta + col);
+      }
+    }
+  }
   float v[NC][8];
   float sum = 0.f;
 #pragma unroll
   for (int c = 0; c < NC; ++c) {
     const int col = c * 256 + lane * 8;
-    if (col < H) {
-      Vec8<T>::load(a + col, v[c]);
-      if (b != nullptr) {
+    if (full || col < H) {
+      ra[c].unpack(v[c]);
+      if (HAS_B) {
         float w[8];
-        Vec8<T>::load(b + col, w);
+        rb[c].unpack(w);
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[c][i] = round_through<T>(v[c][i] + w[i]);
       }
@@ -105,7 +156,7 @@ add_layernorm_kernel(const NormParams p) {
   float sq = 0.f;
 #pragma unroll
   for (int c = 0; c < NC; ++c) {
-    if (c * 256 + lane * 8 < H) {
+    if (full || c * 256 + lane * 8 < H) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float d = v[c][i] - mean;
@@ -117,12 +168,17 @@ add_layernorm_kernel(const NormParams p) {
 #pragma unroll
   for (int c = 0; c < NC; ++c) {
     const int col = c * 256 + lane * 8;
-    if (col < H) {
-      float g[8], bt[8], o[8];
-      Vec8<T>::load(gamma + col, g);
-      Vec8<T>::load(beta + col, bt);
+    if (full || col < H) {
+      float gf[8], bf[8], o[8];
+      if constexpr (kEarly) {
+        g[c].unpack(gf);
+        bt[c].unpack(bf);
+      } else {
+        Vec8<T>::load(gamma + col, gf);
+        Vec8<T>::load(beta + col, bf);
+      }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = (v[c][i] - mean) * rstd * g[i] + bt[i];
+      for (int i = 0; i < 8; ++i) o[i] = (v[c][i] - mean) * rstd * gf[i] + bf[i];
       Vec8<T>::store(out + col, o);
     }
   }
@@ -184,11 +240,17 @@ __global__ void __launch_bounds__(256) gelu_kernel(const T* __restrict__ x, T* _
 template <typename T>
 int launch_norm(const NormParams& p, cudaStream_t s) {
   const int nc = (p.hidden + 255) / 256;
+  const int full = p.hidden == nc * 256;  // every lane holds NC whole 8-element chunks
   const unsigned blocks = unsigned((p.n_rows + kNormWarps - 1) / kNormWarps);
   const dim3 grid{blocks}, block{32 * kNormWarps};
   switch (nc) {
-#define LF_NORM_CASE(N) \
-  case N: add_layernorm_kernel<T, N><<<grid, block, 0, s>>>(p); break;
+#define LF_NORM_CASE(N)                                              \
+  case N:                                                            \
+    if (p.b != nullptr)                                              \
+      add_layernorm_kernel<T, N, true><<<grid, block, 0, s>>>(p, full); \
+    else                                                             \
+      add_layernorm_kernel<T, N, false><<<grid, block, 0, s>>>(p, full); \
+    break;
     LF_NORM_CASE(1) LF_NORM_CASE(2) LF_NORM_CASE(3) LF_NORM_CASE(4) LF_NORM_CASE(5) LF_NORM_CASE(6)
     LF_NORM_CASE(7) LF_NORM_CASE(8) LF_NORM_CASE(9) LF_NORM_CASE(10) LF_NORM_CASE(11) LF_NORM_CASE(12)
     LF_NORM_CASE(13) LF_NORM_CASE(14) LF_NORM_CASE(15) LF_NORM_CASE(16)
