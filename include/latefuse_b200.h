@@ -314,12 +314,15 @@ int lf_head_forward(void* stream, int dtype,
  * `LayerNorm(sublayer_out + residual)` (src/latefuse/model/encoder.py:137,141)
  * and the embeddings' LayerNorm (:275), i.e. torch's add followed by
  * nn.LayerNorm: the sum is rounded to dtype, mean and biased variance are
- * taken in f32, the result is rounded to dtype.  hidden % 8 == 0, hidden <=
- * 4096; pointers and row strides (elements) 16-byte aligned; gamma/beta in
- * dtype.  out may alias a or b. */
+ * taken in f32, the result is rounded to dtype.  Instead of b, `vec` (hidden
+ * entries, may be NULL, not together with b) is one row added to every row:
+ * LayerNorm(round(a + vec)), for a projection whose GEMM has already
+ * accumulated onto the residual and whose bias is still to be added.
+ * hidden % 8 == 0, hidden <= 4096; pointers and row strides (elements)
+ * 16-byte aligned; gamma/beta/vec in dtype.  out may alias a or b. */
 int lf_add_layernorm(void* stream, int dtype, const void* a, int64_t lda, const void* b, int64_t ldb,
-                     const void* gamma, const void* beta, float eps, int64_t n_rows, int hidden,
-                     void* out, int64_t ldo);
+                     const void* vec, const void* gamma, const void* beta, float eps, int64_t n_rows,
+                     int hidden, void* out, int64_t ldo);
 
 /* out = x * 0.5 * (1 + erf(x / sqrt(2))) in f32, rounded to dtype: the exact
  * GELU of the FFN (ACT2FN["gelu"], src/latefuse/model/encoder.py:122,139).

@@ -113,6 +113,7 @@ struct NormParams {
   const void* a;
   const void* b;       // may be null
   int64_t lda, ldb;
+  const void* vec;     // row vector added to every row, may be null (not with b)
   const void* gamma;
   const void* beta;
   float eps;

@@ -4,6 +4,8 @@
 // src/latefuse/model/encoder.py:137,141, and the embeddings' LayerNorm at :275
 // with no residual):
 //     s   = round_T(a + b)                       the add materialises in T first
+// or, with a row vector v instead of b (a projection bias, when the GEMM has
+// already added the residual), s = round_T(a + v);
 //     out = round_T((s - mean) * rsqrt(var + eps) * gamma + beta)
 // mean and biased variance in f32 over the row (two passes over registers).
 // One warp per row: lane l holds elements [256 c + 8 l, 256 c + 8 l + 8) of
@@ -97,14 +99,17 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 constexpr int kNormWarps = 8;
 
-template <typename T, int NC, bool HAS_B>
+// MODE 0: a alone; 1: a + b (a second matrix); 2: a + v (one row vector).
+template <typename T, int NC, int MODE>
 __global__ void __launch_bounds__(32 * kNormWarps)
 add_layernorm_kernel(const NormParams p, int full) {
+  constexpr bool HAS_B = MODE != 0;
   const int lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * kNormWarps + (threadIdx.x >> 5);
   if (row >= p.n_rows) return;
   const T* a = reinterpret_cast<const T*>(p.a) + row * p.lda;
-  const T* b = HAS_B ? reinterpret_cast<const T*>(p.b) + row * p.ldb : nullptr;
+  const T* b = MODE == 1 ? reinterpret_cast<const T*>(p.b) + row * p.ldb
+               : MODE == 2 ? reinterpret_cast<const T*>(p.vec) : nullptr;
   const T* gamma = reinterpret_cast<const T*>(p.gamma);
   const T* beta = reinterpret_cast<const T*>(p.beta);
   T* out = reinterpret_cast<T*>(p.out) + row * p.ldo;
@@ -244,12 +249,14 @@ int launch_norm(const NormParams& p, cudaStream_t s) {
   const unsigned blocks = unsigned((p.n_rows + kNormWarps - 1) / kNormWarps);
   const dim3 grid{blocks}, block{32 * kNormWarps};
   switch (nc) {
-#define LF_NORM_CASE(N)                                              \
-  case N:                                                            \
-    if (p.b != nullptr)                                              \
-      add_layernorm_kernel<T, N, true><<<grid, block, 0, s>>>(p, full); \
-    else                                                             \
-      add_layernorm_kernel<T, N, false><<<grid, block, 0, s>>>(p, full); \
+#define LF_NORM_CASE(N)                                                \
+  case N:                                                              \
+    if (p.b != nullptr)                                                \
+      add_layernorm_kernel<T, N, 1><<<grid, block, 0, s>>>(p, full);   \
+    else if (p.vec != nullptr)                                         \
+      add_layernorm_kernel<T, N, 2><<<grid, block, 0, s>>>(p, full);   \
+    else                                                               \
+      add_layernorm_kernel<T, N, 0><<<grid, block, 0, s>>>(p, full);   \
     break;
     LF_NORM_CASE(1) LF_NORM_CASE(2) LF_NORM_CASE(3) LF_NORM_CASE(4) LF_NORM_CASE(5) LF_NORM_CASE(6)
     LF_NORM_CASE(7) LF_NORM_CASE(8) LF_NORM_CASE(9) LF_NORM_CASE(10) LF_NORM_CASE(11) LF_NORM_CASE(12)
@@ -333,12 +340,13 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 using namespace lf;
 
 extern "C" int lf_add_layernorm(void* stream, int dtype, const void* a, int64_t lda, const void* b, int64_t ldb,
-                                const void* gamma, const void* beta, float eps, int64_t n_rows, int hidden,
-                                void* out, int64_t ldo) {
+                                const void* vec, const void* gamma, const void* beta, float eps, int64_t n_rows,
+                                int hidden, void* out, int64_t ldo) {
   if (dtype != LF_DTYPE_BF16 && dtype != LF_DTYPE_F16 && dtype != LF_DTYPE_F32)
     return set_error(LF_ERR_INVALID, "lf_add_layernorm: unknown dtype %d", dtype);
   if (a == nullptr || gamma == nullptr || beta == nullptr || out == nullptr)
     return set_error(LF_ERR_INVALID, "lf_add_layernorm: null a, gamma, beta or out");
+  if (b != nullptr && vec != nullptr) return set_error(LF_ERR_INVALID, "lf_add_layernorm: b and vec together");
   if (n_rows < 0 || hidden <= 0 || hidden % 8 != 0)
     return set_error(LF_ERR_INVALID, "lf_add_layernorm: hidden %d must be a positive multiple of 8", hidden);
   if (hidden > 4096) return set_error(LF_ERR_UNSUPPORTED, "lf_add_layernorm: hidden %d above 4096", hidden);
@@ -346,6 +354,7 @@ extern "C" int lf_add_layernorm(void* stream, int dtype, const void* a, int64_t 
     return set_error(LF_ERR_INVALID, "lf_add_layernorm: a row stride is below hidden %d", hidden);
   const int es = dtype == LF_DTYPE_F32 ? 4 : 2;
   if (!aligned16(a) || !aligned16(out) || !aligned16(gamma) || !aligned16(beta) || (b != nullptr && !aligned16(b)) ||
+      (vec != nullptr && !aligned16(vec)) ||
       (lda * es) % 16 != 0 || (ldo * es) % 16 != 0 || (b != nullptr && (ldb * es) % 16 != 0))
     return set_error(LF_ERR_INVALID, "lf_add_layernorm: pointers and row strides must be 16-byte aligned");
   if (n_rows == 0) return LF_OK;
@@ -354,6 +363,7 @@ extern "C" int lf_add_layernorm(void* stream, int dtype, const void* a, int64_t 
   p.b = b;
   p.lda = lda;
   p.ldb = ldb;
+  p.vec = vec;
   p.gamma = gamma;
   p.beta = beta;
   p.eps = eps;

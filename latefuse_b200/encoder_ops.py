@@ -24,9 +24,10 @@ def _rows(t: Tensor) -> tuple[Tensor, int]:
 
 
 def add_layernorm(a: Tensor, b: Tensor | None, weight: Tensor, bias: Tensor, eps: float,
-                  out: Tensor | None = None) -> Tensor:
-    """``layer_norm(a + b)`` (``b`` may be None) over the last dimension."""
-    dev = nat.require_cuda(a, b, weight, bias, out)
+                  out: Tensor | None = None, vec: Tensor | None = None) -> Tensor:
+    """``layer_norm(a + b)`` (``b`` may be None) over the last dimension; or, with
+    ``vec`` (one row, e.g. a projection bias) instead of ``b``, ``layer_norm(a + vec)``."""
+    dev = nat.require_cuda(a, b, weight, bias, out, vec)
     H = a.shape[-1]
     a2, lda = _rows(a)
     b2, ldb = _rows(b) if b is not None else (None, 0)
@@ -35,9 +36,10 @@ def add_layernorm(a: Tensor, b: Tensor | None, weight: Tensor, bias: Tensor, eps
     o2, ldo = _rows(out)
     w = weight if weight.dtype == a.dtype else weight.to(a.dtype)
     bb = bias if bias.dtype == a.dtype else bias.to(a.dtype)
+    v = None if vec is None else (vec if vec.dtype == a.dtype else vec.to(a.dtype)).contiguous()
     rc = nat.lib().lf_add_layernorm(nat.stream_ptr(dev), nat.dtype_code(a.dtype), a2.data_ptr(), lda,
-                                    nat.ptr(b2), ldb, w.contiguous().data_ptr(), bb.contiguous().data_ptr(),
-                                    float(eps), a2.shape[0], H, o2.data_ptr(), ldo)
+                                    nat.ptr(b2), ldb, nat.ptr(v), w.contiguous().data_ptr(),
+                                    bb.contiguous().data_ptr(), float(eps), a2.shape[0], H, o2.data_ptr(), ldo)
     nat.check(rc, "lf_add_layernorm")
     return out
 

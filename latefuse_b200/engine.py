@@ -492,18 +492,23 @@ class EncoderWithLora(nn.Module):
                 else:
                     cache = _DeltaRunner.layerwise_cache(lora_weights[l], "dense")
                     lora_apply(ctx, ao, cache, segs, [0], [0], ws, status)
-            h1, h = self._ffn(layer, ao, h)
+            h = self._ffn(layer, ao, h)
         return h.view(B, S, H)
 
-    def _ffn(self, layer: _Layer, ao: Tensor, h: Tensor) -> tuple[Tensor, Tensor]:
+    def _ffn(self, layer: _Layer, ao: Tensor, h: Tensor | None) -> Tensor:
         """``h1 = LN1(ao + h)`` (``LN1(ao)`` when ``h`` is None: the residual is already
-        in ``ao``), ``LN2(W2 act(W1 h1) + h1)``, on the native add+LayerNorm and GELU
-        kernels."""
+        in ``ao``), then ``LN2(W2 act(W1 h1) + b2 + h1)``, on the native add+LayerNorm and
+        GELU kernels.  For bf16/f16 the down-projection GEMM accumulates onto ``h1`` in
+        place (beta = 1; ``h1`` is not read again) and LayerNorm adds ``b2``, so the
+        residual is not read a second time."""
         h1 = add_layernorm(ao, h, layer.ln1.weight, layer.ln1.bias, self.eps)
         mid = F.linear(h1, layer.wi, layer.bi)
         mid = gelu(mid, out=mid) if self._native_gelu else self.act(mid)
+        if h1.dtype in (torch.bfloat16, torch.float16):
+            h1.view(-1, h1.shape[-1]).addmm_(mid.view(-1, mid.shape[-1]), layer.wo2.t())
+            return add_layernorm(h1, None, layer.ln2.weight, layer.ln2.bias, self.eps, out=h1, vec=layer.bo2)
         o = F.linear(mid, layer.wo2, layer.bo2)
-        return h1, add_layernorm(o, h1, layer.ln2.weight, layer.ln2.bias, self.eps, out=o)
+        return add_layernorm(o, h1, layer.ln2.weight, layer.ln2.bias, self.eps, out=o)
 
     def _fused_dense_ok(self, dtype: torch.dtype, rank: int) -> bool:
         """Whether the packed forward writes the attention-output delta (with bias and
@@ -579,7 +584,7 @@ class EncoderWithLora(nn.Module):
                 if ev is not None:
                     ev[1].record()
                 ao.addmm_(ctx, layer.wo.t())
-                h1, h = self._ffn(layer, ao, None)
+                h = self._ffn(layer, ao, None)
             else:
                 ao = F.linear(ctx, layer.wo, layer.bo)
                 if do_lora and self._dense_target:
@@ -587,7 +592,7 @@ class EncoderWithLora(nn.Module):
                     lora_apply(ctx, ao, store.factor_cache(l), segs, dense_idx, [0], ws, status)
                     if ev is not None:
                         ev[1].record()
-                h1, h = self._ffn(layer, ao, h)
+                h = self._ffn(layer, ao, h)
         return h
 
     def encode_pooled_packed(self, pb: PackedBatch, store, pooling: str = "auto",

@@ -100,3 +100,17 @@ def test_gelu_under_stream_capture(cuda):
         g.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_layernorm_with_row_vector_matches_torch(cuda, dtype):
+    """LayerNorm(round(a + v)) for one row v added to every row (a projection bias)."""
+    a = torch.randn(3000, 1024, device=cuda).to(dtype)
+    v = torch.randn(1024, device=cuda).to(dtype)
+    w = (torch.rand(1024, device=cuda) + 0.5).to(dtype)
+    bias = torch.randn(1024, device=cuda).to(dtype)
+    ours = add_layernorm(a, None, w, bias, 1e-5, vec=v)
+    ref = F.layer_norm((a + v).float(), (1024,), w.float(), bias.float(), 1e-5).to(dtype)
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    torch.testing.assert_close(ours, ref, atol=tol, rtol=tol)
+    assert (ours.float() - ref.float()).abs().max().item() <= (1e-5 if dtype == torch.float32 else 2 ** -6 * 8)

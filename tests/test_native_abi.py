@@ -81,10 +81,13 @@ def test_argument_validation_happens_before_any_device_work(lib):
     rc = lib.lf_cache_write_slot(None, addr, 64, 5, 4, 0, addr, 16)
     assert rc == LF_ERR_INVALID
     # layernorm: hidden not a multiple of 8; gelu: size not a multiple of 8
-    rc = lib.lf_add_layernorm(None, 1, addr, 12, None, 0, addr, addr, 1e-5, 4, 12, addr, 12)
+    rc = lib.lf_add_layernorm(None, 1, addr, 12, None, 0, None, addr, addr, 1e-5, 4, 12, addr, 12)
     assert rc == LF_ERR_INVALID and b"multiple of 8" in lib.lf_last_error()
     rc = lib.lf_gelu(None, 1, addr, addr, 7)
     assert rc == LF_ERR_INVALID and b"multiple of 8" in lib.lf_last_error()
+    # layernorm: a second matrix and a row vector together
+    rc = lib.lf_add_layernorm(None, 1, addr, 16, addr, 16, addr, addr, addr, 1e-5, 4, 16, addr, 16)
+    assert rc == LF_ERR_INVALID and b"together" in lib.lf_last_error()
 
 
 def test_workspace_size(lib):
