@@ -306,6 +306,24 @@ int lf_head_forward(void* stream, int dtype,
                     int32_t* status);
 
 /* ------------------------------------------------------------------------
+ * Projection GEMM
+ * ------------------------------------------------------------------------ */
+
+#define LF_ACT_NONE 0
+#define LF_ACT_GELU 1   /* exact erf GELU, ACT2FN["gelu"] */
+
+/* y = act(x w^T + bias) for x (m, k), w (n, k) (an nn.Linear weight), y (m, n),
+ * row-major with row strides ldx / ldw / ldy (elements); bias has n entries or
+ * is NULL.  bf16 or f16, f32 accumulation; the sum is rounded to dtype, then for
+ * LF_ACT_GELU gelu_f32 of that rounded value is rounded again (torch's
+ * F.linear followed by F.gelu).  Replaces the encoder's projections
+ * (src/latefuse/model/encoder.py: q/k/v, attention output, FFN up with its GELU
+ * at :122,139, FFN down).  n % 256 == 0, k % 64 == 0, pointers and strides
+ * 16-byte aligned (LF_ERR_UNSUPPORTED / LF_ERR_INVALID otherwise). */
+int lf_linear(void* stream, int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,
+              const void* bias, void* y, int64_t ldy, int64_t m, int n, int k, int act, int32_t* status);
+
+/* ------------------------------------------------------------------------
  * Encoder elementwise ops around the projections
  * ------------------------------------------------------------------------ */
 

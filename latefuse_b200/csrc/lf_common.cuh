@@ -72,6 +72,10 @@ template <> struct Pack2<__half> {
 template <typename T>
 __device__ __forceinline__ float round_through(float v) { return DT<T>::to_f(DT<T>::from_f(v)); }
 
+// The exact (erf) GELU in f32, as ACT2FN["gelu"] computes it (the GELU kernels
+// and the GEMM epilogue share this one definition, so their results agree).
+__device__ __forceinline__ float gelu_f32(float v) { return v * 0.5f * (1.0f + erff(v * 0.70710678118654752440f)); }
+
 // ---------------------------------------------------------------------------
 // misc
 // ---------------------------------------------------------------------------

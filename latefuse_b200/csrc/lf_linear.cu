@@ -1,0 +1,312 @@
+// Projection GEMM on tcgen05: Y = act(X W^T + bias), bf16 / f16 in, f32 accumulate.
+//
+// Replaces the encoder's nn.Linear projections (src/latefuse/model/encoder.py:
+// the fused q/k/v, attention-output, FFN up and down projections) with an
+// sm_100a kernel of this library, so that work around a projection can be
+// fused into it (the FFN's GELU in the epilogue: ACT2FN["gelu"] of
+// encoder.py:122,139).  Rounding follows torch: round(acc + bias) to the dtype,
+// then for GELU round(gelu_f32(that)).
+//
+// Persistent, one CTA per SM, 128 x 256 output tiles in m-major order (the CTAs
+// working at one time share the rows of X and all of W through L2):
+//   warp 0      TMA producer: per 64-wide K block an X box {64, 128} and a W box
+//               {64, 256} (both K-major, SW128) into a 4-stage ring of 48 KB;
+//   warp 1      MMA issuer: four tcgen05.mma (M=128, N=256, K=16) per K block
+//               into one of two TMEM accumulators (256 columns each), so the
+//               epilogue of one tile overlaps the main loop of the next;
+//   warps 2-5   epilogue, one output row per thread (its TMEM lane): 32 columns
+//               per tcgen05.ld, bias and activation in f32, rounded, staged per
+//               warp in a double-buffered 32 x 32 SW64 tile and written by TMA
+//               (rows past M are clipped by the tensor map).
+// Every wait is bounded: a timeout sets LF_STATUS_TIMEOUT and the roles unwind.
+#include "lf_common.cuh"
+#include "lf_internal.h"
+
+namespace lf {
+
+namespace {
+
+constexpr int kBM = 128, kBN = 256, kBK = 64;
+constexpr int kABytes = kBM * kBK * 2;           // 16 KB
+constexpr int kBBytes = kBN * kBK * 2;           // 32 KB
+constexpr int kStageBytes = kABytes + kBBytes;   // 48 KB
+constexpr int kStages = 4;
+constexpr int kEpiWarps = 4;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kOutCols = 32;                     // output columns per epilogue store
+constexpr int kOutBuf = 32 * kOutCols * 2;       // one warp's 32 x 32 staging tile: 2 KB
+constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kEpiWarps * 2 * kOutBuf + 1024;
+
+struct alignas(64) LinearParams {
+  CUtensorMap x_map;  // 2D {K, M}, box {64, 128}, SW128
+  CUtensorMap w_map;  // 2D {K, N}, box {64, 256}, SW128
+  CUtensorMap y_map;  // 2D {N, M}, box {32, 32}, SW64
+  const void* bias;   // N entries or null
+  int64_t n_tiles;
+  int32_t n_tiles_n;
+  int32_t n_kb;
+  int32_t act;        // LF_ACT_*
+  int32_t* status;
+};
+
+__device__ __forceinline__ bool aborted_flag(const int32_t* f) {
+  return *reinterpret_cast<const volatile int32_t*>(f) != 0;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_constant__ LinearParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  const uint32_t s_stage0 = base;
+  const uint32_t s_out0 = base + kStages * kStageBytes;  // [warp][buffer] 2 KB tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + (s_out0 + kEpiWarps * 2 * kOutBuf - base));
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  const int FULL = 0, EMPTY = kStages, ACC_FULL = 2 * kStages, ACC_EMPTY = 2 * kStages + 2,
+            DRAIN = 2 * kStages + 4, N_BARS = DRAIN + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(&bars[N_BARS]);
+  int32_t* s_abort = reinterpret_cast<int32_t*>(tmem_slot + 1);
+
+  if (tid == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(bar(FULL + i), 1);
+      mbar_init(bar(EMPTY + i), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(ACC_FULL + i), 1);
+      mbar_init(bar(ACC_EMPTY + i), kEpiWarps);
+    }
+    mbar_init(bar(DRAIN), 1);
+    *s_abort = 0;
+    fence_mbar_init();
+    prefetch_tmap(&p.x_map);
+    prefetch_tmap(&p.w_map);
+    prefetch_tmap(&p.y_map);
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc(smem_u32(tmem_slot), 2 * kBN);
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto fail = [&]() {
+    set_status(p.status, LF_STATUS_TIMEOUT);
+    atomicExch(s_abort, 1);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int kk = 0;
+      bool stop = false;
+      for (int64_t t = blockIdx.x; t < p.n_tiles && !stop; t += gridDim.x) {
+        const int32_t m0 = int32_t(t / p.n_tiles_n) * kBM, n0 = int32_t(t % p.n_tiles_n) * kBN;
+        for (int kb = 0; kb < p.n_kb; ++kb, ++kk) {
+          const int s = kk % kStages;
+          if (aborted_flag(s_abort) || !mbar_wait(bar(EMPTY + s), ((kk / kStages) & 1) ^ 1)) {
+            if (!aborted_flag(s_abort)) fail();
+            stop = true;
+            break;
+          }
+          const uint32_t st = s_stage0 + s * kStageBytes;
+          mbar_arrive_expect_tx(bar(FULL + s), kStageBytes);
+          tma_load_2d(st, &p.x_map, bar(FULL + s), kb * kBK, m0);
+          tma_load_2d(st + kABytes, &p.w_map, bar(FULL + s), kb * kBK, n0);
+        }
+      }
+      if (aborted_flag(s_abort)) {  // loads nobody consumed land before the CTA exits (bounded)
+        for (int q = (kk > kStages ? kk - kStages : 0); q < kk; ++q)
+          mbar_wait(bar(FULL + q % kStages), (q / kStages) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(DT<T>::umma_fmt, kBM, kBN, 0, 0);
+      int kk = 0, it = 0;
+      bool stop = false;
+      for (int64_t t = blockIdx.x; t < p.n_tiles && !stop; t += gridDim.x, ++it) {
+        const int a = it & 1;
+        if (aborted_flag(s_abort) || !mbar_wait(bar(ACC_EMPTY + a), ((it >> 1) & 1) ^ 1)) {
+          if (!aborted_flag(s_abort)) fail();
+          break;
+        }
+        for (int kb = 0; kb < p.n_kb; ++kb, ++kk) {
+          const int s = kk % kStages;
+          if (aborted_flag(s_abort) || !mbar_wait(bar(FULL + s), (kk / kStages) & 1)) {
+            if (!aborted_flag(s_abort)) fail();
+            stop = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = s_stage0 + s * kStageBytes;
+#pragma unroll
+          for (int q = 0; q < kBK / 16; ++q)
+            umma_f16(tmem + a * kBN, smem_desc(st + q * 32, 16, 1024, 2), smem_desc(st + kABytes + q * 32, 16, 1024, 2),
+                     idesc, (kb | q) != 0 ? 1u : 0u);
+          umma_commit(bar(EMPTY + s));
+        }
+        if (!stop) umma_commit(bar(ACC_FULL + a));
+      }
+      if (aborted_flag(s_abort)) {  // every issued MMA finishes before TMEM is released (bounded)
+        umma_commit(bar(DRAIN));
+        mbar_wait(bar(DRAIN), 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    const int quad = warp & 3;
+    const uint32_t taddr = tmem + (uint32_t(quad * 32) << 16);
+    const uint32_t my_out = s_out0 + (warp - 2) * 2 * kOutBuf;
+    const T* bias = static_cast<const T*>(p.bias);
+    int it = 0, sb = 0;
+    for (int64_t t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++it) {
+      const int a = it & 1;
+      const int32_t m0 = int32_t(t / p.n_tiles_n) * kBM, n0 = int32_t(t % p.n_tiles_n) * kBN;
+      bool ok = !aborted_flag(s_abort);
+      if (ok && !mbar_wait(bar(ACC_FULL + a), (it >> 1) & 1)) {
+        fail();
+        ok = false;
+      }
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      for (int c = 0; c < kBN / kOutCols; ++c) {
+        uint32_t v[32];
+        tmem_ld32(taddr + a * kBN + c * kOutCols, v);
+        const int col0 = n0 + c * kOutCols;
+        float bf[32];
+        if (bias != nullptr) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 w = __ldg(reinterpret_cast<const uint4*>(bias + col0) + q);
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 f = Pack2<T>::unpack(ws[i]);
+              bf[q * 8 + 2 * i] = f.x;
+              bf[q * 8 + 2 * i + 1] = f.y;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) bf[i] = 0.f;
+        }
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float y0 = __uint_as_float(v[2 * i]) + bf[2 * i];
+          float y1 = __uint_as_float(v[2 * i + 1]) + bf[2 * i + 1];
+          if (p.act == LF_ACT_GELU) {
+            y0 = gelu_f32(round_through<T>(y0));
+            y1 = gelu_f32(round_through<T>(y1));
+          }
+          packed[i] = Pack2<T>::pack(y0, y1);
+        }
+        // the store that last read this staging buffer must be done with it
+        if (lane == 0) tma_store_wait_read_le1();
+        __syncwarp();
+        const uint32_t buf = my_out + sb * kOutBuf;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)  // SW64: 16-byte chunk q of row `lane` at q ^ ((lane >> 1) & 3)
+          *reinterpret_cast<uint4*>(gbase + (buf - base) + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
+              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&p.y_map, buf, col0, m0 + quad * 32);
+          tma_store_commit();
+        }
+        sb ^= 1;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(ACC_EMPTY + a));  // this warp's TMEM reads of the tile are done
+    }
+    if (lane == 0) tma_store_wait_all();
+  }
+
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, 2 * kBN);
+  }
+}
+
+bool aligned16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; }
+
+}  // namespace
+
+}  // namespace lf
+
+using namespace lf;
+
+extern "C" int lf_linear(void* stream, int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,
+                         const void* bias, void* y, int64_t ldy, int64_t m, int n, int k, int act,
+                         int32_t* status) {
+  if (dtype != LF_DTYPE_BF16 && dtype != LF_DTYPE_F16)
+    return set_error(LF_ERR_UNSUPPORTED, "lf_linear: dtype %d (bf16 or f16 only)", dtype);
+  if (act != LF_ACT_NONE && act != LF_ACT_GELU) return set_error(LF_ERR_INVALID, "lf_linear: unknown act %d", act);
+  if (m < 0 || m > INT32_MAX || n <= 0 || k <= 0 || n % kBN != 0 || k % kBK != 0)
+    return set_error(LF_ERR_UNSUPPORTED, "lf_linear: n %d must be a multiple of 256 and k %d of 64", n, k);
+  if (x == nullptr || w == nullptr || y == nullptr) return set_error(LF_ERR_INVALID, "lf_linear: null x, w or y");
+  if (ldx < k || ldw < k || ldy < n) return set_error(LF_ERR_INVALID, "lf_linear: a row stride is below its row");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (bias != nullptr && !aligned16(bias)) || (ldx * 2) % 16 ||
+      (ldw * 2) % 16 || (ldy * 2) % 16)
+    return set_error(LF_ERR_INVALID, "lf_linear: pointers and row strides must be 16-byte aligned");
+  if (m == 0) return LF_OK;
+  PFN_encodeTiled enc = get_encode_tiled();
+  if (enc == nullptr) return set_error(LF_ERR_DRIVER, "cuTensorMapEncodeTiled unavailable");
+  LinearParams p;
+  memset(&p, 0, sizeof(p));
+  const CUtensorMapDataType dt = dtype == LF_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const cuuint32_t estr[2] = {1, 1};
+  {
+    const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(m)};
+    const cuuint64_t strides[1] = {cuuint64_t(ldx) * 2};
+    const cuuint32_t box[2] = {kBK, kBM};
+    if (enc(&p.x_map, dt, 2, const_cast<void*>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return set_error(LF_ERR_CUDA, "cuTensorMapEncodeTiled(x) failed");
+  }
+  {
+    const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(n)};
+    const cuuint64_t strides[1] = {cuuint64_t(ldw) * 2};
+    const cuuint32_t box[2] = {kBK, kBN};
+    if (enc(&p.w_map, dt, 2, const_cast<void*>(w), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return set_error(LF_ERR_CUDA, "cuTensorMapEncodeTiled(w) failed");
+  }
+  {
+    const cuuint64_t dims[2] = {cuuint64_t(n), cuuint64_t(m)};
+    const cuuint64_t strides[1] = {cuuint64_t(ldy) * 2};
+    const cuuint32_t box[2] = {kOutCols, 32};
+    if (enc(&p.y_map, dt, 2, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return set_error(LF_ERR_CUDA, "cuTensorMapEncodeTiled(y) failed");
+  }
+  p.bias = bias;
+  p.n_tiles_n = n / kBN;
+  p.n_tiles = ((m + kBM - 1) / kBM) * p.n_tiles_n;
+  p.n_kb = k / kBK;
+  p.act = act;
+  p.status = status;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = int(p.n_tiles < sms ? p.n_tiles : sms);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto kern = dtype == LF_DTYPE_BF16 ? linear_kernel<__nv_bfloat16> : linear_kernel<__half>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(linear)");
+  kern<<<grid, kThreads, kSmemBytes, s>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, "launch linear");
+  count_launch();
+  return LF_OK;
+}

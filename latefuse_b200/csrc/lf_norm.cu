@@ -189,8 +189,6 @@ add_layernorm_kernel(const NormParams p, int full) {
   }
 }
 
-__device__ __forceinline__ float gelu_f32(float v) { return v * 0.5f * (1.0f + erff(v * 0.70710678118654752440f)); }
-
 // One table per 2-byte dtype and device: entry i is GELU of the value whose bits are i.
 __device__ uint16_t g_gelu_table[2][65536];
 

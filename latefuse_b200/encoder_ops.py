@@ -1,6 +1,7 @@
 """The encoder's elementwise ops on the native kernels.
 
-``add_layernorm`` is ``nn.LayerNorm(sublayer_out + residual)`` in one pass over
+``linear`` is ``nn.Linear`` (with the FFN's GELU fused when asked) on this
+library's tcgen05 GEMM; ``add_layernorm`` is ``nn.LayerNorm(sublayer_out + residual)`` in one pass over
 HBM (``src/latefuse/model/encoder.py:137,141``; with no residual, the embeddings'
 LayerNorm at ``:275``), ``gelu`` is the exact erf GELU of the FFN (``:122,139``),
 both with torch's rounding points, and ``attention_varlen`` is the encoder's
@@ -73,4 +74,28 @@ def attention_varlen(qkv: Tensor, n_heads: int, items: Tensor, scale: float, out
                                        T, 0, H, 2 * H, n_heads, H // n_heads, items.data_ptr(), items.shape[0],
                                        float(scale), out.data_ptr(), out.stride(0), nat.ptr(status))
     nat.check(rc, "lf_attention_varlen")
+    return out
+
+
+ACT_NONE, ACT_GELU = 0, 1
+
+
+def linear(x: Tensor, weight: Tensor, bias: Tensor | None, act: int = ACT_NONE,
+           out: Tensor | None = None) -> Tensor:
+    """``act(x @ weight.T + bias)`` (``act``: ``ACT_NONE`` or ``ACT_GELU``, the exact erf
+    GELU) for bf16/f16 ``x (..., K)`` and an ``nn.Linear`` weight ``(N, K)``;
+    N % 256 == 0, K % 64 == 0."""
+    dev = nat.require_cuda(x, weight, bias, out)
+    x2, ldx = _rows(x)
+    N, K = weight.shape
+    if x2.shape[1] != K:
+        raise ValueError(f"x has {x2.shape[1]} columns, weight expects {K}")
+    w = weight if weight.stride(-1) == 1 else weight.contiguous()
+    if out is None:
+        out = torch.empty(*x.shape[:-1], N, dtype=x.dtype, device=x.device)
+    o2, ldo = _rows(out)
+    b = None if bias is None else (bias if bias.dtype == x.dtype else bias.to(x.dtype)).contiguous()
+    rc = nat.lib().lf_linear(nat.stream_ptr(dev), nat.dtype_code(x.dtype), x2.data_ptr(), ldx, w.data_ptr(),
+                             w.stride(0), nat.ptr(b), o2.data_ptr(), ldo, x2.shape[0], N, K, int(act), None)
+    nat.check(rc, "lf_linear")
     return out

@@ -1,0 +1,64 @@
+"""The tcgen05 projection GEMM (``lf_linear``) against torch's ``F.linear`` (cuBLAS).
+
+Both accumulate in f32 and round once, in different orders, so outputs agree to
+the bf16/f16 rounding of the result: the serving tolerance (2e-2 relative, max
+error over max magnitude) with a far tighter norm-wise bound written below.  The
+fused GELU is the f32 formula on the rounded projection, as ``F.gelu`` applies
+it to the bf16 tensor.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from latefuse_b200 import _native as nat
+from latefuse_b200.encoder_ops import ACT_GELU, linear
+
+pytestmark = pytest.mark.gpu
+
+
+def close(ours, ref):
+    o, r = ours.float(), ref.float()
+    err = (o - r).abs().max().item()
+    assert err <= 2e-2 * r.abs().max().item(), err
+    rel = ((o - r).norm() / r.norm().clamp_min(1e-12)).item()
+    assert rel < 4e-3, rel
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m,n,k", [(16401, 3072, 1024), (300, 1024, 1024), (129, 4096, 1024), (1000, 1024, 4096),
+                                   (1, 256, 64), (128, 512, 192)])
+def test_linear_matches_torch(cuda, dtype, m, n, k):
+    g = torch.Generator(device="cpu").manual_seed(m + n + k)
+    x = torch.randn(m, k, generator=g).to(dtype).to(cuda)
+    w = (torch.randn(n, k, generator=g) * k ** -0.5).to(dtype).to(cuda)
+    b = torch.randn(n, generator=g).to(dtype).to(cuda)
+    close(linear(x, w, b), F.linear(x, w, b))
+    close(linear(x, w, None), F.linear(x, w))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_linear_gelu_matches_torch(cuda, dtype):
+    g = torch.Generator(device="cpu").manual_seed(7)
+    x = torch.randn(2000, 1024, generator=g).to(dtype).to(cuda)
+    w = (torch.randn(4096, 1024, generator=g) * 1024 ** -0.5).to(dtype).to(cuda)
+    b = torch.randn(4096, generator=g).to(dtype).to(cuda)
+    ours = linear(x, w, b, act=ACT_GELU)
+    close(ours, F.gelu(F.linear(x, w, b)))
+    # the fused GELU is exactly the formula applied to the kernel's own projection
+    xf = linear(x, w, b).float()
+    assert torch.equal(ours, (xf * 0.5 * (1.0 + torch.erf(xf * 0.70710678118654752440))).to(dtype))
+
+
+def test_linear_strided_rows_and_rejections(cuda):
+    x = torch.randn(500, 2048, device=cuda, dtype=torch.bfloat16)[:, :1024]   # row stride 2048
+    w = torch.randn(768, 1024, device=cuda, dtype=torch.bfloat16) * 0.03
+    out = torch.empty(500, 1024, device=cuda, dtype=torch.bfloat16)[:, :768]  # row stride 1024
+    linear(x, w, None, out=out)
+    close(out, F.linear(x, w))
+    with pytest.raises(nat.NativeLibraryError, match="multiple of 256"):
+        linear(x, torch.randn(100, 1024, device=cuda, dtype=torch.bfloat16), None)
+    with pytest.raises(nat.NativeLibraryError, match="bf16 or f16"):
+        linear(x.float(), w.float(), None)
