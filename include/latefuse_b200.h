@@ -142,6 +142,25 @@ int lf_lora_shrink(void* stream, int dtype,
                    int n_segs, const int32_t* tiles, int n_tiles, int n_multi,
                    void* u, int32_t* status);
 
+/* lf_lora_shrink writing u in the blocked layout lf_linear_lora reads: one
+ * block of 128 * rank elements per (128-token tile b, segment g) pair, at
+ * (m * (ceil(n_tokens / 128) + n_segs) + b + g) * 128 * rank for module m,
+ * holding the tile's rows that lie in segment g (other rows 0).  Inside a block
+ * the 8 elements [8q, 8q + 8) of tile row r sit at
+ * ((r / 8) * (rank / 8) + q) * 64 + (r % 8) * 8 (the canonical no-swizzle
+ * K-major operand layout of tcgen05.mma, so one bulk copy stages a block).
+ * u holds n_modules * (ceil(n_tokens / 128) + n_segs) * 128 * rank elements;
+ * blocks of pairs without shared tokens are not written.  Needs tile records,
+ * rank 16/32/64, bf16/f16 (LF_ERR_UNSUPPORTED otherwise). */
+int lf_lora_shrink_blocked(void* stream, int dtype,
+                           const void* x, int64_t ldx,
+                           int64_t n_tokens, int hidden, int rank,
+                           const void* cache_a, int64_t a_slot_stride, int64_t a_module_stride,
+                           int n_slots, int n_modules, const int32_t* modules,
+                           const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot,
+                           int n_segs, const int32_t* tiles, int n_tiles, int n_multi,
+                           void* u, int32_t* status);
+
 /* Expand: for every token t and op-module m,
  *     delta = round(u[m][t] . B(slot(t), m))
  *     y[t, y_col_offsets[m] + n] = accumulate ? round(y + delta) : delta     (n < hidden)
@@ -322,6 +341,28 @@ int lf_head_forward(void* stream, int dtype,
  * 16-byte aligned (LF_ERR_UNSUPPORTED / LF_ERR_INVALID otherwise). */
 int lf_linear(void* stream, int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,
               const void* bias, void* y, int64_t ldy, int64_t m, int n, int k, int act, int32_t* status);
+
+/* lf_linear with the late-fusion LoRA delta in the same accumulator:
+ *     y[t, c] = act(round(x[t] . w[c] + bias[c] + u[i][t] . B(slot(t), i)[:, c - i * module_cols]))
+ * for output column block i = c / module_cols < n_modules (columns of blocks
+ * past n_modules get no delta), with u the shrink output in the blocked layout
+ * of lf_lora_shrink_blocked (n_segs as there) and B read in place from the slot
+ * cache (cache module modules[i], (rank, module_cols) row-major per slot, as
+ * lf_lora_expand reads it).  tile_pairs / pairs (device int32) list, for each
+ * 128-token tile b, the segments with tokens in it: entries tile_pairs[b] ..
+ * tile_pairs[b + 1] - 1 of pairs, each {segment, slot}, in segment order
+ * (latefuse_b200.lora.SegmentTable builds them).  The delta is not rounded
+ * separately: the result is rounded once, where the reference rounds the
+ * projection and the delta apart and then their sum
+ * (src/latefuse/model/hf_wrapper.py:217, `output + lora_ops.output`; the fused
+ * q/k/v and attention-output projections of src/latefuse/model/encoder.py:70-80).
+ * Tokens in no segment, or in a segment whose slot is out of range, get no
+ * delta.  rank 16, 32 or 64; module_cols a multiple of 256 dividing n. */
+int lf_linear_lora(void* stream, int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,
+                   const void* bias, void* y, int64_t ldy, int64_t m, int n, int k, int act,
+                   const void* u, int rank, const void* cache_b, int64_t b_slot_stride, int64_t b_module_stride,
+                   int n_slots, int n_modules, const int32_t* modules, int module_cols, int n_segs,
+                   const int32_t* tile_pairs, const int32_t* pairs, int32_t* status);
 
 /* ------------------------------------------------------------------------
  * Encoder elementwise ops around the projections

@@ -44,6 +44,10 @@ SIGNATURES: dict[str, tuple] = {
         c_void_p, c_int, c_void_p, c_int64, c_int64, c_int, c_int,
         c_void_p, c_int64, c_int64, c_int, c_int, POINTER(c_int32),
         c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "lf_lora_shrink_blocked": (c_int, [
+        c_void_p, c_int, c_void_p, c_int64, c_int64, c_int, c_int,
+        c_void_p, c_int64, c_int64, c_int, c_int, POINTER(c_int32),
+        c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "lf_lora_expand": (c_int, [
         c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int,
         c_void_p, c_int64, c_int64, c_int, c_int, POINTER(c_int32), POINTER(c_int64),
@@ -81,6 +85,10 @@ SIGNATURES: dict[str, tuple] = {
     "lf_linear": (c_int, [
         c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int,
         c_int, c_int, c_void_p]),
+    "lf_linear_lora": (c_int, [
+        c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int,
+        c_int, c_int, c_void_p, c_int, c_void_p, c_int64, c_int64, c_int, c_int, POINTER(c_int32), c_int,
+        c_int, c_void_p, c_void_p, c_void_p]),
     "lf_add_layernorm": (c_int, [
         c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, ctypes.c_float,
         c_int64, c_int, c_void_p, c_int64]),

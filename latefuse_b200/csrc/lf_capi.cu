@@ -138,12 +138,17 @@ static int shrink_impl(cudaStream_t stream, int dtype, const void* x, int64_t ld
                        int hidden, int rank, const void* cache_a, int64_t a_slot_stride,
                        int64_t a_module_stride, int n_slots, int n_modules, const int32_t* modules,
                        const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot,
-                       int n_segs, const int32_t* tiles, int n_tiles, int n_multi, void* u, int32_t* status) {
+                       int n_segs, const int32_t* tiles, int n_tiles, int n_multi, void* u, int32_t* status,
+                       bool blocked = false) {
   const int es = elem_size(dtype);
   const bool tc = !option_force_simt() && dtype != LF_DTYPE_F32 && tc_rank(rank) && hidden % 64 == 0 &&
                   aligned16(x) && aligned16(cache_a) && aligned16(u) && (ldx * es) % 16 == 0 &&
                   (a_slot_stride * es) % 16 == 0 && (a_module_stride * es) % 16 == 0 && ldx >= hidden &&
                   (n_slots == 1 || a_slot_stride >= int64_t(hidden) * rank);
+  if (blocked && !(tc && rank >= 16 && tiles != nullptr && n_tiles > 0 && g_persistent.load()))
+    return set_error(LF_ERR_UNSUPPORTED,
+                     "lf_lora_shrink_blocked: needs bf16/f16, rank 16/32/64, hidden %% 64 == 0, tile records, "
+                     "16-byte aligned buffers and the persistent tcgen05 path");
   if (!tc && g_require_tc.load())
     return set_error(LF_ERR_UNSUPPORTED, "lf_lora_shrink: tcgen05 path required but not applicable");
   if (!tc) {
@@ -201,6 +206,7 @@ static int shrink_impl(cudaStream_t stream, int dtype, const void* x, int64_t ld
     q.n_segs = n_segs;
     q.u = u;
     q.status = status;
+    q.u_blocked = blocked ? 1 : 0;
     return run_shrink_persist(dtype, q, rank, stream);
   }
   // per-tile cluster kernel; modules in groups whose fp32 partials fit on chip
@@ -451,6 +457,24 @@ int lf_lora_shrink(void* stream, int dtype, const void* x, int64_t ldx, int64_t 
   return shrink_impl(static_cast<cudaStream_t>(stream), dtype, x, ldx, n_tokens, hidden, rank, cache_a,
                      a_slot_stride, a_module_stride, n_slots, n_modules, modules, seg_start, seg_len, seg_slot,
                      n_segs, tiles, n_tiles, n_multi, u, status);
+}
+
+int lf_lora_shrink_blocked(void* stream, int dtype, const void* x, int64_t ldx, int64_t n_tokens, int hidden,
+                           int rank, const void* cache_a, int64_t a_slot_stride, int64_t a_module_stride,
+                           int n_slots, int n_modules, const int32_t* modules, const int32_t* seg_start,
+                           const int32_t* seg_len, const int32_t* seg_slot, int n_segs, const int32_t* tiles,
+                           int n_tiles, int n_multi, void* u, int32_t* status) {
+  int rc = check_common("lf_lora_shrink_blocked", dtype, n_tokens, hidden, rank, n_slots, n_modules, modules,
+                        seg_start, seg_len, seg_slot, n_segs);
+  if (rc) return rc;
+  if ((rc = check_tiles("lf_lora_shrink_blocked", tiles, n_tiles, n_multi, n_tokens))) return rc;
+  if (x == nullptr || cache_a == nullptr || u == nullptr)
+    return set_error(LF_ERR_INVALID, "lf_lora_shrink_blocked: NULL buffer");
+  if (ldx < hidden) return set_error(LF_ERR_INVALID, "lf_lora_shrink_blocked: ldx < hidden");
+  if (n_tokens == 0) return LF_OK;
+  return shrink_impl(static_cast<cudaStream_t>(stream), dtype, x, ldx, n_tokens, hidden, rank, cache_a,
+                     a_slot_stride, a_module_stride, n_slots, n_modules, modules, seg_start, seg_len, seg_slot,
+                     n_segs, tiles, n_tiles, n_multi, u, status, true);
 }
 
 int lf_lora_expand(void* stream, int dtype, const void* u, void* y, int64_t ldy, int64_t n_tokens, int hidden,

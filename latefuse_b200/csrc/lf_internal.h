@@ -92,8 +92,14 @@ struct alignas(64) ShrinkPersistParams {
   const int32_t* seg_len;
   const int32_t* seg_slot;
   int32_t n_segs;
-  void* u;                           // (n_modules, n_tokens, rank)
+  void* u;                           // (n_modules, n_tokens, rank), or blocked (u_blocked)
   int32_t* status;
+  // u_blocked: u as (n_modules, ceil(n_tokens / 128) + n_segs) blocks of 128 rows
+  // x rank, block (tile + segment) holding the tile's rows of that segment (other
+  // rows 0), each in the canonical no-swizzle K-major layout of a tcgen05 operand
+  // (8-row x 16-byte core matrices, K direction 128 bytes apart, row groups
+  // 16 * rank bytes apart), so that one bulk copy stages a (tile, segment) pair
+  int32_t u_blocked;
 };
 
 // Packed varlen attention, head_dim 64 (see lf_attention.cu).

@@ -14,10 +14,20 @@
 //   warp 1      MMA issuer: four tcgen05.mma (M=128, N=256, K=16) per K block
 //               into one of two TMEM accumulators (256 columns each), so the
 //               epilogue of one tile overlaps the main loop of the next;
-//   warps 2-5   epilogue, one output row per thread (its TMEM lane): 32 columns
-//               per tcgen05.ld, bias and activation in f32, rounded, staged per
-//               warp in a double-buffered 32 x 32 SW64 tile and written by TMA
-//               (rows past M are clipped by the tensor map).
+//   warps 2-9   epilogue, two warps per TMEM lane quadrant (128 columns each),
+//               one output row per thread: 32 columns per tcgen05.ld, bias and
+//               activation in f32, rounded, staged per warp in a double-buffered
+//               32 x 32 SW64 tile and written by TMA (rows past M are clipped by
+//               the tensor map).
+// With LoRA (lf_linear_lora) the per-row delta joins the same accumulator: after
+// a tile's K blocks come one "delta block" per adapter segment overlapping the
+// tile's rows, staged through the same ring: the (tile, segment) block of the
+// shrink output u (written by lf_lora_shrink_blocked: the tile's rows of that
+// segment, other rows 0, in the no-swizzle K-major operand layout, so one bulk
+// copy stages it) and the segment's B factor columns (MN-major SW128, four
+// 64-column boxes straight from the slot cache, prefetched into L2 one tile
+// ahead), multiplied with K = R, so every row gets its own adapter's delta:
+// y = act(round(x W^T + bias + u B)).
 // Every wait is bounded: a timeout sets LF_STATUS_TIMEOUT and the roles unwind.
 #include "lf_common.cuh"
 #include "lf_internal.h"
@@ -31,7 +41,7 @@ constexpr int kABytes = kBM * kBK * 2;           // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;           // 32 KB
 constexpr int kStageBytes = kABytes + kBBytes;   // 48 KB
 constexpr int kStages = 4;
-constexpr int kEpiWarps = 4;
+constexpr int kEpiWarps = 8;                    // two per TMEM lane quadrant, 128 columns each
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kOutCols = 32;                     // output columns per epilogue store
 constexpr int kOutBuf = 32 * kOutCols * 2;       // one warp's 32 x 32 staging tile: 2 KB
@@ -41,13 +51,35 @@ struct alignas(64) LinearParams {
   CUtensorMap x_map;  // 2D {K, M}, box {64, 128}, SW128
   CUtensorMap w_map;  // 2D {K, N}, box {64, 256}, SW128
   CUtensorMap y_map;  // 2D {N, M}, box {32, 32}, SW64
+  CUtensorMap b_map[kMaxModules];     // LoRA: 3D {module_cols, R, n_slots}, box {64, R, 1}, SW128
+  const void* u;                      // LoRA: blocked shrink output (lf_lora_shrink_blocked)
+  const void* b_ptr[kMaxModules];     // LoRA: (slot 0, module i) B factors, for L2 prefetch
+  int64_t b_slot_stride;              // elements
+  int32_t n_slots;
   const void* bias;   // N entries or null
+  const int32_t* tile_pairs;          // LoRA: tile b's (segment, slot) pairs are entries
+  const int32_t* pairs;               //   tile_pairs[b] .. tile_pairs[b + 1] of pairs; null: no delta
+  int32_t n_segs;
+  int32_t rank;
+  int32_t n_mod;                      // output column block i (module_cols wide) takes module i's delta
+  int32_t module_cols;
+  int64_t m_rows;
   int64_t n_tiles;
   int32_t n_tiles_n;
   int32_t n_kb;
   int32_t act;        // LF_ACT_*
   int32_t* status;
 };
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 
 __device__ __forceinline__ bool aborted_flag(const int32_t* f) {
   return *reinterpret_cast<const volatile int32_t*>(f) != 0;
@@ -104,8 +136,28 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     if (lane == 0) {
       int kk = 0;
       bool stop = false;
+      // the B factors of a tile's segments, into L2 (whole rank x module_cols block)
+      auto prefetch_b = [&](int64_t tt) {
+        if (p.pairs == nullptr || tt >= p.n_tiles) return;
+        const int pmod = int32_t(tt % p.n_tiles_n) * kBN / p.module_cols;
+        if (pmod >= p.n_mod) return;
+        const int mb = int32_t(tt / p.n_tiles_n);
+        for (int q = __ldg(p.tile_pairs + mb), qe = __ldg(p.tile_pairs + mb + 1); q < qe; ++q) {
+          const int32_t slot = __ldg(p.pairs + 2 * q + 1);
+          if (slot >= 0 && slot < p.n_slots)
+            prefetch_l2(static_cast<const T*>(p.b_ptr[pmod]) + int64_t(slot) * p.b_slot_stride,
+                        uint32_t(p.rank) * uint32_t(p.module_cols) * 2u);
+        }
+      };
+      prefetch_b(blockIdx.x);
       for (int64_t t = blockIdx.x; t < p.n_tiles && !stop; t += gridDim.x) {
         const int32_t m0 = int32_t(t / p.n_tiles_n) * kBM, n0 = int32_t(t % p.n_tiles_n) * kBN;
+        const int mod = p.pairs != nullptr ? n0 / p.module_cols : p.n_mod;
+        int q0 = 0, q1 = 0;
+        if (mod < p.n_mod) {  // loaded now, used after the K blocks
+          q0 = __ldg(p.tile_pairs + m0 / kBM);
+          q1 = __ldg(p.tile_pairs + m0 / kBM + 1);
+        }
         for (int kb = 0; kb < p.n_kb; ++kb, ++kk) {
           const int s = kk % kStages;
           if (aborted_flag(s_abort) || !mbar_wait(bar(EMPTY + s), ((kk / kStages) & 1) ^ 1)) {
@@ -118,6 +170,28 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
           tma_load_2d(st, &p.x_map, bar(FULL + s), kb * kBK, m0);
           tma_load_2d(st + kABytes, &p.w_map, bar(FULL + s), kb * kBK, n0);
         }
+        if (!stop) prefetch_b(t + gridDim.x);  // the ring is full here: the producer has time
+        if (stop || mod >= p.n_mod) continue;
+        const int32_t n_loc = n0 - mod * p.module_cols;
+        for (int q = q0; q < q1; ++q) {
+          const int j = __ldg(p.pairs + 2 * q);
+          const int s = kk % kStages;
+          if (aborted_flag(s_abort) || !mbar_wait(bar(EMPTY + s), ((kk / kStages) & 1) ^ 1)) {
+            if (!aborted_flag(s_abort)) fail();
+            stop = true;
+            break;
+          }
+          const uint32_t st = s_stage0 + s * kStageBytes;
+          mbar_arrive_expect_tx(bar(FULL + s), 768 * p.rank);  // u 128 x R + B R x 256
+          // the (tile, segment) block of u: this tile's rows of segment j, other rows 0
+          const int64_t n_blk = (p.m_rows + kBM - 1) / kBM + p.n_segs;
+          bulk_load(st, static_cast<const T*>(p.u) + (int64_t(mod) * n_blk + m0 / kBM + j) * kBM * p.rank,
+                    256 * p.rank, bar(FULL + s));
+          const int32_t slot = __ldg(p.pairs + 2 * q + 1);  // out of range: zero fill, no delta
+          for (int b = 0; b < kBN / 64; ++b)
+            tma_load_3d(st + kABytes + b * p.rank * 128, &p.b_map[mod], bar(FULL + s), n_loc + b * 64, 0, slot);
+          ++kk;
+        }
       }
       if (aborted_flag(s_abort)) {  // loads nobody consumed land before the CTA exits (bounded)
         for (int q = (kk > kStages ? kk - kStages : 0); q < kk; ++q)
@@ -125,21 +199,29 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------ MMA issuer (lane 0)
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_f16(DT<T>::umma_fmt, kBM, kBN, 0, 0);
+      const uint32_t idesc_d = umma_idesc_f16(DT<T>::umma_fmt, kBM, kBN, 0, 1);
       int kk = 0, it = 0;
       bool stop = false;
+      auto wait = [&](uint32_t b, uint32_t parity) {
+        if (aborted_flag(s_abort)) return false;
+        if (mbar_wait(b, parity)) return true;
+        if (!aborted_flag(s_abort)) fail();
+        return false;
+      };
       for (int64_t t = blockIdx.x; t < p.n_tiles && !stop; t += gridDim.x, ++it) {
         const int a = it & 1;
-        if (aborted_flag(s_abort) || !mbar_wait(bar(ACC_EMPTY + a), ((it >> 1) & 1) ^ 1)) {
-          if (!aborted_flag(s_abort)) fail();
-          break;
-        }
+        const int32_t m0 = int32_t(t / p.n_tiles_n) * kBM, n0 = int32_t(t % p.n_tiles_n) * kBN;
+        const int mod = p.pairs != nullptr ? n0 / p.module_cols : p.n_mod;
+        int n_delta = 0;
+        if (mod < p.n_mod)  // loaded now, used after the K blocks
+          n_delta = __ldg(p.tile_pairs + m0 / kBM + 1) - __ldg(p.tile_pairs + m0 / kBM);
+        if (!wait(bar(ACC_EMPTY + a), ((it >> 1) & 1) ^ 1)) break;
         for (int kb = 0; kb < p.n_kb; ++kb, ++kk) {
           const int s = kk % kStages;
-          if (aborted_flag(s_abort) || !mbar_wait(bar(FULL + s), (kk / kStages) & 1)) {
-            if (!aborted_flag(s_abort)) fail();
+          if (!wait(bar(FULL + s), (kk / kStages) & 1)) {
             stop = true;
             break;
           }
@@ -151,6 +233,23 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
                      idesc, (kb | q) != 0 ? 1u : 0u);
           umma_commit(bar(EMPTY + s));
         }
+        if (!stop && n_delta > 0) {
+          const int nq = p.rank / 8;  // 16-byte chunks of a u row
+          for (int d = 0; d < n_delta; ++d) {
+            const int s = kk % kStages;
+            if (!wait(bar(FULL + s), (kk / kStages) & 1)) {
+              stop = true;
+              break;
+            }
+            const uint32_t st = s_stage0 + s * kStageBytes;
+            tc_fence_after();
+            for (int q = 0; q < p.rank / 16; ++q)
+              umma_f16(tmem + a * kBN, smem_desc(st + q * 256, 128, uint32_t(nq) * 128, 0),
+                       smem_desc(st + kABytes + q * 2048, p.rank * 128, 1024, 2), idesc_d, 1u);
+            umma_commit(bar(EMPTY + s));
+            ++kk;
+          }
+        }
         if (!stop) umma_commit(bar(ACC_FULL + a));
       }
       if (aborted_flag(s_abort)) {  // every issued MMA finishes before TMEM is released (bounded)
@@ -159,8 +258,9 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2..5)
+    // ------------------------------------------------------------ epilogue (warps 2..9)
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;  // columns [128 half, 128 half + 128) of the tile
     const uint32_t taddr = tmem + (uint32_t(quad * 32) << 16);
     const uint32_t my_out = s_out0 + (warp - 2) * 2 * kOutBuf;
     const T* bias = static_cast<const T*>(p.bias);
@@ -175,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
       }
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      for (int c = 0; c < kBN / kOutCols; ++c) {
+      for (int c = half * (kBN / kOutCols / 2); c < (half + 1) * (kBN / kOutCols / 2); ++c) {
         uint32_t v[32];
         tmem_ld32(taddr + a * kBN + c * kOutCols, v);
         const int col0 = n0 + c * kOutCols;
@@ -246,51 +346,108 @@ bool aligned16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) ==
 
 using namespace lf;
 
-extern "C" int lf_linear(void* stream, int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,
-                         const void* bias, void* y, int64_t ldy, int64_t m, int n, int k, int act,
-                         int32_t* status) {
+// Shared by lf_linear and lf_linear_lora; `lora` null for the plain GEMM.
+struct LoraArgs {
+  const void* u;
+  int rank;
+  const void* cache_b;
+  int64_t b_slot_stride, b_module_stride;
+  int n_slots, n_modules;
+  const int32_t* modules;
+  int module_cols;
+  int n_segs;
+  const int32_t *tile_pairs, *pairs;
+};
+
+static int linear_impl(const char* fn, void* stream, int dtype, const void* x, int64_t ldx, const void* w,
+                       int64_t ldw, const void* bias, void* y, int64_t ldy, int64_t m, int n, int k, int act,
+                       const LoraArgs* lora, int32_t* status) {
   if (dtype != LF_DTYPE_BF16 && dtype != LF_DTYPE_F16)
-    return set_error(LF_ERR_UNSUPPORTED, "lf_linear: dtype %d (bf16 or f16 only)", dtype);
-  if (act != LF_ACT_NONE && act != LF_ACT_GELU) return set_error(LF_ERR_INVALID, "lf_linear: unknown act %d", act);
+    return set_error(LF_ERR_UNSUPPORTED, "%s: dtype %d (bf16 or f16 only)", fn, dtype);
+  if (act != LF_ACT_NONE && act != LF_ACT_GELU) return set_error(LF_ERR_INVALID, "%s: unknown act %d", fn, act);
   if (m < 0 || m > INT32_MAX || n <= 0 || k <= 0 || n % kBN != 0 || k % kBK != 0)
-    return set_error(LF_ERR_UNSUPPORTED, "lf_linear: n %d must be a multiple of 256 and k %d of 64", n, k);
-  if (x == nullptr || w == nullptr || y == nullptr) return set_error(LF_ERR_INVALID, "lf_linear: null x, w or y");
-  if (ldx < k || ldw < k || ldy < n) return set_error(LF_ERR_INVALID, "lf_linear: a row stride is below its row");
+    return set_error(LF_ERR_UNSUPPORTED, "%s: n %d must be a multiple of 256 and k %d of 64", fn, n, k);
+  if (x == nullptr || w == nullptr || y == nullptr) return set_error(LF_ERR_INVALID, "%s: null x, w or y", fn);
+  if (ldx < k || ldw < k || ldy < n) return set_error(LF_ERR_INVALID, "%s: a row stride is below its row", fn);
   if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (bias != nullptr && !aligned16(bias)) || (ldx * 2) % 16 ||
       (ldw * 2) % 16 || (ldy * 2) % 16)
-    return set_error(LF_ERR_INVALID, "lf_linear: pointers and row strides must be 16-byte aligned");
+    return set_error(LF_ERR_INVALID, "%s: pointers and row strides must be 16-byte aligned", fn);
+  if (lora != nullptr) {
+    const LoraArgs& L = *lora;
+    if (L.rank != 16 && L.rank != 32 && L.rank != 64)
+      return set_error(LF_ERR_UNSUPPORTED, "%s: rank %d (16, 32 or 64)", fn, L.rank);
+    if (L.n_modules < 1 || L.n_modules > kMaxModules || L.modules == nullptr)
+      return set_error(LF_ERR_INVALID, "%s: n_modules %d not in [1, %d]", fn, L.n_modules, kMaxModules);
+    if (L.module_cols <= 0 || L.module_cols % kBN != 0 || n % L.module_cols != 0)
+      return set_error(LF_ERR_UNSUPPORTED, "%s: module_cols %d must be a multiple of 256 dividing n %d", fn,
+                       L.module_cols, n);
+    if (L.u == nullptr || L.cache_b == nullptr || L.n_slots <= 0 || L.n_segs < 0 || L.tile_pairs == nullptr ||
+        L.pairs == nullptr)
+      return set_error(LF_ERR_INVALID, "%s: null u, cache_b or pair table", fn);
+    for (int i = 0; i < L.n_modules; ++i)
+      if (L.modules[i] < 0) return set_error(LF_ERR_INVALID, "%s: negative module index", fn);
+    if (!aligned16(L.u) || !aligned16(L.cache_b) || (L.b_slot_stride * 2) % 16 || (L.b_module_stride * 2) % 16 ||
+        (L.n_slots > 1 && L.b_slot_stride < int64_t(L.module_cols) * L.rank))
+      return set_error(LF_ERR_INVALID, "%s: u / cache_b alignment or slot stride", fn);
+  }
   if (m == 0) return LF_OK;
   PFN_encodeTiled enc = get_encode_tiled();
   if (enc == nullptr) return set_error(LF_ERR_DRIVER, "cuTensorMapEncodeTiled unavailable");
   LinearParams p;
   memset(&p, 0, sizeof(p));
   const CUtensorMapDataType dt = dtype == LF_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const cuuint32_t estr[2] = {1, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  auto tmap = [&](CUtensorMap* map, int rank, const void* base, const cuuint64_t* dims, const cuuint64_t* strides,
+                  const cuuint32_t* box, CUtensorMapSwizzle swz, const char* what) {
+    if (enc(map, dt, cuuint32_t(rank), const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return set_error(LF_ERR_CUDA, "%s: cuTensorMapEncodeTiled(%s) failed", fn, what);
+    return int(LF_OK);
+  };
+  int rc;
   {
     const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(m)};
     const cuuint64_t strides[1] = {cuuint64_t(ldx) * 2};
     const cuuint32_t box[2] = {kBK, kBM};
-    if (enc(&p.x_map, dt, 2, const_cast<void*>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return set_error(LF_ERR_CUDA, "cuTensorMapEncodeTiled(x) failed");
+    if ((rc = tmap(&p.x_map, 2, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "x"))) return rc;
   }
   {
     const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(n)};
     const cuuint64_t strides[1] = {cuuint64_t(ldw) * 2};
     const cuuint32_t box[2] = {kBK, kBN};
-    if (enc(&p.w_map, dt, 2, const_cast<void*>(w), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return set_error(LF_ERR_CUDA, "cuTensorMapEncodeTiled(w) failed");
+    if ((rc = tmap(&p.w_map, 2, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "w"))) return rc;
   }
   {
     const cuuint64_t dims[2] = {cuuint64_t(n), cuuint64_t(m)};
     const cuuint64_t strides[1] = {cuuint64_t(ldy) * 2};
     const cuuint32_t box[2] = {kOutCols, 32};
-    if (enc(&p.y_map, dt, 2, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return set_error(LF_ERR_CUDA, "cuTensorMapEncodeTiled(y) failed");
+    if ((rc = tmap(&p.y_map, 2, y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B, "y"))) return rc;
+  }
+  if (lora != nullptr) {
+    const LoraArgs& L = *lora;
+    const cuuint32_t R = cuuint32_t(L.rank);
+    p.u = L.u;
+    for (int i = 0; i < L.n_modules; ++i) {
+      const void* b = static_cast<const uint8_t*>(L.cache_b) + int64_t(L.modules[i]) * L.b_module_stride * 2;
+      const int64_t ss = L.n_slots == 1 ? int64_t(L.module_cols) * L.rank : L.b_slot_stride;
+      p.b_ptr[i] = b;
+      p.b_slot_stride = ss;
+      const cuuint64_t dims[3] = {cuuint64_t(L.module_cols), R, cuuint64_t(L.n_slots)};
+      const cuuint64_t strides[2] = {cuuint64_t(L.module_cols) * 2, cuuint64_t(ss) * 2};
+      const cuuint32_t box[3] = {64, R, 1};
+      if ((rc = tmap(&p.b_map[i], 3, b, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "b"))) return rc;
+    }
+    p.tile_pairs = L.tile_pairs;
+    p.pairs = L.pairs;
+    p.n_segs = L.n_segs;
+    p.rank = L.rank;
+    p.n_slots = L.n_slots;
+    p.n_mod = L.n_modules;
+    p.module_cols = L.module_cols;
   }
   p.bias = bias;
+  p.m_rows = m;
   p.n_tiles_n = n / kBN;
   p.n_tiles = ((m + kBM - 1) / kBM) * p.n_tiles_n;
   p.n_kb = k / kBK;
@@ -309,4 +466,21 @@ extern "C" int lf_linear(void* stream, int dtype, const void* x, int64_t ldx, co
   if (e != cudaSuccess) return cuda_error(e, "launch linear");
   count_launch();
   return LF_OK;
+}
+
+extern "C" int lf_linear(void* stream, int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,
+                         const void* bias, void* y, int64_t ldy, int64_t m, int n, int k, int act,
+                         int32_t* status) {
+  return linear_impl("lf_linear", stream, dtype, x, ldx, w, ldw, bias, y, ldy, m, n, k, act, nullptr, status);
+}
+
+extern "C" int lf_linear_lora(void* stream, int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,
+                              const void* bias, void* y, int64_t ldy, int64_t m, int n, int k, int act,
+                              const void* u, int rank, const void* cache_b, int64_t b_slot_stride,
+                              int64_t b_module_stride, int n_slots, int n_modules, const int32_t* modules,
+                              int module_cols, int n_segs, const int32_t* tile_pairs, const int32_t* pairs,
+                              int32_t* status) {
+  LoraArgs L{u, rank, cache_b, b_slot_stride, b_module_stride, n_slots, n_modules, modules, module_cols,
+             n_segs, tile_pairs, pairs};
+  return linear_impl("lf_linear_lora", stream, dtype, x, ldx, w, ldw, bias, y, ldy, m, n, k, act, &L, status);
 }

@@ -651,11 +651,33 @@ lora_shrink_persist_kernel(const __grid_constant__ ShrinkPersistParams p, int st
         if (work) {
           for (int m = 0; m < n_mod; ++m) {
             T* dst = reinterpret_cast<T*>(p.u) + (int64_t(m) * p.n_tokens + t) * R;
+            // blocked: one 128 x R block per (tile, segment) pair, index tile + segment
+            const int64_t n_blk = (p.n_tokens + kTile - 1) / kTile + p.n_segs;
             for (int jj = 0; jj < kp; ++jj) {
 #pragma unroll
               for (int c = 0; c < RP / 16; ++c) {
                 float v[16];
                 tmem_ld16(tmem + (uint32_t(quad * 32) << 16) + a * acc_cols + (jj * n_mod + m) * RP + c * 16, v);
+                if (p.u_blocked) {
+                  // every row of the tile: its product if it lies in this segment, else 0
+                  T* blk = reinterpret_cast<T*>(p.u) +
+                           (int64_t(m) * n_blk + rec.x + rec.y + j0 + jj) * (kTile * R);
+                  const bool in = j_row == jj && t < p.n_tokens;
+#pragma unroll
+                  for (int h = 0; h < 2; ++h) {
+                    if (c * 16 + h * 8 < R) {
+                      uint4 pk;
+                      pk.x = Pack2<T>::pack(in ? v[h * 8 + 0] : 0.f, in ? v[h * 8 + 1] : 0.f);
+                      pk.y = Pack2<T>::pack(in ? v[h * 8 + 2] : 0.f, in ? v[h * 8 + 3] : 0.f);
+                      pk.z = Pack2<T>::pack(in ? v[h * 8 + 4] : 0.f, in ? v[h * 8 + 5] : 0.f);
+                      pk.w = Pack2<T>::pack(in ? v[h * 8 + 6] : 0.f, in ? v[h * 8 + 7] : 0.f);
+                      // 8-element chunk q of tile row r in core matrix (r / 8, q)
+                      const int q = c * 2 + h;
+                      *reinterpret_cast<uint4*>(blk + ((row >> 3) * (R / 8) + q) * 64 + (row & 7) * 8) = pk;
+                    }
+                  }
+                  continue;
+                }
                 // a row in no segment of this pass writes zeros once (with jj == 0)
                 if (mine && (j_row == jj || (j_row < 0 && jj == 0))) {
 #pragma unroll
@@ -666,7 +688,8 @@ lora_shrink_persist_kernel(const __grid_constant__ ShrinkPersistParams p, int st
                       pk.y = Pack2<T>::pack(j_row < 0 ? 0.f : v[h * 8 + 2], j_row < 0 ? 0.f : v[h * 8 + 3]);
                       pk.z = Pack2<T>::pack(j_row < 0 ? 0.f : v[h * 8 + 4], j_row < 0 ? 0.f : v[h * 8 + 5]);
                       pk.w = Pack2<T>::pack(j_row < 0 ? 0.f : v[h * 8 + 6], j_row < 0 ? 0.f : v[h * 8 + 7]);
-                      *reinterpret_cast<uint4*>(dst + c * 16 + h * 8) = pk;
+                      const int64_t off = (c * 2 + h) * 8;
+                      *reinterpret_cast<uint4*>(dst + off) = pk;
                     }
                   }
                 }

@@ -55,7 +55,8 @@ class SegmentTable:
         records = _tile_records(starts, lengths, slots) if records else []
         self.n_tiles = len(records) // 4
         self.n_multi = sum(1 for i in range(2, len(records), 4) if records[i] != 1)
-        self.host = torch.tensor(records + starts + lengths + slots, dtype=torch.int32)
+        pairs = _tile_pairs(starts, lengths, slots, self.n_tokens) if self.use_records else []
+        self.host = torch.tensor(records + starts + lengths + slots + pairs, dtype=torch.int32)
         if self.device.type == "cuda":
             self.table = self.host.pin_memory().to(self.device, non_blocking=True)
         else:
@@ -77,6 +78,38 @@ class SegmentTable:
         if not self.use_records:
             return base, base + 4 * n, base + 8 * n, None, 0, 0
         return base + r, base + r + 4 * n, base + r + 8 * n, base, self.n_tiles, self.n_multi
+
+    def pair_ptrs(self) -> tuple[int, int]:
+        """(tile_pairs, pairs) for ``lf_linear_lora``: per 128-token tile b, the
+        (segment, slot) pairs of the segments with tokens in it are entries
+        ``tile_pairs[b] .. tile_pairs[b + 1]`` of ``pairs`` (two int32 each), in
+        segment order.  Built with the tile records."""
+        if not self.use_records:
+            raise ValueError("the pair table is built with the tile records")
+        off = self.table.data_ptr() + 16 * self.n_tiles + 12 * self.n_segs
+        n_rt = (self.n_tokens + 127) // 128
+        return off, off + 4 * (n_rt + 1)
+
+
+def _tile_pairs(starts, lengths, slots, n_tokens: int) -> list[int]:
+    """``[tile_pairs (n_rt + 1) | pairs (2 per entry)]``: the (segment, slot) pairs of
+    every 128-token tile, by tile then segment; segments of no tokens are left out."""
+    tile = nat.TILE_TOKENS
+    n_rt = (int(n_tokens) + tile - 1) // tile
+    st = np.asarray(starts, dtype=np.int64)
+    ln = np.asarray(lengths, dtype=np.int64)
+    seg = np.nonzero(ln > 0)[0]
+    if seg.size == 0:
+        return [0] * (n_rt + 1)
+    t0 = st[seg] // tile
+    nt = (st[seg] + ln[seg] - 1) // tile - t0 + 1
+    seg_of = np.repeat(seg, nt)
+    tile_of = np.repeat(t0, nt) + np.arange(int(nt.sum())) - np.repeat(np.cumsum(nt) - nt, nt)
+    order = np.argsort(tile_of, kind="stable")
+    seg_of, tile_of = seg_of[order], tile_of[order]
+    begin = np.searchsorted(tile_of, np.arange(n_rt + 1), side="left")
+    pairs = np.stack([seg_of, np.asarray(slots, dtype=np.int64)[seg_of]], axis=1)
+    return begin.tolist() + pairs.reshape(-1).tolist()
 
 
 def _tile_records(starts, lengths, slots) -> list[int]:
@@ -222,6 +255,65 @@ def lora_apply_into(x: Tensor, y: Tensor, cache: FactorCache, segs: SegmentTable
         workspace.data_ptr(), workspace.numel() * workspace.element_size(),
         nat.ptr(status))
     nat.check(rc, "lf_lora_apply_into")
+
+
+def blocked_u(n_modules: int, n_tokens: int, n_segs: int, rank: int, dtype: torch.dtype, device) -> Tensor:
+    """An empty shrink output in the blocked layout of :func:`lora_shrink_blocked`:
+    one 128 x rank block per (token tile, segment) pair, per module."""
+    return torch.empty(n_modules, ((n_tokens + 127) // 128 + n_segs) * 128, rank, dtype=dtype, device=device)
+
+
+def _blocked_elems(n_modules: int, n_tokens: int, n_segs: int, rank: int) -> int:
+    return n_modules * ((n_tokens + 127) // 128 + n_segs) * 128 * rank
+
+
+def lora_shrink_blocked(x: Tensor, u: Tensor, cache: FactorCache, segs: SegmentTable, modules,
+                        status: Tensor | None = None) -> None:
+    """:func:`lora_shrink` writing ``u`` (from :func:`blocked_u`) in the tile-blocked
+    operand layout that :func:`linear_lora` stages with one bulk copy per tile."""
+    dev = nat.require_cuda(x, u, segs.table)
+    x2, ldx = _rows(x)
+    T = x2.shape[0]
+    if u.numel() < _blocked_elems(len(modules), T, segs.n_segs, cache.rank) or not u.is_contiguous():
+        raise ValueError("u must be a contiguous blocked_u(n_modules, n_tokens, n_segs, rank) buffer")
+    rc = nat.lib().lf_lora_shrink_blocked(
+        nat.stream_ptr(dev), nat.dtype_code(x.dtype), x2.data_ptr(), ldx, T,
+        cache.hidden, cache.rank, cache.a_ptr, cache.a_slot_stride, cache.a_module_stride,
+        cache.n_slots, len(modules), nat.i32_array(modules), *_seg_args(segs),
+        u.data_ptr(), nat.ptr(status))
+    nat.check(rc, "lf_lora_shrink_blocked")
+
+
+def linear_lora(x: Tensor, weight: Tensor, bias: Tensor | None, u: Tensor, cache: FactorCache,
+                segs: SegmentTable, modules, module_cols: int, act: int = 0, out: Tensor | None = None,
+                status: Tensor | None = None) -> Tensor:
+    """``act(x @ weight.T + bias + delta)`` on the tcgen05 GEMM with the LoRA delta in
+    its accumulator: output columns ``[i * module_cols, (i + 1) * module_cols)`` get
+    ``u[i] @ B(slot(t), modules[i])`` (``u`` from :func:`lora_shrink_blocked`).
+    One rounding of the sum, where the reference rounds the projection and the delta
+    apart; see ``lf_linear_lora``."""
+    dev = nat.require_cuda(x, weight, bias, u, segs.table, out, status)
+    x2, ldx = _rows(x)
+    N, K = weight.shape
+    if u.numel() < _blocked_elems(len(modules), x2.shape[0], segs.n_segs, cache.rank):
+        raise ValueError("u must be a blocked_u(n_modules, n_tokens, n_segs, rank) buffer")
+    w = weight if weight.stride(-1) == 1 else weight.contiguous()
+    if out is None:
+        out = torch.empty(*x.shape[:-1], N, dtype=x.dtype, device=x.device)
+    o2 = out.reshape(-1, N)
+    if o2.data_ptr() != out.data_ptr() or o2.stride(-1) != 1:
+        raise ValueError("out must be viewable as rows without a copy")
+    b = None if bias is None else (bias if bias.dtype == x.dtype else bias.to(x.dtype)).contiguous()
+    if segs.n_tokens != x2.shape[0]:
+        raise ValueError(f"segment table for {segs.n_tokens} tokens, x has {x2.shape[0]}")
+    tp, pp = segs.pair_ptrs()
+    rc = nat.lib().lf_linear_lora(
+        nat.stream_ptr(dev), nat.dtype_code(x.dtype), x2.data_ptr(), ldx, w.data_ptr(), w.stride(0), nat.ptr(b),
+        o2.data_ptr(), o2.stride(0), x2.shape[0], N, K, int(act), u.data_ptr(), cache.rank, cache.b_ptr,
+        cache.b_slot_stride, cache.b_module_stride, cache.n_slots, len(modules), nat.i32_array(modules),
+        int(module_cols), segs.n_segs, tp, pp, nat.ptr(status))
+    nat.check(rc, "lf_linear_lora")
+    return out
 
 
 def lora_shrink(x: Tensor, u: Tensor, cache: FactorCache, segs: SegmentTable, modules,

@@ -89,8 +89,11 @@ def test_pack_rows_layout():
     assert pb.row_lengths.tolist() == lengths
     segs = pb.segments
     assert segs.n_segs == 2 and segs.slots == [3, 5]
-    starts, seg_lens = segs.host[4 * segs.n_tiles:].view(3, -1)[:2].tolist()
+    n = segs.n_segs
+    starts, seg_lens = segs.host[4 * segs.n_tiles:4 * segs.n_tiles + 3 * n].view(3, -1)[:2].tolist()
     assert starts == [0, 3] and seg_lens == [3, 10]
+    # per-tile (segment, slot) pairs after the segment arrays: one tile, both segments
+    assert segs.host[4 * segs.n_tiles + 3 * n:].tolist() == [0, 2, 0, 3, 1, 5]
     # attention work list: one record per (sequence, 128-query tile)
     assert pb.attn_items.tolist() == [[0, 2, 0, 0], [2, 1, 0, 0], [3, 6, 0, 0], [9, 4, 0, 0]]
     arange = pack_rows(ids, lengths, slots, None, None, torch.device("cpu"))  # BERT numbering
