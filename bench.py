@@ -48,6 +48,7 @@ METRIC = "sequences/sec at bge-m3 shape, 10k adapters; LoRA-kernel HBM GB/s vs p
 NCU_TRAFFIC_PER_OP_R16 = (182.85e6 + 70.34e6) / 2
 TARGETS = ["query", "key", "value", "dense"]
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS_SUSTAINED = 1400.0
 
 
 def bge_m3_config(layers: int = 24):
@@ -94,6 +95,18 @@ def measured_hbm_peak() -> tuple[float, str]:
         except Exception:
             pass
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def measured_tensor_peak() -> tuple[float, str]:
+    """Dense bf16 TFLOP/s for a kernel timed inside a long step: the sustained figure."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return (float(json.loads(p.read_text())["bf16_tflops_sustained"]),
+                    "measured (MEASURED_PEAKS.json bf16_tflops_sustained)")
+        except Exception:
+            pass
+    return FALLBACK_BF16_TFLOPS_SUSTAINED, "fallback (sustained)"
 
 
 class ClockSampler:
@@ -266,12 +279,17 @@ def run_ours(args):
     ms = start.elapsed_time(end) / args.steps
     events = model.lora_events
     model.lora_events = None
-    lora_ms_total = sum(s.elapsed_time(e) for _, s, e in events)
-    lora_ms_step = lora_ms_total / args.steps
+    by_kind: dict[str, list[float]] = {}
+    for kind, s_ev, e_ev in events:
+        by_kind.setdefault(kind, []).append(s_ev.elapsed_time(e_ev))
+    lora_ms_step = sum(sum(v) for v in by_kind.values()) / args.steps
+    fused = "qkv_gemm" in by_kind
+    gemm_ms = statistics.median(by_kind["qkv_gemm"]) if fused else 0.0
+    shrink_ms_step = sum(sum(by_kind.get(k, [])) for k in ("qkv_shrink", "dense_shrink")) / args.steps
     if world > 1:
-        t = torch.tensor([ms, lora_ms_step], device=dev)
+        t = torch.tensor([ms, lora_ms_step, gemm_ms, shrink_ms_step], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, lora_ms_step = t.tolist()
+        ms, lora_ms_step, gemm_ms, shrink_ms_step = t.tolist()
     emb.check_device_status()
 
     segs = packed.segments if packed is not None else batch.segments
@@ -279,6 +297,49 @@ def run_ours(args):
     bytes_step, ops_step = lora_bytes_per_step(segs, n_unique, args.layers, H, args.rank)
     achieved = bytes_step / (lora_ms_step * 1e-3) / 1e9
     peak, peak_src = measured_hbm_peak()
+    if fused:
+        # the dominant kernel of this library: the q/k/v projection GEMM with the LoRA
+        # delta in its accumulator (tensor-bound); and the shrink launches (HBM-bound)
+        T_tok = segs.n_tokens
+        R = args.rank
+        gemm_flops = 2.0 * T_tok * 3 * H * (H + R)
+        tpeak, tpeak_src = measured_tensor_peak()
+        tach = gemm_flops / (gemm_ms * 1e-3) / 1e12
+        n_blk = (T_tok + 127) // 128 + segs.n_segs
+        shrink_bytes_step = args.layers * sum(
+            T_tok * H * 2 + n_unique * m * H * R * 2 + m * n_blk * 128 * R * 2 for m in (3, 1))
+        shrink_gbs = shrink_bytes_step / (shrink_ms_step * 1e-3) / 1e9
+        roofline = {
+            "bound": "tensor", "achieved": tach, "peak": tpeak, "unit": "TFLOP/s", "frac": tach / tpeak,
+            "traffic": None,
+            "kernel": "lf_linear_lora: q/k/v projection (T x 3072 x 1024) with the per-row LoRA delta in the "
+                      "tcgen05 accumulator (one launch per layer)",
+            "algorithmic_flops_per_launch": gemm_flops, "launch_ms": gemm_ms, "peak_source": tpeak_src,
+        }
+        lora_hbm = {
+            "kernel": "lf_lora_shrink_blocked (per layer: q/k/v and attention-output shrinks)",
+            "achieved": shrink_gbs, "peak": peak, "unit": "GB/s", "frac": shrink_gbs / peak,
+            "algorithmic_bytes_per_step": shrink_bytes_step, "ms_per_step": shrink_ms_step, "peak_source": peak_src,
+            "note": "the expand no longer exists as a kernel: the delta (u and B reads, K = rank MMAs) runs inside "
+                    "the projection GEMM",
+        }
+    else:
+        roofline = {
+            "bound": "hbm",
+            "achieved": achieved,
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "traffic": (NCU_TRAFFIC_PER_OP_R16 if packed is not None and args.rank == 16 and args.batch == 64
+                        and args.seq == 512 else None),
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per LoRA op (shrink + expand) "
+                              "of this workload; y writes still in L2 at kernel end are not counted",
+            "kernel": "LoRA delta op = tcgen05 shrink + expand launches (per layer: q/k/v op, dense op)",
+            "algorithmic_bytes_per_op": bytes_step / ops_step,
+            "op_ms": lora_ms_step / ops_step,
+            "peak_source": peak_src,
+        }
+        lora_hbm = None
 
     # ---- end to end through the public API from pinned host buffers ----
     e2e = None
@@ -354,26 +415,16 @@ def run_ours(args):
             "unique_tenants_per_batch": n_unique,
             "l2": "inputs larger than L2: every step streams 1.1 GB of weights and >0.5 GB of activations",
         },
-        "roofline": {
-            "bound": "hbm",
-            "achieved": achieved,
-            "peak": peak,
-            "unit": "GB/s",
-            "frac": achieved / peak,
-            "traffic": (NCU_TRAFFIC_PER_OP_R16 if packed is not None and args.rank == 16 and args.batch == 64
-                        and args.seq == 512 else None),
-            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per LoRA op (shrink + expand) "
-                              "of this workload; y writes still in L2 at kernel end are not counted",
-            "kernel": "LoRA delta op = tcgen05 shrink + expand launches (per layer: q/k/v op, dense op)",
-            "algorithmic_bytes_per_op": bytes_step / ops_step,
-            "op_ms": lora_ms_step / ops_step,
-            "peak_source": peak_src,
-        },
+        "roofline": roofline,
         "lora_share_of_step": lora_ms_step / ms,
+        "lora_share_note": ("shrink + fused projection GEMM launches (the GEMM includes the base projection)"
+                            if fused else "shrink + expand launches"),
         "gpu_launches": launches,
         "gpu_launches_per_step": launches / args.steps,
         "clocks": clocks.summary(),
     }
+    if lora_hbm is not None:
+        line["lora_hbm"] = lora_hbm
     if e2e is not None:
         line["e2e"] = e2e
     if cpu is not None:

@@ -31,8 +31,8 @@ from torch.utils.hooks import RemovableHandle
 from latefuse_b200.batch import BatchedLRWeights, BatchLora, LayerwiseBatchedWeights
 from latefuse_b200.config import LoraServingConfig
 from latefuse_b200.head import LRHeadOps, pool_tokens, validate_pooling
-from latefuse_b200.lora import (FactorCache, SegmentTable, lora_apply, lora_apply_into, per_row_cache,
-                                 workspace_bytes)
+from latefuse_b200.lora import (FactorCache, SegmentTable, blocked_u, linear_lora, lora_apply, lora_apply_into,
+                                 lora_shrink_blocked, per_row_cache, workspace_bytes)
 from latefuse_b200.encoder_ops import add_layernorm, attention_varlen, gelu
 from latefuse_b200.packing import PackedBatch, pack_rows
 
@@ -510,6 +510,12 @@ class EncoderWithLora(nn.Module):
         o = F.linear(mid, layer.wo2, layer.bo2)
         return add_layernorm(o, h1, layer.ln2.weight, layer.ln2.bias, self.eps, out=o)
 
+    def _lora_gemm_ok(self, dtype: torch.dtype, rank: int) -> bool:
+        """Whether the packed forward runs the LoRA'd projections on this library's
+        GEMM with the delta in its accumulator (``linear_lora``)."""
+        return dtype in (torch.bfloat16, torch.float16) and self.config.hidden_size % 256 == 0 and \
+            rank in (16, 32, 64)
+
     def _fused_dense_ok(self, dtype: torch.dtype, rank: int) -> bool:
         """Whether the packed forward writes the attention-output delta (with bias and
         residual) first and lets the projection GEMM accumulate onto it
@@ -557,23 +563,56 @@ class EncoderWithLora(nn.Module):
             status = self._runner.status
             qkv_offs = [j * H for _, j in self._qkv_targets]
             segs = pb.segments
-            fuse_dense = self._fused_dense_ok(h.dtype, store.factor_cache(0).rank)
+            rank = store.factor_cache(0).rank
+            # q/k/v and the attention output on the tcgen05 GEMM with the delta in
+            # its accumulator (shrink first, into (tile, segment) blocks of u)
+            gemm_ok = self._lora_gemm_ok(h.dtype, rank) and segs.use_records
+            gemm_qkv = gemm_ok and sorted(j for _, j in self._qkv_targets) == [0, 1, 2]
+            qkv_by_col = [store.module_index(m) for m, _ in sorted(self._qkv_targets, key=lambda t: t[1])]
+            gemm_dense = gemm_ok and bool(self._dense_target)
+            fuse_dense = not gemm_dense and self._fused_dense_ok(h.dtype, rank)
+            if gemm_qkv:
+                u_qkv = blocked_u(3, T, segs.n_segs, rank, h.dtype, h.device)
+            if gemm_dense:
+                u_dense = blocked_u(1, T, segs.n_segs, rank, h.dtype, h.device)
         else:
-            fuse_dense = False
+            fuse_dense = gemm_qkv = gemm_dense = False
 
         for l, layer in enumerate(self.layers):
-            qkv = F.linear(h, layer.wqkv, layer.bqkv)  # (T, 3H)
-            if do_lora and self._qkv_targets:
-                ev = self._event_pair("qkv")
-                lora_apply(h, qkv, store.factor_cache(l), segs, qkv_idx, qkv_offs, ws, status)
+            if gemm_qkv:
+                cache = store.factor_cache(l)
+                ev = self._event_pair("qkv_shrink")
+                lora_shrink_blocked(h, u_qkv, cache, segs, qkv_by_col, status)
                 if ev is not None:
                     ev[1].record()
+                ev = self._event_pair("qkv_gemm")
+                qkv = linear_lora(h, layer.wqkv, layer.bqkv, u_qkv, cache, segs, qkv_by_col, H, status=status)
+                if ev is not None:
+                    ev[1].record()
+            else:
+                qkv = F.linear(h, layer.wqkv, layer.bqkv)  # (T, 3H)
+                if do_lora and self._qkv_targets:
+                    ev = self._event_pair("qkv")
+                    lora_apply(h, qkv, store.factor_cache(l), segs, qkv_idx, qkv_offs, ws, status)
+                    if ev is not None:
+                        ev[1].record()
             if hd == 64:
                 ctx = attention_varlen(qkv, nh, pb.attn_items, hd ** -0.5, status=self._runner.status)
             else:  # head sizes the tcgen05 kernel does not tile
                 q, k, v = qkv.view(T, 3, nh, hd).unbind(1)
                 ctx = varlen_attention(q, k, v, pb.cu_seqlens, pb.max_len).view(T, H)
-            if fuse_dense:
+            if gemm_dense:
+                cache = store.factor_cache(l)
+                ev = self._event_pair("dense_shrink")
+                lora_shrink_blocked(ctx, u_dense, cache, segs, dense_idx, status)
+                if ev is not None:
+                    ev[1].record()
+                ev = self._event_pair("dense_gemm")
+                ao = linear_lora(ctx, layer.wo, layer.bo, u_dense, cache, segs, dense_idx, H, status=status)
+                if ev is not None:
+                    ev[1].record()
+                h = self._ffn(layer, ao, h)
+            elif fuse_dense:
                 # The delta, bias and residual go first, into a fresh output that
                 # the projection GEMM accumulates onto (beta = 1); the LayerNorm
                 # then reads one tensor instead of two.
