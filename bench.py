@@ -46,6 +46,9 @@ METRIC = "sequences/sec at bge-m3 shape, 10k adapters; LoRA-kernel HBM GB/s vs p
 # dense op (70.34 MB) of the bge-m3 step at r=16, from one ncu capture of the same launch
 # shapes (the serve-traffic summary under profiles/ holds the command and the table).
 NCU_TRAFFIC_PER_OP_R16 = (182.85e6 + 70.34e6) / 2
+# DRAM bytes of one fused q/k/v projection launch (lf_linear_lora) of the same step, from one
+# ncu capture (profiles/ holds the command and the table).
+NCU_TRAFFIC_QKV_GEMM_R16 = 45.25e6 + 51.91e6
 TARGETS = ["query", "key", "value", "dense"]
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS_SUSTAINED = 1400.0
@@ -311,7 +314,10 @@ def run_ours(args):
         shrink_gbs = shrink_bytes_step / (shrink_ms_step * 1e-3) / 1e9
         roofline = {
             "bound": "tensor", "achieved": tach, "peak": tpeak, "unit": "TFLOP/s", "frac": tach / tpeak,
-            "traffic": None,
+            "traffic": (NCU_TRAFFIC_QKV_GEMM_R16 if packed is not None and args.rank == 16 and args.batch == 64
+                        and args.seq == 512 else None),
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one lf_linear_lora q/k/v "
+                              "launch of this workload (output writes still in L2 at kernel end not counted)",
             "kernel": "lf_linear_lora: q/k/v projection (T x 3072 x 1024) with the per-row LoRA delta in the "
                       "tcgen05 accumulator (one launch per layer)",
             "algorithmic_flops_per_launch": gemm_flops, "launch_ms": gemm_ms, "peak_source": tpeak_src,
