@@ -16,8 +16,8 @@
 //               epilogue of one tile overlaps the main loop of the next;
 //   warps 2-9   epilogue, two warps per TMEM lane quadrant (128 columns each),
 //               one output row per thread: 32 columns per tcgen05.ld, bias and
-//               activation in f32, rounded, staged per warp in a double-buffered
-//               32 x 32 SW64 tile and written by TMA (rows past M are clipped by
+//               activation in f32, rounded, staged per warp in a 32 x 32 SW64
+//               tile and written by TMA (rows past M are clipped by
 //               the tensor map).
 // With LoRA (lf_linear_lora) the per-row delta joins the same accumulator: after
 // a tile's K blocks come one "delta block" per adapter segment overlapping the
@@ -45,7 +45,8 @@ constexpr int kEpiWarps = 8;                    // two per TMEM lane quadrant, 1
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kOutCols = 32;                     // output columns per epilogue store
 constexpr int kOutBuf = 32 * kOutCols * 2;       // one warp's 32 x 32 staging tile: 2 KB
-constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kEpiWarps * 2 * kOutBuf + 1024;
+constexpr int kDeltaBuf = 16384;                 // one delta block (rank 16) loaded at the tile's start
+constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kEpiWarps * kOutBuf + kDeltaBuf + 1024;
 
 struct alignas(64) LinearParams {
   CUtensorMap x_map;  // 2D {K, M}, box {64, 128}, SW128
@@ -94,11 +95,15 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   const uint32_t s_stage0 = base;
-  const uint32_t s_out0 = base + kStages * kStageBytes;  // [warp][buffer] 2 KB tiles
-  uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + (s_out0 + kEpiWarps * 2 * kOutBuf - base));
+  const uint32_t s_out0 = base + kStages * kStageBytes;  // [warp] 2 KB staging tiles
+  const uint32_t s_delta = s_out0 + kEpiWarps * kOutBuf;  // the tile's first delta block (rank 16)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + (s_delta + kDeltaBuf - base));
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   const int FULL = 0, EMPTY = kStages, ACC_FULL = 2 * kStages, ACC_EMPTY = 2 * kStages + 2,
-            DRAIN = 2 * kStages + 4, N_BARS = DRAIN + 1;
+            DRAIN = 2 * kStages + 4, DFULL = DRAIN + 1, DEMPTY = DRAIN + 2, N_BARS = DRAIN + 3;
+  // a tile's first delta block goes to its own buffer, loaded before the tile's K
+  // blocks, so it has landed when the MMA reaches it (later ones use the ring)
+  const bool dbuf = p.pairs != nullptr && 768 * p.rank <= kDeltaBuf;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(&bars[N_BARS]);
   int32_t* s_abort = reinterpret_cast<int32_t*>(tmem_slot + 1);
 
@@ -112,6 +117,8 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
       mbar_init(bar(ACC_EMPTY + i), kEpiWarps);
     }
     mbar_init(bar(DRAIN), 1);
+    mbar_init(bar(DFULL), 1);
+    mbar_init(bar(DEMPTY), 1);
     *s_abort = 0;
     fence_mbar_init();
     prefetch_tmap(&p.x_map);
@@ -134,7 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      int kk = 0;
+      int kk = 0, dk = 0;
       bool stop = false;
       // the B factors of a tile's segments, into L2 (whole rank x module_cols block)
       auto prefetch_b = [&](int64_t tt) {
@@ -158,6 +165,23 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
           q0 = __ldg(p.tile_pairs + m0 / kBM);
           q1 = __ldg(p.tile_pairs + m0 / kBM + 1);
         }
+        const int32_t n_loc = mod < p.n_mod ? n0 - mod * p.module_cols : 0;
+        const int64_t n_blk = (p.m_rows + kBM - 1) / kBM + p.n_segs;
+        // u block of pair q (tile rows of its segment, others 0) and the segment's B columns
+        auto load_delta = [&](uint32_t dst, uint32_t b_dst, uint32_t full, int q) {
+          const int j = __ldg(p.pairs + 2 * q);
+          const int32_t slot = __ldg(p.pairs + 2 * q + 1);  // out of range: zero fill, no delta
+          mbar_arrive_expect_tx(full, 768 * p.rank);        // u 128 x R + B R x 256
+          bulk_load(dst, static_cast<const T*>(p.u) + (int64_t(mod) * n_blk + m0 / kBM + j) * kBM * p.rank,
+                    256 * p.rank, full);
+          for (int b = 0; b < kBN / 64; ++b)
+            tma_load_3d(b_dst + b * p.rank * 128, &p.b_map[mod], full, n_loc + b * 64, 0, slot);
+        };
+        // The first pair goes to the delta buffer once the MMA has started this tile
+        // (after K block kStages of it has been issued, the previous tile's delta is
+        // done): it then has the rest of the tile's K blocks to land.
+        const bool use_dbuf = dbuf && q1 > q0;
+        const int d_after = (p.n_kb < kStages ? p.n_kb : kStages) - 1;
         for (int kb = 0; kb < p.n_kb; ++kb, ++kk) {
           const int s = kk % kStages;
           if (aborted_flag(s_abort) || !mbar_wait(bar(EMPTY + s), ((kk / kStages) & 1) ^ 1)) {
@@ -169,33 +193,36 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
           mbar_arrive_expect_tx(bar(FULL + s), kStageBytes);
           tma_load_2d(st, &p.x_map, bar(FULL + s), kb * kBK, m0);
           tma_load_2d(st + kABytes, &p.w_map, bar(FULL + s), kb * kBK, n0);
+          if (use_dbuf && kb == d_after) {
+            if (aborted_flag(s_abort) || !mbar_wait(bar(DEMPTY), (dk & 1) ^ 1)) {
+              if (!aborted_flag(s_abort)) fail();
+              stop = true;
+              ++kk;
+              break;
+            }
+            // the delta buffer holds u at its start and B right after it (1 KB-aligned)
+            load_delta(s_delta, s_delta + 256 * p.rank, bar(DFULL), q0);
+            ++dk;
+          }
         }
+        if (use_dbuf) ++q0;
         if (!stop) prefetch_b(t + gridDim.x);  // the ring is full here: the producer has time
         if (stop || mod >= p.n_mod) continue;
-        const int32_t n_loc = n0 - mod * p.module_cols;
         for (int q = q0; q < q1; ++q) {
-          const int j = __ldg(p.pairs + 2 * q);
           const int s = kk % kStages;
           if (aborted_flag(s_abort) || !mbar_wait(bar(EMPTY + s), ((kk / kStages) & 1) ^ 1)) {
             if (!aborted_flag(s_abort)) fail();
             stop = true;
             break;
           }
-          const uint32_t st = s_stage0 + s * kStageBytes;
-          mbar_arrive_expect_tx(bar(FULL + s), 768 * p.rank);  // u 128 x R + B R x 256
-          // the (tile, segment) block of u: this tile's rows of segment j, other rows 0
-          const int64_t n_blk = (p.m_rows + kBM - 1) / kBM + p.n_segs;
-          bulk_load(st, static_cast<const T*>(p.u) + (int64_t(mod) * n_blk + m0 / kBM + j) * kBM * p.rank,
-                    256 * p.rank, bar(FULL + s));
-          const int32_t slot = __ldg(p.pairs + 2 * q + 1);  // out of range: zero fill, no delta
-          for (int b = 0; b < kBN / 64; ++b)
-            tma_load_3d(st + kABytes + b * p.rank * 128, &p.b_map[mod], bar(FULL + s), n_loc + b * 64, 0, slot);
+          load_delta(s_stage0 + s * kStageBytes, s_stage0 + s * kStageBytes + kABytes, bar(FULL + s), q);
           ++kk;
         }
       }
       if (aborted_flag(s_abort)) {  // loads nobody consumed land before the CTA exits (bounded)
         for (int q = (kk > kStages ? kk - kStages : 0); q < kk; ++q)
           mbar_wait(bar(FULL + q % kStages), (q / kStages) & 1);
+        if (dk > 0) mbar_wait(bar(DFULL), (dk - 1) & 1);
       }
     }
   } else if (warp == 1) {
@@ -203,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_f16(DT<T>::umma_fmt, kBM, kBN, 0, 0);
       const uint32_t idesc_d = umma_idesc_f16(DT<T>::umma_fmt, kBM, kBN, 0, 1);
-      int kk = 0, it = 0;
+      int kk = 0, it = 0, dk = 0;
       bool stop = false;
       auto wait = [&](uint32_t b, uint32_t parity) {
         if (aborted_flag(s_abort)) return false;
@@ -235,17 +262,31 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
         }
         if (!stop && n_delta > 0) {
           const int nq = p.rank / 8;  // 16-byte chunks of a u row
-          for (int d = 0; d < n_delta; ++d) {
+          auto delta_mma = [&](uint32_t ua, uint32_t ba) {
+            tc_fence_after();
+            for (int q = 0; q < p.rank / 16; ++q)
+              umma_f16(tmem + a * kBN, smem_desc(ua + q * 256, 128, uint32_t(nq) * 128, 0),
+                       smem_desc(ba + q * 2048, p.rank * 128, 1024, 2), idesc_d, 1u);
+          };
+          int d = 0;
+          if (dbuf) {  // the first pair, from the delta buffer
+            if (!wait(bar(DFULL), dk & 1)) {
+              stop = true;
+            } else {
+              delta_mma(s_delta, s_delta + 256 * p.rank);
+              umma_commit(bar(DEMPTY));
+              ++dk;
+              d = 1;
+            }
+          }
+          for (; d < n_delta && !stop; ++d) {
             const int s = kk % kStages;
             if (!wait(bar(FULL + s), (kk / kStages) & 1)) {
               stop = true;
               break;
             }
             const uint32_t st = s_stage0 + s * kStageBytes;
-            tc_fence_after();
-            for (int q = 0; q < p.rank / 16; ++q)
-              umma_f16(tmem + a * kBN, smem_desc(st + q * 256, 128, uint32_t(nq) * 128, 0),
-                       smem_desc(st + kABytes + q * 2048, p.rank * 128, 1024, 2), idesc_d, 1u);
+            delta_mma(st, st + kABytes);
             umma_commit(bar(EMPTY + s));
             ++kk;
           }
@@ -262,9 +303,9 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;  // columns [128 half, 128 half + 128) of the tile
     const uint32_t taddr = tmem + (uint32_t(quad * 32) << 16);
-    const uint32_t my_out = s_out0 + (warp - 2) * 2 * kOutBuf;
+    const uint32_t my_out = s_out0 + (warp - 2) * kOutBuf;
     const T* bias = static_cast<const T*>(p.bias);
-    int it = 0, sb = 0;
+    int it = 0;
     for (int64_t t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++it) {
       const int a = it & 1;
       const int32_t m0 = int32_t(t / p.n_tiles_n) * kBM, n0 = int32_t(t % p.n_tiles_n) * kBN;
@@ -307,10 +348,10 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
           }
           packed[i] = Pack2<T>::pack(y0, y1);
         }
-        // the store that last read this staging buffer must be done with it
-        if (lane == 0) tma_store_wait_read_le1();
+        // the store that last read this staging tile must be done with it
+        if (lane == 0) tma_store_wait_read_all();
         __syncwarp();
-        const uint32_t buf = my_out + sb * kOutBuf;
+        const uint32_t buf = my_out;
 #pragma unroll
         for (int q = 0; q < 4; ++q)  // SW64: 16-byte chunk q of row `lane` at q ^ ((lane >> 1) & 3)
           *reinterpret_cast<uint4*>(gbase + (buf - base) + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
@@ -321,7 +362,6 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
           tma_store_2d(&p.y_map, buf, col0, m0 + quad * 32);
           tma_store_commit();
         }
-        sb ^= 1;
       }
       tc_fence_before();
       __syncwarp();
