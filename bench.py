@@ -65,7 +65,7 @@ def bge_m3_config(layers: int = 24):
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--mode", choices=["serve", "op"], default="serve",
@@ -115,7 +115,7 @@ def measured_tensor_peak() -> tuple[float, str]:
 class ClockSampler:
     """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -129,7 +129,7 @@ class ClockSampler:
             self.path.parent.mkdir(exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", ",".join(map(str, self.gpus))], stdout=self.fh, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -144,15 +144,32 @@ class ClockSampler:
                 self.proc.kill()
             self.fh.close()
 
+    def mark(self, begin: bool) -> None:
+        """Wall-clock bounds of the timed region: only samples inside it count."""
+        if begin:
+            self.t_begin = time.time()
+        else:
+            self.t_end = time.time()
+
     def summary(self) -> dict:
         if self.proc is None or not self.path.exists():
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        import datetime
+
+        t0, t1 = getattr(self, "t_begin", None), getattr(self, "t_end", None)
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.path.read_text().splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
+            try:
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            except ValueError:
+                continue
+            if t0 is not None and t1 is not None and not (t0 <= ts <= t1):
+                continue
+            parts = parts[1:]
             try:
                 sm.append(float(parts[1]))
                 mx.append(float(parts[2]))
@@ -257,6 +274,10 @@ def run_ours(args):
                 dist.all_gather_into_tensor(gathered, out)
         return out
 
+    # clocks are sampled from the warm-up on (nvidia-smi takes a moment to start);
+    # only the samples inside the timed region are reported
+    clocks = ClockSampler(list(range(torch.cuda.device_count())) if rank == 0 else [])
+    clocks.__enter__()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -271,13 +292,15 @@ def run_ours(args):
     model.lora_events = []
     n0 = nat.launch_count()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(list(range(torch.cuda.device_count())) if rank == 0 else []) as clocks:
-        barrier()
-        start.record()
-        for _ in range(args.steps):
-            step()
-        end.record()
-        barrier()
+    barrier()
+    clocks.mark(True)
+    start.record()
+    for _ in range(args.steps):
+        step()
+    end.record()
+    barrier()
+    clocks.mark(False)
+    clocks.__exit__(None, None, None)
     launches = nat.launch_count() - n0
     ms = start.elapsed_time(end) / args.steps
     events = model.lora_events

@@ -160,6 +160,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();
+  pdl_launch_dependents();
 
   auto fail = [&]() {
     set_status(p.status, LF_STATUS_TIMEOUT);
@@ -541,8 +543,7 @@ extern "C" int lf_attention_varlen(void* stream, int dtype, const void* qkv, int
   auto kern = dtype == LF_DTYPE_BF16 ? attention_varlen_kernel<__nv_bfloat16> : attention_varlen_kernel<__half>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(attention)");
-  kern<<<grid, kThreads, kSmemBytes, s>>>(p);
-  e = cudaGetLastError();
+  e = launch_pdl(kern, dim3(grid), dim3(kThreads), kSmemBytes, s, p);
   if (e != cudaSuccess) return cuda_error(e, "launch attention_varlen");
   count_launch();
   return LF_OK;

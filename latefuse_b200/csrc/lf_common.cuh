@@ -15,6 +15,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+#include <utility>
 
 #include "../../include/latefuse_b200.h"
 
@@ -347,6 +348,18 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+// Programmatic dependent launch.  Every kernel of this library that is launched
+// with launch_pdl calls pdl_wait before it touches global memory that an earlier
+// kernel may write, and only then pdl_launch_dependents: so when a kernel starts
+// early, the kernel before it has passed its own wait, and everything before that
+// one has completed.  The setup before pdl_wait (barriers, TMEM, tensor-map
+// prefetch, constant tables) overlaps the previous kernel's tail.  Both return at
+// once in a grid launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Shared-memory matrix descriptor for tcgen05.mma (sm_100 "version 1" format).
 //   start/lbo/sbo in bytes (encoded >> 4), layout: 0 none, 2 SW128, 4 SW64, 6 SW32.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t start, uint32_t lbo, uint32_t sbo,
@@ -416,6 +429,23 @@ __device__ __forceinline__ int first_seg_ending_after(const int32_t* __restrict_
     if (end > t) hi = mid; else lo = mid + 1;
   }
   return lo;
+}
+
+// Launch with cudaLaunchAttributeProgrammaticStreamSerialization (see pdl_wait).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 }  // namespace lf

@@ -132,6 +132,8 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();
+  pdl_launch_dependents();
 
   auto fail = [&]() {
     set_status(p.status, LF_STATUS_TIMEOUT);
@@ -501,8 +503,7 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
   auto kern = dtype == LF_DTYPE_BF16 ? linear_kernel<__nv_bfloat16> : linear_kernel<__half>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(linear)");
-  kern<<<grid, kThreads, kSmemBytes, s>>>(p);
-  e = cudaGetLastError();
+  e = launch_pdl(kern, dim3(grid), dim3(kThreads), kSmemBytes, s, p);
   if (e != cudaSuccess) return cuda_error(e, "launch linear");
   count_launch();
   return LF_OK;

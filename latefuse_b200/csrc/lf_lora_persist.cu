@@ -462,8 +462,6 @@ lora_shrink_persist_kernel(const __grid_constant__ ShrinkPersistParams p, int st
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
 
-  // the expand that follows may be scheduled on SMs this grid leaves free
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ST = stages;
@@ -508,6 +506,10 @@ lora_shrink_persist_kernel(const __grid_constant__ ShrinkPersistParams p, int st
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // x comes from the previous kernel; then the next kernel (the expand, or the
+  // GEMM that reads u) may be scheduled on SMs this grid leaves free
+  pdl_wait();
+  pdl_launch_dependents();
 
   auto fail = [&]() {
     set_status(p.status, LF_STATUS_TIMEOUT);
@@ -775,8 +777,7 @@ int launch_shrink(ShrinkPersistParams p, cudaStream_t stream) {
   const int sms = sm_count();
   const int grid = p.n_tiles < sms ? p.n_tiles : sms;
   if (grid == 0) return LF_OK;
-  kern<<<grid, 192, smem, stream>>>(p, stages, stage_bytes);
-  e = cudaGetLastError();
+  e = launch_pdl(kern, dim3(grid), dim3(192), smem, stream, p, stages, stage_bytes);
   if (e != cudaSuccess) return cuda_error(e, "launch lora_shrink_persist");
   count_launch();
   return LF_OK;

@@ -104,6 +104,8 @@ template <typename T, int NC, int MODE>
 __global__ void __launch_bounds__(32 * kNormWarps)
 add_layernorm_kernel(const NormParams p, int full) {
   constexpr bool HAS_B = MODE != 0;
+  pdl_wait();
+  pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * kNormWarps + (threadIdx.x >> 5);
   if (row >= p.n_rows) return;
@@ -211,6 +213,8 @@ gelu_lut_kernel(const uint4* __restrict__ x, uint4* __restrict__ out, int64_t n8
   const uint4* tab = reinterpret_cast<const uint4*>(g_gelu_table[which]);
   for (int i = threadIdx.x; i < 65536 / 8; i += kLutThreads) s_tab4[i] = tab[i];
   __syncthreads();
+  pdl_wait();  // the table was built long before; x comes from the previous kernel
+  pdl_launch_dependents();
   const uint16_t* s_tab = reinterpret_cast<const uint16_t*>(s_tab4);
   auto map = [&](uint32_t w) {
     return uint32_t(s_tab[w & 0xffffu]) | (uint32_t(s_tab[w >> 16]) << 16);
@@ -244,17 +248,15 @@ template <typename T>
 int launch_norm(const NormParams& p, cudaStream_t s) {
   const int nc = (p.hidden + 255) / 256;
   const int full = p.hidden == nc * 256;  // every lane holds NC whole 8-element chunks
+  cudaError_t e = cudaSuccess;
   const unsigned blocks = unsigned((p.n_rows + kNormWarps - 1) / kNormWarps);
   const dim3 grid{blocks}, block{32 * kNormWarps};
   switch (nc) {
-#define LF_NORM_CASE(N)                                                \
-  case N:                                                              \
-    if (p.b != nullptr)                                                \
-      add_layernorm_kernel<T, N, 1><<<grid, block, 0, s>>>(p, full);   \
-    else if (p.vec != nullptr)                                         \
-      add_layernorm_kernel<T, N, 2><<<grid, block, 0, s>>>(p, full);   \
-    else                                                               \
-      add_layernorm_kernel<T, N, 0><<<grid, block, 0, s>>>(p, full);   \
+#define LF_NORM_CASE(N)                                                                  \
+  case N:                                                                                \
+    e = launch_pdl(p.b != nullptr ? add_layernorm_kernel<T, N, 1>                        \
+                   : p.vec != nullptr ? add_layernorm_kernel<T, N, 2> : add_layernorm_kernel<T, N, 0>, \
+                   grid, block, 0, s, p, full);                                          \
     break;
     LF_NORM_CASE(1) LF_NORM_CASE(2) LF_NORM_CASE(3) LF_NORM_CASE(4) LF_NORM_CASE(5) LF_NORM_CASE(6)
     LF_NORM_CASE(7) LF_NORM_CASE(8) LF_NORM_CASE(9) LF_NORM_CASE(10) LF_NORM_CASE(11) LF_NORM_CASE(12)
@@ -262,7 +264,6 @@ int launch_norm(const NormParams& p, cudaStream_t s) {
 #undef LF_NORM_CASE
     default: return set_error(LF_ERR_UNSUPPORTED, "lf_add_layernorm: hidden %d above 4096", p.hidden);
   }
-  const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "launch add_layernorm");
   count_launch();
   return LF_OK;
@@ -312,9 +313,8 @@ int launch_gelu(const void* x, void* out, int64_t n, cudaStream_t s) {
     if (rc) return rc;
     int64_t blocks = (n8 + kLutThreads - 1) / kLutThreads;
     if (blocks > sms) blocks = sms;
-    gelu_lut_kernel<<<unsigned(blocks), kLutThreads, 65536 * 2, s>>>(static_cast<const uint4*>(x),
-                                                                      static_cast<uint4*>(out), n8, which);
-    const cudaError_t e = cudaGetLastError();
+    const cudaError_t e = launch_pdl(gelu_lut_kernel, dim3(unsigned(blocks)), dim3(kLutThreads), 65536 * 2, s,
+                                     static_cast<const uint4*>(x), static_cast<uint4*>(out), n8, which);
     if (e != cudaSuccess) return cuda_error(e, "launch gelu_lut");
     count_launch();
     return LF_OK;
