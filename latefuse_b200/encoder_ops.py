@@ -84,7 +84,7 @@ def linear(x: Tensor, weight: Tensor, bias: Tensor | None, act: int = ACT_NONE,
            out: Tensor | None = None) -> Tensor:
     """``act(x @ weight.T + bias)`` (``act``: ``ACT_NONE`` or ``ACT_GELU``, the exact erf
     GELU) for bf16/f16 ``x (..., K)`` and an ``nn.Linear`` weight ``(N, K)``;
-    N % 256 == 0, K % 64 == 0."""
+    N % 256 == 0, K % 64 == 0.  ``out`` must be viewable as rows without a copy."""
     dev = nat.require_cuda(x, weight, bias, out)
     x2, ldx = _rows(x)
     N, K = weight.shape
@@ -93,9 +93,11 @@ def linear(x: Tensor, weight: Tensor, bias: Tensor | None, act: int = ACT_NONE,
     w = weight if weight.stride(-1) == 1 else weight.contiguous()
     if out is None:
         out = torch.empty(*x.shape[:-1], N, dtype=x.dtype, device=x.device)
-    o2, ldo = _rows(out)
+    o2 = out.reshape(-1, N)
+    if o2.data_ptr() != out.data_ptr() or o2.stride(-1) != 1 or (out.dim() > 2 and not out.is_contiguous()):
+        raise ValueError("out must be viewable as rows without a copy")
     b = None if bias is None else (bias if bias.dtype == x.dtype else bias.to(x.dtype)).contiguous()
     rc = nat.lib().lf_linear(nat.stream_ptr(dev), nat.dtype_code(x.dtype), x2.data_ptr(), ldx, w.data_ptr(),
-                             w.stride(0), nat.ptr(b), o2.data_ptr(), ldo, x2.shape[0], N, K, int(act), None)
+                             w.stride(0), nat.ptr(b), o2.data_ptr(), o2.stride(0), x2.shape[0], N, K, int(act), None)
     nat.check(rc, "lf_linear")
     return out

@@ -62,3 +62,6 @@ def test_linear_strided_rows_and_rejections(cuda):
         linear(x, torch.randn(100, 1024, device=cuda, dtype=torch.bfloat16), None)
     with pytest.raises(nat.NativeLibraryError, match="bf16 or f16"):
         linear(x.float(), w.float(), None)
+    # an output that would need a copy to be seen as rows is refused, not written to a copy
+    with pytest.raises(ValueError, match="viewable"):
+        linear(x, w, None, out=torch.empty(768, 500, device=cuda, dtype=torch.bfloat16).t())
