@@ -398,7 +398,9 @@ int lf_gelu(void* stream, int dtype, const void* x, void* out, int64_t n);
  * device int32 array of n_items records {row_start, len, q_tile, 0}, one per
  * (sequence, 128-query tile), 16-byte aligned; ordering them longest sequence
  * first balances the work.  head_dim must be 64; dtype bf16 or f16; column
- * offsets multiples of 64.  out row t, head h at columns [64 h, 64 h + 64). */
+ * offsets multiples of 64.  out row t, head h at columns [64 h, 64 h + 64).
+ * A record outside [0, n_tokens) (or with len < 0, or a q_tile past its length)
+ * sets LF_STATUS_BAD_SEGMENT and stores nothing; a zero length stores nothing. */
 int lf_attention_varlen(void* stream, int dtype, const void* qkv, int64_t ld_qkv, int64_t n_tokens,
                         int64_t q_col, int64_t k_col, int64_t v_col, int n_heads, int head_dim,
                         const int32_t* items, int n_items, float scale, void* out, int64_t ld_out,

@@ -26,9 +26,11 @@ LF_OPT_SHRINK_CLUSTER = 2
 LF_OPT_REQUIRE_TC = 3
 LF_OPT_PERSISTENT = 4
 
+LF_STATUS_BAD_SLOT, LF_STATUS_BAD_SEGMENT, LF_STATUS_TIMEOUT, LF_STATUS_BAD_HEAD = 1, 2, 4, 8
+
 STATUS_BITS = {
     1: "segment names a slot outside the cache",
-    2: "segment outside the token range",
+    2: "segment (or attention record) outside the token range",
     4: "on-chip wait timed out",
     8: "head rows outside the head cache",
 }

@@ -167,11 +167,22 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
     set_status(p.status, LF_STATUS_TIMEOUT);
     atomicExch(s_abort, 1);
   };
-  // {row_start, len, q_tile, 0}; a zero length is read as 1 so that every role
-  // walks the same tiles (nothing of such an item is stored)
+  // {row_start, len, q_tile, 0}.  Every role reads a record through here, so
+  // all walk the same tiles.  A zero length is read as one key with w = 1
+  // (nothing stored); a record outside the batch (row_start < 0, len < 0,
+  // row_start + len > n_tokens, or a q_tile past its length) is flagged
+  // LF_STATUS_BAD_SEGMENT and read as one key of row 0 with nothing stored, so
+  // no store leaves out's rows.
   auto item_of = [&](int64_t unit) {
     int4 it = __ldg(p.items + unit / p.n_heads);
-    it.y = max(it.y, 1);
+    const bool in_batch = it.x >= 0 && it.y >= 0 && int64_t(it.x) + it.y <= p.n_tokens && it.z >= 0 &&
+                          (it.y == 0 || int64_t(it.z) * kRows < it.y);
+    if (!in_batch) {
+      set_status(p.status, LF_STATUS_BAD_SEGMENT);
+      return make_int4(0, 1, 0, 1);
+    }
+    if (it.y == 0) return make_int4(it.x, 1, 0, 1);
+    it.w = 0;
     return it;
   };
   // group grp takes the CTA's units 2k + grp
@@ -459,7 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
           uint32_t ov[64];
           tmem_ld64(o_addr, ov);
           const int qr = it.z * kRows + row;
-          if (qr < it.y) {
+          if (qr < it.y && it.w == 0) {
             const float inv = 1.f / l;
             T* dst = reinterpret_cast<T*>(p.out) + int64_t(it.x + qr) * p.ldo + int(unit % p.n_heads) * kHd;
 #pragma unroll
@@ -526,6 +537,7 @@ extern "C" int lf_attention_varlen(void* stream, int dtype, const void* qkv, int
   if (r != CUDA_SUCCESS) return set_error(LF_ERR_CUDA, "cuTensorMapEncodeTiled(qkv) failed: %d", int(r));
   p.items = reinterpret_cast<const int4*>(items);
   p.n_items = n_items;
+  p.n_tokens = n_tokens;
   p.n_heads = n_heads;
   p.q_col = int32_t(q_col);
   p.k_col = int32_t(k_col);

@@ -107,6 +107,7 @@ struct alignas(64) AttnParams {
   CUtensorMap qkv_map;               // 2D {ld_qkv, n_tokens}, box {64, 128}, SW128
   const int4* items;                 // {row_start, len, q_tile, 0} per (sequence, 128-query tile)
   int32_t n_items;
+  int64_t n_tokens;                  // rows of qkv and out: records must lie inside
   int32_t n_heads;
   int32_t q_col, k_col, v_col;       // column of head 0's q / k / v in a qkv row
   void* out;                         // (n_tokens, ld_out): head h at columns [64 h, 64 h + 64)

@@ -64,12 +64,16 @@ def attention_varlen(qkv: Tensor, n_heads: int, items: Tensor, scale: float, out
     ``(n, 4)`` device int32 work list of :class:`~latefuse_b200.packing.PackedBatch`.
     Returns ``(T, H)``."""
     dev = nat.require_cuda(qkv, items, out, status)
+    if items.dtype != torch.int32 or items.dim() != 2 or items.shape[1] != 4 or not items.is_contiguous():
+        raise ValueError("items must be a contiguous (n, 4) int32 tensor (PackedBatch.attn_items)")
     T, W = qkv.shape
     H = W // 3
     if qkv.stride(-1) != 1:
         raise ValueError("qkv rows must be contiguous")
     if out is None:
         out = torch.empty(T, H, dtype=qkv.dtype, device=qkv.device)
+    elif out.dtype != qkv.dtype or out.shape != (T, H) or out.stride(-1) != 1:
+        raise ValueError(f"out must be a ({T}, {H}) {qkv.dtype} tensor with contiguous rows")
     rc = nat.lib().lf_attention_varlen(nat.stream_ptr(dev), nat.dtype_code(qkv.dtype), qkv.data_ptr(), qkv.stride(0),
                                        T, 0, H, 2 * H, n_heads, H // n_heads, items.data_ptr(), items.shape[0],
                                        float(scale), out.data_ptr(), out.stride(0), nat.ptr(status))

@@ -86,3 +86,39 @@ def test_rejects_unsupported_head_dim(cuda):
     items = torch.tensor([[0, 16, 0, 0]], dtype=torch.int32, device=cuda)
     with pytest.raises(nat.NativeLibraryError, match="head_dim"):
         attention_varlen(qkv, 2, items, 1.0)  # head_dim 128
+
+
+def test_records_outside_the_batch_store_nothing(cuda):
+    """A record past the last token, one with a negative start and one with a q-tile
+    past its length set LF_STATUS_BAD_SEGMENT and write no row; a zero-length record
+    writes nothing; the valid records are still exact."""
+    from latefuse_b200 import _native as nat
+
+    lengths = [200, 77, 129]
+    T, H, nh = sum(lengths), 256, 4
+    g = torch.Generator(device=cuda).manual_seed(5)
+    qkv = torch.randn(T, 3 * H, device=cuda, generator=g).to(torch.bfloat16)
+    starts = [0, 200, 277]
+    good = torch.tensor(attention_items(starts, lengths), dtype=torch.int32)
+    bad = torch.tensor([[T - 10, 50, 0, 0], [-1, 3, 0, 0], [200, 77, 1, 0], [5, 0, 0, 0]], dtype=torch.int32)
+    items = torch.cat([good, bad]).to(cuda)
+    big = torch.full((T + 256, H), 7.0, device=cuda, dtype=torch.bfloat16)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    attention_varlen(qkv, nh, items, 64 ** -0.5, out=big[:T], status=status)
+    torch.cuda.synchronize()
+    assert status.item() & nat.LF_STATUS_BAD_SEGMENT
+    assert (big[T:] == 7.0).all(), "a row past the batch was written"
+    q, k, v = qkv.float().view(T, 3, nh, 64).unbind(1)
+    for s0, n in zip(starts, lengths):
+        sc = torch.einsum("ihd,jhd->hij", q[s0:s0 + n], k[s0:s0 + n]) * 64 ** -0.5
+        ref = torch.einsum("hij,jhd->ihd", sc.softmax(-1), v[s0:s0 + n]).reshape(n, H)
+        check(big[s0:s0 + n], ref)
+
+
+def test_rejects_int64_records_and_wrong_out(cuda):
+    qkv = torch.zeros(16, 3 * 256, device=cuda, dtype=torch.bfloat16)
+    items = torch.tensor([[0, 16, 0, 0]], dtype=torch.int64, device=cuda)
+    with pytest.raises(ValueError, match="int32"):
+        attention_varlen(qkv, 4, items, 1.0)
+    with pytest.raises(ValueError, match="out must be"):
+        attention_varlen(qkv, 4, items.int(), 1.0, out=torch.empty(8, 256, device=cuda, dtype=torch.bfloat16))
