@@ -628,6 +628,10 @@ lora_shrink_persist_kernel(const __grid_constant__ ShrinkPersistParams p, int st
       const int64_t row0 = int64_t(rec.x) * kTile;
       const int64_t t = row0 + row;
       const int k = sub_items(rec, p.n_segs);
+      // a record whose tile lies outside the tokens or whose first segment is not
+      // in the table writes nothing (every u address below is then in range)
+      const bool rec_ok = rec.x >= 0 && row0 < p.n_tokens && rec.y >= 0 && rec.y < p.n_segs;
+      if (!rec_ok && row == 0) set_status(p.status, LF_STATUS_BAD_SEGMENT);
       int own_lo = 0;  // rows below were written by an earlier pass
       for (int j0 = 0; j0 < k; j0 += KM, ++it) {
         const int kp = min(KM, k - j0);
@@ -650,7 +654,7 @@ lora_shrink_persist_kernel(const __grid_constant__ ShrinkPersistParams p, int st
         }
         const bool work = __all_sync(0xffffffffu, ok);
         tc_fence_after();
-        if (work) {
+        if (work && rec_ok) {
           for (int m = 0; m < n_mod; ++m) {
             T* dst = reinterpret_cast<T*>(p.u) + (int64_t(m) * p.n_tokens + t) * R;
             // blocked: one 128 x R block per (tile, segment) pair, index tile + segment

@@ -161,3 +161,36 @@ def test_blocked_shrink_is_the_dense_shrink_reordered(cuda, R):
             assert not blk[:, ~inside].any()
             checked += 1
     assert checked >= n_rt
+
+
+def test_shrink_skips_malformed_tile_records(cuda):
+    """A tile record past the tokens or naming a segment outside the table sets
+    LF_STATUS_BAD_SEGMENT and writes nothing: u stays inside its buffer (dense and
+    blocked layouts), and the well-formed records are still computed."""
+    dtype, H, R, n_slots = torch.bfloat16, 512, 16, 5
+    dev = torch.device("cuda")
+    starts, lengths, slots, T = packed_segments(8, n_slots, seed=9, max_len=200)
+    fc, _ = make_cache(n_slots, 2, H, R, dtype, dev, seed=9)
+    st = SegmentTable(starts, lengths, slots, T, dev)
+    x = torch.randn(T, H, device=dev, dtype=dtype)
+    good_dense = torch.empty(2, T, R, dtype=dtype, device=dev)
+    lora_shrink(x, good_dense, fc, st, [0, 1])
+    assert st.n_tiles >= 3
+    st.table[0] = 1 << 20        # record 0: a tile far past the last token
+    st.table[4 + 1] = -5         # record 1: first segment outside the table
+    n_u = 2 * T * R
+    canary = torch.full((n_u + 4096,), 3.0, dtype=dtype, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    lora_shrink(x, canary[:n_u].view(2, T, R), fc, st, [0, 1], status=status)
+    n_b = blocked_u(2, T, st.n_segs, R, dtype, dev).numel()
+    canary_b = torch.full((n_b + 4096,), 3.0, dtype=dtype, device=dev)
+    status_b = torch.zeros(1, dtype=torch.int32, device=dev)
+    lora_shrink_blocked(x, canary_b[:n_b], fc, st, [0, 1], status=status_b)
+    torch.cuda.synchronize()
+    assert status.item() & nat.LF_STATUS_BAD_SEGMENT and status_b.item() & nat.LF_STATUS_BAD_SEGMENT
+    assert (canary[n_u:] == 3.0).all() and (canary_b[n_b:] == 3.0).all()
+    # rows of the well-formed records (tiles 2 and later) are unchanged
+    rec = st.host[: 4 * st.n_tiles].view(-1, 4)
+    row2 = int(rec[2, 0]) * 128
+    dense = canary[:n_u].view(2, T, R)
+    assert torch.equal(dense[:, row2:], good_dense[:, row2:])
