@@ -82,6 +82,16 @@ __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
+// Entries [q0, q1) of the pair table for 128-row tile b.  A range that is not
+// ascending or holds more pairs than there are segments reads as empty, and
+// `bad` says so, so that every role walks the same (no) pairs.
+__device__ __forceinline__ int2 pair_range(const int32_t* tile_pairs, int b, int n_segs, bool* bad = nullptr) {
+  const int q0 = __ldg(tile_pairs + b), q1 = __ldg(tile_pairs + b + 1);
+  const bool ok = q0 >= 0 && q1 >= q0 && q1 - q0 <= n_segs;
+  if (bad != nullptr) *bad = !ok;
+  return ok ? make_int2(q0, q1) : make_int2(0, 0);
+}
+
 __device__ __forceinline__ bool aborted_flag(const int32_t* f) {
   return *reinterpret_cast<const volatile int32_t*>(f) != 0;
 }
@@ -151,7 +161,8 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
         const int pmod = int32_t(tt % p.n_tiles_n) * kBN / p.module_cols;
         if (pmod >= p.n_mod) return;
         const int mb = int32_t(tt / p.n_tiles_n);
-        for (int q = __ldg(p.tile_pairs + mb), qe = __ldg(p.tile_pairs + mb + 1); q < qe; ++q) {
+        const int2 qr = pair_range(p.tile_pairs, mb, p.n_segs);
+        for (int q = qr.x; q < qr.y; ++q) {
           const int32_t slot = __ldg(p.pairs + 2 * q + 1);
           if (slot >= 0 && slot < p.n_slots)
             prefetch_l2(static_cast<const T*>(p.b_ptr[pmod]) + int64_t(slot) * p.b_slot_stride,
@@ -164,15 +175,23 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
         const int mod = p.pairs != nullptr ? n0 / p.module_cols : p.n_mod;
         int q0 = 0, q1 = 0;
         if (mod < p.n_mod) {  // loaded now, used after the K blocks
-          q0 = __ldg(p.tile_pairs + m0 / kBM);
-          q1 = __ldg(p.tile_pairs + m0 / kBM + 1);
+          bool bad = false;
+          const int2 qr = pair_range(p.tile_pairs, m0 / kBM, p.n_segs, &bad);
+          if (bad) set_status(p.status, LF_STATUS_BAD_SEGMENT);
+          q0 = qr.x;
+          q1 = qr.y;
         }
         const int32_t n_loc = mod < p.n_mod ? n0 - mod * p.module_cols : 0;
         const int64_t n_blk = (p.m_rows + kBM - 1) / kBM + p.n_segs;
         // u block of pair q (tile rows of its segment, others 0) and the segment's B columns
         auto load_delta = [&](uint32_t dst, uint32_t b_dst, uint32_t full, int q) {
-          const int j = __ldg(p.pairs + 2 * q);
-          const int32_t slot = __ldg(p.pairs + 2 * q + 1);  // out of range: zero fill, no delta
+          int j = __ldg(p.pairs + 2 * q);
+          const int32_t slot = __ldg(p.pairs + 2 * q + 1);  // out of range: zero fill, no delta, reported
+          if (j < 0 || j >= p.n_segs) {  // a segment outside the table: read block j = 0, reported
+            set_status(p.status, LF_STATUS_BAD_SEGMENT);
+            j = 0;
+          }
+          if (slot < 0 || slot >= p.n_slots) set_status(p.status, LF_STATUS_BAD_SLOT);
           mbar_arrive_expect_tx(full, 768 * p.rank);        // u 128 x R + B R x 256
           bulk_load(dst, static_cast<const T*>(p.u) + (int64_t(mod) * n_blk + m0 / kBM + j) * kBM * p.rank,
                     256 * p.rank, full);
@@ -245,8 +264,10 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
         const int32_t m0 = int32_t(t / p.n_tiles_n) * kBM, n0 = int32_t(t % p.n_tiles_n) * kBN;
         const int mod = p.pairs != nullptr ? n0 / p.module_cols : p.n_mod;
         int n_delta = 0;
-        if (mod < p.n_mod)  // loaded now, used after the K blocks
-          n_delta = __ldg(p.tile_pairs + m0 / kBM + 1) - __ldg(p.tile_pairs + m0 / kBM);
+        if (mod < p.n_mod) {  // loaded now, used after the K blocks
+          const int2 qr = pair_range(p.tile_pairs, m0 / kBM, p.n_segs);
+          n_delta = qr.y - qr.x;
+        }
         if (!wait(bar(ACC_EMPTY + a), ((it >> 1) & 1) ^ 1)) break;
         for (int kb = 0; kb < p.n_kb; ++kb, ++kk) {
           const int s = kk % kStages;

@@ -194,3 +194,39 @@ def test_shrink_skips_malformed_tile_records(cuda):
     row2 = int(rec[2, 0]) * 128
     dense = canary[:n_u].view(2, T, R)
     assert torch.equal(dense[:, row2:], good_dense[:, row2:])
+
+
+@pytest.mark.parametrize("corrupt", ["slot", "segment", "range"])
+def test_fused_gemm_reports_malformed_pair_table(cuda, corrupt):
+    """A pair naming a slot outside the cache (LF_STATUS_BAD_SLOT), a segment outside
+    the table, or a tile whose pair range is not ascending (LF_STATUS_BAD_SEGMENT)
+    is reported and the launch ends normally; the other tiles keep their delta."""
+    dtype, H, R, n_slots = torch.bfloat16, 512, 16, 4
+    dev = torch.device("cuda")
+    starts, lengths, slots, T = packed_segments(6, n_slots, seed=21, max_len=300)
+    fc, _ = make_cache(n_slots, 1, H, R, dtype, dev, seed=21)
+    st = SegmentTable(starts, lengths, slots, T, dev)
+    x = torch.randn(T, H, device=dev, dtype=dtype)
+    W = torch.randn(H, H, device=dev, dtype=dtype) * H ** -0.5
+    u = blocked_u(1, T, st.n_segs, R, dtype, dev)
+    lora_shrink_blocked(x, u, fc, st, [0])
+    good = linear_lora(x, W, None, u, fc, st, [0], H)
+    n_rt = (T + 127) // 128
+    tp = 4 * st.n_tiles + 3 * st.n_segs
+    pairs = tp + n_rt + 1
+    last = n_rt - 1  # a tile whose pairs are changed; tile 0 is left alone
+    q_last = int(st.host[tp + last])
+    if corrupt == "slot":
+        st.table[pairs + 2 * q_last + 1] = n_slots + 7
+        want = nat.LF_STATUS_BAD_SLOT
+    elif corrupt == "segment":
+        st.table[pairs + 2 * q_last] = -3
+        want = nat.LF_STATUS_BAD_SEGMENT
+    else:
+        st.table[tp + last] = 1 << 30
+        want = nat.LF_STATUS_BAD_SEGMENT
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = linear_lora(x, W, None, u, fc, st, [0], H, status=status)
+    torch.cuda.synchronize()
+    assert status.item() & want
+    assert torch.equal(out[:128], good[:128])
