@@ -194,6 +194,23 @@ static int shrink_impl(cudaStream_t stream, int dtype, const void* x, int64_t ld
       int rc = encode(&q.a_map[m], dtype, 3, a, dims, strides, box, a_tma_swizzle(rank), "a");
       if (rc) return rc;
     }
+    // modules whose cache indices step evenly (q/k/v as 0, 1, 2), or a single
+    // module, share one 4D map: module i's A is d * a_module_stride elements after
+    // module i - 1's
+    int d = n_modules > 1 ? modules[1] - modules[0] : 1;
+    for (int m = 2; m < n_modules && d > 0; ++m)
+      if (modules[m] - modules[m - 1] != d) d = 0;
+    const int64_t mstride = n_modules == 1 ? int64_t(hidden) * rank * es : int64_t(d) * a_module_stride * es;
+    if (d > 0 && mstride >= int64_t(hidden) * rank * es && mstride % 16 == 0) {
+      const void* a = static_cast<const uint8_t*>(cache_a) + int64_t(modules[0]) * a_module_stride * es;
+      const int64_t ss = n_slots == 1 ? int64_t(hidden) * rank : a_slot_stride;
+      cuuint64_t dims[4] = {cuuint64_t(rank), cuuint64_t(hidden), cuuint64_t(n_modules), cuuint64_t(n_slots)};
+      cuuint64_t strides[3] = {cuuint64_t(rank) * es, cuuint64_t(mstride), cuuint64_t(ss) * es};
+      cuuint32_t box[4] = {cuuint32_t(rank), 64, cuuint32_t(n_modules), 1};
+      int rc = encode(&q.a_modules_map, dtype, 4, a, dims, strides, box, a_tma_swizzle(rank), "a (modules)");
+      if (rc) return rc;
+      q.a_one_box = 1;
+    }
     q.n_tokens = n_tokens;
     q.hidden = hidden;
     q.n_modules = n_modules;

@@ -80,6 +80,11 @@ struct alignas(64) ExpandPersistParams {
 struct alignas(64) ShrinkPersistParams {
   CUtensorMap x_map;                 // 2D {hidden, n_tokens}, box {64, 128}, SW128
   CUtensorMap a_map[kMaxModules];    // 3D {rank, hidden, n_slots}, box {rank, 64, 1}
+  // a_modules_map: 4D {rank, hidden, n_modules, n_slots}, box {rank, 64, n_modules, 1},
+  // set (a_one_box = 1) when the modules' A factors lie equally spaced in the cache,
+  // so that one copy per segment and K block stages every module's box
+  CUtensorMap a_modules_map;
+  int32_t a_one_box;
   int64_t n_tokens;
   int32_t hidden;
   int32_t n_modules;

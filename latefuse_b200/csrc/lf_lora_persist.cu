@@ -543,8 +543,13 @@ lora_shrink_persist_kernel(const __grid_constant__ ShrinkPersistParams p, int st
             tma_load_2d(st, &p.x_map, bar(FULL + s), kb * 64, row0);
             for (int jj = 0; jj < kp; ++jj) {
               const int32_t slot = sub_slot(cur, j0 + jj, p.seg_slot, p.n_segs);
-              for (int m = 0; m < n_mod; ++m)
-                tma_load_3d(st + kYBox + (jj * n_mod + m) * kABox, &p.a_map[m], bar(FULL + s), 0, kb * 64, slot);
+              // a copy costs about as much to issue as it takes to move 2 KB, so
+              // the modules' boxes go in one copy where the cache layout allows
+              if (p.a_one_box)
+                tma_load_4d(st + kYBox + jj * n_mod * kABox, &p.a_modules_map, bar(FULL + s), 0, kb * 64, 0, slot);
+              else
+                for (int m = 0; m < n_mod; ++m)
+                  tma_load_3d(st + kYBox + (jj * n_mod + m) * kABox, &p.a_map[m], bar(FULL + s), 0, kb * 64, slot);
             }
           }
         }

@@ -490,3 +490,27 @@ def test_tc_persistent_expand_many_items_per_cta(cuda):
     ref = segmented_apply(x.cpu()[rows], y.cpu()[rows], a_of, b_of, local, col_offsets=[0, H, 2 * H],
                           modules=[0, 1, 2])
     check(persistent.cpu()[rows], ref, y.cpu()[rows], dtype)
+
+
+@pytest.mark.parametrize("R", [8, 16, 32, 64])
+def test_shrink_one_copy_for_evenly_spaced_modules(cuda, R):
+    """Modules whose cache indices step evenly ([0, 1, 2], [1, 3]) have their A boxes
+    staged by one 4-D copy per segment; any other order takes one copy per module.
+    Both give the same bits for every module."""
+    dtype, H, n_slots = torch.bfloat16, 512, 7
+    fc, _, _ = make_cache(n_slots, 4, H, R, dtype, cuda, seed=R)
+    g = torch.Generator().manual_seed(R)
+    lens = torch.randint(1, 300, (12,), generator=g).tolist()
+    slots = torch.randint(0, n_slots, (12,), generator=g).tolist()
+    starts = [sum(lens[:i]) for i in range(12)]
+    T = sum(lens)
+    st = SegmentTable(starts, lens, slots, T, cuda)
+    x = torch.randn(T, H, device=cuda, dtype=dtype)
+    for mods, other in (([0, 1, 2], [2, 0, 1]), ([1, 3], [3, 1])):
+        u1 = torch.empty(len(mods), T, R, dtype=dtype, device=cuda)
+        u2 = torch.empty(len(mods), T, R, dtype=dtype, device=cuda)
+        lora_shrink(x, u1, fc, st, mods)
+        lora_shrink(x, u2, fc, st, other)
+        torch.cuda.synchronize()
+        for i, m in enumerate(mods):
+            assert torch.equal(u1[i], u2[other.index(m)]), (mods, m)
