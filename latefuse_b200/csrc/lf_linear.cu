@@ -25,8 +25,8 @@
 // shrink output u (written by lf_lora_shrink_blocked: the tile's rows of that
 // segment, other rows 0, in the no-swizzle K-major operand layout, so one bulk
 // copy stages it) and the segment's B factor columns (MN-major SW128, four
-// 64-column boxes straight from the slot cache, prefetched into L2 one tile
-// ahead), multiplied with K = R, so every row gets its own adapter's delta:
+// 64-column blocks in one copy straight from the slot cache, prefetched into L2
+// one tile ahead), multiplied with K = R, so every row gets its own adapter's delta:
 // y = act(round(x W^T + bias + u B)).
 // Every wait is bounded: a timeout sets LF_STATUS_TIMEOUT and the roles unwind.
 #include "lf_common.cuh"
@@ -52,7 +52,7 @@ struct alignas(64) LinearParams {
   CUtensorMap x_map;  // 2D {K, M}, box {64, 128}, SW128
   CUtensorMap w_map;  // 2D {K, N}, box {64, 256}, SW128
   CUtensorMap y_map;  // 2D {N, M}, box {32, 32}, SW64
-  CUtensorMap b_map[kMaxModules];     // LoRA: 3D {module_cols, R, n_slots}, box {64, R, 1}, SW128
+  CUtensorMap b_map[kMaxModules];     // LoRA: 4D {64, R, module_cols / 64, n_slots}, box {64, R, 4, 1}, SW128
   const void* u;                      // LoRA: blocked shrink output (lf_lora_shrink_blocked)
   const void* b_ptr[kMaxModules];     // LoRA: (slot 0, module i) B factors, for L2 prefetch
   int64_t b_slot_stride;              // elements
@@ -195,8 +195,10 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
           mbar_arrive_expect_tx(full, 768 * p.rank);        // u 128 x R + B R x 256
           bulk_load(dst, static_cast<const T*>(p.u) + (int64_t(mod) * n_blk + m0 / kBM + j) * kBM * p.rank,
                     256 * p.rank, full);
-          for (int b = 0; b < kBN / 64; ++b)
-            tma_load_3d(b_dst + b * p.rank * 128, &p.b_map[mod], full, n_loc + b * 64, 0, slot);
+          // the tile's 256 B columns as four 64-column blocks of R rows, block b at
+          // b_dst + b * R * 128, in one copy (a copy costs about as much to issue as
+          // it takes to move 2 KB)
+          tma_load_4d(b_dst, &p.b_map[mod], full, 0, 0, n_loc / 64, slot);
         };
         // The first pair goes to the delta buffer once the MMA has started this tile
         // (after K block kStages of it has been issued, the previous tile's delta is
@@ -459,7 +461,7 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
   LinearParams p;
   memset(&p, 0, sizeof(p));
   const CUtensorMapDataType dt = dtype == LF_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const cuuint32_t estr[3] = {1, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
   auto tmap = [&](CUtensorMap* map, int rank, const void* base, const cuuint64_t* dims, const cuuint64_t* strides,
                   const cuuint32_t* box, CUtensorMapSwizzle swz, const char* what) {
     if (enc(map, dt, cuuint32_t(rank), const_cast<void*>(base), dims, strides, box, estr,
@@ -496,10 +498,11 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
       const int64_t ss = L.n_slots == 1 ? int64_t(L.module_cols) * L.rank : L.b_slot_stride;
       p.b_ptr[i] = b;
       p.b_slot_stride = ss;
-      const cuuint64_t dims[3] = {cuuint64_t(L.module_cols), R, cuuint64_t(L.n_slots)};
-      const cuuint64_t strides[2] = {cuuint64_t(L.module_cols) * 2, cuuint64_t(ss) * 2};
-      const cuuint32_t box[3] = {64, R, 1};
-      if ((rc = tmap(&p.b_map[i], 3, b, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "b"))) return rc;
+      // (64 columns, R rows, column block, slot): one box holds a tile's four blocks
+      const cuuint64_t dims[4] = {64, R, cuuint64_t(L.module_cols / 64), cuuint64_t(L.n_slots)};
+      const cuuint64_t strides[3] = {cuuint64_t(L.module_cols) * 2, 128, cuuint64_t(ss) * 2};
+      const cuuint32_t box[4] = {64, R, kBN / 64, 1};
+      if ((rc = tmap(&p.b_map[i], 4, b, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "b"))) return rc;
     }
     p.tile_pairs = L.tile_pairs;
     p.pairs = L.pairs;
