@@ -6,6 +6,7 @@ instead of hanging)."""
 from __future__ import annotations
 
 import os
+import queue
 import socket
 from datetime import timedelta
 
@@ -35,8 +36,11 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, mode, q):
+def _worker(rank, world, port, mode, q, ready):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    # both ranks have started (spawning and importing torch can take seconds on a
+    # loaded machine) before the short-timeout rendezvous begins
+    ready.wait(timeout=120)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
     try:
         g = torch.Generator().manual_seed(0)
@@ -68,18 +72,22 @@ def _worker(rank, world, port, mode, q):
 def _run(mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
+    ready = ctx.Barrier(2)
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q, ready)) for r in range(2)]
     for p in procs:
         p.start()
+    results = {}
+    try:
+        for _ in range(2):  # one result per rank, read before joining
+            r, v = q.get(timeout=120)
+            results[r] = v
+    except queue.Empty:
+        pass
     for p in procs:
-        p.join(timeout=120)
+        p.join(timeout=60)
         if p.is_alive():
             p.kill()
-    results = {}
-    while not q.empty():
-        r, v = q.get()
-        results[r] = v
     return results
 
 
