@@ -31,6 +31,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from datetime import timedelta
 from pathlib import Path
@@ -122,7 +123,7 @@ class ClockSampler:
     def __init__(self, gpus: list[int]):
         self.gpus = gpus
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
+        self.path = Path(tempfile.gettempdir()) / f"latefuse_b200_clocks_{os.getpid()}.csv"
 
     def __enter__(self):
         try:
