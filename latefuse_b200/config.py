@@ -10,12 +10,14 @@ import torch
 
 @dataclass
 class LoraServingConfig:
-    """All configuration needed to run LoRA serving. Pass this to every component.
+    """The serving pipeline's shape: which encoder, which LoRA rank and targets,
+    the batch geometry, device and dtype.  Every store, engine and task object is
+    built from one instance of it.
 
-    Dimensions are derived from the HuggingFace model config of ``model_name``
-    (``AutoConfig.from_pretrained``), exactly as the reference does.  ``hf_config``
-    may be given instead to derive them from an in-memory config object (useful
-    offline, for synthetic random-init models).
+    The encoder's dimensions (hidden size, layers, heads, FFN width, LayerNorm
+    epsilon, activation) are read from the HuggingFace config of ``model_name``
+    (``AutoConfig.from_pretrained``), or from ``hf_config`` when one is passed,
+    so that a synthetic random-init encoder needs no checkpoint or network.
     """
 
     model_name: str

@@ -78,36 +78,39 @@ class HeadStore:
         del self._heads[tenant_id]
 
     # -- reference API -------------------------------------------------------
-    def load(self, tenant_id: str, coef, intercept) -> None:
-        """Cache a head from any array-like ``coef`` / ``intercept``.
-
-        Args:
-            coef:      ``(num_labels, H)``, or ``(H,)`` for a single output.
-            intercept: ``(num_labels,)``, or a scalar alongside a ``(H,)`` coef.
-
-        Raises:
-            ValueError: if the hidden size disagrees with the serving config, or
-                        coef and intercept disagree on the label count.
-        """
+    def _checked(self, tenant_id: str, coef, intercept) -> tuple[Tensor, Tensor]:
+        """``coef`` as ``(n, H)`` and ``intercept`` as ``(n,)`` in the serving dtype, or a
+        ``ValueError`` whose wording the reference's callers match on
+        (``src/latefuse/tasks/heads.py:58-96``)."""
         cfg = self._config
-        coef_t = torch.as_tensor(coef, dtype=cfg.dtype, device=cfg.device)
-        intercept_t = torch.as_tensor(intercept, dtype=cfg.dtype, device=cfg.device)
-        if coef_t.ndim == 1:
-            coef_t = coef_t.unsqueeze(0)
-        if intercept_t.ndim == 0:
-            intercept_t = intercept_t.unsqueeze(0)
-        if coef_t.ndim != 2:
-            raise ValueError(f"coef for '{tenant_id}' must be (num_labels, H) or (H,), got {tuple(coef_t.shape)}")
-        if coef_t.shape[1] != cfg.hidden_size:
+        c = torch.as_tensor(coef, dtype=cfg.dtype, device=cfg.device)
+        b = torch.as_tensor(intercept, dtype=cfg.dtype, device=cfg.device)
+        c = c.reshape(1, -1) if c.dim() == 1 else c
+        b = b.reshape(1) if b.dim() == 0 else b
+        if c.dim() != 2:
+            raise ValueError(f"coef for '{tenant_id}' must be (num_labels, H) or (H,), got {tuple(c.shape)}")
+        n, width = c.shape
+        if width != cfg.hidden_size:
             raise ValueError(
-                f"coef for '{tenant_id}' has hidden size {coef_t.shape[1]}, but {cfg.model_name} pools to "
+                f"coef for '{tenant_id}' has hidden size {width}, but {cfg.model_name} pools to "
                 f"{cfg.hidden_size}. A head fitted on a different backbone cannot be served by this one."
             )
-        if intercept_t.shape != (coef_t.shape[0],):
-            raise ValueError(
-                f"intercept for '{tenant_id}' has shape {tuple(intercept_t.shape)}, expected "
-                f"{(coef_t.shape[0],)} to match coef"
-            )
+        if tuple(b.shape) != (n,):
+            raise ValueError(f"intercept for '{tenant_id}' has shape {tuple(b.shape)}, expected {(n,)} to match coef")
+        return c, b
+
+    def load(self, tenant_id: str, coef, intercept) -> None:
+        """Store ``tenant_id``'s head in the packed cache, replacing any earlier one.
+
+        ``coef`` is ``(num_labels, H)``; a 1-D ``(H,)`` vector is a one-logit head
+        (binary, or a reranker's score) and then ``intercept`` may be a scalar.
+        Anything array-like is accepted and cast to the serving dtype.
+
+        Raises:
+            ValueError: ``coef`` is not 1-D or 2-D, its width is not the encoder's
+                        hidden size, or ``intercept`` has a different label count.
+        """
+        coef_t, intercept_t = self._checked(tenant_id, coef, intercept)
         n = coef_t.shape[0]
         if tenant_id in self._range:
             self._release(tenant_id)

@@ -338,12 +338,15 @@ class AdapterStore:
         """Register ``n`` adapters ``{prefix}{i}`` with A and B both ~ N(0, std), drawn
         in one pass over the cache (a fast path for large synthetic populations)."""
         ids = [f"{prefix}{i}" for i in range(n)]
+        # every id is checked before any slot is drawn or committed, so a refused
+        # call leaves the store exactly as it was
+        clash = next((aid for aid in ids if aid in self._slot_of), None)
+        if clash is not None:
+            raise ValueError(f"adapter '{clash}' is already resident")
         start = self._next
         self._ensure_slots(start + n)
         self._buf[start : start + n].normal_(0.0, std, generator=generator)
         for i, aid in enumerate(ids):
-            if aid in self._slot_of:
-                raise ValueError(f"adapter '{aid}' is already resident")
             slot = start + i
             wa, wb = self._views(slot)
             self._commit(aid, slot, LoraWeight._over(wa, wb))

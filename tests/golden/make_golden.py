@@ -2,7 +2,7 @@
 
 Run here (not on the GPU box), with the reference checkout importable:
 
-    python tests/golden/make_golden.py --reference /root/reference/src
+    python tests/golden/make_golden.py --reference <reference checkout>/src
 
 Every fixture is produced by the reference's own code on the CPU (LoraOps,
 IndexSelectBatchAssembler, BatchAssembler, HeadStore, LRHeadOps, pool_tokens,
@@ -267,8 +267,11 @@ def gen_chunking() -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference/src")
+    ap.add_argument("--reference", default=os.environ.get("LATEFUSE_REFERENCE_SRC"),
+                    help="the reference checkout's src/ directory (or set LATEFUSE_REFERENCE_SRC)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("pass --reference <checkout>/src or set LATEFUSE_REFERENCE_SRC")
     sys.path.insert(0, args.reference)
     os.environ.setdefault("HF_HUB_OFFLINE", "1")
     torch.set_num_threads(4)

@@ -304,6 +304,60 @@ def test_mixed_rank_padding_preserves_the_delta(tmp_path):
             assert (w.wa[m][i][:, 2:] == 0).all() and (w.wb[m][i][2:] == 0).all()
 
 
+@pytest.mark.parametrize("fmt", ["safetensors", "bin"])
+def test_registrar_matches_the_reference_fold_bit_for_bit(tmp_path, fmt):
+    """A slot staged by the registrar holds the bits of the reference's
+    ``LoraWeight.copy_from_tensors``: cast to bf16, transpose, multiply by
+    alpha / r in bf16 (``src/latefuse/weights/store.py:51-56``)."""
+    from safetensors.torch import save_file
+
+    c = cfg(rank=4, dtype=torch.bfloat16)
+    d, sd = _peft_dir(tmp_path, c, rank=4, alpha=12, seed=7)
+    if fmt == "safetensors":
+        (d / "adapter_model.bin").unlink()
+        save_file(sd, str(d / "adapter_model.safetensors"))
+    store = lf.AdapterStore(c)
+    lf.load_peft_adapter(store, "t", str(d))
+    w = store.get("t")
+    for m in c.target_modules:
+        a = torch.stack([sd[lf.peft_key_fn("bert")(i, m)[0]] for i in range(c.num_layers)])
+        b = torch.stack([sd[lf.peft_key_fn("bert")(i, m)[1]] for i in range(c.num_layers)])
+        assert torch.equal(w.wa[m], a.to(torch.bfloat16).transpose(1, 2))
+        assert torch.equal(w.wb[m], b.to(torch.bfloat16).transpose(1, 2).mul_(12 / 4))
+
+
+def test_registrar_reports_shapes_and_missing_keys(tmp_path):
+    c = cfg(rank=4)
+    d, sd = _peft_dir(tmp_path, c, rank=4, alpha=4, seed=8)
+    ka, _ = lf.peft_key_fn("bert")(1, "value")
+    bad = dict(sd)
+    bad[ka] = torch.randn(4, c.hidden_size + 1)
+    torch.save(bad, d / "adapter_model.bin")
+    with pytest.raises(ValueError, match="expected"):
+        lf.load_peft_adapter(lf.AdapterStore(c), "t", str(d))
+    del bad[ka]
+    torch.save(bad, d / "adapter_model.bin")
+    with pytest.raises(KeyError, match="has no tensor"):
+        lf.load_peft_adapter(lf.AdapterStore(c), "t", str(d))
+    with pytest.raises(FileNotFoundError):
+        lf.load_peft_adapter(lf.AdapterStore(c), "t", str(tmp_path / "missing"))
+
+
+def test_fill_random_refuses_a_resident_id_without_touching_the_store():
+    store = lf.AdapterStore(cfg(), capacity=4)
+    store.load_synthetic("adapter_1", seed=0)
+    before = store.get("adapter_1").wa["query"].clone()
+    with pytest.raises(ValueError, match="adapter_1"):
+        store.fill_random_(3)
+    assert store.adapter_ids() == ["adapter_1"]
+    assert torch.equal(store.get("adapter_1").wa["query"], before)
+    store.load_synthetic("next", seed=1)  # takes a fresh slot: the resident adapter is untouched
+    assert store.slot_of("next") != store.slot_of("adapter_1")
+    assert torch.equal(store.get("adapter_1").wa["query"], before)
+    ids = store.fill_random_(2, prefix="bulk_")
+    assert len({store.slot_of(i) for i in ids + ["adapter_1", "next"]}) == 4
+
+
 def test_mixed_rank_no_stale_weights_in_a_reused_slot(tmp_path):
     """A padded adapter loaded into the slot a full-rank adapter left behind
     carries none of its columns."""
