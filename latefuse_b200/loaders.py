@@ -4,15 +4,16 @@ A registration is a file read followed by one copy into a cache slot:
 
 1. ``adapter_config.json`` (rank ``r``, ``lora_alpha``, ``target_modules``) is
    checked against the serving config before anything is read or written.
-2. Every ``lora_A`` / ``lora_B`` tensor of the weights file is read on the host
-   once (a ``.safetensors`` file key by key, a ``.bin`` file memory-mapped) and
-   written straight into a *slot image* in pinned host memory: the slot's own
-   device layout ``[module][A (L, H, R) | B (L, R, H)]``, transposed, cast to the
-   model dtype, ``alpha / r`` folded into B, and a rank below the store's
-   zero-padded.
-3. One host-to-device copy (``lf_cache_write_slot``) moves the whole image into
-   the slot on the current stream.  Two images alternate, each guarded by an
-   event, so the host reads the next file while the previous copy runs.
+2. A ``.safetensors`` file is read whole, by one ``readinto``, into a reused
+   pinned buffer; for a CUDA store its bytes go to the device in one copy, and
+   the device casts each module's ``lora_A`` / ``lora_B`` tensors to the model
+   dtype, transposes them into the slot's layout
+   ``[module][A (L, H, R) | B (L, R, H)]``, folds ``alpha / r`` into B and
+   zero-pads a rank below the store's, writing straight into the slot.
+3. Otherwise (a ``.bin`` file, a CPU store) the same fold fills a *slot image*
+   in pinned host memory and one host-to-device copy (``lf_cache_write_slot``)
+   moves it into the slot.  Two images alternate, each guarded by an event, so
+   the host reads the next file while the previous copy runs.
 
 The file format is PEFT's, as the reference reads it
 (``src/latefuse/loaders.py:35-190``): keys
@@ -111,16 +112,40 @@ def _weights_file(path: str) -> str:
     raise FileNotFoundError(f"{path} holds none of {list(WEIGHT_FILES)}; expected a PEFT adapter directory")
 
 
+_SAFETENSORS_DTYPES = {"F32": torch.float32, "F16": torch.float16, "BF16": torch.bfloat16, "F64": torch.float64}
+
+
 class _TensorSource:
-    """Host tensors of a weights file by key, read lazily (safetensors) or memory-mapped (.bin)."""
+    """Host tensors of a weights file by key.
 
-    def __init__(self, path: str):
-        self._st = None
+    A ``.safetensors`` file (an 8-byte little-endian header length, a JSON header
+    ``{key: {dtype, shape, data_offsets}}``, then the raw data) is read whole with
+    one ``readinto`` into ``buffer``, a byte tensor the caller reuses from file to
+    file (pinned, for a CUDA store), and every tensor is a view of it: mapping the
+    file instead costs a page fault per 4 KB on every registration, several times
+    the read.  A ``.bin`` file goes through ``torch.load``.
+    """
+
+    def __init__(self, path: str, buffer: torch.Tensor | None = None, pin: bool = False):
+        self._st: dict | None = None
+        self.buffer = buffer
+        self.size = 0
         if path.endswith(".safetensors"):
-            from safetensors import safe_open
-
-            self._st = safe_open(path, framework="pt", device="cpu")
-            self._keys = set(self._st.keys())
+            size = os.path.getsize(path)
+            if self.buffer is None or self.buffer.numel() < size:
+                self.buffer = torch.empty(max(size, 1 << 20), dtype=torch.uint8, pin_memory=pin)
+            view = memoryview(self.buffer.numpy())[:size]
+            with open(path, "rb", buffering=0) as fh:
+                got = fh.readinto(view)
+            if got != size:
+                raise OSError(f"{path}: read {got} of {size} bytes")
+            n = int.from_bytes(bytes(view[:8]), "little")
+            header = json.loads(bytes(view[8 : 8 + n]))
+            header.pop("__metadata__", None)
+            self._st = header
+            self._base = 8 + n
+            self._keys = set(header)
+            self.size = size
         else:
             try:
                 self._sd = torch.load(path, map_location="cpu", weights_only=True, mmap=True)
@@ -128,21 +153,48 @@ class _TensorSource:
                 self._sd = torch.load(path, map_location="cpu", weights_only=True)
             self._keys = set(self._sd)
 
+    @property
+    def raw(self) -> bool:
+        """Whether every tensor is a view of :attr:`buffer` (a safetensors file)."""
+        return self._st is not None
+
     def __contains__(self, key: str) -> bool:
         return key in self._keys
 
+    def locate(self, key: str) -> tuple[int, torch.dtype, list[int]]:
+        """(byte offset in :attr:`buffer`, dtype, shape) of a raw tensor."""
+        meta = self._st[key]
+        dtype = _SAFETENSORS_DTYPES.get(meta["dtype"])
+        if dtype is None:
+            raise ValueError(f"tensor '{key}' has dtype {meta['dtype']}; expected a floating-point LoRA factor")
+        return self._base + meta["data_offsets"][0], dtype, list(meta["shape"])
+
     def __getitem__(self, key: str) -> torch.Tensor:
-        return self._st.get_tensor(key) if self._st is not None else self._sd[key]
+        if self._st is None:
+            return self._sd[key]
+        off, dtype, shape = self.locate(key)
+        n = dtype.itemsize
+        for d in shape:
+            n *= d
+        return self.buffer[off : off + n].view(dtype).view(shape)
+
+    def shape(self, key: str) -> tuple[int, ...]:
+        return tuple(self.locate(key)[2]) if self._st is not None else tuple(self._sd[key].shape)
 
     def sample_keys(self) -> list[str]:
         return sorted(self._keys)[:3]
 
 
 class AdapterRegistrar:
-    """Registers adapter files into one :class:`AdapterStore` through pinned slot images.
+    """Registers adapter files into one :class:`AdapterStore`.
 
     One registrar per store; :func:`load_peft_adapter` keeps one on the store.
-    A registration returns once its copy is queued on the current stream: kernels
+    For a CUDA store a ``.safetensors`` file goes to the device as it is, in one
+    copy from a pinned buffer, and the device casts, transposes and scales each
+    module's factors straight into the slot; other files (``.bin``, or tensors
+    whose offsets do not suit a device view) are staged on the host into a pinned
+    image of the slot and copied with ``lf_cache_write_slot``.  Either way a
+    registration returns once its work is queued on the current stream: kernels
     queued after it on that stream see the adapter.
     """
 
@@ -154,6 +206,9 @@ class AdapterRegistrar:
         self._images = [torch.empty(shape, dtype=cfg.dtype, pin_memory=self._cuda) for _ in range(max(1, images))]
         self._done = [None] * len(self._images)
         self._turn = 0
+        self._file_buffer: torch.Tensor | None = None  # the last weights file read, reused
+        self._file_done = None                          # event: the device has copied that buffer
+        self._dev_raw: torch.Tensor | None = None       # the file's bytes on the device
 
     def _image(self) -> torch.Tensor:
         i = self._turn
@@ -162,30 +217,50 @@ class AdapterRegistrar:
             self._done[i].synchronize()  # the copy that last read this image has finished
         return i, self._images[i]
 
-    def stage(self, image: torch.Tensor, source, key_fn, rank: int, scale: float, adapter_id: str) -> None:
-        """Fill a slot image from ``source[key]`` tensors (A ``(r, H)``, B ``(H, r)``)."""
+    def _factors(self, source, key_fn, rank: int, adapter_id: str) -> list[tuple[list[str], list[str]]]:
+        """Every module's A and B keys in layer order, checked for presence and shape."""
         cfg = self.store.config
-        L, H, R = cfg.num_layers, cfg.hidden_size, cfg.lora_rank
-        for mi, module in enumerate(cfg.target_modules):
-            a_img = image[mi, 0].view(L, H, R)
-            b_img = image[mi, 1].view(L, R, H)
-            if rank < R:  # nothing of a previous occupant may survive in the padding
-                a_img[:, :, rank:].zero_()
-                b_img[:, rank:, :].zero_()
-            for layer in range(L):
+        H = cfg.hidden_size
+        out = []
+        for module in cfg.target_modules:
+            keys_a, keys_b = [], []
+            for layer in range(cfg.num_layers):
                 key_a, key_b = key_fn(layer, module)
                 for key in (key_a, key_b):
                     if key not in source:
                         raise KeyError(f"adapter '{adapter_id}' has no tensor '{key}'. The key layout does not "
                                        f"match this key_fn; available keys start with {source.sample_keys()}")
-                a, b = source[key_a], source[key_b]
-                if tuple(a.shape) != (rank, H) or tuple(b.shape) != (H, rank):
-                    raise ValueError(f"adapter '{adapter_id}': {key_a} is {tuple(a.shape)} and {key_b} is "
-                                     f"{tuple(b.shape)}; expected ({rank}, {H}) and ({H}, {rank}) at rank {rank}")
-                a_img[layer, :, :rank].copy_(a.t())
-                b_img[layer, :rank, :].copy_(b.t())
-            if scale != 1.0:
-                b_img[:, :rank, :].mul_(scale)  # in the model dtype, after the cast, as the reference folds it
+                sa, sb = source.shape(key_a), source.shape(key_b)
+                if sa != (rank, H) or sb != (H, rank):
+                    raise ValueError(f"adapter '{adapter_id}': {key_a} is {sa} and {key_b} is {sb}; expected "
+                                     f"({rank}, {H}) and ({H}, {rank}) at rank {rank}")
+                keys_a.append(key_a)
+                keys_b.append(key_b)
+            out.append((keys_a, keys_b))
+        return out
+
+    @staticmethod
+    def _fold(wa: torch.Tensor, wb: torch.Tensor, a_layers, b_layers, rank: int, scale: float) -> None:
+        """Write one module's factors into ``wa (L, H, R)`` / ``wb (L, R, H)``: cast to the
+        model dtype, transpose, ``alpha / r`` folded into B in the model dtype (the
+        reference's order), padding beyond ``rank`` zeroed.  One copy per factor."""
+        R = wa.shape[2]
+        if rank < R:  # nothing of a previous occupant may survive in the padding
+            wa[:, :, rank:].zero_()
+            wb[:, rank:, :].zero_()
+        dt = wa.dtype
+        wa[:, :, :rank].copy_(torch.stack(a_layers).to(dt).transpose(1, 2))
+        wb[:, :rank, :].copy_(torch.stack(b_layers).to(dt).transpose(1, 2))
+        if scale != 1.0:
+            wb[:, :rank, :].mul_(scale)
+
+    def stage(self, image: torch.Tensor, source, plan, rank: int, scale: float) -> None:
+        """Fill a host slot image from the file's tensors."""
+        cfg = self.store.config
+        L, H, R = cfg.num_layers, cfg.hidden_size, cfg.lora_rank
+        for mi, (keys_a, keys_b) in enumerate(plan):
+            self._fold(image[mi, 0].view(L, H, R), image[mi, 1].view(L, R, H), [source[k] for k in keys_a],
+                       [source[k] for k in keys_b], rank, scale)
 
     def commit(self, adapter_id: str, index: int, image: torch.Tensor) -> None:
         """Copy a staged image into ``adapter_id``'s slot and make it resident."""
@@ -205,6 +280,44 @@ class AdapterRegistrar:
             store.cache[slot].copy_(image)
         store._commit(adapter_id, slot, weight)
 
+    def _device_ready(self, source, plan) -> bool:
+        """Whether every tensor can be viewed in place on the device (element-aligned offsets)."""
+        if not (self._cuda and source.raw):
+            return False
+        for keys_a, keys_b in plan:
+            for key in keys_a + keys_b:
+                off, dtype, _ = source.locate(key)
+                if off % dtype.itemsize:
+                    return False
+        return True
+
+    def commit_on_device(self, adapter_id: str, source, plan, rank: int, scale: float) -> None:
+        """One copy of the file's bytes to the device, then the fold into the slot there."""
+        store = self.store
+        dev = store.cache.device
+        stream = torch.cuda.current_stream(dev)
+        if self._dev_raw is None or self._dev_raw.numel() < source.size:
+            self._dev_raw = torch.empty(source.buffer.numel(), dtype=torch.uint8, device=dev)
+        raw = self._dev_raw
+        raw[: source.size].copy_(source.buffer[: source.size], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self._file_done = ev  # the next read into the pinned buffer waits for this copy
+
+        def view(key: str) -> torch.Tensor:
+            off, dtype, shape = source.locate(key)
+            n = dtype.itemsize
+            for d in shape:
+                n *= d
+            return raw[off : off + n].view(dtype).view(shape)
+
+        slot, weight = store._claim(adapter_id)
+        for mi, m in enumerate(store.config.target_modules):
+            keys_a, keys_b = plan[mi]
+            self._fold(weight.wa[m], weight.wb[m], [view(k) for k in keys_a], [view(k) for k in keys_b], rank,
+                       scale)
+        store._commit(adapter_id, slot, weight)
+
     def register(self, adapter_id: str, path: str, *, adapter_name: str = "default",
                  lora_alpha: float | None = None, strict: bool = True, pad_rank: bool = False) -> None:
         """Check, stage and copy one PEFT adapter (directory or weights file) into a slot."""
@@ -219,16 +332,23 @@ class AdapterRegistrar:
                     raise ValueError(msg + " Pass strict=False to load anyway.")
                 warnings.warn(msg, stacklevel=3)
         alpha = lora_alpha if lora_alpha is not None else (meta.alpha if meta is not None else None)
-        source = _TensorSource(_weights_file(path))
+        if self._file_done is not None:
+            self._file_done.synchronize()  # the pinned buffer's previous contents have reached the device
+        source = _TensorSource(_weights_file(path), self._file_buffer, pin=self._cuda)
+        self._file_buffer = source.buffer
         key_fn = peft_key_fn(cfg.hf_config.model_type, adapter_name)
         first = key_fn(0, cfg.target_modules[0])[0]
-        rank = source[first].shape[0] if first in source else cfg.lora_rank  # stage() reports a missing key
+        rank = source.shape(first)[0] if first in source else cfg.lora_rank  # _factors reports a missing key
         if rank > cfg.lora_rank or (rank < cfg.lora_rank and not (pad_rank or not strict)):
             raise ValueError(f"adapter '{adapter_id}' has rank {rank} but this store serves rank {cfg.lora_rank}"
                              + ("" if rank > cfg.lora_rank else "; pass pad_rank=True to zero-pad it into a slot"))
         scale = 1.0 if alpha is None else alpha / rank
+        plan = self._factors(source, key_fn, rank, adapter_id)  # everything checked before a slot is taken
+        if self._device_ready(source, plan):
+            self.commit_on_device(adapter_id, source, plan, rank, scale)
+            return
         index, image = self._image()
-        self.stage(image, source, key_fn, rank, scale, adapter_id)
+        self.stage(image, source, plan, rank, scale)
         self.commit(adapter_id, index, image)
 
 

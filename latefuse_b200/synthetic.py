@@ -45,12 +45,25 @@ def zipf_tenants(n_population: int, n_rows: int, alpha: float = 1.1, seed: int =
 
 
 def ragged_batch(batch: int, seq: int, *, min_len: int, max_len: int, vocab: int, pad_id: int = 1,
-                 cls_id: int = 0, low_id: int = 5, seed: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+                 cls_id: int = 0, low_id: int = 5, seed: int = 0,
+                 stratified: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
     """Host ``(input_ids, attention_mask)`` of ``batch`` right-padded rows with lengths
     uniform in ``[min_len, max_len]``: CLS at position 0, ids uniform in ``[low_id, vocab)``
-    elsewhere in the real part, ``pad_id`` with mask 0 after it."""
+    elsewhere in the real part, ``pad_id`` with mask 0 after it.
+
+    With ``stratified`` the lengths are a Latin-hypercube draw: row ``i`` of a random
+    permutation takes one uniform draw from the ``i``-th of ``batch`` equal bands of
+    ``[min_len, max_len + 1)``.  Each length is still uniform over the range, and the
+    batch's total is within one band of its expectation, so batches of one seed and
+    different sizes carry the same work per row."""
     g = torch.Generator().manual_seed(seed)
-    lengths = torch.randint(min_len, max_len + 1, (batch,), generator=g)
+    if stratified:
+        band = (max_len + 1 - min_len) / batch
+        u = torch.rand(batch, generator=g, dtype=torch.float64)
+        perm = torch.randperm(batch, generator=g).to(torch.float64)
+        lengths = (min_len + (perm + u) * band).floor().clamp(max=max_len).to(torch.int64)
+    else:
+        lengths = torch.randint(min_len, max_len + 1, (batch,), generator=g)
     ids = torch.randint(low_id, vocab, (batch, seq), generator=g)
     pos = torch.arange(seq).unsqueeze(0)
     mask = (pos < lengths.unsqueeze(1)).to(torch.int64)

@@ -7,6 +7,8 @@ from pathlib import Path
 
 import torch
 
+import latefuse_b200 as lf
+
 GOLD = Path(__file__).resolve().parent / "golden"
 
 
@@ -52,3 +54,52 @@ def insert_adapters(store, adapters: dict, config) -> None:
 
 def texts(n: int) -> list[str]:
     return [f"tok{i % 40} tok{(i * 7) % 40}" for i in range(n)]
+
+
+def hf_model(kind: str, conf: dict, dev, dtype, seed: int = 0):
+    """A HuggingFace encoder with N(0, 0.02) weights, zero biases and unit LayerNorms,
+    drawn on ``dev`` from ``seed`` (the models' own initialisation, without the CPU pass)."""
+    from transformers import BertConfig, BertModel, XLMRobertaConfig, XLMRobertaModel
+
+    cfg_cls, model_cls = (BertConfig, BertModel) if kind == "bert" else (XLMRobertaConfig, XLMRobertaModel)
+    hf = cfg_cls(**conf)
+    with torch.device("meta"):
+        model = model_cls(hf)
+    model = model.to_empty(device=dev).eval()
+    g = torch.Generator(device=dev).manual_seed(seed)
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if "LayerNorm.weight" in name:
+                p.fill_(1.0)
+            elif name.endswith("bias"):
+                p.zero_()
+            else:
+                p.normal_(0.0, 0.02, generator=g)
+        if hf.pad_token_id is not None:
+            model.embeddings.word_embeddings.weight[hf.pad_token_id].zero_()
+        for name, b in model.named_buffers():
+            if name.endswith("position_ids"):
+                b.copy_(torch.arange(b.shape[-1], device=dev).expand_as(b))
+            else:
+                b.zero_()
+    return model.to(dtype), hf
+
+
+def serving_config(hf, dev, dtype, rank, targets, batch, seq):
+    return lf.LoraServingConfig(model_name=f"{hf.model_type}-shape (synthetic)", lora_rank=rank, batch_size=batch,
+                                max_seq_len=seq, target_modules=list(targets), device=dev, dtype=dtype,
+                                hf_config=hf)
+
+
+def adapters_of(store, tenants) -> dict:
+    """The oracle's view of the store's adapters (the slot views themselves)."""
+    out = {}
+    for t in set(tenants):
+        w = store.get(t)
+        out[t] = {"wa": dict(w.wa), "wb": dict(w.wb)}
+    return out
+
+
+def row_rel(a, b) -> float:
+    a, b = a.float(), b.float()
+    return ((a - b).norm(dim=-1) / b.norm(dim=-1).clamp_min(1e-12)).max().item()
