@@ -324,6 +324,29 @@ int lf_head_forward(void* stream, int dtype,
                     void* logits_out, float* probs_out,
                     int32_t* status);
 
+/* The same heads for the padding-free forward, whose hidden states are packed
+ * (n_tokens, H) with row stride ld: row b is token row_index[b] (its first, CLS,
+ * token; NULL: row b).  With pooler_w (H x H) and pooler_b the rows first go
+ * through the encoder's pooler,
+ *     pooled[b] = round(tanh(round(hidden[row_index[b]] . pooler_w^T + pooler_b)))
+ * (the HF pooler the reference's "auto" pooling returns,
+ * src/latefuse/model/hf_wrapper.py:337-342, src/latefuse/model/encoder.py:281:
+ * nn.Linear then tanh), written to
+ * pooled_out, which is then required; then normalisation / head / softmax as
+ * lf_head_forward with LF_POOL_NONE.  This fuses the reference classifier's CLS
+ * gather, pooler and padded head bmm (src/latefuse/tasks/classification.py:42-119,
+ * src/latefuse/ops/head.py:50-51) into one call of two launches (the head
+ * kernel is a programmatic dependent of the pooler). */
+int lf_head_forward_rows(void* stream, int dtype,
+                         const void* hidden, int64_t ld, const int32_t* row_index,
+                         int batch, int hidden_size,
+                         const void* pooler_w, const void* pooler_b,
+                         void* pooled_out, void* normed_out,
+                         const void* coef, const void* bias, int64_t head_rows,
+                         const int32_t* head_off, const int32_t* head_n, int n_max,
+                         void* logits_out, float* probs_out,
+                         int32_t* status);
+
 /* ------------------------------------------------------------------------
  * Projection GEMM
  * ------------------------------------------------------------------------ */

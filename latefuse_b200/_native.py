@@ -84,6 +84,9 @@ SIGNATURES: dict[str, tuple] = {
         c_void_p, c_int, c_void_p, c_int64, c_int64, c_void_p, c_int, c_int, c_int, c_int,
         c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int,
         c_void_p, c_void_p, c_void_p]),
+    "lf_head_forward_rows": (c_int, [
+        c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+        c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "lf_linear": (c_int, [
         c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int,
         c_int, c_int, c_void_p]),

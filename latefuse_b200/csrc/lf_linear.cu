@@ -1,4 +1,4 @@
-// Projection GEMM on tcgen05: Y = act(X W^T + bias), bf16 / f16 in, f32 accumulate.
+// Projection GEMM on tcgen05 CTA pairs: Y = act(X W^T + bias), bf16 / f16 in, f32 accumulate.
 //
 // Replaces the encoder's nn.Linear projections (src/latefuse/model/encoder.py:
 // the fused q/k/v, attention-output, FFN up and down projections) with an
@@ -7,28 +7,38 @@
 // encoder.py:122,139).  Rounding follows torch: round(acc + bias) to the dtype,
 // then for GELU round(gelu_f32(that)).
 //
-// Persistent, one CTA per SM, 128 x 256 output tiles in m-major order (the CTAs
-// working at one time share the rows of X and all of W through L2):
-//   warp 0      TMA producer: per 64-wide K block an X box {64, 128} and a W box
-//               {64, 256} (both K-major, SW128) into a 4-stage ring of 48 KB;
-//   warp 1      MMA issuer: four tcgen05.mma (M=128, N=256, K=16) per K block
-//               into one of two TMEM accumulators (256 columns each), so the
-//               epilogue of one tile overlaps the main loop of the next;
-//   warps 2-9   epilogue, two warps per TMEM lane quadrant (128 columns each),
-//               one output row per thread: 32 columns per tcgen05.ld, bias and
-//               activation in f32, rounded, staged per warp in a 32 x 32 SW64
-//               tile and written by TMA (rows past M are clipped by
-//               the tensor map).
+// Persistent, one cluster of two CTAs per SM pair, 256 x 256 output tiles in
+// m-major order (the pairs working at one time share the rows of X and all of
+// W through L2).  The MMAs are tcgen05.mma.cta_group::2 with M = 256: CTA r of
+// the pair stages its own 128 rows of X and W rows [n0 + 128 r, n0 + 128 r + 128)
+// per 64-wide K block, and the leader's MMA reads both CTAs' shared memory, so
+// each SM stages 32 KB per K block instead of the 48 KB of a 128 x 256 tile on
+// one SM (less L2 -> SM traffic and fewer shared-memory writes per FLOP: more
+// work per joule, which is what the 1000 W cap rations).  Each CTA's TMEM holds
+// its 128 rows x 256 columns, twice (the epilogue of one tile overlaps the main
+// loop of the next).
+//   warp 0      TMA producer (both CTAs): an X box {64, 128} and a W box {64, 128}
+//               (K-major, SW128) per K block into a 6-stage ring of 32 KB; every
+//               copy completes on the leader's "full" barrier, which the leader's
+//               producer arms with both CTAs' bytes;
+//   warp 1      MMA issuer (leader only): four tcgen05.mma (M=256, N=256, K=16) per
+//               K block; each commit arrives on both CTAs' barriers (multicast);
+//   warps 2-9   epilogue (both CTAs), two warps per TMEM lane quadrant (128 columns
+//               each), one output row per thread: 32 columns per tcgen05.ld, bias
+//               and activation in f32, rounded, staged per warp in a 32 x 32 SW64
+//               tile and written by TMA (rows past M are clipped by the tensor map);
+//               each warp then arrives on the leader's "accumulator empty" barrier.
 // With LoRA (lf_linear_lora) the per-row delta joins the same accumulator: after
-// a tile's K blocks come one "delta block" per adapter segment overlapping the
-// tile's rows, staged through the same ring: the (tile, segment) block of the
-// shrink output u (written by lf_lora_shrink_blocked: the tile's rows of that
-// segment, other rows 0, in the no-swizzle K-major operand layout, so one bulk
-// copy stages it) and the segment's B factor columns (MN-major SW128, four
-// 64-column blocks in one copy straight from the slot cache, prefetched into L2
-// one tile ahead), multiplied with K = R, so every row gets its own adapter's delta:
-// y = act(round(x W^T + bias + u B)).
+// a tile's K blocks come one "delta block" per adapter segment with tokens in the
+// tile's 256 rows: each CTA stages its 128 rows of the segment's shrink output u
+// (written by lf_lora_shrink_blocked in the no-swizzle K-major operand layout: the
+// block of (128-row tile, segment), or zeros when the segment has no token in this
+// CTA's rows, fetched from past the end of u) and its 128 columns of the segment's
+// B factor (MN-major SW128, straight from the slot cache, prefetched into L2 one
+// tile ahead), and the leader multiplies them with K = R, so every row gets its
+// own adapter's delta: y = act(round(x W^T + bias + u B)).
 // Every wait is bounded: a timeout sets LF_STATUS_TIMEOUT and the roles unwind.
+// No load uses cluster multicast: each CTA loads only its own operands.
 #include "lf_common.cuh"
 #include "lf_internal.h"
 
@@ -36,31 +46,32 @@ namespace lf {
 
 namespace {
 
-constexpr int kBM = 128, kBN = 256, kBK = 64;
-constexpr int kABytes = kBM * kBK * 2;           // 16 KB
-constexpr int kBBytes = kBN * kBK * 2;           // 32 KB
-constexpr int kStageBytes = kABytes + kBBytes;   // 48 KB
-constexpr int kStages = 4;
-constexpr int kEpiWarps = 8;                    // two per TMEM lane quadrant, 128 columns each
+constexpr int kBM = 128, kBN = 256, kBK = 64;     // kBM rows per CTA, 2 kBM per pair
+constexpr int kABytes = kBM * kBK * 2;            // 16 KB: this CTA's X rows
+constexpr int kBBytes = (kBN / 2) * kBK * 2;      // 16 KB: this CTA's half of the W rows
+constexpr int kStageBytes = kABytes + kBBytes;    // 32 KB
+constexpr int kStages = 6;
+constexpr int kEpiWarps = 8;                      // two per TMEM lane quadrant, 128 columns each
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kOutCols = 32;                     // output columns per epilogue store
-constexpr int kOutBuf = 32 * kOutCols * 2;       // one warp's 32 x 32 staging tile: 2 KB
-constexpr int kDeltaBuf = 16384;                 // one delta block (rank 16) loaded at the tile's start
+constexpr int kOutCols = 32;                      // output columns per epilogue store
+constexpr int kOutBuf = 32 * kOutCols * 2;        // one warp's 32 x 32 staging tile: 2 KB
+constexpr int kDeltaBuf = 8192;                   // a tile's first delta block at rank 16: u 4 KB + B 4 KB
 constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kEpiWarps * kOutBuf + kDeltaBuf + 1024;
 
 struct alignas(64) LinearParams {
   CUtensorMap x_map;  // 2D {K, M}, box {64, 128}, SW128
-  CUtensorMap w_map;  // 2D {K, N}, box {64, 256}, SW128
+  CUtensorMap w_map;  // 2D {K, N}, box {64, 128}, SW128
   CUtensorMap y_map;  // 2D {N, M}, box {32, 32}, SW64
-  CUtensorMap b_map[kMaxModules];     // LoRA: 4D {64, R, module_cols / 64, n_slots}, box {64, R, 4, 1}, SW128
-  const void* u;                      // LoRA: blocked shrink output (lf_lora_shrink_blocked)
+  CUtensorMap u_map;  // LoRA: 3D {256, R / 2, n_mod * n_blk}, box {256, R / 2, 1}: one 128 x R block
+  CUtensorMap b_map[kMaxModules];     // LoRA: 4D {64, R, module_cols / 64, n_slots}, box {64, R, 2, 1}, SW128
   const void* b_ptr[kMaxModules];     // LoRA: (slot 0, module i) B factors, for L2 prefetch
   int64_t b_slot_stride;              // elements
   int32_t n_slots;
   const void* bias;   // N entries or null
-  const int32_t* tile_pairs;          // LoRA: tile b's (segment, slot) pairs are entries
-  const int32_t* pairs;               //   tile_pairs[b] .. tile_pairs[b + 1] of pairs; null: no delta
+  const int32_t* tile_pairs;          // LoRA: 256-row tile q's delta blocks are entries
+  const int32_t* pairs;               //   tile_pairs[q] .. tile_pairs[q + 1] of pairs (3 each); null: no delta
   int32_t n_segs;
+  int32_t n_blk;                      // LoRA: u blocks per module (128-row tiles + segments)
   int32_t rank;
   int32_t n_mod;                      // output column block i (module_cols wide) takes module i's delta
   int32_t module_cols;
@@ -72,21 +83,74 @@ struct alignas(64) LinearParams {
   int32_t* status;
 };
 
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-               "l"(src), "r"(bytes), "r"(bar)
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster,
+                                                 int32_t c0, int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster,
+                                                 int32_t c0, int32_t c1, int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster,
+                                                 int32_t c0, int32_t c1, int32_t c2, int32_t c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// D[tmem] (+)= A * B over the CTA pair (M = 256: each CTA supplies 128 rows of A and
+// half of B's columns from the same shared-memory offsets).
+__device__ __forceinline__ void umma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on the barrier at offset `bar` in both CTAs of the pair once every MMA
+// issued so far has completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  const uint16_t both = 3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          bar),
+      "h"(both)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit_pair_local(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
 
 __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
-// Entries [q0, q1) of the pair table for 128-row tile b.  A range that is not
-// ascending or holds more pairs than there are segments reads as empty, and
-// `bad` says so, so that every role walks the same (no) pairs.
-__device__ __forceinline__ int2 pair_range(const int32_t* tile_pairs, int b, int n_segs, bool* bad = nullptr) {
-  const int q0 = __ldg(tile_pairs + b), q1 = __ldg(tile_pairs + b + 1);
+// Entries [q0, q1) of the pair table for 256-row tile q.  A range that is not
+// ascending or holds more entries than there are segments reads as empty, and
+// `bad` says so, so that every role walks the same (no) entries.
+__device__ __forceinline__ int2 pair_range(const int32_t* tile_pairs, int q, int n_segs, bool* bad = nullptr) {
+  const int q0 = __ldg(tile_pairs + q), q1 = __ldg(tile_pairs + q + 1);
   const bool ok = q0 >= 0 && q1 >= q0 && q1 - q0 <= n_segs;
   if (bad != nullptr) *bad = !ok;
   return ok ? make_int2(q0, q1) : make_int2(0, 0);
@@ -103,6 +167,8 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_ctarank();          // 0: the leader, which issues the MMAs
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
 
   const uint32_t s_stage0 = base;
   const uint32_t s_out0 = base + kStages * kStageBytes;  // [warp] 2 KB staging tiles
@@ -111,35 +177,36 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   const int FULL = 0, EMPTY = kStages, ACC_FULL = 2 * kStages, ACC_EMPTY = 2 * kStages + 2,
             DRAIN = 2 * kStages + 4, DFULL = DRAIN + 1, DEMPTY = DRAIN + 2, N_BARS = DRAIN + 3;
-  // a tile's first delta block goes to its own buffer, loaded before the tile's K
-  // blocks, so it has landed when the MMA reaches it (later ones use the ring)
-  const bool dbuf = p.pairs != nullptr && 768 * p.rank <= kDeltaBuf;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(&bars[N_BARS]);
   int32_t* s_abort = reinterpret_cast<int32_t*>(tmem_slot + 1);
 
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) {
-      mbar_init(bar(FULL + i), 1);
-      mbar_init(bar(EMPTY + i), 1);
+      mbar_init(bar(FULL + i), 1);   // the leader's arrive, with both CTAs' bytes
+      mbar_init(bar(EMPTY + i), 1);  // the leader's MMA commit
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(ACC_FULL + i), 1);
-      mbar_init(bar(ACC_EMPTY + i), kEpiWarps);
+      mbar_init(bar(ACC_EMPTY + i), 2 * kEpiWarps);  // both CTAs' epilogue warps
     }
     mbar_init(bar(DRAIN), 1);
-    mbar_init(bar(DFULL), 1);
-    mbar_init(bar(DEMPTY), 1);
+    mbar_init(bar(DFULL), 1);   // the leader's arrive, with both CTAs' bytes
+    mbar_init(bar(DEMPTY), 1);  // the leader's MMA commit
     *s_abort = 0;
     fence_mbar_init();
     prefetch_tmap(&p.x_map);
     prefetch_tmap(&p.w_map);
     prefetch_tmap(&p.y_map);
   }
-  if (warp == 1) {
+  if (warp == 1) {  // the same warp in both CTAs allocates the pair's TMEM
     __syncwarp();
-    tmem_alloc(smem_u32(tmem_slot), 2 * kBN);
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(2 * kBN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
   __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before either signals the other's
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_wait();
@@ -149,61 +216,69 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     set_status(p.status, LF_STATUS_TIMEOUT);
     atomicExch(s_abort, 1);
   };
+  const bool lora = p.pairs != nullptr;
+  // a tile's first delta block goes to its own buffer, loaded while the tile's K
+  // blocks stream, so it has landed when the MMA reaches it (later ones use the ring)
+  const bool dbuf = lora && 512 * p.rank <= kDeltaBuf;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------------ producer (both CTAs)
     if (lane == 0) {
-      int kk = 0, dk = 0;
+      int kk = 0;
       bool stop = false;
-      // the B factors of a tile's segments, into L2 (whole rank x module_cols block)
+      const int32_t half_cols = int32_t(rank) * (kBN / 2);
+      // this CTA's half of the B factors of a tile's segments, into L2
       auto prefetch_b = [&](int64_t tt) {
-        if (p.pairs == nullptr || tt >= p.n_tiles) return;
-        const int pmod = int32_t(tt % p.n_tiles_n) * kBN / p.module_cols;
+        if (!lora || tt >= p.n_tiles) return;
+        const int32_t nn0 = int32_t(tt % p.n_tiles_n) * kBN;
+        const int pmod = nn0 / p.module_cols;
         if (pmod >= p.n_mod) return;
-        const int mb = int32_t(tt / p.n_tiles_n);
-        const int2 qr = pair_range(p.tile_pairs, mb, p.n_segs);
+        const int2 qr = pair_range(p.tile_pairs, int(tt / p.n_tiles_n), p.n_segs);
         for (int q = qr.x; q < qr.y; ++q) {
-          const int32_t slot = __ldg(p.pairs + 2 * q + 1);
+          const int32_t slot = __ldg(p.pairs + 3 * q + 1);
           if (slot >= 0 && slot < p.n_slots)
             prefetch_l2(static_cast<const T*>(p.b_ptr[pmod]) + int64_t(slot) * p.b_slot_stride,
                         uint32_t(p.rank) * uint32_t(p.module_cols) * 2u);
         }
       };
-      prefetch_b(blockIdx.x);
-      for (int64_t t = blockIdx.x; t < p.n_tiles && !stop; t += gridDim.x) {
-        const int32_t m0 = int32_t(t / p.n_tiles_n) * kBM, n0 = int32_t(t % p.n_tiles_n) * kBN;
-        const int mod = p.pairs != nullptr ? n0 / p.module_cols : p.n_mod;
+      prefetch_b(pair);
+      int dk = 0;
+      for (int64_t t = pair; t < p.n_tiles && !stop; t += n_pairs) {
+        const int32_t tq = int32_t(t / p.n_tiles_n);
+        const int32_t m0 = tq * (2 * kBM) + int32_t(rank) * kBM;
+        const int32_t n0 = int32_t(t % p.n_tiles_n) * kBN;
+        const int mod = lora ? n0 / p.module_cols : p.n_mod;
         int q0 = 0, q1 = 0;
-        if (mod < p.n_mod) {  // loaded now, used after the K blocks
+        if (mod < p.n_mod) {
           bool bad = false;
-          const int2 qr = pair_range(p.tile_pairs, m0 / kBM, p.n_segs, &bad);
-          if (bad) set_status(p.status, LF_STATUS_BAD_SEGMENT);
+          const int2 qr = pair_range(p.tile_pairs, tq, p.n_segs, &bad);
+          if (bad && rank == 0) set_status(p.status, LF_STATUS_BAD_SEGMENT);
           q0 = qr.x;
           q1 = qr.y;
         }
         const int32_t n_loc = mod < p.n_mod ? n0 - mod * p.module_cols : 0;
-        const int64_t n_blk = (p.m_rows + kBM - 1) / kBM + p.n_segs;
-        // u block of pair q (tile rows of its segment, others 0) and the segment's B columns
-        auto load_delta = [&](uint32_t dst, uint32_t b_dst, uint32_t full, int q) {
-          int j = __ldg(p.pairs + 2 * q);
-          const int32_t slot = __ldg(p.pairs + 2 * q + 1);  // out of range: zero fill, no delta, reported
-          if (j < 0 || j >= p.n_segs) {  // a segment outside the table: read block j = 0, reported
-            set_status(p.status, LF_STATUS_BAD_SEGMENT);
-            j = 0;
+        const int32_t zero_blk = p.n_mod * p.n_blk;  // past the last block: the copy reads zeros
+        // delta block q: this CTA's 128 rows of u (its block of (128-row tile, segment), or
+        // zeros) and its 128 columns of the segment's B, completing on the leader's `full`
+        auto load_delta = [&](uint32_t dst_u, uint32_t dst_b, uint32_t full_local, int q) {
+          int j = __ldg(p.pairs + 3 * q);
+          const int32_t slot = __ldg(p.pairs + 3 * q + 1);  // out of range: zero fill, no delta, reported
+          const int32_t mask = __ldg(p.pairs + 3 * q + 2);
+          if (j < 0 || j >= p.n_segs) {  // a segment outside the table: treated as absent, reported
+            if (rank == 0) set_status(p.status, LF_STATUS_BAD_SEGMENT);
+            j = -1;
           }
-          if (slot < 0 || slot >= p.n_slots) set_status(p.status, LF_STATUS_BAD_SLOT);
-          mbar_arrive_expect_tx(full, 768 * p.rank);        // u 128 x R + B R x 256
-          bulk_load(dst, static_cast<const T*>(p.u) + (int64_t(mod) * n_blk + m0 / kBM + j) * kBM * p.rank,
-                    256 * p.rank, full);
-          // the tile's 256 B columns as four 64-column blocks of R rows, block b at
-          // b_dst + b * R * 128, in one copy (a copy costs about as much to issue as
-          // it takes to move 2 KB)
-          tma_load_4d(b_dst, &p.b_map[mod], full, 0, 0, n_loc / 64, slot);
+          if ((slot < 0 || slot >= p.n_slots) && rank == 0) set_status(p.status, LF_STATUS_BAD_SLOT);
+          const int32_t blk = (j >= 0 && ((mask >> rank) & 1)) ? mod * p.n_blk + 2 * tq + int32_t(rank) + j
+                                                               : zero_blk;
+          const uint32_t full = mapa_shared(full_local, 0);
+          if (rank == 0) mbar_arrive_expect_tx(full_local, 2 * 512 * p.rank);  // u 128 x R + B R x 128, twice
+          tma_load_3d_pair(dst_u, &p.u_map, full, 0, 0, blk);
+          tma_load_4d_pair(dst_b, &p.b_map[mod], full, 0, 0, (n_loc + half_cols) / 64, slot);
         };
-        // The first pair goes to the delta buffer once the MMA has started this tile
-        // (after K block kStages of it has been issued, the previous tile's delta is
-        // done): it then has the rest of the tile's K blocks to land.
         const bool use_dbuf = dbuf && q1 > q0;
+        // the first block is loaded once the MMA has started this tile (by then the
+        // previous tile's first block has been multiplied)
         const int d_after = (p.n_kb < kStages ? p.n_kb : kStages) - 1;
         for (int kb = 0; kb < p.n_kb; ++kb, ++kk) {
           const int s = kk % kStages;
@@ -213,9 +288,10 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
             break;
           }
           const uint32_t st = s_stage0 + s * kStageBytes;
-          mbar_arrive_expect_tx(bar(FULL + s), kStageBytes);
-          tma_load_2d(st, &p.x_map, bar(FULL + s), kb * kBK, m0);
-          tma_load_2d(st + kABytes, &p.w_map, bar(FULL + s), kb * kBK, n0);
+          const uint32_t full = mapa_shared(bar(FULL + s), 0);
+          if (rank == 0) mbar_arrive_expect_tx(bar(FULL + s), 2 * kStageBytes);
+          tma_load_2d_pair(st, &p.x_map, full, kb * kBK, m0);
+          tma_load_2d_pair(st + kABytes, &p.w_map, full, kb * kBK, n0 + half_cols);
           if (use_dbuf && kb == d_after) {
             if (aborted_flag(s_abort) || !mbar_wait(bar(DEMPTY), (dk & 1) ^ 1)) {
               if (!aborted_flag(s_abort)) fail();
@@ -223,36 +299,37 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
               ++kk;
               break;
             }
-            // the delta buffer holds u at its start and B right after it (1 KB-aligned)
             load_delta(s_delta, s_delta + 256 * p.rank, bar(DFULL), q0);
             ++dk;
           }
         }
         if (use_dbuf) ++q0;
-        if (!stop) prefetch_b(t + gridDim.x);  // the ring is full here: the producer has time
+        if (!stop) prefetch_b(t + n_pairs);  // the ring is full here: the producer has time
         if (stop || mod >= p.n_mod) continue;
-        for (int q = q0; q < q1; ++q) {
+        for (int q = q0; q < q1; ++q, ++kk) {
           const int s = kk % kStages;
           if (aborted_flag(s_abort) || !mbar_wait(bar(EMPTY + s), ((kk / kStages) & 1) ^ 1)) {
             if (!aborted_flag(s_abort)) fail();
             stop = true;
             break;
           }
-          load_delta(s_stage0 + s * kStageBytes, s_stage0 + s * kStageBytes + kABytes, bar(FULL + s), q);
-          ++kk;
+          const uint32_t st = s_stage0 + s * kStageBytes;
+          load_delta(st, st + kABytes, bar(FULL + s), q);
         }
       }
       if (aborted_flag(s_abort)) {  // loads nobody consumed land before the CTA exits (bounded)
-        for (int q = (kk > kStages ? kk - kStages : 0); q < kk; ++q)
-          mbar_wait(bar(FULL + q % kStages), (q / kStages) & 1);
-        if (dk > 0) mbar_wait(bar(DFULL), (dk - 1) & 1);
+        if (rank == 0) {
+          for (int q = (kk > kStages ? kk - kStages : 0); q < kk; ++q)
+            mbar_wait(bar(FULL + q % kStages), (q / kStages) & 1);
+          if (dk > 0) mbar_wait(bar(DFULL), (dk - 1) & 1);
+        }
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer (lane 0)
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16(DT<T>::umma_fmt, kBM, kBN, 0, 0);
-      const uint32_t idesc_d = umma_idesc_f16(DT<T>::umma_fmt, kBM, kBN, 0, 1);
+    // ------------------------------------------------------------ MMA issuer (the leader's lane 0)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(DT<T>::umma_fmt, 2 * kBM, kBN, 0, 0);
+      constexpr uint32_t idesc_d = umma_idesc_f16(DT<T>::umma_fmt, 2 * kBM, kBN, 0, 1);
       int kk = 0, it = 0, dk = 0;
       bool stop = false;
       auto wait = [&](uint32_t b, uint32_t parity) {
@@ -261,16 +338,17 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
         if (!aborted_flag(s_abort)) fail();
         return false;
       };
-      for (int64_t t = blockIdx.x; t < p.n_tiles && !stop; t += gridDim.x, ++it) {
+      for (int64_t t = pair; t < p.n_tiles && !stop; t += n_pairs, ++it) {
         const int a = it & 1;
-        const int32_t m0 = int32_t(t / p.n_tiles_n) * kBM, n0 = int32_t(t % p.n_tiles_n) * kBN;
-        const int mod = p.pairs != nullptr ? n0 / p.module_cols : p.n_mod;
+        const int32_t n0 = int32_t(t % p.n_tiles_n) * kBN;
+        const int mod = lora ? n0 / p.module_cols : p.n_mod;
         int n_delta = 0;
-        if (mod < p.n_mod) {  // loaded now, used after the K blocks
-          const int2 qr = pair_range(p.tile_pairs, m0 / kBM, p.n_segs);
+        if (mod < p.n_mod) {
+          const int2 qr = pair_range(p.tile_pairs, int(t / p.n_tiles_n), p.n_segs);
           n_delta = qr.y - qr.x;
         }
         if (!wait(bar(ACC_EMPTY + a), ((it >> 1) & 1) ^ 1)) break;
+        tc_fence_after();
         for (int kb = 0; kb < p.n_kb; ++kb, ++kk) {
           const int s = kk % kStages;
           if (!wait(bar(FULL + s), (kk / kStages) & 1)) {
@@ -281,59 +359,58 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
           const uint32_t st = s_stage0 + s * kStageBytes;
 #pragma unroll
           for (int q = 0; q < kBK / 16; ++q)
-            umma_f16(tmem + a * kBN, smem_desc(st + q * 32, 16, 1024, 2), smem_desc(st + kABytes + q * 32, 16, 1024, 2),
-                     idesc, (kb | q) != 0 ? 1u : 0u);
-          umma_commit(bar(EMPTY + s));
+            umma_pair(tmem + a * kBN, smem_desc(st + q * 32, 16, 1024, 2), smem_desc(st + kABytes + q * 32, 16, 1024, 2),
+                      idesc, (kb | q) != 0 ? 1u : 0u);
+          umma_commit_pair(bar(EMPTY + s));
         }
-        if (!stop && n_delta > 0) {
-          const int nq = p.rank / 8;  // 16-byte chunks of a u row
-          auto delta_mma = [&](uint32_t ua, uint32_t ba) {
-            tc_fence_after();
-            for (int q = 0; q < p.rank / 16; ++q)
-              umma_f16(tmem + a * kBN, smem_desc(ua + q * 256, 128, uint32_t(nq) * 128, 0),
-                       smem_desc(ba + q * 2048, p.rank * 128, 1024, 2), idesc_d, 1u);
-          };
-          int d = 0;
-          if (dbuf) {  // the first pair, from the delta buffer
-            if (!wait(bar(DFULL), dk & 1)) {
-              stop = true;
-            } else {
-              delta_mma(s_delta, s_delta + 256 * p.rank);
-              umma_commit(bar(DEMPTY));
-              ++dk;
-              d = 1;
-            }
-          }
-          for (; d < n_delta && !stop; ++d) {
-            const int s = kk % kStages;
-            if (!wait(bar(FULL + s), (kk / kStages) & 1)) {
-              stop = true;
-              break;
-            }
-            const uint32_t st = s_stage0 + s * kStageBytes;
-            delta_mma(st, st + kABytes);
-            umma_commit(bar(EMPTY + s));
-            ++kk;
+        const int nq = p.rank / 8;  // 16-byte chunks of a u row
+        auto delta_mma = [&](uint32_t ua, uint32_t ba) {
+          tc_fence_after();
+          for (int q = 0; q < p.rank / 16; ++q)
+            umma_pair(tmem + a * kBN, smem_desc(ua + q * 256, 128, uint32_t(nq) * 128, 0),
+                      smem_desc(ba + q * 2048, p.rank * 128, 1024, 2), idesc_d, 1u);
+        };
+        int d = 0;
+        if (!stop && dbuf && n_delta > 0) {  // the first block, from the delta buffer
+          if (!wait(bar(DFULL), dk & 1)) {
+            stop = true;
+          } else {
+            delta_mma(s_delta, s_delta + 256 * p.rank);
+            umma_commit_pair(bar(DEMPTY));
+            ++dk;
+            d = 1;
           }
         }
-        if (!stop) umma_commit(bar(ACC_FULL + a));
+        for (; d < n_delta && !stop; ++d, ++kk) {
+          const int s = kk % kStages;
+          if (!wait(bar(FULL + s), (kk / kStages) & 1)) {
+            stop = true;
+            break;
+          }
+          const uint32_t ua = s_stage0 + s * kStageBytes;
+          delta_mma(ua, ua + kABytes);
+          umma_commit_pair(bar(EMPTY + s));
+        }
+        if (!stop) umma_commit_pair(bar(ACC_FULL + a));
       }
       if (aborted_flag(s_abort)) {  // every issued MMA finishes before TMEM is released (bounded)
-        umma_commit(bar(DRAIN));
+        umma_commit_pair_local(bar(DRAIN));
         mbar_wait(bar(DRAIN), 0);
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2..9)
+    // ------------------------------------------------------------ epilogue (warps 2..9, both CTAs)
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;  // columns [128 half, 128 half + 128) of the tile
     const uint32_t taddr = tmem + (uint32_t(quad * 32) << 16);
     const uint32_t my_out = s_out0 + (warp - 2) * kOutBuf;
+    const uint32_t acc_empty = mapa_shared(bar(ACC_EMPTY), 0);  // the leader's
     const T* bias = static_cast<const T*>(p.bias);
     int it = 0;
-    for (int64_t t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++it) {
+    for (int64_t t = pair; t < p.n_tiles; t += n_pairs, ++it) {
       const int a = it & 1;
-      const int32_t m0 = int32_t(t / p.n_tiles_n) * kBM, n0 = int32_t(t % p.n_tiles_n) * kBN;
+      const int32_t m0 = int32_t(t / p.n_tiles_n) * (2 * kBM) + int32_t(rank) * kBM;
+      const int32_t n0 = int32_t(t % p.n_tiles_n) * kBN;
       bool ok = !aborted_flag(s_abort);
       if (ok && !mbar_wait(bar(ACC_FULL + a), (it >> 1) & 1)) {
         fail();
@@ -376,30 +453,30 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
         // the store that last read this staging tile must be done with it
         if (lane == 0) tma_store_wait_read_all();
         __syncwarp();
-        const uint32_t buf = my_out;
 #pragma unroll
         for (int q = 0; q < 4; ++q)  // SW64: 16-byte chunk q of row `lane` at q ^ ((lane >> 1) & 3)
-          *reinterpret_cast<uint4*>(gbase + (buf - base) + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
+          *reinterpret_cast<uint4*>(gbase + (my_out - base) + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) =
               make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&p.y_map, buf, col0, m0 + quad * 32);
+          tma_store_2d(&p.y_map, my_out, col0, m0 + quad * 32);
           tma_store_commit();
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(ACC_EMPTY + a));  // this warp's TMEM reads of the tile are done
+      if (lane == 0) mbar_arrive_cluster(acc_empty + a * 8);  // this warp's TMEM reads of the tile are done
     }
     if (lane == 0) tma_store_wait_all();
   }
 
   __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still signal its barriers or read its operands
   tc_fence_after();
   if (warp == 1) {
     __syncwarp();
-    tmem_dealloc(tmem, 2 * kBN);
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kBN) : "memory");
   }
 }
 
@@ -480,7 +557,7 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
   {
     const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(n)};
     const cuuint64_t strides[1] = {cuuint64_t(ldw) * 2};
-    const cuuint32_t box[2] = {kBK, kBN};
+    const cuuint32_t box[2] = {kBK, kBN / 2};
     if ((rc = tmap(&p.w_map, 2, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "w"))) return rc;
   }
   {
@@ -492,16 +569,23 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
   if (lora != nullptr) {
     const LoraArgs& L = *lora;
     const cuuint32_t R = cuuint32_t(L.rank);
-    p.u = L.u;
+    // u: n_modules x n_blk blocks of 128 x R, each viewed as R/2 rows of 256 elements
+    p.n_blk = int32_t((m + kBM - 1) / kBM + L.n_segs);
+    {
+      const cuuint64_t dims[3] = {256, R / 2, cuuint64_t(L.n_modules) * cuuint64_t(p.n_blk)};
+      const cuuint64_t strides[2] = {512, cuuint64_t(kBM) * R * 2};
+      const cuuint32_t box[3] = {256, R / 2, 1};
+      if ((rc = tmap(&p.u_map, 3, L.u, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE, "u"))) return rc;
+    }
     for (int i = 0; i < L.n_modules; ++i) {
       const void* b = static_cast<const uint8_t*>(L.cache_b) + int64_t(L.modules[i]) * L.b_module_stride * 2;
       const int64_t ss = L.n_slots == 1 ? int64_t(L.module_cols) * L.rank : L.b_slot_stride;
       p.b_ptr[i] = b;
       p.b_slot_stride = ss;
-      // (64 columns, R rows, column block, slot): one box holds a tile's four blocks
+      // (64 columns, R rows, column block, slot): one box holds a CTA's two blocks
       const cuuint64_t dims[4] = {64, R, cuuint64_t(L.module_cols / 64), cuuint64_t(L.n_slots)};
       const cuuint64_t strides[3] = {cuuint64_t(L.module_cols) * 2, 128, cuuint64_t(ss) * 2};
-      const cuuint32_t box[4] = {64, R, kBN / 64, 1};
+      const cuuint32_t box[4] = {64, R, kBN / 128, 1};
       if ((rc = tmap(&p.b_map[i], 4, b, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "b"))) return rc;
     }
     p.tile_pairs = L.tile_pairs;
@@ -515,19 +599,49 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
   p.bias = bias;
   p.m_rows = m;
   p.n_tiles_n = n / kBN;
-  p.n_tiles = ((m + kBM - 1) / kBM) * p.n_tiles_n;
+  p.n_tiles = ((m + 2 * kBM - 1) / (2 * kBM)) * p.n_tiles_n;
   p.n_kb = k / kBK;
   p.act = act;
   p.status = status;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int grid = int(p.n_tiles < sms ? p.n_tiles : sms);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto kern = dtype == LF_DTYPE_BF16 ? linear_kernel<__nv_bfloat16> : linear_kernel<__half>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(linear)");
-  e = launch_pdl(kern, dim3(grid), dim3(kThreads), kSmemBytes, s, p);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  // as many pairs as can be resident at once (a GPC with an odd SM count leaves one idle)
+  static int resident_pairs[64] = {0};
+  int pairs = sms / 2;
+  if (dev >= 0 && dev < 64) {
+    if (resident_pairs[dev] == 0) {
+      cudaLaunchConfig_t q = {};
+      q.gridDim = dim3(unsigned(sms & ~1));
+      q.blockDim = dim3(kThreads);
+      q.dynamicSmemBytes = kSmemBytes;
+      q.attrs = attr;
+      q.numAttrs = 1;
+      int nc = 0;
+      resident_pairs[dev] = (cudaOccupancyMaxActiveClusters(&nc, kern, &q) == cudaSuccess && nc > 0) ? nc : sms / 2;
+    }
+    pairs = resident_pairs[dev] < sms / 2 ? resident_pairs[dev] : sms / 2;
+  }
+  if (p.n_tiles < pairs) pairs = int(p.n_tiles);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(2 * pairs));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  e = cudaLaunchKernelEx(&cfg, kern, p);
   if (e != cudaSuccess) return cuda_error(e, "launch linear");
   count_launch();
   return LF_OK;

@@ -30,10 +30,10 @@ from torch.utils.hooks import RemovableHandle
 
 from latefuse_b200.batch import BatchedLRWeights, BatchLora, LayerwiseBatchedWeights
 from latefuse_b200.config import LoraServingConfig
-from latefuse_b200.head import LRHeadOps, pool_tokens, validate_pooling
+from latefuse_b200.head import LRHeadOps, head_forward, head_forward_rows, pool_tokens, validate_pooling
 from latefuse_b200.lora import (FactorCache, SegmentTable, blocked_u, linear_lora, lora_apply, lora_apply_into,
                                  lora_shrink_blocked, per_row_cache, workspace_bytes)
-from latefuse_b200.encoder_ops import add_layernorm, attention_varlen, gelu
+from latefuse_b200.encoder_ops import ACT_GELU, add_layernorm, attention_varlen, gelu, linear
 from latefuse_b200.packing import PackedBatch, pack_rows
 
 # Per-layer module paths (relative to "encoder.layer.{i}.") for each logical target.
@@ -498,17 +498,28 @@ class EncoderWithLora(nn.Module):
     def _ffn(self, layer: _Layer, ao: Tensor, h: Tensor | None) -> Tensor:
         """``h1 = LN1(ao + h)`` (``LN1(ao)`` when ``h`` is None: the residual is already
         in ``ao``), then ``LN2(W2 act(W1 h1) + b2 + h1)``, on the native add+LayerNorm and
-        GELU kernels.  For bf16/f16 the down-projection GEMM accumulates onto ``h1`` in
-        place (beta = 1; ``h1`` is not read again) and LayerNorm adds ``b2``, so the
-        residual is not read a second time."""
+        GELU kernels.  For bf16/f16 the up projection and its exact GELU run as one launch
+        of this library's tcgen05 GEMM (the GELU in its epilogue), the down-projection
+        GEMM accumulates onto ``h1`` in place (beta = 1; ``h1`` is not read again) and
+        LayerNorm adds ``b2``, so the residual is not read a second time."""
         h1 = add_layernorm(ao, h, layer.ln1.weight, layer.ln1.bias, self.eps)
-        mid = F.linear(h1, layer.wi, layer.bi)
-        mid = gelu(mid, out=mid) if self._native_gelu else self.act(mid)
+        if self._native_gelu and self._gemm_ok(h1.dtype, layer.wi.shape):
+            mid = linear(h1, layer.wi, layer.bi, act=ACT_GELU)
+        else:
+            mid = F.linear(h1, layer.wi, layer.bi)
+            mid = gelu(mid, out=mid) if self._native_gelu else self.act(mid)
         if h1.dtype in (torch.bfloat16, torch.float16):
             h1.view(-1, h1.shape[-1]).addmm_(mid.view(-1, mid.shape[-1]), layer.wo2.t())
             return add_layernorm(h1, None, layer.ln2.weight, layer.ln2.bias, self.eps, out=h1, vec=layer.bo2)
         o = F.linear(mid, layer.wo2, layer.bo2)
         return add_layernorm(o, h1, layer.ln2.weight, layer.ln2.bias, self.eps, out=o)
+
+    @staticmethod
+    def _gemm_ok(dtype: torch.dtype, weight_shape) -> bool:
+        """Whether this library's GEMM (``lf_linear``) takes a projection of this weight:
+        bf16/f16, output width a multiple of 256, input width a multiple of 64."""
+        n, k = weight_shape
+        return dtype in (torch.bfloat16, torch.float16) and n % 256 == 0 and k % 64 == 0
 
     def _lora_gemm_ok(self, dtype: torch.dtype, rank: int) -> bool:
         """Whether the packed forward runs the LoRA'd projections on this library's
@@ -639,12 +650,27 @@ class EncoderWithLora(nn.Module):
         """Pooled ``(B, H)`` rows in input order from a packed batch."""
         validate_pooling(pooling)
         h = self.encode_packed(pb, store, apply_lora)
+        return self.heads_packed(h, pb, pooling)
+
+    def heads_packed(self, h: Tensor, pb: PackedBatch, pooling: str, *, coef: Tensor | None = None,
+                     bias: Tensor | None = None, head_table: Tensor | None = None, n_max: int = 0,
+                     logits_out: Tensor | None = None, probs_out: Tensor | None = None) -> Tensor:
+        """The pooled ``(B, H)`` rows of packed hidden states ``h`` and, given a head
+        table, the per-tenant logits and probabilities, in one native call for CLS
+        and ``"auto"`` pooling (row gather -> pooler -> head -> softmax,
+        ``lf_head_forward_rows``)."""
+        B, H = pb.n_rows, h.shape[1]
+        pooled = torch.empty(B, H, dtype=h.dtype, device=h.device)
+        head = dict(coef=coef, bias=bias, head_table=head_table, n_max=n_max, logits_out=logits_out,
+                    probs_out=probs_out, status=self._runner.status)
         if pooling == "mean":
-            return packed_mean(h, pb)
-        cls = h.index_select(0, pb.first_token)
-        if pooling == "auto":
-            return torch.tanh(F.linear(cls, self.pooler_w, self.pooler_b))
-        return cls
+            pooled = packed_mean(h, pb)
+            if coef is not None:
+                head_forward(pooled, pooling="none", **head)
+            return pooled
+        pooler = dict(pooler_w=self.pooler_w, pooler_b=self.pooler_b) if pooling == "auto" else {}
+        head_forward_rows(h, pb.first_token, pooled_out=pooled, **pooler, **head)
+        return pooled
 
     def forward(self, input_ids: Tensor, attention_mask: Tensor | None, lora_weights,
                 lr_weights: BatchedLRWeights, output_lr: Tensor, token_type_ids: Tensor | None = None,

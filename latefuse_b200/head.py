@@ -66,6 +66,46 @@ def head_forward(hidden: Tensor, *, pooling: str, mask: Tensor | None = None, po
     nat.check(rc, "lf_head_forward")
 
 
+def head_forward_rows(hidden: Tensor, row_index: Tensor | None, *, pooler_w: Tensor | None = None,
+                      pooler_b: Tensor | None = None, pooled_out: Tensor | None = None,
+                      normed_out: Tensor | None = None, coef: Tensor | None = None, bias: Tensor | None = None,
+                      head_table: Tensor | None = None, n_max: int = 0, logits_out: Tensor | None = None,
+                      probs_out: Tensor | None = None, status: Tensor | None = None) -> None:
+    """Run ``lf_head_forward_rows`` on the current stream: rows ``row_index`` (int32,
+    ``(B,)``) of the packed ``(n_tokens, H)`` ``hidden``, optionally through the
+    pooler ``tanh(pooler_w x + pooler_b)`` (then ``pooled_out`` is required), then
+    the L2 norm / per-tenant head / softmax of :func:`head_forward`."""
+    dev = nat.require_cuda(hidden, row_index, pooler_w, pooler_b, pooled_out, normed_out, coef, bias, head_table,
+                           logits_out, probs_out)
+    if hidden.dim() != 2 or hidden.stride(-1) != 1:
+        raise ValueError("head_forward_rows: hidden must be (n_tokens, H) with unit column stride")
+    T, H = hidden.shape
+    if row_index is not None:
+        if row_index.dtype != torch.int32 or not row_index.is_contiguous():
+            raise ValueError("head_forward_rows: row_index must be a contiguous int32 tensor")
+        B = row_index.numel()
+    else:
+        B = T
+    if pooler_w is not None:
+        if pooled_out is None:
+            raise ValueError("head_forward_rows: the pooler writes its rows to pooled_out")
+        if tuple(pooler_w.shape) != (H, H) or not pooler_w.is_contiguous():
+            raise ValueError(f"head_forward_rows: pooler_w must be a contiguous ({H}, {H}) tensor")
+    for name, t in (("pooled_out", pooled_out), ("normed_out", normed_out)):
+        if t is not None and (tuple(t.shape) != (B, H) or not t.is_contiguous()):
+            raise ValueError(f"head_forward_rows: {name} must be a contiguous ({B}, {H}) tensor")
+    off_ptr = n_ptr = None
+    if head_table is not None:
+        off_ptr = head_table.data_ptr()
+        n_ptr = off_ptr + head_table.stride(0) * 4
+    rc = nat.lib().lf_head_forward_rows(
+        nat.stream_ptr(dev), nat.dtype_code(hidden.dtype), hidden.data_ptr(), hidden.stride(0), nat.ptr(row_index),
+        B, H, nat.ptr(pooler_w), nat.ptr(pooler_b), nat.ptr(pooled_out), nat.ptr(normed_out), nat.ptr(coef),
+        nat.ptr(bias), coef.shape[0] if coef is not None else 0, off_ptr, n_ptr, n_max, nat.ptr(logits_out),
+        nat.ptr(probs_out), nat.ptr(status))
+    nat.check(rc, "lf_head_forward_rows")
+
+
 def pool_tokens(hidden_states: Tensor, attention_mask: Tensor | None, strategy: str) -> Tensor:
     """Reduce ``(B, S, H)`` to ``(B, H)`` under ``"cls"`` or ``"mean"`` (native kernel).
 

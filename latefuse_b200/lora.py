@@ -55,7 +55,7 @@ class SegmentTable:
         records = _tile_records(starts, lengths, slots) if records else []
         self.n_tiles = len(records) // 4
         self.n_multi = sum(1 for i in range(2, len(records), 4) if records[i] != 1)
-        pairs = _tile_pairs(starts, lengths, slots, self.n_tokens) if self.use_records else []
+        pairs = _pair_tiles(starts, lengths, slots, self.n_tokens) if self.use_records else []
         self.host = torch.tensor(records + starts + lengths + slots + pairs, dtype=torch.int32)
         if self.device.type == "cuda":
             self.table = self.host.pin_memory().to(self.device, non_blocking=True)
@@ -80,36 +80,47 @@ class SegmentTable:
         return base + r, base + r + 4 * n, base + r + 8 * n, base, self.n_tiles, self.n_multi
 
     def pair_ptrs(self) -> tuple[int, int]:
-        """(tile_pairs, pairs) for ``lf_linear_lora``: per 128-token tile b, the
-        (segment, slot) pairs of the segments with tokens in it are entries
-        ``tile_pairs[b] .. tile_pairs[b + 1]`` of ``pairs`` (two int32 each), in
-        segment order.  Built with the tile records."""
+        """(tile_pairs, pairs) for ``lf_linear_lora``: per 256-token tile q, the
+        segments with tokens in it are entries ``tile_pairs[q] .. tile_pairs[q + 1]``
+        of ``pairs`` (three int32 each: segment, slot, and a mask of the tile's
+        128-token halves the segment has tokens in), in segment order.  Built with
+        the tile records."""
         if not self.use_records:
             raise ValueError("the pair table is built with the tile records")
         off = self.table.data_ptr() + 16 * self.n_tiles + 12 * self.n_segs
-        n_rt = (self.n_tokens + 127) // 128
-        return off, off + 4 * (n_rt + 1)
+        n_q = (self.n_tokens + 255) // 256
+        return off, off + 4 * (n_q + 1)
 
 
-def _tile_pairs(starts, lengths, slots, n_tokens: int) -> list[int]:
-    """``[tile_pairs (n_rt + 1) | pairs (2 per entry)]``: the (segment, slot) pairs of
-    every 128-token tile, by tile then segment; segments of no tokens are left out."""
+def _pair_tiles(starts, lengths, slots, n_tokens: int) -> list[int]:
+    """``[offsets (n_q + 1) | entries (3 per entry)]``: for every 256-token tile q (the
+    rows one CTA pair of ``lf_linear_lora`` computes), the segments with tokens in
+    it, in segment order, as ``{segment, slot, mask}`` with mask bit r set when the
+    segment has tokens in the tile's 128-token half r (128-token tile 2q + r);
+    segments of no tokens are left out."""
     tile = nat.TILE_TOKENS
-    n_rt = (int(n_tokens) + tile - 1) // tile
+    n_q = (int(n_tokens) + 2 * tile - 1) // (2 * tile)
     st = np.asarray(starts, dtype=np.int64)
     ln = np.asarray(lengths, dtype=np.int64)
     seg = np.nonzero(ln > 0)[0]
     if seg.size == 0:
-        return [0] * (n_rt + 1)
+        return [0] * (n_q + 1)
+    # one (segment, 128-token tile) entry per tile a segment touches
     t0 = st[seg] // tile
     nt = (st[seg] + ln[seg] - 1) // tile - t0 + 1
     seg_of = np.repeat(seg, nt)
     tile_of = np.repeat(t0, nt) + np.arange(int(nt.sum())) - np.repeat(np.cumsum(nt) - nt, nt)
-    order = np.argsort(tile_of, kind="stable")
-    seg_of, tile_of = seg_of[order], tile_of[order]
-    begin = np.searchsorted(tile_of, np.arange(n_rt + 1), side="left")
-    pairs = np.stack([seg_of, np.asarray(slots, dtype=np.int64)[seg_of]], axis=1)
-    return begin.tolist() + pairs.reshape(-1).tolist()
+    q_of, bit = tile_of // 2, np.left_shift(1, tile_of % 2)
+    # merge the two halves' entries of one (256-token tile, segment)
+    key = q_of * (int(seg.max()) + 1) + seg_of
+    order = np.argsort(key, kind="stable")
+    key, q_of, seg_of, bit = key[order], q_of[order], seg_of[order], bit[order]
+    uniq, first = np.unique(key, return_index=True)
+    mask = np.bitwise_or.reduceat(bit, first)
+    q_u, seg_u = q_of[first], seg_of[first]
+    begin = np.searchsorted(q_u, np.arange(n_q + 1), side="left")
+    entries = np.stack([seg_u, np.asarray(slots, dtype=np.int64)[seg_u], mask], axis=1)
+    return begin.tolist() + entries.reshape(-1).tolist()
 
 
 def _tile_records(starts, lengths, slots) -> list[int]:

@@ -163,10 +163,15 @@ class TaskPipeline:
                               return_tensors="pt")
 
     def encode_tokens(self, input_ids: Tensor, attention_mask: Tensor | None, tenants: Sequence[str],
-                      token_type_ids: Tensor | None = None, pooling: str | None = None) -> Tensor:
+                      token_type_ids: Tensor | None = None, pooling: str | None = None,
+                      head: dict | None = None) -> Tensor:
         """Pooled ``(B, H)`` rows for one pre-tokenized batch (host or device tensors).
 
-        Host tensors are copied to the device here (pinned, asynchronous).
+        Host tensors are copied to the device here (pinned, asynchronous).  With
+        ``head`` (the keyword arguments of :func:`~latefuse_b200.head.head_forward`'s
+        head: coef, bias, head_table, n_max, logits_out, probs_out) the per-tenant
+        heads run too; on the padding-free path the row gather, pooler, head and
+        softmax are then one native call.
         """
         pooling = validate_pooling(pooling or self.pooling)
         cfg = self.config
@@ -184,7 +189,10 @@ class TaskPipeline:
             slots = self.store.slots(list(tenants))
             pb = self.model.pack(input_ids, lengths, slots, token_type_ids)
             with torch.no_grad():
-                return self.model.encode_pooled_packed(pb, self.store, pooling)
+                if head is None:
+                    return self.model.encode_pooled_packed(pb, self.store, pooling)
+                h = self.model.encode_packed(pb, self.store)
+                return self.model.heads_packed(h, pb, pooling, **head)
         batch = self._get_assembler().batch_lora(list(tenants), input_ids.shape[1], lengths)
 
         def dev(t):
@@ -193,8 +201,11 @@ class TaskPipeline:
             return t.pin_memory().to(cfg.device, non_blocking=True) if t.device.type == "cpu" else t.to(cfg.device)
 
         with torch.no_grad():
-            return self.model.encode_pooled(dev(input_ids), dev(attention_mask), batch, dev(token_type_ids),
-                                            True, pooling)
+            pooled = self.model.encode_pooled(dev(input_ids), dev(attention_mask), batch, dev(token_type_ids),
+                                              True, pooling)
+            if head is not None:
+                head_forward(pooled, pooling="none", **head)
+            return pooled
 
     def _encode(self, texts: Sequence[str], tenants: Sequence[str], text_pairs: Sequence[str] | None = None,
                 pooling: str | None = None) -> Tensor:
@@ -291,6 +302,40 @@ class _HeadTask(TaskPipeline):
                      logits_out=logits, probs_out=probs)
         return logits, probs, num_labels
 
+    def _score_tokens(self, input_ids: Tensor, attention_mask: Tensor | None, tenants: list[str],
+                      token_type_ids: Tensor | None = None,
+                      n_max: int | None = None) -> tuple[Tensor, Tensor, list[int]]:
+        """Encode one pre-tokenized batch and score it with its tenants' heads in the
+        same pass: ``(logits (B, n_max), probs (B, n_max), num_labels)`` on the device,
+        ``n_max`` at least the widest head of the batch."""
+        table, num_labels, widest = self.heads.head_table(tenants)
+        n_max = max(widest, n_max or 0)
+        coef, bias = self.heads.packed
+        B, dev = input_ids.shape[0], self.config.device
+        logits = torch.zeros(B, n_max, dtype=self.config.dtype, device=dev)
+        probs = torch.zeros(B, n_max, dtype=torch.float32, device=dev)
+        self.encode_tokens(input_ids, attention_mask, tenants, token_type_ids,
+                           head=dict(coef=coef, bias=bias, head_table=table, n_max=n_max, logits_out=logits,
+                                     probs_out=probs))
+        return logits, probs, num_labels
+
+    def _scored_texts(self, texts, tenants, text_pairs=None) -> tuple[Tensor, Tensor, list[int]]:
+        """Tokenize in fixed-size chunks, encode and score each chunk in one pass."""
+        if len(texts) != len(tenants):
+            raise ValueError(f"got {len(texts)} texts but {len(tenants)} tenant ids")
+        if text_pairs is not None and len(text_pairs) != len(texts):
+            raise ValueError(f"got {len(texts)} texts but {len(text_pairs)} pair texts")
+        _, num_labels, n_max = self.heads.head_table(list(tenants))  # unknown tenants fail before any forward
+        pairs = list(text_pairs) if text_pairs is not None else [None] * len(texts)
+        logits, probs = [], []
+        for chunk, n_valid in chunk_and_pad(list(zip(texts, tenants, pairs)), self.config.batch_size):
+            enc = self._tokenize([c[0] for c in chunk], None if text_pairs is None else [c[2] for c in chunk])
+            lo, pr, _ = self._score_tokens(enc["input_ids"], enc["attention_mask"], [c[1] for c in chunk],
+                                           enc.get("token_type_ids"), n_max)
+            logits.append(lo[:n_valid])
+            probs.append(pr[:n_valid])
+        return torch.cat(logits), torch.cat(probs), num_labels
+
 
 class MultiTenantClassifier(_HeadTask):
     """Classify texts under many tenants' adapters and heads in one forward pass."""
@@ -300,8 +345,7 @@ class MultiTenantClassifier(_HeadTask):
             raise ValueError(f"got {len(texts)} texts but {len(tenants)} tenant ids")
         if not texts:
             return [], [], []
-        pooled = self._encode(texts, tenants)
-        logits, probs, num_labels = self._score(pooled, list(tenants))
+        logits, probs, num_labels = self._scored_texts(texts, list(tenants))
         return logits.tolist(), probs.tolist(), num_labels
 
     def logits(self, texts: Sequence[str], tenants: Sequence[str]) -> list[list[float]]:
@@ -331,8 +375,7 @@ class MultiTenantClassifier(_HeadTask):
     def classify_tokens(self, input_ids: Tensor, attention_mask: Tensor | None, tenants: Sequence[str],
                         token_type_ids: Tensor | None = None) -> tuple[Tensor, Tensor, list[int]]:
         """Device ``(logits, probs, num_labels)`` for one pre-tokenized batch."""
-        pooled = self.encode_tokens(input_ids, attention_mask, list(tenants), token_type_ids)
-        return self._score(pooled, list(tenants))
+        return self._score_tokens(input_ids, attention_mask, list(tenants), token_type_ids)
 
 
 @dataclass(frozen=True)
@@ -357,8 +400,7 @@ class MultiTenantReranker(_HeadTask):
         if not queries:
             return []
         tenant_ids = [tenants] * len(queries) if isinstance(tenants, str) else list(tenants)
-        pooled = self._encode(queries, tenant_ids, text_pairs=list(documents))
-        logits, _, _ = self._score(pooled, tenant_ids)
+        logits, _, _ = self._scored_texts(list(queries), tenant_ids, text_pairs=list(documents))
         return logits[:, 0].tolist()
 
     def rerank(self, query: str, documents: Sequence[str], tenant: str, *, top_k: int | None = None) -> list[RerankResult]:

@@ -135,3 +135,58 @@ def test_lora_ops_api_matches_reference(cuda, dtype):
             assert ((got - ref).norm() / ref.norm()).item() < 2e-2
     with pytest.raises(AssertionError, match="buffer shape"):
         ops.shrink(torch.zeros(2, 8, 64, device=cuda, dtype=dt), g["a"].to(cuda))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("pooler", [True, False])
+def test_head_rows_gather_pooler_head_softmax(cuda, dtype, pooler):
+    """``lf_head_forward_rows`` on packed rows against the reference's steps done
+    one by one with torch: gather each row's CLS token, the HF pooler
+    ``tanh(F.linear(cls, W, b))`` (each result in the dtype), then the oracle's
+    zero-padded head bmm + add and the host softmax / sigmoid.  37 rows span three
+    row blocks of the pooler; H = 1024 spans sixteen column blocks."""
+    from latefuse_b200.head import head_forward_rows
+
+    g = torch.Generator().manual_seed(0)
+    T, B, H = 900, 37, 1024
+    hidden = torch.randn(T, H, generator=g).to(dtype).to(cuda)
+    rows = torch.randperm(T, generator=g)[:B].to(torch.int32)
+    W = (torch.randn(H, H, generator=g) * H ** -0.5).to(dtype).to(cuda)
+    b = (torch.randn(H, generator=g) * 0.1).to(dtype).to(cuda)
+    heads = lf.HeadStore(cfg(cuda, dtype, H=H))
+    raw = {}
+    for i in range(9):
+        n = 1 if i == 4 else int(torch.randint(2, 21, (1,), generator=g))
+        raw[f"t{i}"] = (torch.randn(n, H, generator=g) * 0.05, torch.randn(n, generator=g) * 0.1)
+        heads.load(f"t{i}", *raw[f"t{i}"])
+    tenants = [f"t{int(i)}" for i in torch.randint(0, 9, (B,), generator=g)]
+    table, nl, n_max = heads.head_table(tenants)
+    coef, bias = heads.packed
+    pooled = torch.empty(B, H, dtype=dtype, device=cuda)
+    logits = torch.empty(B, n_max, dtype=dtype, device=cuda)
+    probs = torch.empty(B, n_max, dtype=torch.float32, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    head_forward_rows(hidden, rows.to(cuda), pooler_w=W if pooler else None, pooler_b=b if pooler else None,
+                      pooled_out=pooled, coef=coef, bias=bias, head_table=table, n_max=n_max, logits_out=logits,
+                      probs_out=probs, status=status)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    cls = hidden.index_select(0, rows.to(cuda).long())
+    want_pooled = torch.tanh(torch.nn.functional.linear(cls, W, b)) if pooler else cls
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    if pooler:
+        assert (pooled.float() - want_pooled.float()).abs().max().item() <= tol
+    else:
+        assert torch.equal(pooled, want_pooled)  # a gather is exact
+    c_ref, i_ref, nl_ref = oh.assemble_heads({t: (c.to(dtype), i.to(dtype)) for t, (c, i) in raw.items()}, tenants,
+                                             H, dtype)
+    assert nl == nl_ref
+    ref_logits = oh.head_logits(want_pooled.cpu(), c_ref, i_ref).float()
+    scale = max(1.0, ref_logits.abs().max().item())
+    for i, n in enumerate(nl):
+        assert (logits[i, :n].float().cpu() - ref_logits[i, :n]).abs().max().item() <= tol * scale
+        assert torch.count_nonzero(logits[i, n:]) == 0 and torch.count_nonzero(probs[i, n:]) == 0
+    ref_probs = oh.probabilities(oh.ragged(ref_logits, nl))
+    for i, n in enumerate(nl):
+        assert probs[i, :n].cpu().tolist() == pytest.approx(ref_probs[i], abs=1e-5 if dtype == torch.float32
+                                                            else 2e-2)

@@ -211,16 +211,17 @@ def test_fused_gemm_reports_malformed_pair_table(cuda, corrupt):
     u = blocked_u(1, T, st.n_segs, R, dtype, dev)
     lora_shrink_blocked(x, u, fc, st, [0])
     good = linear_lora(x, W, None, u, fc, st, [0], H)
-    n_rt = (T + 127) // 128
+    n_q = (T + 255) // 256  # 256-token tiles, one per CTA pair
+    assert n_q >= 2
     tp = 4 * st.n_tiles + 3 * st.n_segs
-    pairs = tp + n_rt + 1
-    last = n_rt - 1  # a tile whose pairs are changed; tile 0 is left alone
+    pairs = tp + n_q + 1
+    last = n_q - 1  # a tile whose entries are changed; tile 0 is left alone
     q_last = int(st.host[tp + last])
     if corrupt == "slot":
-        st.table[pairs + 2 * q_last + 1] = n_slots + 7
+        st.table[pairs + 3 * q_last + 1] = n_slots + 7
         want = nat.LF_STATUS_BAD_SLOT
     elif corrupt == "segment":
-        st.table[pairs + 2 * q_last] = -3
+        st.table[pairs + 3 * q_last] = -3
         want = nat.LF_STATUS_BAD_SEGMENT
     else:
         st.table[tp + last] = 1 << 30
@@ -229,4 +230,4 @@ def test_fused_gemm_reports_malformed_pair_table(cuda, corrupt):
     out = linear_lora(x, W, None, u, fc, st, [0], H, status=status)
     torch.cuda.synchronize()
     assert status.item() & want
-    assert torch.equal(out[:128], good[:128])
+    assert torch.equal(out[:256], good[:256])

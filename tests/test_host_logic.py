@@ -40,6 +40,17 @@ def test_chunk_and_pad_matches_reference_cases():
         list(chunk_and_pad([1], 0))
 
 
+def test_pair_tiles_merge_the_halves_of_each_256_token_tile():
+    from latefuse_b200.lora import _pair_tiles
+
+    # segments [0,100) [100,300) [300,700) [700,710) over 710 tokens: 128-token tiles 0..5
+    got = _pair_tiles([0, 100, 300, 700], [100, 200, 400, 10], [5, 6, 7, 8], 710)
+    assert got[:4] == [0, 2, 4, 6]
+    entries = [got[4 + 3 * i: 7 + 3 * i] for i in range(6)]
+    assert entries == [[0, 5, 1], [1, 6, 3], [1, 6, 1], [2, 7, 3], [2, 7, 3], [3, 8, 2]]
+    assert _pair_tiles([0, 5], [0, 0], [1, 2], 300) == [0, 0, 0]  # empty segments are left out
+
+
 def test_right_padded_lengths():
     m = torch.tensor([[1, 1, 1, 0], [1, 0, 0, 0], [1, 1, 1, 1]])
     assert right_padded_lengths(m) == [3, 1, 4]
@@ -92,8 +103,9 @@ def test_pack_rows_layout():
     n = segs.n_segs
     starts, seg_lens = segs.host[4 * segs.n_tiles:4 * segs.n_tiles + 3 * n].view(3, -1)[:2].tolist()
     assert starts == [0, 3] and seg_lens == [3, 10]
-    # per-tile (segment, slot) pairs after the segment arrays: one tile, both segments
-    assert segs.host[4 * segs.n_tiles + 3 * n:].tolist() == [0, 2, 0, 3, 1, 5]
+    # per-256-token-tile {segment, slot, halves} entries after the segment arrays: one
+    # tile, both segments in its first 128-token half
+    assert segs.host[4 * segs.n_tiles + 3 * n:].tolist() == [0, 2, 0, 3, 1, 1, 5, 1]
     # attention work list: one record per (sequence, 128-query tile)
     assert pb.attn_items.tolist() == [[0, 2, 0, 0], [2, 1, 0, 0], [3, 6, 0, 0], [9, 4, 0, 0]]
     arange = pack_rows(ids, lengths, slots, None, None, torch.device("cpu"))  # BERT numbering
