@@ -372,9 +372,11 @@ int lf_linear(void* stream, int dtype, const void* x, int64_t ldx, const void* w
  * of lf_lora_shrink_blocked (n_segs as there) and B read in place from the slot
  * cache (cache module modules[i], (rank, module_cols) row-major per slot, as
  * lf_lora_expand reads it).  tile_pairs / pairs (device int32) list, for each
- * 128-token tile b, the segments with tokens in it: entries tile_pairs[b] ..
- * tile_pairs[b + 1] - 1 of pairs, each {segment, slot}, in segment order
- * (latefuse_b200.lora.SegmentTable builds them).  The delta is not rounded
+ * 256-token tile q (the rows one CTA pair computes), the segments with tokens in
+ * it: entries tile_pairs[q] .. tile_pairs[q + 1] - 1 of pairs, each
+ * {segment, slot, halves} with bit r of halves set when the segment has tokens in
+ * the tile's 128-token half r, in segment order (latefuse_b200.lora.SegmentTable
+ * builds them).  The delta is not rounded
  * separately: the result is rounded once, where the reference rounds the
  * projection and the delta apart and then their sum
  * (src/latefuse/model/hf_wrapper.py:217, `output + lora_ops.output`; the fused
@@ -386,6 +388,26 @@ int lf_linear_lora(void* stream, int dtype, const void* x, int64_t ldx, const vo
                    const void* u, int rank, const void* cache_b, int64_t b_slot_stride, int64_t b_module_stride,
                    int n_slots, int n_modules, const int32_t* modules, int module_cols, int n_segs,
                    const int32_t* tile_pairs, const int32_t* pairs, int32_t* status);
+
+/* lf_linear_lora with the shrink in the same launch: u = round(x A(slot(t), i)) for
+ * every segment and module i is computed by the GEMM's own CTA pairs (a pass over each
+ * 256-token block's x against its segments' A factors, read in place from the slot
+ * cache like lf_lora_shrink_blocked reads them: cache module modules[i], (hidden, rank)
+ * row-major per slot, hidden = k) and written to u, the caller's buffer in the blocked
+ * layout of lf_lora_shrink_blocked, before the block's projection tiles add
+ * u B in their accumulators.  Replaces the two calls lf_lora_shrink_blocked +
+ * lf_linear_lora (the reference's hook body, src/latefuse/model/hf_wrapper.py:212-217,
+ * around the projection): one launch, x read once per block pass.  seg_start /
+ * seg_len (device int32, n_segs) are the segment table; the other arguments are
+ * lf_linear_lora's.  Needs n_modules * rank <= 128 and the modules' A factors evenly
+ * spaced in the cache (or one module); LF_ERR_UNSUPPORTED otherwise. */
+int lf_linear_lora_shrink(void* stream, int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,
+                          const void* bias, void* y, int64_t ldy, int64_t m, int n, int k, int act,
+                          void* u, int rank, const void* cache_a, int64_t a_slot_stride, int64_t a_module_stride,
+                          const void* cache_b, int64_t b_slot_stride, int64_t b_module_stride,
+                          int n_slots, int n_modules, const int32_t* modules, int module_cols,
+                          const int32_t* seg_start, const int32_t* seg_len, int n_segs,
+                          const int32_t* tile_pairs, const int32_t* pairs, int32_t* status);
 
 /* ------------------------------------------------------------------------
  * Encoder elementwise ops around the projections

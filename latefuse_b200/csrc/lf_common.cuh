@@ -152,7 +152,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
 }
 
 // ---------------------------------------------------------------------------
-// TMA (tiled cp.async.bulk.tensor, no multicast anywhere in this library)
+// TMA (tiled cp.async.bulk.tensor; no load in this library uses cluster multicast)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int32_t c0, int32_t c1) {

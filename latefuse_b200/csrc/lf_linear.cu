@@ -37,6 +37,15 @@
 // B factor (MN-major SW128, straight from the slot cache, prefetched into L2 one
 // tile ahead), and the leader multiplies them with K = R, so every row gets its
 // own adapter's delta: y = act(round(x W^T + bias + u B)).
+// With the shrink in the same launch (lf_linear_lora_shrink) each pair owns whole
+// 256-row blocks: before a block's column tiles it runs one or more shrink passes,
+// u = round(x A_slot(t)) for every segment and module of the block, as an MMA of the
+// block's x against the segments' A factors (MN-major, all modules of a segment in one
+// copy from the slot cache, each CTA staging half of the segments); the epilogue
+// writes u in the blocked layout (every row of a (128-row tile, segment) block: its
+// product if it lies in the segment, else 0), fences it for the async proxy and
+// signals the producer, which then stages the blocks for the tiles' delta MMAs from L2.
+// u never leaves the launch except through L2, and x is read in the same launch.
 // Every wait is bounded: a timeout sets LF_STATUS_TIMEOUT and the roles unwind.
 // No load uses cluster multicast: each CTA loads only its own operands.
 #include "lf_common.cuh"
@@ -70,6 +79,13 @@ struct alignas(64) LinearParams {
   const void* bias;   // N entries or null
   const int32_t* tile_pairs;          // LoRA: 256-row tile q's delta blocks are entries
   const int32_t* pairs;               //   tile_pairs[q] .. tile_pairs[q + 1] of pairs (3 each); null: no delta
+  CUtensorMap a_map;                  // shrink: 4D {R, K, n_mod, n_slots}, box {R, 64, n_mod, 1}, MN-major
+  void* u_out;                        // shrink: the blocked u this launch writes (u_map reads it back)
+  const int32_t* seg_start;           // shrink: segment starts and lengths (tokens)
+  const int32_t* seg_len;
+  int32_t shrink;                     // 1: u is computed in this launch
+  int32_t s_epc;                      // shrink: segments per CTA per pass (n_mod * R * s_epc <= 128)
+  int32_t n_rb;                       // 256-row blocks
   int32_t n_segs;
   int32_t n_blk;                      // LoRA: u blocks per module (128-row tiles + segments)
   int32_t rank;
@@ -160,7 +176,63 @@ __device__ __forceinline__ bool aborted_flag(const int32_t* f) {
   return *reinterpret_cast<const volatile int32_t*>(f) != 0;
 }
 
-template <typename T>
+// One work item of a CTA pair: a 256 x 256 output tile (rb, c), or shrink pass `pass`
+// of row block rb.  Every role walks the same sequence: round robin over all tiles
+// without the shrink; with it, whole row blocks (pair, pair + n_pairs, ...), each as
+// its shrink passes followed by its column tiles.
+struct Item {
+  int32_t rb, c, pass;
+  bool shrink;
+};
+
+template <bool kShrinkable>
+struct Sched {
+  int64_t t;       // next tile (round robin)
+  int32_t rb, c;   // current block and next column tile (row blocks)
+  int32_t pass, n_pass;
+  int32_t n_pairs;
+
+  __device__ __forceinline__ static int32_t passes(const LinearParams& p, int32_t rb) {
+    const int2 qr = pair_range(p.tile_pairs, rb, p.n_segs);
+    const int32_t per = 2 * p.s_epc;
+    return (qr.y - qr.x + per - 1) / per;
+  }
+  __device__ __forceinline__ Sched(const LinearParams& p, int pair, int n_pairs_)
+      : t(pair), rb(pair), c(0), pass(0), n_pass(0), n_pairs(n_pairs_) {
+    if (kShrinkable && p.shrink && rb < p.n_rb) n_pass = passes(p, rb);
+  }
+  __device__ __forceinline__ bool next(const LinearParams& p, Item& it) {
+    if (!kShrinkable || !p.shrink) {
+      if (t >= p.n_tiles) return false;
+      it = Item{int32_t(t / p.n_tiles_n), int32_t(t % p.n_tiles_n), 0, false};
+      t += n_pairs;
+      return true;
+    }
+    while (rb < p.n_rb) {
+      if (pass < n_pass) {
+        it = Item{rb, 0, pass++, true};
+        return true;
+      }
+      if (c < p.n_tiles_n) {
+        it = Item{rb, c++, 0, false};
+        return true;
+      }
+      rb += n_pairs;
+      c = 0;
+      pass = 0;
+      n_pass = rb < p.n_rb ? passes(p, rb) : 0;
+    }
+    return false;
+  }
+};
+
+// The MN-major operand layout of an A-factor box (64 K rows of R elements), as the
+// slot cache's TMA copy lands it: (swizzle, stride between 8-row groups).
+__device__ __forceinline__ uint32_t a_box_layout(int R) { return R == 16 ? 6u : R == 32 ? 4u : 2u; }
+
+// kLora: the LoRA delta blocks (and the shrink passes when p.shrink) are compiled in;
+// the plain projection GEMM is its own instantiation without them.
+template <typename T, bool kLora>
 __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_constant__ LinearParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -176,7 +248,8 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
   uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + (s_delta + kDeltaBuf - base));
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   const int FULL = 0, EMPTY = kStages, ACC_FULL = 2 * kStages, ACC_EMPTY = 2 * kStages + 2,
-            DRAIN = 2 * kStages + 4, DFULL = DRAIN + 1, DEMPTY = DRAIN + 2, N_BARS = DRAIN + 3;
+            DRAIN = 2 * kStages + 4, DFULL = DRAIN + 1, DEMPTY = DRAIN + 2, U_READY = DRAIN + 3,
+            N_BARS = DRAIN + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(&bars[N_BARS]);
   int32_t* s_abort = reinterpret_cast<int32_t*>(tmem_slot + 1);
 
@@ -192,6 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     mbar_init(bar(DRAIN), 1);
     mbar_init(bar(DFULL), 1);   // the leader's arrive, with both CTAs' bytes
     mbar_init(bar(DEMPTY), 1);  // the leader's MMA commit
+    mbar_init(bar(U_READY), kEpiWarps);  // this CTA's epilogue warps: a shrink pass's u is written
     *s_abort = 0;
     fence_mbar_init();
     prefetch_tmap(&p.x_map);
@@ -216,24 +290,24 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     set_status(p.status, LF_STATUS_TIMEOUT);
     atomicExch(s_abort, 1);
   };
-  const bool lora = p.pairs != nullptr;
+  constexpr bool lora = kLora;
   // a tile's first delta block goes to its own buffer, loaded while the tile's K
   // blocks stream, so it has landed when the MMA reaches it (later ones use the ring)
   const bool dbuf = lora && 512 * p.rank <= kDeltaBuf;
+  auto dbuf_tile = [&](const Item& it) { return !(kLora && p.shrink && it.c == 0); };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
     if (lane == 0) {
-      int kk = 0;
+      int kk = 0, dk = 0, u_wait = 0, u_ph = 0;
       bool stop = false;
       const int32_t half_cols = int32_t(rank) * (kBN / 2);
       // this CTA's half of the B factors of a tile's segments, into L2
-      auto prefetch_b = [&](int64_t tt) {
-        if (!lora || tt >= p.n_tiles) return;
-        const int32_t nn0 = int32_t(tt % p.n_tiles_n) * kBN;
-        const int pmod = nn0 / p.module_cols;
+      auto prefetch_b = [&](int32_t trb, int32_t tc) {
+        if (!lora || trb < 0) return;
+        const int pmod = tc * kBN / p.module_cols;
         if (pmod >= p.n_mod) return;
-        const int2 qr = pair_range(p.tile_pairs, int(tt / p.n_tiles_n), p.n_segs);
+        const int2 qr = pair_range(p.tile_pairs, trb, p.n_segs);
         for (int q = qr.x; q < qr.y; ++q) {
           const int32_t slot = __ldg(p.pairs + 3 * q + 1);
           if (slot >= 0 && slot < p.n_slots)
@@ -241,21 +315,66 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
                         uint32_t(p.rank) * uint32_t(p.module_cols) * 2u);
         }
       };
-      prefetch_b(pair);
-      int dk = 0;
-      for (int64_t t = pair; t < p.n_tiles && !stop; t += n_pairs) {
-        const int32_t tq = int32_t(t / p.n_tiles_n);
-        const int32_t m0 = tq * (2 * kBM) + int32_t(rank) * kBM;
-        const int32_t n0 = int32_t(t % p.n_tiles_n) * kBN;
-        const int mod = lora ? n0 / p.module_cols : p.n_mod;
+      // the stage of K block kb is free: arm it (leader) and return its address
+      auto take = [&](uint32_t bytes, uint32_t& st, uint32_t& full) {
+        const int s = kk % kStages;
+        if (aborted_flag(s_abort) || !mbar_wait(bar(EMPTY + s), ((kk / kStages) & 1) ^ 1)) {
+          if (!aborted_flag(s_abort)) fail();
+          return false;
+        }
+        st = s_stage0 + s * kStageBytes;
+        full = mapa_shared(bar(FULL + s), 0);
+        if (rank == 0) mbar_arrive_expect_tx(bar(FULL + s), bytes);
+        return true;
+      };
+      // `ahead` walks the same items as `sched`, one output tile in front of it
+      Sched<kLora> sched(p, pair, n_pairs), ahead(p, pair, n_pairs);
+      Item it, nx;
+      auto next_tile = [&](Item& x) {
+        while (ahead.next(p, x))
+          if (!x.shrink) return true;
+        return false;
+      };
+      if (next_tile(nx)) prefetch_b(nx.rb, nx.c);
+      while (!stop && sched.next(p, it)) {
+        const int32_t m0 = it.rb * (2 * kBM) + int32_t(rank) * kBM;
         int q0 = 0, q1 = 0;
-        if (mod < p.n_mod) {
+        if (lora) {
           bool bad = false;
-          const int2 qr = pair_range(p.tile_pairs, tq, p.n_segs, &bad);
-          if (bad && rank == 0) set_status(p.status, LF_STATUS_BAD_SEGMENT);
+          const int2 qr = pair_range(p.tile_pairs, it.rb, p.n_segs, &bad);
+          if (bad && rank == 0 && (it.shrink || it.c == 0)) set_status(p.status, LF_STATUS_BAD_SEGMENT);
           q0 = qr.x;
           q1 = qr.y;
         }
+        if (it.shrink) {
+          // pass `it.pass`: this CTA stages the x rows and the A factors (all modules of a
+          // segment in one copy) of its half of the pass's segments; the other half's
+          // columns come from the peer; a missing segment reads zeros (slot past the cache)
+          const int32_t e0 = it.pass * 2 * p.s_epc;
+          const int32_t ne_p = min(2 * p.s_epc, q1 - q0 - e0);
+          const int32_t ne_h = (ne_p + 1) / 2;
+          const uint32_t box = uint32_t(p.n_mod) * 128u * uint32_t(p.rank);  // one segment's modules
+          for (int kb = 0; kb < p.n_kb; ++kb, ++kk) {
+            uint32_t st, full;
+            if (!take(2 * (kABytes + ne_h * box), st, full)) {
+              stop = true;
+              break;
+            }
+            tma_load_2d_pair(st, &p.x_map, full, kb * kBK, m0);
+            for (int i = 0; i < ne_h; ++i) {
+              const int32_t e = e0 + int32_t(rank) * ne_h + i;
+              const int32_t slot = e < ne_p + e0 ? __ldg(p.pairs + 3 * (q0 + e) + 1) : p.n_slots;
+              tma_load_4d_pair(st + kABytes + i * box, &p.a_map, full, 0, kb * kBK, 0, slot);
+            }
+          }
+          // the block's tiles wait for the epilogue to have written u: one phase of U_READY
+          // per block (after its last pass), so the producer never trails it by two phases
+          u_wait = 1;
+          continue;
+        }
+        const int32_t n0 = it.c * kBN;
+        const int mod = lora ? n0 / p.module_cols : p.n_mod;
+        if (mod >= p.n_mod) q0 = q1 = 0;
         const int32_t n_loc = mod < p.n_mod ? n0 - mod * p.module_cols : 0;
         const int32_t zero_blk = p.n_mod * p.n_blk;  // past the last block: the copy reads zeros
         // delta block q: this CTA's 128 rows of u (its block of (128-row tile, segment), or
@@ -269,27 +388,33 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
             j = -1;
           }
           if ((slot < 0 || slot >= p.n_slots) && rank == 0) set_status(p.status, LF_STATUS_BAD_SLOT);
-          const int32_t blk = (j >= 0 && ((mask >> rank) & 1)) ? mod * p.n_blk + 2 * tq + int32_t(rank) + j
+          const int32_t blk = (j >= 0 && ((mask >> rank) & 1)) ? mod * p.n_blk + 2 * it.rb + int32_t(rank) + j
                                                                : zero_blk;
           const uint32_t full = mapa_shared(full_local, 0);
           if (rank == 0) mbar_arrive_expect_tx(full_local, 2 * 512 * p.rank);  // u 128 x R + B R x 128, twice
           tma_load_3d_pair(dst_u, &p.u_map, full, 0, 0, blk);
           tma_load_4d_pair(dst_b, &p.b_map[mod], full, 0, 0, (n_loc + half_cols) / 64, slot);
         };
-        const bool use_dbuf = dbuf && q1 > q0;
+        // u written in this launch must be there before its blocks are staged
+        auto wait_u = [&]() {
+          for (; u_wait > 0; --u_wait, u_ph ^= 1)  // at most one phase pending
+            if (aborted_flag(s_abort) || !mbar_wait(bar(U_READY), u_ph)) {
+              if (!aborted_flag(s_abort)) fail();
+              return false;
+            }
+          return true;
+        };
         // the first block is loaded once the MMA has started this tile (by then the
-        // previous tile's first block has been multiplied)
+        // previous tile's first block has been multiplied); not for a block's first tile
+        // when this launch writes u (its delta blocks wait for the shrink's epilogue)
+        const bool use_dbuf = dbuf && q1 > q0 && dbuf_tile(it);
         const int d_after = (p.n_kb < kStages ? p.n_kb : kStages) - 1;
         for (int kb = 0; kb < p.n_kb; ++kb, ++kk) {
-          const int s = kk % kStages;
-          if (aborted_flag(s_abort) || !mbar_wait(bar(EMPTY + s), ((kk / kStages) & 1) ^ 1)) {
-            if (!aborted_flag(s_abort)) fail();
+          uint32_t st, full;
+          if (!take(2 * kStageBytes, st, full)) {
             stop = true;
             break;
           }
-          const uint32_t st = s_stage0 + s * kStageBytes;
-          const uint32_t full = mapa_shared(bar(FULL + s), 0);
-          if (rank == 0) mbar_arrive_expect_tx(bar(FULL + s), 2 * kStageBytes);
           tma_load_2d_pair(st, &p.x_map, full, kb * kBK, m0);
           tma_load_2d_pair(st + kABytes, &p.w_map, full, kb * kBK, n0 + half_cols);
           if (use_dbuf && kb == d_after) {
@@ -304,8 +429,12 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
           }
         }
         if (use_dbuf) ++q0;
-        if (!stop) prefetch_b(t + n_pairs);  // the ring is full here: the producer has time
-        if (stop || mod >= p.n_mod) continue;
+        if (!stop && next_tile(nx)) prefetch_b(nx.rb, nx.c);  // the ring is full here: the producer has time
+        if (stop || q1 <= q0) continue;
+        if (!wait_u()) {
+          stop = true;
+          break;
+        }
         for (int q = q0; q < q1; ++q, ++kk) {
           const int s = kk % kStages;
           if (aborted_flag(s_abort) || !mbar_wait(bar(EMPTY + s), ((kk / kStages) & 1) ^ 1)) {
@@ -330,7 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     if (lane == 0 && rank == 0) {
       constexpr uint32_t idesc = umma_idesc_f16(DT<T>::umma_fmt, 2 * kBM, kBN, 0, 0);
       constexpr uint32_t idesc_d = umma_idesc_f16(DT<T>::umma_fmt, 2 * kBM, kBN, 0, 1);
-      int kk = 0, it = 0, dk = 0;
+      int kk = 0, n_it = 0, dk = 0;
       bool stop = false;
       auto wait = [&](uint32_t b, uint32_t parity) {
         if (aborted_flag(s_abort)) return false;
@@ -338,17 +467,46 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
         if (!aborted_flag(s_abort)) fail();
         return false;
       };
-      for (int64_t t = pair; t < p.n_tiles && !stop; t += n_pairs, ++it) {
-        const int a = it & 1;
-        const int32_t n0 = int32_t(t % p.n_tiles_n) * kBN;
-        const int mod = lora ? n0 / p.module_cols : p.n_mod;
-        int n_delta = 0;
-        if (mod < p.n_mod) {
-          const int2 qr = pair_range(p.tile_pairs, int(t / p.n_tiles_n), p.n_segs);
-          n_delta = qr.y - qr.x;
+      Sched<kLora> sched(p, pair, n_pairs);
+      Item it;
+      for (; !stop && sched.next(p, it); ++n_it) {
+        const int a = n_it & 1;
+        int n_delta = 0, ne_p = 0;
+        if (lora) {
+          const int2 qr = pair_range(p.tile_pairs, it.rb, p.n_segs);
+          if (it.shrink) {
+            ne_p = min(2 * p.s_epc, qr.y - qr.x - it.pass * 2 * p.s_epc);
+          } else if (it.c * kBN / p.module_cols < p.n_mod) {
+            n_delta = qr.y - qr.x;
+          }
         }
-        if (!wait(bar(ACC_EMPTY + a), ((it >> 1) & 1) ^ 1)) break;
+        if (!wait(bar(ACC_EMPTY + a), ((n_it >> 1) & 1) ^ 1)) break;
         tc_fence_after();
+        if (it.shrink) {
+          // u = x A over the pass's segments: N = both halves' A boxes (MN-major atoms of
+          // R columns, one box of R x 64 per segment and module, box bytes apart)
+          const int ne_h = (ne_p + 1) / 2;
+          const uint32_t n_cols = uint32_t(2 * ne_h * p.n_mod * p.rank);
+          const uint32_t idesc_s = umma_idesc_f16(DT<T>::umma_fmt, 2 * kBM, n_cols, 0, 1);
+          const uint32_t abox = 128u * uint32_t(p.rank), row_b = 2u * uint32_t(p.rank);
+          for (int kb = 0; kb < p.n_kb; ++kb, ++kk) {
+            const int s = kk % kStages;
+            if (!wait(bar(FULL + s), (kk / kStages) & 1)) {
+              stop = true;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t st = s_stage0 + s * kStageBytes;
+#pragma unroll
+            for (int q = 0; q < kBK / 16; ++q)
+              umma_pair(tmem + a * kBN, smem_desc(st + q * 32, 16, 1024, 2),
+                        smem_desc(st + kABytes + q * 16 * row_b, abox, 8 * row_b, a_box_layout(p.rank)), idesc_s,
+                        (kb | q) != 0 ? 1u : 0u);
+            umma_commit_pair(bar(EMPTY + s));
+          }
+          if (!stop) umma_commit_pair(bar(ACC_FULL + a));
+          continue;
+        }
         for (int kb = 0; kb < p.n_kb; ++kb, ++kk) {
           const int s = kk % kStages;
           if (!wait(bar(FULL + s), (kk / kStages) & 1)) {
@@ -371,7 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
                       smem_desc(ba + q * 2048, p.rank * 128, 1024, 2), idesc_d, 1u);
         };
         int d = 0;
-        if (!stop && dbuf && n_delta > 0) {  // the first block, from the delta buffer
+        if (!stop && dbuf && n_delta > 0 && dbuf_tile(it)) {  // the first block, from the delta buffer
           if (!wait(bar(DFULL), dk & 1)) {
             stop = true;
           } else {
@@ -405,19 +563,77 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     const uint32_t taddr = tmem + (uint32_t(quad * 32) << 16);
     const uint32_t my_out = s_out0 + (warp - 2) * kOutBuf;
     const uint32_t acc_empty = mapa_shared(bar(ACC_EMPTY), 0);  // the leader's
+    // A shrink pass's u: for each segment of the pass with tokens in this CTA's 128 rows
+    // and each module, its (128-row tile, segment) block, every row of it (the product
+    // for rows in the segment, else 0), in the no-swizzle K-major operand layout the
+    // delta MMA reads (8-element chunk q of row r at core matrix (r / 8, q)).  The two
+    // warps of a lane quadrant take alternate boxes.  The writes are fenced for the
+    // async proxy before the producer's copies read them.
+    auto write_u = [&](const Item& it, int a, int32_t m0, int quad_, int half_) {
+      const int2 qr = pair_range(p.tile_pairs, it.rb, p.n_segs);
+      const int32_t e0 = it.pass * 2 * p.s_epc;
+      const int32_t ne_p = min(2 * p.s_epc, qr.y - qr.x - e0);
+      const int32_t ne_h = (ne_p + 1) / 2;
+      const int R = p.rank;
+      const int row = quad_ * 32 + lane;
+      const int64_t t = int64_t(m0) + row;
+      T* u = static_cast<T*>(p.u_out);
+      int box = 0;
+      for (int owner = 0; owner < 2; ++owner) {
+        for (int i = 0; i < ne_h; ++i) {
+          const int32_t e = owner * ne_h + i;  // entry within the pass
+          for (int m = 0; m < p.n_mod; ++m, ++box) {
+            if ((box & 1) != half_ || e >= ne_p) continue;
+            const int q = qr.x + e0 + e;
+            const int j = __ldg(p.pairs + 3 * q);
+            const int mask = __ldg(p.pairs + 3 * q + 2);
+            if (j < 0 || j >= p.n_segs || !((mask >> rank) & 1)) continue;  // no block of this CTA's tile
+            const int64_t s0 = __ldg(p.seg_start + j), s1 = s0 + __ldg(p.seg_len + j);
+            const bool in = t >= s0 && t < s1 && t < p.m_rows;
+            T* blk = u + (int64_t(m) * p.n_blk + 2 * it.rb + int32_t(rank) + j) * (int64_t(kBM) * R);
+            const uint32_t col = uint32_t(owner) * uint32_t(ne_h * p.n_mod * R) + uint32_t((i * p.n_mod + m) * R);
+            for (int c = 0; c < R / 16; ++c) {
+              float v[16];
+              tmem_ld16(taddr + a * kBN + col + c * 16, v);
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                uint4 pk;
+                pk.x = Pack2<T>::pack(in ? v[h * 8 + 0] : 0.f, in ? v[h * 8 + 1] : 0.f);
+                pk.y = Pack2<T>::pack(in ? v[h * 8 + 2] : 0.f, in ? v[h * 8 + 3] : 0.f);
+                pk.z = Pack2<T>::pack(in ? v[h * 8 + 4] : 0.f, in ? v[h * 8 + 5] : 0.f);
+                pk.w = Pack2<T>::pack(in ? v[h * 8 + 6] : 0.f, in ? v[h * 8 + 7] : 0.f);
+                *reinterpret_cast<uint4*>(blk + ((row >> 3) * (R / 8) + c * 2 + h) * 64 + (row & 7) * 8) = pk;
+              }
+            }
+          }
+        }
+      }
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+    };
     const T* bias = static_cast<const T*>(p.bias);
-    int it = 0;
-    for (int64_t t = pair; t < p.n_tiles; t += n_pairs, ++it) {
-      const int a = it & 1;
-      const int32_t m0 = int32_t(t / p.n_tiles_n) * (2 * kBM) + int32_t(rank) * kBM;
-      const int32_t n0 = int32_t(t % p.n_tiles_n) * kBN;
+    Sched<kLora> sched(p, pair, n_pairs);
+    Item item;
+    for (int n_it = 0; sched.next(p, item); ++n_it) {
+      const int a = n_it & 1;
+      const int32_t m0 = item.rb * (2 * kBM) + int32_t(rank) * kBM;
+      const int32_t n0 = item.c * kBN;
       bool ok = !aborted_flag(s_abort);
-      if (ok && !mbar_wait(bar(ACC_FULL + a), (it >> 1) & 1)) {
+      if (ok && !mbar_wait(bar(ACC_FULL + a), (n_it >> 1) & 1)) {
         fail();
         ok = false;
       }
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
+      if (item.shrink) {
+        write_u(item, a, m0, quad, half);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (item.pass == sched.n_pass - 1) mbar_arrive(bar(U_READY));  // the block's u is complete
+          mbar_arrive_cluster(acc_empty + a * 8);
+        }
+        continue;
+      }
       for (int c = half * (kBN / kOutCols / 2); c < (half + 1) * (kBN / kOutCols / 2); ++c) {
         uint32_t v[32];
         tmem_ld32(taddr + a * kBN + c * kOutCols, v);
@@ -499,6 +715,10 @@ struct LoraArgs {
   int module_cols;
   int n_segs;
   const int32_t *tile_pairs, *pairs;
+  // the shrink in the same launch (cache_a null: u was written before the launch)
+  const void* cache_a;
+  int64_t a_slot_stride, a_module_stride;
+  const int32_t *seg_start, *seg_len;
 };
 
 static int linear_impl(const char* fn, void* stream, int dtype, const void* x, int64_t ldx, const void* w,
@@ -531,6 +751,14 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
     if (!aligned16(L.u) || !aligned16(L.cache_b) || (L.b_slot_stride * 2) % 16 || (L.b_module_stride * 2) % 16 ||
         (L.n_slots > 1 && L.b_slot_stride < int64_t(L.module_cols) * L.rank))
       return set_error(LF_ERR_INVALID, "%s: u / cache_b alignment or slot stride", fn);
+    if (L.cache_a != nullptr) {
+      if (L.n_modules * L.rank > 128)
+        return set_error(LF_ERR_UNSUPPORTED, "%s: n_modules * rank %d above 128; run lf_lora_shrink_blocked and "
+                         "lf_linear_lora instead", fn, L.n_modules * L.rank);
+      if (L.seg_start == nullptr || L.seg_len == nullptr || !aligned16(L.cache_a) || (L.a_slot_stride * 2) % 16 ||
+          (L.a_module_stride * 2) % 16 || (L.n_slots > 1 && L.a_slot_stride < int64_t(k) * L.rank))
+        return set_error(LF_ERR_INVALID, "%s: null segment arrays, or cache_a alignment or slot stride", fn);
+    }
   }
   if (m == 0) return LF_OK;
   PFN_encodeTiled enc = get_encode_tiled();
@@ -588,6 +816,29 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
       const cuuint32_t box[4] = {64, R, kBN / 128, 1};
       if ((rc = tmap(&p.b_map[i], 4, b, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "b"))) return rc;
     }
+    if (L.cache_a != nullptr) {
+      // every module's A box of a segment in one copy: the modules' A factors must lie
+      // evenly spaced in the cache (q/k/v as 0, 1, 2), or there is one module
+      const int64_t es = 2;
+      int d = L.n_modules > 1 ? L.modules[1] - L.modules[0] : 1;
+      for (int i = 2; i < L.n_modules && d > 0; ++i)
+        if (L.modules[i] - L.modules[i - 1] != d) d = 0;
+      const int64_t mstride = L.n_modules == 1 ? int64_t(k) * L.rank * es : int64_t(d) * L.a_module_stride * es;
+      if (d <= 0 || mstride < int64_t(k) * L.rank * es || mstride % 16 != 0)
+        return set_error(LF_ERR_UNSUPPORTED, "%s: the modules' A factors are not evenly spaced in the cache; "
+                         "run lf_lora_shrink_blocked and lf_linear_lora instead", fn);
+      const void* a = static_cast<const uint8_t*>(L.cache_a) + int64_t(L.modules[0]) * L.a_module_stride * es;
+      const int64_t ss = L.n_slots == 1 ? int64_t(k) * L.rank : L.a_slot_stride;
+      const cuuint64_t dims[4] = {R, cuuint64_t(k), cuuint64_t(L.n_modules), cuuint64_t(L.n_slots)};
+      const cuuint64_t strides[3] = {cuuint64_t(R) * es, cuuint64_t(mstride), cuuint64_t(ss) * es};
+      const cuuint32_t box[4] = {R, 64, cuuint32_t(L.n_modules), 1};
+      if ((rc = tmap(&p.a_map, 4, a, dims, strides, box, a_tma_swizzle(L.rank), "a"))) return rc;
+      p.shrink = 1;
+      p.s_epc = 128 / (L.n_modules * L.rank);
+      p.u_out = const_cast<void*>(L.u);
+      p.seg_start = L.seg_start;
+      p.seg_len = L.seg_len;
+    }
     p.tile_pairs = L.tile_pairs;
     p.pairs = L.pairs;
     p.n_segs = L.n_segs;
@@ -599,7 +850,8 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
   p.bias = bias;
   p.m_rows = m;
   p.n_tiles_n = n / kBN;
-  p.n_tiles = ((m + 2 * kBM - 1) / (2 * kBM)) * p.n_tiles_n;
+  p.n_rb = int32_t((m + 2 * kBM - 1) / (2 * kBM));
+  p.n_tiles = int64_t(p.n_rb) * p.n_tiles_n;
   p.n_kb = k / kBK;
   p.act = act;
   p.status = status;
@@ -607,7 +859,8 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  auto kern = dtype == LF_DTYPE_BF16 ? linear_kernel<__nv_bfloat16> : linear_kernel<__half>;
+  auto kern = lora != nullptr ? (dtype == LF_DTYPE_BF16 ? linear_kernel<__nv_bfloat16, true> : linear_kernel<__half, true>)
+                              : (dtype == LF_DTYPE_BF16 ? linear_kernel<__nv_bfloat16, false> : linear_kernel<__half, false>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(linear)");
   cudaLaunchAttribute attr[2];
@@ -618,10 +871,11 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   // as many pairs as can be resident at once (a GPC with an odd SM count leaves one idle)
-  static int resident_pairs[64] = {0};
+  static int resident_pairs[64][2] = {};
   int pairs = sms / 2;
   if (dev >= 0 && dev < 64) {
-    if (resident_pairs[dev] == 0) {
+    int& resident = resident_pairs[dev][lora != nullptr];
+    if (resident == 0) {
       cudaLaunchConfig_t q = {};
       q.gridDim = dim3(unsigned(sms & ~1));
       q.blockDim = dim3(kThreads);
@@ -629,11 +883,12 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
       q.attrs = attr;
       q.numAttrs = 1;
       int nc = 0;
-      resident_pairs[dev] = (cudaOccupancyMaxActiveClusters(&nc, kern, &q) == cudaSuccess && nc > 0) ? nc : sms / 2;
+      resident = (cudaOccupancyMaxActiveClusters(&nc, kern, &q) == cudaSuccess && nc > 0) ? nc : sms / 2;
     }
-    pairs = resident_pairs[dev] < sms / 2 ? resident_pairs[dev] : sms / 2;
+    pairs = resident < sms / 2 ? resident : sms / 2;
   }
   if (p.n_tiles < pairs) pairs = int(p.n_tiles);
+  if (p.shrink && p.n_rb < pairs) pairs = p.n_rb;  // a pair owns whole row blocks
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(2 * pairs));
   cfg.blockDim = dim3(kThreads);
@@ -660,6 +915,19 @@ extern "C" int lf_linear_lora(void* stream, int dtype, const void* x, int64_t ld
                               int module_cols, int n_segs, const int32_t* tile_pairs, const int32_t* pairs,
                               int32_t* status) {
   LoraArgs L{u, rank, cache_b, b_slot_stride, b_module_stride, n_slots, n_modules, modules, module_cols,
-             n_segs, tile_pairs, pairs};
+             n_segs, tile_pairs, pairs, nullptr, 0, 0, nullptr, nullptr};
   return linear_impl("lf_linear_lora", stream, dtype, x, ldx, w, ldw, bias, y, ldy, m, n, k, act, &L, status);
+}
+
+extern "C" int lf_linear_lora_shrink(void* stream, int dtype, const void* x, int64_t ldx, const void* w,
+                                     int64_t ldw, const void* bias, void* y, int64_t ldy, int64_t m, int n, int k,
+                                     int act, void* u, int rank, const void* cache_a, int64_t a_slot_stride,
+                                     int64_t a_module_stride, const void* cache_b, int64_t b_slot_stride,
+                                     int64_t b_module_stride, int n_slots, int n_modules, const int32_t* modules,
+                                     int module_cols, const int32_t* seg_start, const int32_t* seg_len, int n_segs,
+                                     const int32_t* tile_pairs, const int32_t* pairs, int32_t* status) {
+  if (cache_a == nullptr) return set_error(LF_ERR_INVALID, "lf_linear_lora_shrink: null cache_a");
+  LoraArgs L{u, rank, cache_b, b_slot_stride, b_module_stride, n_slots, n_modules, modules, module_cols,
+             n_segs, tile_pairs, pairs, cache_a, a_slot_stride, a_module_stride, seg_start, seg_len};
+  return linear_impl("lf_linear_lora_shrink", stream, dtype, x, ldx, w, ldw, bias, y, ldy, m, n, k, act, &L, status);
 }

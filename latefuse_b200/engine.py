@@ -31,8 +31,8 @@ from torch.utils.hooks import RemovableHandle
 from latefuse_b200.batch import BatchedLRWeights, BatchLora, LayerwiseBatchedWeights
 from latefuse_b200.config import LoraServingConfig
 from latefuse_b200.head import LRHeadOps, head_forward, head_forward_rows, pool_tokens, validate_pooling
-from latefuse_b200.lora import (FactorCache, SegmentTable, blocked_u, linear_lora, lora_apply, lora_apply_into,
-                                 lora_shrink_blocked, per_row_cache, workspace_bytes)
+from latefuse_b200.lora import (FactorCache, SegmentTable, blocked_u, fused_shrink_ok, linear_lora, lora_apply,
+                                 lora_apply_into, lora_shrink_blocked, per_row_cache, workspace_bytes)
 from latefuse_b200.encoder_ops import ACT_GELU, add_layernorm, attention_varlen, gelu, linear
 from latefuse_b200.packing import PackedBatch, pack_rows
 
@@ -322,6 +322,9 @@ class EncoderWithLora(nn.Module):
         #: when a list, every LoRA delta op appends (start, end) CUDA events recorded
         #: around it on the current stream (used by the benchmark's roofline timing)
         self.lora_events: list | None = None
+        #: compute the shrink inside the projection GEMM's launch where the kernel can
+        #: (``lf_linear_lora_shrink``); False runs ``lf_lora_shrink_blocked`` first
+        self.fuse_shrink = True
         targets = serving_config.target_modules
         self._qkv_targets = [(m, _QKV.index(m)) for m in targets if m in _QKV]
         self._dense_target = "dense" in targets
@@ -586,18 +589,22 @@ class EncoderWithLora(nn.Module):
                 u_qkv = blocked_u(3, T, segs.n_segs, rank, h.dtype, h.device)
             if gemm_dense:
                 u_dense = blocked_u(1, T, segs.n_segs, rank, h.dtype, h.device)
+            fuse_qkv = gemm_qkv and self.fuse_shrink and fused_shrink_ok(qkv_by_col, rank)
+            fuse_dense_shrink = gemm_dense and self.fuse_shrink and fused_shrink_ok(dense_idx, rank)
         else:
-            fuse_dense = gemm_qkv = gemm_dense = False
+            fuse_dense = gemm_qkv = gemm_dense = fuse_qkv = fuse_dense_shrink = False
 
         for l, layer in enumerate(self.layers):
             if gemm_qkv:
                 cache = store.factor_cache(l)
-                ev = self._event_pair("qkv_shrink")
-                lora_shrink_blocked(h, u_qkv, cache, segs, qkv_by_col, status)
-                if ev is not None:
-                    ev[1].record()
+                if not fuse_qkv:
+                    ev = self._event_pair("qkv_shrink")
+                    lora_shrink_blocked(h, u_qkv, cache, segs, qkv_by_col, status)
+                    if ev is not None:
+                        ev[1].record()
                 ev = self._event_pair("qkv_gemm")
-                qkv = linear_lora(h, layer.wqkv, layer.bqkv, u_qkv, cache, segs, qkv_by_col, H, status=status)
+                qkv = linear_lora(h, layer.wqkv, layer.bqkv, u_qkv, cache, segs, qkv_by_col, H, status=status,
+                                  shrink=fuse_qkv)
                 if ev is not None:
                     ev[1].record()
             else:
@@ -614,12 +621,14 @@ class EncoderWithLora(nn.Module):
                 ctx = varlen_attention(q, k, v, pb.cu_seqlens, pb.max_len).view(T, H)
             if gemm_dense:
                 cache = store.factor_cache(l)
-                ev = self._event_pair("dense_shrink")
-                lora_shrink_blocked(ctx, u_dense, cache, segs, dense_idx, status)
-                if ev is not None:
-                    ev[1].record()
+                if not fuse_dense_shrink:
+                    ev = self._event_pair("dense_shrink")
+                    lora_shrink_blocked(ctx, u_dense, cache, segs, dense_idx, status)
+                    if ev is not None:
+                        ev[1].record()
                 ev = self._event_pair("dense_gemm")
-                ao = linear_lora(ctx, layer.wo, layer.bo, u_dense, cache, segs, dense_idx, H, status=status)
+                ao = linear_lora(ctx, layer.wo, layer.bo, u_dense, cache, segs, dense_idx, H, status=status,
+                                 shrink=fuse_dense_shrink)
                 if ev is not None:
                     ev[1].record()
                 h = self._ffn(layer, ao, h)

@@ -278,6 +278,17 @@ def _blocked_elems(n_modules: int, n_tokens: int, n_segs: int, rank: int) -> int
     return n_modules * ((n_tokens + 127) // 128 + n_segs) * 128 * rank
 
 
+def fused_shrink_ok(modules, rank: int) -> bool:
+    """Whether :func:`linear_lora` can compute ``u`` in its own launch (``shrink=True``):
+    every module's A factors fit one pass (``n_modules * rank <= 128``) and lie evenly
+    spaced in the cache (or there is one module)."""
+    mods = list(modules)
+    if len(mods) * rank > 128 or rank not in (16, 32, 64):
+        return False
+    d = mods[1] - mods[0] if len(mods) > 1 else 1
+    return d > 0 and all(b - a == d for a, b in zip(mods, mods[1:]))
+
+
 def lora_shrink_blocked(x: Tensor, u: Tensor, cache: FactorCache, segs: SegmentTable, modules,
                         status: Tensor | None = None) -> None:
     """:func:`lora_shrink` writing ``u`` (from :func:`blocked_u`) in the tile-blocked
@@ -297,17 +308,19 @@ def lora_shrink_blocked(x: Tensor, u: Tensor, cache: FactorCache, segs: SegmentT
 
 def linear_lora(x: Tensor, weight: Tensor, bias: Tensor | None, u: Tensor, cache: FactorCache,
                 segs: SegmentTable, modules, module_cols: int, act: int = 0, out: Tensor | None = None,
-                status: Tensor | None = None) -> Tensor:
+                status: Tensor | None = None, shrink: bool = False) -> Tensor:
     """``act(x @ weight.T + bias + delta)`` on the tcgen05 GEMM with the LoRA delta in
     its accumulator: output columns ``[i * module_cols, (i + 1) * module_cols)`` get
     ``u[i] @ B(slot(t), modules[i])`` (``u`` from :func:`lora_shrink_blocked`).
     One rounding of the sum, where the reference rounds the projection and the delta
-    apart; see ``lf_linear_lora``."""
+    apart; see ``lf_linear_lora``.  With ``shrink`` the same launch computes ``u`` first
+    (``lf_linear_lora_shrink``; ``u`` is then an output, in the same blocked layout)."""
     dev = nat.require_cuda(x, weight, bias, u, segs.table, out, status)
     x2, ldx = _rows(x)
     N, K = weight.shape
-    if u.numel() < _blocked_elems(len(modules), x2.shape[0], segs.n_segs, cache.rank):
-        raise ValueError("u must be a blocked_u(n_modules, n_tokens, n_segs, rank) buffer")
+    if u.numel() < _blocked_elems(len(modules), x2.shape[0], segs.n_segs, cache.rank) or not u.is_contiguous() \
+            or u.dtype != x.dtype:
+        raise ValueError("u must be a contiguous blocked_u(n_modules, n_tokens, n_segs, rank) buffer of x's dtype")
     w = weight if weight.stride(-1) == 1 else weight.contiguous()
     if out is None:
         out = torch.empty(*x.shape[:-1], N, dtype=x.dtype, device=x.device)
@@ -318,6 +331,18 @@ def linear_lora(x: Tensor, weight: Tensor, bias: Tensor | None, u: Tensor, cache
     if segs.n_tokens != x2.shape[0]:
         raise ValueError(f"segment table for {segs.n_tokens} tokens, x has {x2.shape[0]}")
     tp, pp = segs.pair_ptrs()
+    if shrink:
+        if cache.hidden != K:
+            raise ValueError(f"the A factors take {cache.hidden} inputs, x has {K}")
+        s_start, s_len, _, _, _, _ = segs.ptrs()
+        rc = nat.lib().lf_linear_lora_shrink(
+            nat.stream_ptr(dev), nat.dtype_code(x.dtype), x2.data_ptr(), ldx, w.data_ptr(), w.stride(0),
+            nat.ptr(b), o2.data_ptr(), o2.stride(0), x2.shape[0], N, K, int(act), u.data_ptr(), cache.rank,
+            cache.a_ptr, cache.a_slot_stride, cache.a_module_stride, cache.b_ptr, cache.b_slot_stride,
+            cache.b_module_stride, cache.n_slots, len(modules), nat.i32_array(modules), int(module_cols), s_start,
+            s_len, segs.n_segs, tp, pp, nat.ptr(status))
+        nat.check(rc, "lf_linear_lora_shrink")
+        return out
     rc = nat.lib().lf_linear_lora(
         nat.stream_ptr(dev), nat.dtype_code(x.dtype), x2.data_ptr(), ldx, w.data_ptr(), w.stride(0), nat.ptr(b),
         o2.data_ptr(), o2.stride(0), x2.shape[0], N, K, int(act), u.data_ptr(), cache.rank, cache.b_ptr,

@@ -54,24 +54,31 @@ def test_bge_m3_shape_packed_serving_matches_oracle(cuda):
 
     ids, mask = ragged_batch(64, 512, min_len=32, max_len=512, vocab=250002, pad_id=1, cls_id=0, low_id=5, seed=3)
     tenants = [f"adapter_{int(t)}" for t in zipf_tenants(slots, 64, alpha=1.1, seed=3)]
-    model.lora_events = []
-    ours = emb.embed_tokens(ids, mask, tenants)
-    kinds = {k for k, _, _ in model.lora_events}
-    model.lora_events = None
-    emb.check_device_status()
-    # the benchmark's path: shrink + projection GEMM with the delta in its accumulator
-    assert {"qkv_shrink", "qkv_gemm", "dense_shrink", "dense_gemm"} <= kinds, kinds
+    outs = {}
+    for fused in (True, False):
+        # the benchmark's path: the shrink inside the projection GEMM's launch; and the
+        # shrink as its own launch before the GEMM with the delta in its accumulator
+        model.fuse_shrink = fused
+        model.lora_events = []
+        outs[fused] = emb.embed_tokens(ids, mask, tenants)
+        kinds = {k for k, _, _ in model.lora_events}
+        model.lora_events = None
+        emb.check_device_status()
+        want = {"qkv_gemm", "dense_gemm"} | (set() if fused else {"qkv_shrink", "dense_shrink"})
+        assert kinds == want, kinds
+    model.fuse_shrink = True
 
     oracle = HookedEncoder(base, adapters_of(store, tenants), cfg.target_modules)
     ref = F.normalize(oracle.encode_pooled(ids.to(cuda), mask.to(cuda), tenants, "cls").float(), dim=-1)
     base_only = F.normalize(oracle.encode_pooled(ids.to(cuda), mask.to(cuda), tenants, "cls", apply_lora=False)
                             .float(), dim=-1)
     oracle.close()
-    err = row_rel(ours, ref)
-    assert err < 2e-2, err
-    # the adapters move the output by more than the tolerance, so a missing or
-    # misrouted delta cannot pass
-    assert row_rel(base_only, ref) > 2 * err
+    for fused, ours in outs.items():
+        err = row_rel(ours, ref)
+        assert err < 2e-2, (fused, err)
+        # the adapters move the output by more than the tolerance, so a missing or
+        # misrouted delta cannot pass
+        assert row_rel(base_only, ref) > 2 * err
 
 
 @pytest.mark.parametrize("engine", ["hf", "bert"])

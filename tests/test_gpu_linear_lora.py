@@ -231,3 +231,67 @@ def test_fused_gemm_reports_malformed_pair_table(cuda, corrupt):
     torch.cuda.synchronize()
     assert status.item() & want
     assert torch.equal(out[:256], good[:256])
+
+
+def _u_rows(u, st, n_mod, R):
+    """The blocked u as {(module, tile, segment): 128 x R block}, for the blocks the pair
+    table names (the others are never read)."""
+    n_blk = (st.n_tokens + 127) // 128 + st.n_segs
+    blocks = u.view(n_mod, n_blk, 128 * R)
+    tp = 4 * st.n_tiles + 3 * st.n_segs
+    n_q = (st.n_tokens + 255) // 256
+    h = st.host.tolist()
+    out = {}
+    for q in range(n_q):
+        for e in range(h[tp + q], h[tp + q + 1]):
+            j, _, mask = h[tp + n_q + 1 + 3 * e: tp + n_q + 4 + 3 * e]
+            for r in range(2):
+                if (mask >> r) & 1:
+                    for m in range(n_mod):
+                        out[(m, 2 * q + r, j)] = blocks[m, 2 * q + r + j]
+    return out
+
+
+@pytest.mark.parametrize("R,n_mod,max_len", [(16, 3, 400), (16, 3, 40), (32, 3, 300), (64, 1, 300), (16, 1, 25)])
+def test_shrink_in_the_gemm_launch_matches_the_two_launches(cuda, R, n_mod, max_len):
+    """``lf_linear_lora_shrink`` computes u in the GEMM's own launch: its u blocks and its
+    output against ``lf_lora_shrink_blocked`` + ``lf_linear_lora`` on the same inputs.
+    Short segments put many segments in one 256-token block (several shrink passes)."""
+    dtype, H, n_slots = torch.bfloat16, 1024 if n_mod == 1 else 512, 37
+    dev = torch.device("cuda")
+    starts, lengths, slots, T = packed_segments(30 if max_len > 100 else 80, n_slots, seed=R + max_len,
+                                                max_len=max_len)
+    fc, _ = make_cache(n_slots, n_mod + 1, H, R, dtype, dev, seed=R)
+    st = SegmentTable(starts, lengths, slots, T, dev)
+    g = torch.Generator(device="cpu").manual_seed(9)
+    x = torch.randn(T, H, generator=g).to(dtype).to(dev)
+    N = n_mod * H
+    W = (torch.randn(N, H, generator=g) * H ** -0.5).to(dtype).to(dev)
+    b = torch.randn(N, generator=g).to(dtype).to(dev)
+    modules = list(range(1, n_mod + 1))
+    u_two = blocked_u(n_mod, T, st.n_segs, R, dtype, dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    lora_shrink_blocked(x, u_two, fc, st, modules, status)
+    two = linear_lora(x, W, b, u_two, fc, st, modules, H, status=status)
+    u_one = torch.full_like(u_two, float("nan"))  # every block the table names must be written
+    one = linear_lora(x, W, b, u_one, fc, st, modules, H, status=status, shrink=True)
+    torch.cuda.synchronize()
+    assert status.item() == 0, nat.decode_status(status.item())
+    got, want = _u_rows(u_one, st, n_mod, R), _u_rows(u_two, st, n_mod, R)
+    assert got.keys() == want.keys()
+    for k in want:
+        assert not torch.isnan(got[k]).any(), k
+        assert (got[k].float() - want[k].float()).abs().max().item() <= 2e-2 * want[k].float().abs().max().item() + 1e-6
+    check(one, two, two)
+
+
+def test_shrink_in_the_gemm_launch_rejects_what_it_cannot_stage(cuda):
+    dtype, H, R = torch.bfloat16, 512, 64
+    dev = torch.device("cuda")
+    fc, _ = make_cache(4, 3, H, R, dtype, dev)
+    st = SegmentTable([0], [300], [1], 300, dev)
+    x = torch.randn(300, H, device=dev, dtype=dtype)
+    W = torch.randn(3 * H, H, device=dev, dtype=dtype)
+    u = blocked_u(3, 300, 1, R, dtype, dev)
+    with pytest.raises(nat.NativeLibraryError, match="above 128"):  # 3 modules x rank 64
+        linear_lora(x, W, None, u, fc, st, [0, 1, 2], H, shrink=True)
