@@ -365,6 +365,14 @@ int lf_head_forward_rows(void* stream, int dtype,
 int lf_linear(void* stream, int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,
               const void* bias, void* y, int64_t ldy, int64_t m, int n, int k, int act, int32_t* status);
 
+/* y = y + x w^T + bias, in place: the projection accumulated onto y's current
+ * values (cuBLAS's beta = 1), summed in f32 and rounded once; bias may be NULL.
+ * Shapes, dtypes and alignment as lf_linear.  Replaces the encoder's FFN output
+ * projection onto its residual (src/latefuse/model/encoder.py:139-141,
+ * `output(intermediate) + h`, with the bias added where the caller chooses). */
+int lf_linear_accumulate(void* stream, int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,
+                         const void* bias, void* y, int64_t ldy, int64_t m, int n, int k, int32_t* status);
+
 /* lf_linear with the late-fusion LoRA delta in the same accumulator:
  *     y[t, c] = act(round(x[t] . w[c] + bias[c] + u[i][t] . B(slot(t), i)[:, c - i * module_cols]))
  * for output column block i = c / module_cols < n_modules (columns of blocks

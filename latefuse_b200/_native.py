@@ -90,6 +90,9 @@ SIGNATURES: dict[str, tuple] = {
     "lf_linear": (c_int, [
         c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int,
         c_int, c_int, c_void_p]),
+    "lf_linear_accumulate": (c_int, [
+        c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int,
+        c_int, c_void_p]),
     "lf_linear_lora": (c_int, [
         c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int,
         c_int, c_int, c_void_p, c_int, c_void_p, c_int64, c_int64, c_int, c_int, POINTER(c_int32), c_int,

@@ -261,8 +261,10 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_f16(DT<T>::umma_fmt, kRows, kRows, /*a_mn=*/0, /*b_mn=*/0);
+      // a key tile with at most 64 keys of its sequence: S over those 64 only
+      constexpr uint32_t idesc_s64 = umma_idesc_f16(DT<T>::umma_fmt, kRows, kRows / 2, /*a_mn=*/0, /*b_mn=*/0);
       constexpr uint32_t idesc_o = umma_idesc_f16(DT<T>::umma_fmt, kRows, kHd, /*a_mn=*/0, /*b_mn=*/1);
-      struct Prev { bool valid, first, last; int t, u, kv; };
+      struct Prev { bool valid, first, last; int t, u, kv, nk; };  // nk: 16-key steps of O += P V
       Cursor c[kGroups];
       Prev prev[kGroups];
       for (int grp = 0; grp < kGroups; ++grp) {
@@ -280,8 +282,11 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
         tc_fence_after();
         const uint32_t pb = sP + grp * 2 * kTileBytes;
         const uint32_t vb = sV + sv * kTileBytes;
+        // keys past the sequence end stop at the last 16-key step that holds one
+        // (that step's other keys have p = 0)
 #pragma unroll
         for (int t = 0; t < kRows / 16; ++t) {
+          if (t >= e.nk) break;
           const uint64_t ad = smem_desc(pb + (t >> 2) * kTileBytes + (t & 3) * 32, 16, 1024, 2);
           const uint64_t bd = smem_desc(vb + t * 2048, kTileBytes, 1024, 2);
           umma_f16(tmem + kOCol + kHd * grp, ad, bd, idesc_o, (e.first && t == 0) ? 0u : 1u);
@@ -296,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
       while (!stop && (live(c[0]) || live(c[1]) || prev[0].valid || prev[1].valid)) {
         for (int grp = 0; grp < kGroups && !stop; ++grp) {
           Cursor& cg = c[grp];
-          Prev cur{false, false, false, 0, 0, 0};
+          Prev cur{false, false, false, 0, 0, 0, 0};
           if (live(cg)) {
             const int sk = kc % kKStages, sb = kc % kSBufs;
             if (aborted(s_abort) || (cg.j == 0 && !mbar_wait(gbar(Q_FULL, grp), cg.u & 1)) ||
@@ -308,14 +313,16 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
             }
             tc_fence_after();
             const uint32_t qa = sQ + grp * kTileBytes, kb = sK + sk * kTileBytes;
+            const int nvalid = min(kRows, cg.it.y - cg.j * kRows);
+            const uint32_t idesc = nvalid > kRows / 2 ? idesc_s : idesc_s64;
 #pragma unroll
             for (int t = 0; t < kHd / 16; ++t)
               umma_f16(tmem + kRows * sb, smem_desc(qa + t * 32, 16, 1024, 2), smem_desc(kb + t * 32, 16, 1024, 2),
-                       idesc_s, t > 0 ? 1u : 0u);
+                       idesc, t > 0 ? 1u : 0u);
             umma_commit(bar(S_FULL + sb));
             umma_commit(bar(K_EMPTY + sk));
             if (cg.j == cg.n_kv - 1) umma_commit(gbar(Q_EMPTY, grp));
-            cur = Prev{true, cg.j == 0, cg.j == cg.n_kv - 1, cg.t, cg.u, kc};
+            cur = Prev{true, cg.j == 0, cg.j == cg.n_kv - 1, cg.t, cg.u, kc, (nvalid + 15) / 16};
             ++kc;
             advance(cg);
           }
@@ -368,6 +375,12 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
       const int uu = c.u;
       const bool last = j == c.n_kv - 1;
       const int nvalid = min(kRows, it.y - j * kRows);
+      // warp-uniform skips of what the sequence does not reach: a warp whose 32 query
+      // rows all lie past its end does no softmax (its P rows only feed O rows that
+      // are never stored), and a key tile with at most 64 keys reads one 64-column
+      // half of S (the MMA computed only that half, and O += P V stops there)
+      const bool rows_live = quad * 32 < it.y - it.z * kRows;
+      const int n_half = nvalid > kRows / 2 ? 2 : 1;
       bool ok = !aborted(s_abort);
       if (ok && !mbar_wait(bar(S_FULL + sb), (kc / kSBufs) & 1)) {
         fail();
@@ -377,9 +390,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
       tc_fence_after();
       // pass 1: the row max over the valid keys, 64 columns at a time
       float mx = -INFINITY;
-      if (work) {
+      if (work && rows_live) {
 #pragma unroll 1
-        for (int hh = 0; hh < 2; ++hh) {
+        for (int hh = 0; hh < n_half; ++hh) {
           uint32_t sv[64];
           tmem_ld64(s_addr + hh * 64, sv);
           if (nvalid < hh * 64 + 64) {  // warp-uniform: keys past the end do not count
@@ -410,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
         ok = false;
       }
       const bool go = __all_sync(0xffffffffu, ok);
-      if (go && j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
+      if (go && rows_live && j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
         tc_fence_after();
         uint32_t ov[64];
         tmem_ld64(o_addr, ov);
@@ -420,10 +433,10 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
       }
       // pass 2: p = 2^(s - max), rounded to T into the group's SW128 K-major P tile
       float2 sums[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      if (go) {
+      if (go && rows_live) {
         const float2 neg_m = make_float2(-m_new, -m_new);
 #pragma unroll 1
-        for (int hh = 0; hh < 2; ++hh) {
+        for (int hh = 0; hh < n_half; ++hh) {
           uint32_t sv[64];
           tmem_ld64(s_addr + hh * 64, sv);
           if (nvalid < hh * 64 + 64) {  // warp-uniform: keys past the end score -inf, so p = 0
@@ -465,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_varlen_kernel(const __g
           fail();
           ok = false;
         }
-        if (__all_sync(0xffffffffu, ok)) {
+        if (__all_sync(0xffffffffu, ok) && rows_live) {
           tc_fence_after();
           uint32_t ov[64];
           tmem_ld64(o_addr, ov);

@@ -97,6 +97,8 @@ struct alignas(64) LinearParams {
   int32_t n_kb;
   int32_t act;        // LF_ACT_*
   int32_t* status;
+  const void* y_in;   // accumulate: y's current values (the output itself), row stride ldy
+  int64_t ldy;
 };
 
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster,
@@ -231,8 +233,9 @@ struct Sched {
 __device__ __forceinline__ uint32_t a_box_layout(int R) { return R == 16 ? 6u : R == 32 ? 4u : 2u; }
 
 // kLora: the LoRA delta blocks (and the shrink passes when p.shrink) are compiled in;
-// the plain projection GEMM is its own instantiation without them.
-template <typename T, bool kLora>
+// the plain projection GEMM is its own instantiation without them.  kAcc: the epilogue
+// adds y's current values (y += x W^T + bias, rounded once).
+template <typename T, bool kLora, bool kAcc>
 __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_constant__ LinearParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -613,10 +616,22 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     const T* bias = static_cast<const T*>(p.bias);
     Sched<kLora> sched(p, pair, n_pairs);
     Item item;
+    // accumulate: this lane's row of y at a chunk's 32 columns, loaded one chunk ahead
+    // (the tile's first chunk before its accumulator is waited for); rows past m read
+    // as 0 and are stored nowhere
+    const int c_begin = half * (kBN / kOutCols / 2), c_end = c_begin + kBN / kOutCols / 2;
+    auto load_y = [&](uint4 (&dst)[4], int32_t m0_, int col0_) {
+      const int64_t r = int64_t(m0_) + quad * 32 + lane;
+      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(p.y_in) + r * p.ldy + col0_);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) dst[q] = r < p.m_rows ? src[q] : make_uint4(0u, 0u, 0u, 0u);
+    };
+    uint4 y_next[4];
     for (int n_it = 0; sched.next(p, item); ++n_it) {
       const int a = n_it & 1;
       const int32_t m0 = item.rb * (2 * kBM) + int32_t(rank) * kBM;
       const int32_t n0 = item.c * kBN;
+      if constexpr (kAcc) load_y(y_next, m0, n0 + c_begin * kOutCols);
       bool ok = !aborted_flag(s_abort);
       if (ok && !mbar_wait(bar(ACC_FULL + a), (n_it >> 1) & 1)) {
         fail();
@@ -634,10 +649,16 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
         }
         continue;
       }
-      for (int c = half * (kBN / kOutCols / 2); c < (half + 1) * (kBN / kOutCols / 2); ++c) {
+      for (int c = c_begin; c < c_end; ++c) {
+        const int col0 = n0 + c * kOutCols;
+        uint4 yq[4];
+        if constexpr (kAcc) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) yq[q] = y_next[q];
+          if (c + 1 < c_end) load_y(y_next, m0, col0 + kOutCols);
+        }
         uint32_t v[32];
         tmem_ld32(taddr + a * kBN + c * kOutCols, v);
-        const int col0 = n0 + c * kOutCols;
         float bf[32];
         if (bias != nullptr) {
 #pragma unroll
@@ -654,6 +675,18 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) bf[i] = 0.f;
+        }
+        if constexpr (kAcc) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t ws[4] = {yq[q].x, yq[q].y, yq[q].z, yq[q].w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 f = Pack2<T>::unpack(ws[i]);
+              bf[q * 8 + 2 * i] += f.x;
+              bf[q * 8 + 2 * i + 1] += f.y;
+            }
+          }
         }
         uint32_t packed[16];
 #pragma unroll
@@ -723,10 +756,12 @@ struct LoraArgs {
 
 static int linear_impl(const char* fn, void* stream, int dtype, const void* x, int64_t ldx, const void* w,
                        int64_t ldw, const void* bias, void* y, int64_t ldy, int64_t m, int n, int k, int act,
-                       const LoraArgs* lora, int32_t* status) {
+                       const LoraArgs* lora, int32_t* status, bool accumulate = false) {
   if (dtype != LF_DTYPE_BF16 && dtype != LF_DTYPE_F16)
     return set_error(LF_ERR_UNSUPPORTED, "%s: dtype %d (bf16 or f16 only)", fn, dtype);
   if (act != LF_ACT_NONE && act != LF_ACT_GELU) return set_error(LF_ERR_INVALID, "%s: unknown act %d", fn, act);
+  if (accumulate && (act != LF_ACT_NONE || lora != nullptr))
+    return set_error(LF_ERR_INVALID, "%s: accumulation takes no activation and no LoRA", fn);
   if (m < 0 || m > INT32_MAX || n <= 0 || k <= 0 || n % kBN != 0 || k % kBK != 0)
     return set_error(LF_ERR_UNSUPPORTED, "%s: n %d must be a multiple of 256 and k %d of 64", fn, n, k);
   if (x == nullptr || w == nullptr || y == nullptr) return set_error(LF_ERR_INVALID, "%s: null x, w or y", fn);
@@ -855,12 +890,17 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
   p.n_kb = k / kBK;
   p.act = act;
   p.status = status;
+  p.y_in = accumulate ? y : nullptr;
+  p.ldy = ldy;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  auto kern = lora != nullptr ? (dtype == LF_DTYPE_BF16 ? linear_kernel<__nv_bfloat16, true> : linear_kernel<__half, true>)
-                              : (dtype == LF_DTYPE_BF16 ? linear_kernel<__nv_bfloat16, false> : linear_kernel<__half, false>);
+  const bool bf = dtype == LF_DTYPE_BF16;
+  const int mode = lora != nullptr ? 1 : accumulate ? 2 : 0;
+  auto kern = mode == 1   ? (bf ? linear_kernel<__nv_bfloat16, true, false> : linear_kernel<__half, true, false>)
+              : mode == 2 ? (bf ? linear_kernel<__nv_bfloat16, false, true> : linear_kernel<__half, false, true>)
+                          : (bf ? linear_kernel<__nv_bfloat16, false, false> : linear_kernel<__half, false, false>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(linear)");
   cudaLaunchAttribute attr[2];
@@ -871,10 +911,10 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   // as many pairs as can be resident at once (a GPC with an odd SM count leaves one idle)
-  static int resident_pairs[64][2] = {};
+  static int resident_pairs[64][3] = {};
   int pairs = sms / 2;
   if (dev >= 0 && dev < 64) {
-    int& resident = resident_pairs[dev][lora != nullptr];
+    int& resident = resident_pairs[dev][mode];
     if (resident == 0) {
       cudaLaunchConfig_t q = {};
       q.gridDim = dim3(unsigned(sms & ~1));
@@ -906,6 +946,13 @@ extern "C" int lf_linear(void* stream, int dtype, const void* x, int64_t ldx, co
                          const void* bias, void* y, int64_t ldy, int64_t m, int n, int k, int act,
                          int32_t* status) {
   return linear_impl("lf_linear", stream, dtype, x, ldx, w, ldw, bias, y, ldy, m, n, k, act, nullptr, status);
+}
+
+extern "C" int lf_linear_accumulate(void* stream, int dtype, const void* x, int64_t ldx, const void* w,
+                                    int64_t ldw, const void* bias, void* y, int64_t ldy, int64_t m, int n, int k,
+                                    int32_t* status) {
+  return linear_impl("lf_linear_accumulate", stream, dtype, x, ldx, w, ldw, bias, y, ldy, m, n, k, LF_ACT_NONE,
+                     nullptr, status, true);
 }
 
 extern "C" int lf_linear_lora(void* stream, int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,

@@ -105,3 +105,28 @@ def linear(x: Tensor, weight: Tensor, bias: Tensor | None, act: int = ACT_NONE,
                              w.stride(0), nat.ptr(b), o2.data_ptr(), o2.stride(0), x2.shape[0], N, K, int(act), None)
     nat.check(rc, "lf_linear")
     return out
+
+
+def linear_accumulate(x: Tensor, weight: Tensor, y: Tensor, bias: Tensor | None = None) -> Tensor:
+    """``y += x @ weight.T (+ bias)`` in place, summed in f32 and rounded once (cuBLAS's
+    ``addmm_`` with beta = 1) for bf16/f16 ``x (..., K)``, an ``nn.Linear`` weight
+    ``(N, K)`` and ``y (..., N)`` viewable as rows without a copy; N % 256 == 0,
+    K % 64 == 0.  Returns ``y``."""
+    dev = nat.require_cuda(x, weight, y, bias)
+    x2, ldx = _rows(x)
+    N, K = weight.shape
+    if x2.shape[1] != K:
+        raise ValueError(f"x has {x2.shape[1]} columns, weight expects {K}")
+    if y.dtype != x.dtype:
+        raise ValueError(f"y is {y.dtype}, x is {x.dtype}")
+    y2 = y.reshape(-1, N)
+    if y2.data_ptr() != y.data_ptr() or y2.stride(-1) != 1 or (y.dim() > 2 and not y.is_contiguous()) or \
+            y2.shape[0] != x2.shape[0]:
+        raise ValueError(f"y must be ({x2.shape[0]}, {N}) rows viewable without a copy")
+    w = weight if weight.stride(-1) == 1 else weight.contiguous()
+    b = None if bias is None else (bias if bias.dtype == x.dtype else bias.to(x.dtype)).contiguous()
+    rc = nat.lib().lf_linear_accumulate(nat.stream_ptr(dev), nat.dtype_code(x.dtype), x2.data_ptr(), ldx,
+                                        w.data_ptr(), w.stride(0), nat.ptr(b), y2.data_ptr(), y2.stride(0),
+                                        x2.shape[0], N, K, None)
+    nat.check(rc, "lf_linear_accumulate")
+    return y

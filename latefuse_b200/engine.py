@@ -33,7 +33,7 @@ from latefuse_b200.config import LoraServingConfig
 from latefuse_b200.head import LRHeadOps, head_forward, head_forward_rows, pool_tokens, validate_pooling
 from latefuse_b200.lora import (FactorCache, SegmentTable, blocked_u, fused_shrink_ok, linear_lora, lora_apply,
                                  lora_apply_into, lora_shrink_blocked, per_row_cache, workspace_bytes)
-from latefuse_b200.encoder_ops import ACT_GELU, add_layernorm, attention_varlen, gelu, linear
+from latefuse_b200.encoder_ops import ACT_GELU, add_layernorm, attention_varlen, gelu, linear, linear_accumulate
 from latefuse_b200.packing import PackedBatch, pack_rows
 
 # Per-layer module paths (relative to "encoder.layer.{i}.") for each logical target.
@@ -325,6 +325,13 @@ class EncoderWithLora(nn.Module):
         #: compute the shrink inside the projection GEMM's launch where the kernel can
         #: (``lf_linear_lora_shrink``); False runs ``lf_lora_shrink_blocked`` first
         self.fuse_shrink = True
+        #: bf16/f16 FFN down projection on this library's GEMM accumulating onto its
+        #: residual (``lf_linear_accumulate``) instead of torch's ``addmm_`` (cuBLAS,
+        #: beta = 1).  Off by default: at the bge-m3 serving shape (17,410 tokens x 1,024
+        #: x 4,096) cuBLAS's 240-token tiles fill the last wave that the 256-token CTA
+        #: pair leaves 73% full (98 vs 103-109 us alone), and the serving step measured
+        #: 0.45 ms faster with cuBLAS here.
+        self.native_ffn_down = False
         targets = serving_config.target_modules
         self._qkv_targets = [(m, _QKV.index(m)) for m in targets if m in _QKV]
         self._dense_target = "dense" in targets
@@ -502,9 +509,10 @@ class EncoderWithLora(nn.Module):
         """``h1 = LN1(ao + h)`` (``LN1(ao)`` when ``h`` is None: the residual is already
         in ``ao``), then ``LN2(W2 act(W1 h1) + b2 + h1)``, on the native add+LayerNorm and
         GELU kernels.  For bf16/f16 the up projection and its exact GELU run as one launch
-        of this library's tcgen05 GEMM (the GELU in its epilogue), the down-projection
-        GEMM accumulates onto ``h1`` in place (beta = 1; ``h1`` is not read again) and
-        LayerNorm adds ``b2``, so the residual is not read a second time."""
+        of this library's tcgen05 GEMM (the GELU in its epilogue), the down projection
+        accumulates onto ``h1`` in place (beta = 1: cuBLAS, or this library's GEMM when
+        ``native_ffn_down``; ``h1`` is not read again) and LayerNorm adds ``b2``, so the
+        residual is not read a second time."""
         h1 = add_layernorm(ao, h, layer.ln1.weight, layer.ln1.bias, self.eps)
         if self._native_gelu and self._gemm_ok(h1.dtype, layer.wi.shape):
             mid = linear(h1, layer.wi, layer.bi, act=ACT_GELU)
@@ -512,7 +520,10 @@ class EncoderWithLora(nn.Module):
             mid = F.linear(h1, layer.wi, layer.bi)
             mid = gelu(mid, out=mid) if self._native_gelu else self.act(mid)
         if h1.dtype in (torch.bfloat16, torch.float16):
-            h1.view(-1, h1.shape[-1]).addmm_(mid.view(-1, mid.shape[-1]), layer.wo2.t())
+            if self.native_ffn_down and self._gemm_ok(h1.dtype, layer.wo2.shape):
+                linear_accumulate(mid, layer.wo2, h1)
+            else:
+                h1.view(-1, h1.shape[-1]).addmm_(mid.view(-1, mid.shape[-1]), layer.wo2.t())
             return add_layernorm(h1, None, layer.ln2.weight, layer.ln2.bias, self.eps, out=h1, vec=layer.bo2)
         o = F.linear(mid, layer.wo2, layer.bo2)
         return add_layernorm(o, h1, layer.ln2.weight, layer.ln2.bias, self.eps, out=o)

@@ -52,7 +52,8 @@ def check(out, ref):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_ragged_lengths(cuda, dtype):
-    lengths = [1, 7, 128, 129, 300, 512, 64, 33, 255, 256, 257]
+    # last tiles of 1..128 rows: every 32-row warp and 64-key half boundary, either side
+    lengths = [1, 7, 128, 129, 300, 512, 64, 33, 255, 256, 257, 65, 96, 97, 160, 161, 192, 193, 224, 225, 31, 32]
     out, ref, _, _ = run_case(cuda, lengths, 16, dtype, seed=1)
     check(out, ref)
 

@@ -58,7 +58,9 @@ def test_bge_m3_shape_packed_serving_matches_oracle(cuda):
     for fused in (True, False):
         # the benchmark's path: the shrink inside the projection GEMM's launch; and the
         # shrink as its own launch before the GEMM with the delta in its accumulator
+        # (that run also takes the FFN down projection on this library's GEMM)
         model.fuse_shrink = fused
+        model.native_ffn_down = not fused
         model.lora_events = []
         outs[fused] = emb.embed_tokens(ids, mask, tenants)
         kinds = {k for k, _, _ in model.lora_events}
@@ -66,7 +68,7 @@ def test_bge_m3_shape_packed_serving_matches_oracle(cuda):
         emb.check_device_status()
         want = {"qkv_gemm", "dense_gemm"} | (set() if fused else {"qkv_shrink", "dense_shrink"})
         assert kinds == want, kinds
-    model.fuse_shrink = True
+    model.fuse_shrink, model.native_ffn_down = True, False
 
     oracle = HookedEncoder(base, adapters_of(store, tenants), cfg.target_modules)
     ref = F.normalize(oracle.encode_pooled(ids.to(cuda), mask.to(cuda), tenants, "cls").float(), dim=-1)

@@ -14,7 +14,7 @@ import torch
 import torch.nn.functional as F
 
 from latefuse_b200 import _native as nat
-from latefuse_b200.encoder_ops import ACT_GELU, linear
+from latefuse_b200.encoder_ops import ACT_GELU, linear, linear_accumulate
 
 pytestmark = pytest.mark.gpu
 
@@ -50,6 +50,38 @@ def test_linear_gelu_matches_torch(cuda, dtype):
     # the fused GELU is exactly the formula applied to the kernel's own projection
     xf = linear(x, w, b).float()
     assert torch.equal(ours, (xf * 0.5 * (1.0 + torch.erf(xf * 0.70710678118654752440))).to(dtype))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m,n,k", [(16401, 1024, 4096), (300, 1024, 1024), (1, 256, 64), (129, 512, 192)])
+def test_linear_accumulate_matches_f32(cuda, dtype, m, n, k):
+    """y += x W^T (+ b) in place, rounded once: against the f32 sum and torch's addmm_
+    (beta = 1), with y a strided view whose other rows and columns stay untouched."""
+    g = torch.Generator(device="cpu").manual_seed(m * 7 + n + k)
+    x = torch.randn(m, k, generator=g).to(dtype).to(cuda)
+    w = (torch.randn(n, k, generator=g) * k ** -0.5).to(dtype).to(cuda)
+    b = torch.randn(n, generator=g).to(dtype).to(cuda)
+    big = torch.randn(m + 3, n + 256, generator=g).to(dtype).to(cuda)
+    before = big.clone()
+    y = big[:m, :n]
+    y0 = y.clone()
+    assert linear_accumulate(x, w, y, b) is y
+    close(y, y0.float() + x.float() @ w.float().T + b.float())
+    assert torch.equal(big[m:], before[m:]) and torch.equal(big[:, n:], before[:, n:])
+    y.copy_(y0)
+    linear_accumulate(x, w, y)
+    close(y, y0.clone().addmm_(x, w.t()))
+
+
+def test_linear_accumulate_rejections(cuda):
+    x = torch.randn(64, 1024, device=cuda, dtype=torch.bfloat16)
+    w = torch.randn(1024, 1024, device=cuda, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="rows"):
+        linear_accumulate(x, w, torch.zeros(63, 1024, device=cuda, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="float16"):
+        linear_accumulate(x, w, torch.zeros(64, 1024, device=cuda, dtype=torch.float16))
+    with pytest.raises(nat.NativeLibraryError, match="multiple of 256"):
+        linear_accumulate(x, w[:1000], torch.zeros(64, 1000, device=cuda, dtype=torch.bfloat16))
 
 
 def test_linear_strided_rows_and_rejections(cuda):
