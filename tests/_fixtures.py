@@ -59,9 +59,11 @@ def texts(n: int) -> list[str]:
 def hf_model(kind: str, conf: dict, dev, dtype, seed: int = 0):
     """A HuggingFace encoder with N(0, 0.02) weights, zero biases and unit LayerNorms,
     drawn on ``dev`` from ``seed`` (the models' own initialisation, without the CPU pass)."""
-    from transformers import BertConfig, BertModel, XLMRobertaConfig, XLMRobertaModel
+    from transformers import (BertConfig, BertModel, XLMRobertaConfig, XLMRobertaModel, XLMRobertaXLConfig,
+                              XLMRobertaXLModel)
 
-    cfg_cls, model_cls = (BertConfig, BertModel) if kind == "bert" else (XLMRobertaConfig, XLMRobertaModel)
+    cfg_cls, model_cls = {"bert": (BertConfig, BertModel), "xlmr": (XLMRobertaConfig, XLMRobertaModel),
+                          "xlmr-xl": (XLMRobertaXLConfig, XLMRobertaXLModel)}[kind]
     hf = cfg_cls(**conf)
     with torch.device("meta"):
         model = model_cls(hf)
@@ -69,7 +71,7 @@ def hf_model(kind: str, conf: dict, dev, dtype, seed: int = 0):
     g = torch.Generator(device=dev).manual_seed(seed)
     with torch.no_grad():
         for name, p in model.named_parameters():
-            if "LayerNorm.weight" in name:
+            if "LayerNorm.weight" in name or "layer_norm.weight" in name:
                 p.fill_(1.0)
             elif name.endswith("bias"):
                 p.zero_()

@@ -83,6 +83,35 @@ def test_bge_m3_shape_packed_serving_matches_oracle(cuda):
         assert row_rel(base_only, ref) > 2 * err
 
 
+XLMR_XL = dict(vocab_size=250002, hidden_size=2560, num_attention_heads=32, intermediate_size=10240,
+               max_position_embeddings=514, pad_token_id=1, type_vocab_size=1, layer_norm_eps=1e-5)
+
+
+def test_xlmr_xl_shape_matches_oracle(cuda):
+    """The XLM-R-XL scale-out shape (pre-LayerNorm layers, hidden 2560, 32 heads of 80,
+    FFN 10240; 2 of its 36 layers) with rank 32 on query+value over 600 resident slots,
+    full-length 256-token rows, through the public API (stock HF encoder, this library's
+    kernels in its hooks), against the reference's per-row bmm hooks."""
+    base, hf = hf_model("xlmr-xl", dict(XLMR_XL, num_hidden_layers=2), cuda, torch.bfloat16)
+    cfg = serving_config(hf, cuda, torch.bfloat16, 32, ["query", "value"], 48, 256)
+    model = lf.HFEncoderWithLora(base, cfg)
+    store = lf.AdapterStore(cfg, capacity=600)
+    store.fill_random_(600, std=0.02, generator=torch.Generator(device=cuda).manual_seed(4))
+    emb = lf.MultiTenantEmbedder(cfg, engine="hf", model=model, store=store, tokenizer=False)
+    ids, mask = ragged_batch(48, 256, min_len=256, max_len=256, vocab=250002, pad_id=1, cls_id=0, low_id=5, seed=4)
+    tenants = [f"adapter_{int(t)}" for t in zipf_tenants(600, 48, alpha=1.1, seed=4)]
+    ours = emb.embed_tokens(ids, mask, tenants).float()
+    emb.check_device_status()
+    oracle = HookedEncoder(base, adapters_of(store, tenants), cfg.target_modules)
+    ref = F.normalize(oracle.encode_pooled(ids.to(cuda), mask.to(cuda), tenants, "cls").float(), dim=-1)
+    base_only = F.normalize(oracle.encode_pooled(ids.to(cuda), mask.to(cuda), tenants, "cls", apply_lora=False)
+                            .float(), dim=-1)
+    oracle.close()
+    err = row_rel(ours, ref)
+    assert err < 2e-2, err
+    assert row_rel(base_only, ref) > 2 * err
+
+
 @pytest.mark.parametrize("engine", ["hf", "bert"])
 def test_bert_base_f32_matches_oracle(cuda, engine):
     base, hf = hf_model("bert", BERT_BASE, cuda, torch.float32)
