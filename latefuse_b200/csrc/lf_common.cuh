@@ -77,6 +77,76 @@ __device__ __forceinline__ float round_through(float v) { return DT<T>::to_f(DT<
 // and the GEMM epilogue share this one definition, so their results agree).
 __device__ __forceinline__ float gelu_f32(float v) { return v * 0.5f * (1.0f + erff(v * 0.70710678118654752440f)); }
 
+// Two lanes of f32 arithmetic in one paired instruction, each lane rounded as its
+// scalar form (fma / add / mul .rn.f32x2).
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 pa, pb, pc, pd;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+      "mov.b64 pc, {%6, %7};\n\tfma.rn.f32x2 pd, pa, pb, pc;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 pa, pb, pd;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+      "add.rn.f32x2 pd, pa, pb;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 pa, pb, pd;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+      "mul.rn.f32x2 pd, pa, pb;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 f2(float s) { return make_float2(s, s); }
+
+// The SFU's approximate reciprocal and base-2 exponential (denormal results flush to 0).
+__device__ __forceinline__ float sfu_rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float sfu_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// gelu_f32 for two values at once at a fraction of erff's instruction count, for the
+// GEMM epilogue, where the GELU's issue slots set the FFN-up projection's time.  erf
+// comes from erfc by the Chebyshev fit of Press et al., Numerical Recipes in C (2nd
+// ed., section 6.2, `erfcc`: fractional error below 1.2e-7 for every argument),
+//     erfc(z) = t exp(-z^2 + P(t)),  t = 1 / (1 + z / 2),
+// with the reciprocal and the exponential on the SFU and P (degree 9) on paired f32x2
+// FMAs.  1 + erf is formed as the formula forms it, from erf rounded to f32, so for
+// negative v the cancellation matches the erff form's; the results agree with gelu_f32
+// to one bf16 ulp (and bit for bit on nearly every input: the GEMM's tests count).
+__device__ __forceinline__ float2 gelu2_fast(float2 v) {
+  const float2 z = f2_mul(make_float2(fabsf(v.x), fabsf(v.y)), f2(0.70710678118654752440f));
+  const float2 d = f2_fma(z, f2(0.5f), f2(1.0f));
+  const float2 t = make_float2(sfu_rcp(d.x), sfu_rcp(d.y));
+  float2 p = f2_fma(t, f2(0.17087277f), f2(-0.82215223f));
+  p = f2_fma(p, t, f2(1.48851587f));
+  p = f2_fma(p, t, f2(-1.13520398f));
+  p = f2_fma(p, t, f2(0.27886807f));
+  p = f2_fma(p, t, f2(-0.18628806f));
+  p = f2_fma(p, t, f2(0.09678418f));
+  p = f2_fma(p, t, f2(0.37409196f));
+  p = f2_fma(p, t, f2(1.00002368f));
+  p = f2_fma(p, t, f2(-1.26551223f));
+  const float2 arg = f2_fma(make_float2(-z.x, -z.y), z, p);        // -z^2 + P(t)
+  const float2 l = f2_mul(arg, f2(1.44269504088896340736f));        // to base 2
+  const float2 erfc = f2_mul(t, make_float2(sfu_ex2(l.x), sfu_ex2(l.y)));
+  float2 e = f2_add(f2(1.0f), make_float2(-erfc.x, -erfc.y));        // erf(|z|)
+  e = make_float2(copysignf(e.x, v.x), copysignf(e.y, v.y));         // erf(v / sqrt 2)
+  return f2_mul(f2_mul(v, f2(0.5f)), f2_add(f2(1.0f), e));
+}
+
 // ---------------------------------------------------------------------------
 // misc
 // ---------------------------------------------------------------------------

@@ -86,6 +86,7 @@ struct alignas(64) LinearParams {
   int32_t shrink;                     // 1: u is computed in this launch
   int32_t s_epc;                      // shrink: segments per CTA per pass (n_mod * R * s_epc <= 128)
   int32_t n_rb;                       // 256-row blocks
+  int64_t tiles_per_pair;             // shrink: each pair's contiguous range of tiles
   int32_t n_segs;
   int32_t n_blk;                      // LoRA: u blocks per module (128-row tiles + segments)
   int32_t rank;
@@ -180,19 +181,24 @@ __device__ __forceinline__ bool aborted_flag(const int32_t* f) {
 
 // One work item of a CTA pair: a 256 x 256 output tile (rb, c), or shrink pass `pass`
 // of row block rb.  Every role walks the same sequence: round robin over all tiles
-// without the shrink; with it, whole row blocks (pair, pair + n_pairs, ...), each as
-// its shrink passes followed by its column tiles.
+// without the shrink; with it, a contiguous range of tiles in row-block order
+// (p.tiles_per_pair of them), each row block the range touches preceded by its shrink
+// passes.  A range that shares a row block with its neighbour computes that block's u
+// too: both write identical values, and each pair reads only after its own writes.
 struct Item {
   int32_t rb, c, pass;
   bool shrink;
+  bool first;  // the first tile after its row block's shrink passes
 };
 
 template <bool kShrinkable>
 struct Sched {
-  int64_t t;       // next tile (round robin)
-  int32_t rb, c;   // current block and next column tile (row blocks)
+  int64_t t;       // next tile
+  int64_t t_end;   // shrink: end of this pair's range
+  int32_t rb;      // shrink: the row block whose passes were emitted last (-1: none)
   int32_t pass, n_pass;
   int32_t n_pairs;
+  bool fresh;      // shrink: the next tile is the first after its block's passes
 
   __device__ __forceinline__ static int32_t passes(const LinearParams& p, int32_t rb) {
     const int2 qr = pair_range(p.tile_pairs, rb, p.n_segs);
@@ -200,31 +206,35 @@ struct Sched {
     return (qr.y - qr.x + per - 1) / per;
   }
   __device__ __forceinline__ Sched(const LinearParams& p, int pair, int n_pairs_)
-      : t(pair), rb(pair), c(0), pass(0), n_pass(0), n_pairs(n_pairs_) {
-    if (kShrinkable && p.shrink && rb < p.n_rb) n_pass = passes(p, rb);
+      : t(pair), t_end(0), rb(-1), pass(0), n_pass(0), n_pairs(n_pairs_), fresh(false) {
+    if (kShrinkable && p.shrink) {
+      t = int64_t(pair) * p.tiles_per_pair;
+      t_end = t + p.tiles_per_pair < p.n_tiles ? t + p.tiles_per_pair : p.n_tiles;
+    }
   }
   __device__ __forceinline__ bool next(const LinearParams& p, Item& it) {
     if (!kShrinkable || !p.shrink) {
       if (t >= p.n_tiles) return false;
-      it = Item{int32_t(t / p.n_tiles_n), int32_t(t % p.n_tiles_n), 0, false};
+      it = Item{int32_t(t / p.n_tiles_n), int32_t(t % p.n_tiles_n), 0, false, false};
       t += n_pairs;
       return true;
     }
-    while (rb < p.n_rb) {
-      if (pass < n_pass) {
-        it = Item{rb, 0, pass++, true};
-        return true;
-      }
-      if (c < p.n_tiles_n) {
-        it = Item{rb, c++, 0, false};
-        return true;
-      }
-      rb += n_pairs;
-      c = 0;
+    if (t >= t_end) return false;
+    const int32_t trb = int32_t(t / p.n_tiles_n);
+    if (trb != rb) {  // entering a row block: its shrink passes first
+      rb = trb;
       pass = 0;
-      n_pass = rb < p.n_rb ? passes(p, rb) : 0;
+      n_pass = passes(p, rb);
+      fresh = true;
     }
-    return false;
+    if (pass < n_pass) {
+      it = Item{rb, 0, pass++, true, false};
+      return true;
+    }
+    it = Item{trb, int32_t(t % p.n_tiles_n), 0, false, fresh};
+    fresh = false;
+    ++t;
+    return true;
   }
 };
 
@@ -234,8 +244,9 @@ __device__ __forceinline__ uint32_t a_box_layout(int R) { return R == 16 ? 6u : 
 
 // kLora: the LoRA delta blocks (and the shrink passes when p.shrink) are compiled in;
 // the plain projection GEMM is its own instantiation without them.  kAcc: the epilogue
-// adds y's current values (y += x W^T + bias, rounded once).
-template <typename T, bool kLora, bool kAcc>
+// adds y's current values (y += x W^T + bias, rounded once).  kAct: the activation
+// (LF_ACT_NONE / LF_ACT_GELU), or -1 to read p.act at run time.
+template <typename T, bool kLora, bool kAcc, int kAct>
 __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_constant__ LinearParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -297,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
   // a tile's first delta block goes to its own buffer, loaded while the tile's K
   // blocks stream, so it has landed when the MMA reaches it (later ones use the ring)
   const bool dbuf = lora && 512 * p.rank <= kDeltaBuf;
-  auto dbuf_tile = [&](const Item& it) { return !(kLora && p.shrink && it.c == 0); };
+  auto dbuf_tile = [&](const Item& it) { return !(kLora && p.shrink && it.first); };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
@@ -330,6 +341,18 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
         if (rank == 0) mbar_arrive_expect_tx(bar(FULL + s), bytes);
         return true;
       };
+      // u written in this launch must be there before its blocks are staged: one phase of
+      // U_READY per row block with shrink passes, waited before that block's first delta
+      // copy, or before the next block's passes when the range had no delta for it, so no
+      // more than one phase is ever pending
+      auto wait_u = [&]() {
+        for (; u_wait > 0; --u_wait, u_ph ^= 1)
+          if (aborted_flag(s_abort) || !mbar_wait(bar(U_READY), u_ph)) {
+            if (!aborted_flag(s_abort)) fail();
+            return false;
+          }
+        return true;
+      };
       // `ahead` walks the same items as `sched`, one output tile in front of it
       Sched<kLora> sched(p, pair, n_pairs), ahead(p, pair, n_pairs);
       Item it, nx;
@@ -345,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
         if (lora) {
           bool bad = false;
           const int2 qr = pair_range(p.tile_pairs, it.rb, p.n_segs, &bad);
-          if (bad && rank == 0 && (it.shrink || it.c == 0)) set_status(p.status, LF_STATUS_BAD_SEGMENT);
+          if (bad && rank == 0) set_status(p.status, LF_STATUS_BAD_SEGMENT);
           q0 = qr.x;
           q1 = qr.y;
         }
@@ -357,6 +380,10 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
           const int32_t ne_p = min(2 * p.s_epc, q1 - q0 - e0);
           const int32_t ne_h = (ne_p + 1) / 2;
           const uint32_t box = uint32_t(p.n_mod) * 128u * uint32_t(p.rank);  // one segment's modules
+          if (it.pass == 0 && !wait_u()) {
+            stop = true;
+            break;
+          }
           for (int kb = 0; kb < p.n_kb; ++kb, ++kk) {
             uint32_t st, full;
             if (!take(2 * (kABytes + ne_h * box), st, full)) {
@@ -370,9 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
               tma_load_4d_pair(st + kABytes + i * box, &p.a_map, full, 0, kb * kBK, 0, slot);
             }
           }
-          // the block's tiles wait for the epilogue to have written u: one phase of U_READY
-          // per block (after its last pass), so the producer never trails it by two phases
-          u_wait = 1;
+          u_wait = 1;  // the epilogue arrives once per block, after its last pass
           continue;
         }
         const int32_t n0 = it.c * kBN;
@@ -397,15 +422,6 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
           if (rank == 0) mbar_arrive_expect_tx(full_local, 2 * 512 * p.rank);  // u 128 x R + B R x 128, twice
           tma_load_3d_pair(dst_u, &p.u_map, full, 0, 0, blk);
           tma_load_4d_pair(dst_b, &p.b_map[mod], full, 0, 0, (n_loc + half_cols) / 64, slot);
-        };
-        // u written in this launch must be there before its blocks are staged
-        auto wait_u = [&]() {
-          for (; u_wait > 0; --u_wait, u_ph ^= 1)  // at most one phase pending
-            if (aborted_flag(s_abort) || !mbar_wait(bar(U_READY), u_ph)) {
-              if (!aborted_flag(s_abort)) fail();
-              return false;
-            }
-          return true;
         };
         // the first block is loaded once the MMA has started this tile (by then the
         // previous tile's first block has been multiplied); not for a block's first tile
@@ -689,15 +705,18 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
           }
         }
         uint32_t packed[16];
+        if (kAct == LF_ACT_GELU || (kAct < 0 && p.act == LF_ACT_GELU)) {  // warp-uniform
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float y0 = __uint_as_float(v[2 * i]) + bf[2 * i];
-          float y1 = __uint_as_float(v[2 * i + 1]) + bf[2 * i + 1];
-          if (p.act == LF_ACT_GELU) {
-            y0 = gelu_f32(round_through<T>(y0));
-            y1 = gelu_f32(round_through<T>(y1));
+          for (int i = 0; i < 16; ++i) {
+            const float2 y = f2_add(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])),
+                                    make_float2(bf[2 * i], bf[2 * i + 1]));
+            const float2 g = gelu2_fast(make_float2(round_through<T>(y.x), round_through<T>(y.y)));
+            packed[i] = Pack2<T>::pack(g.x, g.y);
           }
-          packed[i] = Pack2<T>::pack(y0, y1);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            packed[i] = Pack2<T>::pack(__uint_as_float(v[2 * i]) + bf[2 * i], __uint_as_float(v[2 * i + 1]) + bf[2 * i + 1]);
         }
         // the store that last read this staging tile must be done with it
         if (lane == 0) tma_store_wait_read_all();
@@ -898,9 +917,14 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool bf = dtype == LF_DTYPE_BF16;
   const int mode = lora != nullptr ? 1 : accumulate ? 2 : 0;
-  auto kern = mode == 1   ? (bf ? linear_kernel<__nv_bfloat16, true, false> : linear_kernel<__half, true, false>)
-              : mode == 2 ? (bf ? linear_kernel<__nv_bfloat16, false, true> : linear_kernel<__half, false, true>)
-                          : (bf ? linear_kernel<__nv_bfloat16, false, false> : linear_kernel<__half, false, false>);
+  const bool gelu = act == LF_ACT_GELU;
+  auto kern = mode == 1   ? (bf ? linear_kernel<__nv_bfloat16, true, false, -1> : linear_kernel<__half, true, false, -1>)
+              : mode == 2 ? (bf ? linear_kernel<__nv_bfloat16, false, true, LF_ACT_NONE>
+                                : linear_kernel<__half, false, true, LF_ACT_NONE>)
+              : gelu      ? (bf ? linear_kernel<__nv_bfloat16, false, false, LF_ACT_GELU>
+                                : linear_kernel<__half, false, false, LF_ACT_GELU>)
+                          : (bf ? linear_kernel<__nv_bfloat16, false, false, LF_ACT_NONE>
+                                : linear_kernel<__half, false, false, LF_ACT_NONE>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(linear)");
   cudaLaunchAttribute attr[2];
@@ -911,10 +935,10 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   // as many pairs as can be resident at once (a GPC with an odd SM count leaves one idle)
-  static int resident_pairs[64][3] = {};
+  static int resident_pairs[64][4] = {};
   int pairs = sms / 2;
   if (dev >= 0 && dev < 64) {
-    int& resident = resident_pairs[dev][mode];
+    int& resident = resident_pairs[dev][mode == 0 && gelu ? 3 : mode];
     if (resident == 0) {
       cudaLaunchConfig_t q = {};
       q.gridDim = dim3(unsigned(sms & ~1));
@@ -928,7 +952,10 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
     pairs = resident < sms / 2 ? resident : sms / 2;
   }
   if (p.n_tiles < pairs) pairs = int(p.n_tiles);
-  if (p.shrink && p.n_rb < pairs) pairs = p.n_rb;  // a pair owns whole row blocks
+  if (p.shrink) {  // each pair takes a contiguous range of tiles (and its blocks' shrink passes)
+    p.tiles_per_pair = (p.n_tiles + pairs - 1) / pairs;
+    pairs = int((p.n_tiles + p.tiles_per_pair - 1) / p.tiles_per_pair);
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(2 * pairs));
   cfg.blockDim = dim3(kThreads);

@@ -252,11 +252,14 @@ def _u_rows(u, st, n_mod, R):
     return out
 
 
-@pytest.mark.parametrize("R,n_mod,max_len", [(16, 3, 400), (16, 3, 40), (32, 3, 300), (64, 1, 300), (16, 1, 25)])
+@pytest.mark.parametrize("R,n_mod,max_len", [(16, 3, 400), (16, 3, 40), (32, 3, 300), (64, 1, 300), (16, 1, 25),
+                                             (16, 3, 2000), (16, 1, 3000)])
 def test_shrink_in_the_gemm_launch_matches_the_two_launches(cuda, R, n_mod, max_len):
     """``lf_linear_lora_shrink`` computes u in the GEMM's own launch: its u blocks and its
     output against ``lf_lora_shrink_blocked`` + ``lf_linear_lora`` on the same inputs.
-    Short segments put many segments in one 256-token block (several shrink passes)."""
+    Short segments put many segments in one 256-token block (several shrink passes);
+    the small batches give several CTA pairs each part of one row block (each computes
+    that block's u), the long ones give pairs ranges that cross row blocks."""
     dtype, H, n_slots = torch.bfloat16, 1024 if n_mod == 1 else 512, 37
     dev = torch.device("cuda")
     starts, lengths, slots, T = packed_segments(30 if max_len > 100 else 80, n_slots, seed=R + max_len,
