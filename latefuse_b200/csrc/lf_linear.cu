@@ -175,6 +175,22 @@ __device__ __forceinline__ int2 pair_range(const int32_t* tile_pairs, int q, int
   return ok ? make_int2(q0, q1) : make_int2(0, 0);
 }
 
+// A tile's pair-table range loaded ahead of its use: the loads are issued one work item
+// early and checked (as pair_range does) only when the item starts, so their latency
+// overlaps the previous item instead of stalling the thread that issues copies or MMAs.
+struct RangeAhead {
+  int32_t q0, q1;
+  __device__ __forceinline__ void load(const int32_t* tile_pairs, int q) {
+    q0 = __ldg(tile_pairs + q);
+    q1 = __ldg(tile_pairs + q + 1);
+  }
+  __device__ __forceinline__ int2 get(int n_segs, bool* bad = nullptr) const {
+    const bool ok = q0 >= 0 && q1 >= q0 && q1 - q0 <= n_segs;
+    if (bad != nullptr) *bad = !ok;
+    return ok ? make_int2(q0, q1) : make_int2(0, 0);
+  }
+};
+
 __device__ __forceinline__ bool aborted_flag(const int32_t* f) {
   return *reinterpret_cast<const volatile int32_t*>(f) != 0;
 }
@@ -245,7 +261,7 @@ __device__ __forceinline__ uint32_t a_box_layout(int R) { return R == 16 ? 6u : 
 // kLora: the LoRA delta blocks (and the shrink passes when p.shrink) are compiled in;
 // the plain projection GEMM is its own instantiation without them.  kAcc: the epilogue
 // adds y's current values (y += x W^T + bias, rounded once).  kAct: the activation
-// (LF_ACT_NONE / LF_ACT_GELU), or -1 to read p.act at run time.
+// (LF_ACT_NONE / LF_ACT_GELU).
 template <typename T, bool kLora, bool kAcc, int kAct>
 __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_constant__ LinearParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -316,19 +332,6 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
       int kk = 0, dk = 0, u_wait = 0, u_ph = 0;
       bool stop = false;
       const int32_t half_cols = int32_t(rank) * (kBN / 2);
-      // this CTA's half of the B factors of a tile's segments, into L2
-      auto prefetch_b = [&](int32_t trb, int32_t tc) {
-        if (!lora || trb < 0) return;
-        const int pmod = tc * kBN / p.module_cols;
-        if (pmod >= p.n_mod) return;
-        const int2 qr = pair_range(p.tile_pairs, trb, p.n_segs);
-        for (int q = qr.x; q < qr.y; ++q) {
-          const int32_t slot = __ldg(p.pairs + 3 * q + 1);
-          if (slot >= 0 && slot < p.n_slots)
-            prefetch_l2(static_cast<const T*>(p.b_ptr[pmod]) + int64_t(slot) * p.b_slot_stride,
-                        uint32_t(p.rank) * uint32_t(p.module_cols) * 2u);
-        }
-      };
       // the stage of K block kb is free: arm it (leader) and return its address
       auto take = [&](uint32_t bytes, uint32_t& st, uint32_t& full) {
         const int s = kk % kStages;
@@ -353,21 +356,21 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
           }
         return true;
       };
-      // `ahead` walks the same items as `sched`, one output tile in front of it
-      Sched<kLora> sched(p, pair, n_pairs), ahead(p, pair, n_pairs);
-      Item it, nx;
-      auto next_tile = [&](Item& x) {
-        while (ahead.next(p, x))
-          if (!x.shrink) return true;
-        return false;
-      };
-      if (next_tile(nx)) prefetch_b(nx.rb, nx.c);
-      while (!stop && sched.next(p, it)) {
+      Sched<kLora> sched(p, pair, n_pairs);
+      Item it, nit;
+      bool more = sched.next(p, nit);
+      RangeAhead ahead_r{0, 0};
+      if (lora && more) ahead_r.load(p.tile_pairs, nit.rb);
+      while (!stop && more) {
+        it = nit;
+        const RangeAhead cur_r = ahead_r;
+        more = sched.next(p, nit);
+        if (lora && more) ahead_r.load(p.tile_pairs, nit.rb);  // in flight while this item runs
         const int32_t m0 = it.rb * (2 * kBM) + int32_t(rank) * kBM;
         int q0 = 0, q1 = 0;
         if (lora) {
           bool bad = false;
-          const int2 qr = pair_range(p.tile_pairs, it.rb, p.n_segs, &bad);
+          const int2 qr = cur_r.get(p.n_segs, &bad);
           if (bad && rank == 0) set_status(p.status, LF_STATUS_BAD_SEGMENT);
           q0 = qr.x;
           q1 = qr.y;
@@ -407,10 +410,15 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
         const int32_t zero_blk = p.n_mod * p.n_blk;  // past the last block: the copy reads zeros
         // delta block q: this CTA's 128 rows of u (its block of (128-row tile, segment), or
         // zeros) and its 128 columns of the segment's B, completing on the leader's `full`
-        auto load_delta = [&](uint32_t dst_u, uint32_t dst_b, uint32_t full_local, int q) {
-          int j = __ldg(p.pairs + 3 * q);
-          const int32_t slot = __ldg(p.pairs + 3 * q + 1);  // out of range: zero fill, no delta, reported
-          const int32_t mask = __ldg(p.pairs + 3 * q + 2);
+        // entry q's {segment, slot, halves}, loaded ahead where the caller can
+        struct Entry { int32_t j, slot, mask; };
+        auto entry = [&](int q) {
+          return Entry{__ldg(p.pairs + 3 * q), __ldg(p.pairs + 3 * q + 1), __ldg(p.pairs + 3 * q + 2)};
+        };
+        auto load_delta = [&](uint32_t dst_u, uint32_t dst_b, uint32_t full_local, Entry e) {
+          int j = e.j;
+          const int32_t slot = e.slot;  // out of range: zero fill, no delta, reported
+          const int32_t mask = e.mask;
           if (j < 0 || j >= p.n_segs) {  // a segment outside the table: treated as absent, reported
             if (rank == 0) set_status(p.status, LF_STATUS_BAD_SEGMENT);
             j = -1;
@@ -428,6 +436,10 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
         // when this launch writes u (its delta blocks wait for the shrink's epilogue)
         const bool use_dbuf = dbuf && q1 > q0 && dbuf_tile(it);
         const int d_after = (p.n_kb < kStages ? p.n_kb : kStages) - 1;
+        // the tile's first two delta entries, in flight while its K blocks stream
+        Entry e_first{0, 0, 0}, e_second{0, 0, 0};
+        if (q1 > q0) e_first = entry(q0);
+        if (q1 > q0 + 1) e_second = entry(q0 + 1);
         for (int kb = 0; kb < p.n_kb; ++kb, ++kk) {
           uint32_t st, full;
           if (!take(2 * kStageBytes, st, full)) {
@@ -443,12 +455,11 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
               ++kk;
               break;
             }
-            load_delta(s_delta, s_delta + 256 * p.rank, bar(DFULL), q0);
+            load_delta(s_delta, s_delta + 256 * p.rank, bar(DFULL), e_first);
             ++dk;
           }
         }
         if (use_dbuf) ++q0;
-        if (!stop && next_tile(nx)) prefetch_b(nx.rb, nx.c);  // the ring is full here: the producer has time
         if (stop || q1 <= q0) continue;
         if (!wait_u()) {
           stop = true;
@@ -462,7 +473,9 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
             break;
           }
           const uint32_t st = s_stage0 + s * kStageBytes;
-          load_delta(st, st + kABytes, bar(FULL + s), q);
+          const int q_first = use_dbuf ? q0 - 1 : q0;  // the tile's first entry
+          load_delta(st, st + kABytes, bar(FULL + s),
+                     q == q_first ? e_first : q == q_first + 1 ? e_second : entry(q));
         }
       }
       if (aborted_flag(s_abort)) {  // loads nobody consumed land before the CTA exits (bounded)
@@ -487,12 +500,19 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
         return false;
       };
       Sched<kLora> sched(p, pair, n_pairs);
-      Item it;
-      for (; !stop && sched.next(p, it); ++n_it) {
+      Item it, nit;
+      bool more = sched.next(p, nit);
+      RangeAhead ahead_r{0, 0};
+      if (lora && more) ahead_r.load(p.tile_pairs, nit.rb);
+      for (; !stop && more; ++n_it) {
+        it = nit;
+        const RangeAhead cur_r = ahead_r;
+        more = sched.next(p, nit);
+        if (lora && more) ahead_r.load(p.tile_pairs, nit.rb);  // in flight while this item runs
         const int a = n_it & 1;
         int n_delta = 0, ne_p = 0;
         if (lora) {
-          const int2 qr = pair_range(p.tile_pairs, it.rb, p.n_segs);
+          const int2 qr = cur_r.get(p.n_segs);
           if (it.shrink) {
             ne_p = min(2 * p.s_epc, qr.y - qr.x - it.pass * 2 * p.s_epc);
           } else if (it.c * kBN / p.module_cols < p.n_mod) {
@@ -629,6 +649,27 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
       }
       asm volatile("fence.proxy.async.global;" ::: "memory");
     };
+    // LoRA: the B factors of every delta block this pair will stage, prefetched into L2
+    // once at the start by the epilogue warps (idle until the first accumulator is
+    // ready), each warp taking every kEpiWarps-th tile of the pair's sequence, so the
+    // copy-issuing thread never waits on the table reads behind these addresses
+    if (kLora && lane == 0) {
+      Sched<kLora> walk(p, pair, n_pairs);
+      Item w;
+      for (int i = 0; walk.next(p, w);) {
+        if (w.shrink) continue;
+        if (i++ % kEpiWarps != warp - 2) continue;
+        const int pmod = w.c * kBN / p.module_cols;
+        if (pmod >= p.n_mod) continue;
+        const int2 qr = pair_range(p.tile_pairs, w.rb, p.n_segs);
+        for (int q = qr.x; q < qr.y; ++q) {
+          const int32_t slot = __ldg(p.pairs + 3 * q + 1);
+          if (slot >= 0 && slot < p.n_slots)
+            prefetch_l2(static_cast<const T*>(p.b_ptr[pmod]) + int64_t(slot) * p.b_slot_stride,
+                        uint32_t(p.rank) * uint32_t(p.module_cols) * 2u);
+        }
+      }
+    }
     const T* bias = static_cast<const T*>(p.bias);
     Sched<kLora> sched(p, pair, n_pairs);
     Item item;
@@ -705,7 +746,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
           }
         }
         uint32_t packed[16];
-        if (kAct == LF_ACT_GELU || (kAct < 0 && p.act == LF_ACT_GELU)) {  // warp-uniform
+        if constexpr (kAct == LF_ACT_GELU) {
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const float2 y = f2_add(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])),
@@ -918,7 +959,10 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
   const bool bf = dtype == LF_DTYPE_BF16;
   const int mode = lora != nullptr ? 1 : accumulate ? 2 : 0;
   const bool gelu = act == LF_ACT_GELU;
-  auto kern = mode == 1   ? (bf ? linear_kernel<__nv_bfloat16, true, false, -1> : linear_kernel<__half, true, false, -1>)
+  auto kern = mode == 1   ? (gelu ? (bf ? linear_kernel<__nv_bfloat16, true, false, LF_ACT_GELU>
+                                         : linear_kernel<__half, true, false, LF_ACT_GELU>)
+                                  : (bf ? linear_kernel<__nv_bfloat16, true, false, LF_ACT_NONE>
+                                        : linear_kernel<__half, true, false, LF_ACT_NONE>))
               : mode == 2 ? (bf ? linear_kernel<__nv_bfloat16, false, true, LF_ACT_NONE>
                                 : linear_kernel<__half, false, true, LF_ACT_NONE>)
               : gelu      ? (bf ? linear_kernel<__nv_bfloat16, false, false, LF_ACT_GELU>
@@ -935,10 +979,10 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   // as many pairs as can be resident at once (a GPC with an odd SM count leaves one idle)
-  static int resident_pairs[64][4] = {};
+  static int resident_pairs[64][6] = {};
   int pairs = sms / 2;
   if (dev >= 0 && dev < 64) {
-    int& resident = resident_pairs[dev][mode == 0 && gelu ? 3 : mode];
+    int& resident = resident_pairs[dev][2 * mode + (gelu ? 1 : 0)];
     if (resident == 0) {
       cudaLaunchConfig_t q = {};
       q.gridDim = dim3(unsigned(sms & ~1));

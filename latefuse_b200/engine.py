@@ -323,8 +323,9 @@ class EncoderWithLora(nn.Module):
         #: around it on the current stream (used by the benchmark's roofline timing)
         self.lora_events: list | None = None
         #: compute the shrink inside the projection GEMM's launch where the kernel can
-        #: (``lf_linear_lora_shrink``); False runs ``lf_lora_shrink_blocked`` first
-        self.fuse_shrink = True
+        #: (``lf_linear_lora_shrink``); False runs ``lf_lora_shrink_blocked`` first; or
+        #: the set of projections to fuse (``{"qkv"}``, ``{"dense"}``)
+        self.fuse_shrink: bool | set = True
         #: bf16/f16 FFN down projection on this library's GEMM accumulating onto its
         #: residual (``lf_linear_accumulate``) instead of torch's ``addmm_`` (cuBLAS,
         #: beta = 1).  Off by default: at the bge-m3 serving shape (17,410 tokens x 1,024
@@ -600,8 +601,10 @@ class EncoderWithLora(nn.Module):
                 u_qkv = blocked_u(3, T, segs.n_segs, rank, h.dtype, h.device)
             if gemm_dense:
                 u_dense = blocked_u(1, T, segs.n_segs, rank, h.dtype, h.device)
-            fuse_qkv = gemm_qkv and self.fuse_shrink and fused_shrink_ok(qkv_by_col, rank)
-            fuse_dense_shrink = gemm_dense and self.fuse_shrink and fused_shrink_ok(dense_idx, rank)
+            fuse = self.fuse_shrink if isinstance(self.fuse_shrink, (set, frozenset)) else \
+                ({"qkv", "dense"} if self.fuse_shrink else set())
+            fuse_qkv = gemm_qkv and "qkv" in fuse and fused_shrink_ok(qkv_by_col, rank)
+            fuse_dense_shrink = gemm_dense and "dense" in fuse and fused_shrink_ok(dense_idx, rank)
         else:
             fuse_dense = gemm_qkv = gemm_dense = fuse_qkv = fuse_dense_shrink = False
 

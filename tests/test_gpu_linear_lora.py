@@ -16,6 +16,7 @@ import torch
 import torch.nn.functional as F
 
 from latefuse_b200 import _native as nat
+from latefuse_b200.encoder_ops import ACT_GELU
 from latefuse_b200.lora import (FactorCache, SegmentTable, blocked_u, linear_lora, lora_apply, lora_shrink,
                                 lora_shrink_blocked, workspace_bytes)
 
@@ -286,6 +287,34 @@ def test_shrink_in_the_gemm_launch_matches_the_two_launches(cuda, R, n_mod, max_
         assert not torch.isnan(got[k]).any(), k
         assert (got[k].float() - want[k].float()).abs().max().item() <= 2e-2 * want[k].float().abs().max().item() + 1e-6
     check(one, two, two)
+
+
+@pytest.mark.parametrize("shrink", [False, True])
+def test_lora_gemm_with_gelu_is_the_gelu_of_the_lora_gemm(cuda, shrink):
+    """act = GELU on the LoRA GEMM: the epilogue's GELU applied to the same rounded sum the
+    plain LoRA GEMM returns (within one bf16 ulp; the formula's f32 cancellation for
+    inputs below about -4 allowed for as in the plain GEMM's test)."""
+    dtype, H, R, n_slots = torch.bfloat16, 512, 16, 37
+    dev = torch.device("cuda")
+    starts, lengths, slots, T = packed_segments(30, n_slots, seed=5)
+    fc, _ = make_cache(n_slots, 4, H, R, dtype, dev, seed=5)
+    st = SegmentTable(starts, lengths, slots, T, dev)
+    g = torch.Generator(device="cpu").manual_seed(6)
+    x = torch.randn(T, H, generator=g).to(dtype).to(dev)
+    W = (torch.randn(3 * H, H, generator=g) * H ** -0.5).to(dtype).to(dev)
+    b = torch.randn(3 * H, generator=g).to(dtype).to(dev)
+    mods = [1, 2, 3]
+    u = blocked_u(3, T, st.n_segs, R, dtype, dev)
+    if not shrink:
+        lora_shrink_blocked(x, u, fc, st, mods)
+    plain = linear_lora(x, W, b, u, fc, st, mods, H, shrink=shrink).float()
+    act = linear_lora(x, W, b, u, fc, st, mods, H, act=ACT_GELU, shrink=shrink)
+    want = (plain * 0.5 * (1.0 + torch.erf(plain * 0.70710678118654752440))).to(dtype)
+    lo, hi = act.view(torch.int16).int(), want.view(torch.int16).int()
+    dist = (torch.where(lo < 0, -(lo & 0x7FFF), lo) - torch.where(hi < 0, -(hi & 0x7FFF), hi)).abs()
+    near = (act.float() - want.float()).abs() <= plain.abs() * 2.0 ** -22
+    assert not ((dist > 1) & ~near).any()
+    assert (dist != 0).float().mean().item() < 2e-3
 
 
 def test_shrink_in_the_gemm_launch_rejects_what_it_cannot_stage(cuda):
