@@ -422,20 +422,21 @@ def run_serve(args):
                                                             + segs.host.numel() * 4)
         d2h = out_h.numel() * 2
 
-        def e2e_step(_i=0):
+        def e2e_run(n):
+            # every step: its host batch packed and copied in, its embeddings copied out to
+            # pinned host memory and waited for; the next batch is prepared and launched
+            # while the previous one computes (two in flight)
             if runner is not None:
-                vec = runner.embed_tokens(ids_h, mask_h, tenants)
+                outs = runner.embed_tokens_stream(((ids_h, mask_h, tenants) for _ in range(n)), depth=2)
             else:
-                vec = emb.embed_tokens(my_ids_h, my_mask_h, my_tenants)
-            out_h.copy_(vec, non_blocking=True)
-            torch.cuda.current_stream().synchronize()
+                outs = emb.embed_tokens_stream(((my_ids_h, my_mask_h, my_tenants) for _ in range(n)), depth=2)
+            for host in outs:
+                out_h[:host.shape[0]].copy_(host)
 
-        for _ in range(args.warmup):
-            e2e_step()
+        e2e_run(args.warmup)
         barrier()
         t0 = time.perf_counter()
-        for _ in range(args.steps):
-            e2e_step()
+        e2e_run(args.steps)
         barrier()
         e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
         if world > 1:
@@ -444,8 +445,10 @@ def run_serve(args):
             e2e_ms = t.item()
         e2e = {"value": n_glob / (e2e_ms * 1e-3), "unit": "sequences/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "path": ("DataParallelEmbedder.embed_tokens" if world > 1 else "MultiTenantEmbedder.embed_tokens")
-                       + "(pinned host ids/mask, tenant ids) -> pinned host embeddings"}
+               "path": ("DataParallelEmbedder.embed_tokens_stream" if world > 1
+                        else "MultiTenantEmbedder.embed_tokens_stream")
+                       + "(pinned host ids/mask, tenant ids; two batches in flight) -> pinned host embeddings, "
+                         "each waited for"}
     clocks.__exit__(None, None, None)
 
     op = ref_gpu = cpu = None

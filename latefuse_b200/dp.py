@@ -110,3 +110,11 @@ class DataParallelEmbedder:
         out = torch.empty_like(rows)
         out[order] = rows
         return out
+
+    def embed_tokens_stream(self, batches, *, depth: int = 2, **kw):
+        """:meth:`embed_tokens` over an iterable of global ``(input_ids, attention_mask,
+        tenants)`` batches with up to ``depth`` in flight; yields each full result as a
+        pinned host tensor, in order (every rank the same)."""
+        from latefuse_b200.tasks import stream_to_host
+
+        return stream_to_host(lambda ids, mask, tenants: self.embed_tokens(ids, mask, tenants, **kw), batches, depth)

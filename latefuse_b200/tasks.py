@@ -54,6 +54,38 @@ def chunk_and_pad(items: Sequence[T], batch_size: int) -> Iterator[tuple[list[T]
         yield chunk, n_valid
 
 
+def stream_to_host(step, batches, depth: int = 2) -> Iterator[Tensor]:
+    """Run ``step(*batch)`` (queues device work, returns a device tensor) over
+    ``batches`` with up to ``depth`` batches in flight, yielding each result as a pinned
+    host tensor in batch order.  With ``depth`` 2 the host packs, copies and launches
+    batch i + 1 while the device computes batch i, so host preparation stops adding to
+    the step time; ``depth`` 1 waits for every batch before starting the next."""
+    from collections import deque
+
+    if depth < 1:
+        raise ValueError(f"depth must be at least 1, got {depth}")
+    pending: deque = deque()
+    for batch in batches:
+        out = step(*batch)
+        host = torch.empty(out.shape, dtype=out.dtype, pin_memory=out.is_cuda)
+        host.copy_(out, non_blocking=out.is_cuda)
+        done = None
+        if out.is_cuda:
+            done = torch.cuda.Event()
+            done.record()
+        pending.append((host, done))
+        if len(pending) >= depth:
+            host, done = pending.popleft()
+            if done is not None:
+                done.synchronize()
+            yield host
+    while pending:
+        host, done = pending.popleft()
+        if done is not None:
+            done.synchronize()
+        yield host
+
+
 def _default_device() -> torch.device:
     return torch.device("cuda") if torch.cuda.is_available() else torch.device("cpu")
 
@@ -278,6 +310,14 @@ class MultiTenantEmbedder(TaskPipeline):
         if normalize and vectors.numel():
             vectors = l2_normalize(vectors)
         return vectors
+
+    def embed_tokens_stream(self, batches, *, depth: int = 2, normalize: bool = True,
+                            pooling: str | None = None) -> Iterator[Tensor]:
+        """:meth:`embed_tokens` over an iterable of ``(input_ids, attention_mask, tenants)``
+        host batches with up to ``depth`` in flight (:func:`stream_to_host`): each batch's
+        embeddings come back as a pinned host tensor, in order."""
+        return stream_to_host(lambda ids, mask, tenants: self.embed_tokens(ids, mask, tenants, normalize=normalize,
+                                                                          pooling=pooling), batches, depth)
 
     @staticmethod
     def _broadcast_tenants(tenants: Sequence[str] | str, n: int) -> list[str]:

@@ -72,3 +72,10 @@ def test_head_dim_64_packed_matches_oracle(cuda):
             assert row_rel(emb.embed_tokens(ids, mask, tenants, pooling=pooling), ref) < 2e-2
     oracle.close()
     packed.check_device_status()
+    # the streaming form (two batches in flight) returns the same rows, in batch order
+    one = packed.embed_tokens(ids, mask, tenants).cpu()
+    rev = packed.embed_tokens(ids.flip(0), mask.flip(0), tenants[::-1]).cpu()
+    outs = list(packed.embed_tokens_stream([(ids, mask, tenants), (ids.flip(0), mask.flip(0), tenants[::-1]),
+                                            (ids, mask, tenants)], depth=2))
+    assert [o.is_pinned() for o in outs] == [True] * 3
+    assert torch.equal(outs[0], one) and torch.equal(outs[1], rev) and torch.equal(outs[2], one)

@@ -446,3 +446,23 @@ def test_cpu_serving_path_fails_loudly():
 
     with pytest.raises(NativeLibraryError, match="CUDA"):
         lf.pool_tokens(torch.randn(2, 3, 32), None, "cls")
+
+
+def test_stream_to_host_yields_every_result_in_order_with_bounded_lookahead():
+    from latefuse_b200.tasks import stream_to_host
+
+    started = []
+
+    def step(i):
+        started.append(i)
+        return torch.full((2, 3), float(i))
+
+    seen = []
+    for i, host in enumerate(stream_to_host(step, ((i,) for i in range(5)), depth=2)):
+        assert torch.equal(host, torch.full((2, 3), float(i)))
+        seen.append(i)
+        assert len(started) <= i + 2  # never more than depth batches started ahead
+    assert seen == list(range(5)) and started == list(range(5))
+    assert [h[0, 0].item() for h in stream_to_host(step, [(7,)], depth=1)] == [7.0]
+    with pytest.raises(ValueError, match="depth"):
+        list(stream_to_host(step, [(0,)], depth=0))
