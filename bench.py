@@ -54,11 +54,12 @@ METRIC = "sequences/sec at bge-m3 shape, 10k adapters; LoRA-kernel HBM GB/s vs p
 TARGETS = ["query", "key", "value", "dense"]
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
-# DRAM bytes (read + write) of one q/k/v lf_linear_lora launch at 16,401 tokens x 3072 x
-# 1024, rank 16, 33 segments, from one ncu capture (dram__bytes_read.sum +
-# dram__bytes_write.sum) of `bench.py --layers 2 --adapters 500 --steps 1 --warmup 1`.
-# None until captured for the current kernel.
-NCU_TRAFFIC_QKV_GEMM = None
+# DRAM bytes (read + write) of one q/k/v lf_linear_lora_shrink launch at 17,410 tokens x
+# 3072 x 1024, rank 16, 39 segments, from one ncu capture (dram__bytes_read.sum 52.9 MB +
+# dram__bytes_write.sum 66.7 MB) of `bench.py --layers 2 --adapters 500 --steps 1
+# --warmup 1 --no-cpu-baseline --no-e2e --no-extras` (same tokens and segments as the
+# full workload; the adapters read are the batch's tenants in both).
+NCU_TRAFFIC_QKV_GEMM = 119.5e6
 
 
 def bge_m3_config(layers: int = 24):
@@ -385,7 +386,8 @@ def run_serve(args):
         roofline = {
             "bound": "tensor", "achieved": tach, "peak": tpeak, "unit": "TFLOP/s", "frac": tach / tpeak,
             "traffic": NCU_TRAFFIC_QKV_GEMM if (pack and R == 16 and args.batch == 64 and args.seq == 512) else None,
-            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one lf_linear_lora q/k/v launch"
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one lf_linear_lora_shrink q/k/v "
+                              "launch (2-layer, 500-adapter capture of the same 17,410-token batch)"
                               if NCU_TRAFFIC_QKV_GEMM is not None else "not captured for this kernel build",
             "kernel": "lf_linear_lora: q/k/v projection (T x 3072 x 1024) with the per-row LoRA delta in the "
                       "tcgen05 accumulator (one launch per layer)",
