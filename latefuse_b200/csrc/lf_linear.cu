@@ -617,17 +617,29 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
       const int row = quad_ * 32 + lane;
       const int64_t t = int64_t(m0) + row;
       T* u = static_cast<T*>(p.u_out);
+      // the pass's entries (at most 2 * s_epc <= 16), lane e holding entry e, fetched in
+      // one round of loads and handed out by shuffles
+      int ej = -1, emask = 0;
+      int64_t es0 = 0, es1 = 0;
+      if (lane < ne_p) {
+        const int q = qr.x + e0 + lane;
+        ej = __ldg(p.pairs + 3 * q);
+        emask = __ldg(p.pairs + 3 * q + 2);
+        if (ej >= 0 && ej < p.n_segs) {
+          es0 = __ldg(p.seg_start + ej);
+          es1 = es0 + __ldg(p.seg_len + ej);
+        }
+      }
       int box = 0;
       for (int owner = 0; owner < 2; ++owner) {
         for (int i = 0; i < ne_h; ++i) {
           const int32_t e = owner * ne_h + i;  // entry within the pass
           for (int m = 0; m < p.n_mod; ++m, ++box) {
             if ((box & 1) != half_ || e >= ne_p) continue;
-            const int q = qr.x + e0 + e;
-            const int j = __ldg(p.pairs + 3 * q);
-            const int mask = __ldg(p.pairs + 3 * q + 2);
+            const int j = __shfl_sync(0xffffffffu, ej, e);
+            const int mask = __shfl_sync(0xffffffffu, emask, e);
             if (j < 0 || j >= p.n_segs || !((mask >> rank) & 1)) continue;  // no block of this CTA's tile
-            const int64_t s0 = __ldg(p.seg_start + j), s1 = s0 + __ldg(p.seg_len + j);
+            const int64_t s0 = __shfl_sync(0xffffffffu, es0, e), s1 = __shfl_sync(0xffffffffu, es1, e);
             const bool in = t >= s0 && t < s1 && t < p.m_rows;
             T* blk = u + (int64_t(m) * p.n_blk + 2 * it.rb + int32_t(rank) + j) * (int64_t(kBM) * R);
             const uint32_t col = uint32_t(owner) * uint32_t(ne_h * p.n_mod * R) + uint32_t((i * p.n_mod + m) * R);
@@ -650,10 +662,11 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
       asm volatile("fence.proxy.async.global;" ::: "memory");
     };
     // LoRA: the B factors of every delta block this pair will stage, prefetched into L2
-    // once at the start by the epilogue warps (idle until the first accumulator is
-    // ready), each warp taking every kEpiWarps-th tile of the pair's sequence, so the
+    // once by the epilogue warps after their first item (a shrink pass's u must not wait
+    // for it), each warp taking every kEpiWarps-th tile of the pair's sequence, so the
     // copy-issuing thread never waits on the table reads behind these addresses
-    if (kLora && lane == 0) {
+    auto prefetch_walk = [&]() {
+      if (!kLora || lane != 0) return;
       Sched<kLora> walk(p, pair, n_pairs);
       Item w;
       for (int i = 0; walk.next(p, w);) {
@@ -669,7 +682,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
                         uint32_t(p.rank) * uint32_t(p.module_cols) * 2u);
         }
       }
-    }
+    };
     const T* bias = static_cast<const T*>(p.bias);
     Sched<kLora> sched(p, pair, n_pairs);
     Item item;
@@ -685,6 +698,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     };
     uint4 y_next[4];
     for (int n_it = 0; sched.next(p, item); ++n_it) {
+      if (n_it == 1) prefetch_walk();
       const int a = n_it & 1;
       const int32_t m0 = item.rb * (2 * kBM) + int32_t(rank) * kBM;
       const int32_t n0 = item.c * kBN;
