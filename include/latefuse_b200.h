@@ -390,8 +390,11 @@ int lf_linear_accumulate(void* stream, int dtype, const void* x, int64_t ldx, co
  * (src/latefuse/model/hf_wrapper.py:217, `output + lora_ops.output`; the fused
  * q/k/v and attention-output projections of src/latefuse/model/encoder.py:70-80).
  * Tokens in no segment, or in a segment whose slot is out of range, get no
- * delta.  rank 16, 32 or 64; module_cols a multiple of 256 dividing n. */
-int lf_linear_lora(void* stream, int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,
+ * delta.  rank 16, 32 or 64; module_cols a multiple of 256 dividing n.
+ * w_kn = 0: w is (n, k), the nn.Linear weight, as for lf_linear.  w_kn = 1: w is
+ * (k, n) row-major (its transpose, ldw >= n), read in the same operand form as the
+ * cache's B factors (results agree to the dtype's rounding; the speed is the same). */
+int lf_linear_lora(void* stream, int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw, int w_kn,
                    const void* bias, void* y, int64_t ldy, int64_t m, int n, int k, int act,
                    const void* u, int rank, const void* cache_b, int64_t b_slot_stride, int64_t b_module_stride,
                    int n_slots, int n_modules, const int32_t* modules, int module_cols, int n_segs,
@@ -409,7 +412,7 @@ int lf_linear_lora(void* stream, int dtype, const void* x, int64_t ldx, const vo
  * seg_len (device int32, n_segs) are the segment table; the other arguments are
  * lf_linear_lora's.  Needs n_modules * rank <= 128 and the modules' A factors evenly
  * spaced in the cache (or one module); LF_ERR_UNSUPPORTED otherwise. */
-int lf_linear_lora_shrink(void* stream, int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,
+int lf_linear_lora_shrink(void* stream, int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw, int w_kn,
                           const void* bias, void* y, int64_t ldy, int64_t m, int n, int k, int act,
                           void* u, int rank, const void* cache_a, int64_t a_slot_stride, int64_t a_module_stride,
                           const void* cache_b, int64_t b_slot_stride, int64_t b_module_stride,

@@ -94,11 +94,11 @@ SIGNATURES: dict[str, tuple] = {
         c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int,
         c_int, c_void_p]),
     "lf_linear_lora": (c_int, [
-        c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int,
+        c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int,
         c_int, c_int, c_void_p, c_int, c_void_p, c_int64, c_int64, c_int, c_int, POINTER(c_int32), c_int,
         c_int, c_void_p, c_void_p, c_void_p]),
     "lf_linear_lora_shrink": (c_int, [
-        c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int,
+        c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int,
         c_int, c_int, c_void_p, c_int, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int,
         POINTER(c_int32), c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "lf_add_layernorm": (c_int, [

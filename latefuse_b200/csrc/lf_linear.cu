@@ -64,12 +64,14 @@ constexpr int kEpiWarps = 8;                      // two per TMEM lane quadrant,
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kOutCols = 32;                      // output columns per epilogue store
 constexpr int kOutBuf = 32 * kOutCols * 2;        // one warp's 32 x 32 staging tile: 2 KB
-constexpr int kDeltaBuf = 8192;                   // a tile's first delta block at rank 16: u 4 KB + B 4 KB
-constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kEpiWarps * kOutBuf + kDeltaBuf + 1024;
+constexpr int kDeltaBuf = 16384;                  // a tile's first delta blocks: two at rank 16 (u 4 KB + B 4 KB each), one at 32
+constexpr int kDeltaBufs = 1;
+constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kEpiWarps * kOutBuf + kDeltaBufs * kDeltaBuf + 1024;
+static_assert(kSmemBytes <= 232448, "above the 227 KB of shared memory a CTA may use");
 
 struct alignas(64) LinearParams {
   CUtensorMap x_map;  // 2D {K, M}, box {64, 128}, SW128
-  CUtensorMap w_map;  // 2D {K, N}, box {64, 128}, SW128
+  CUtensorMap w_map;  // 2D {K, N}, box {64, 128}, SW128; w_kn: 3D {64, K, N / 64}, box {64, 64, 2}, SW128
   CUtensorMap y_map;  // 2D {N, M}, box {32, 32}, SW64
   CUtensorMap u_map;  // LoRA: 3D {256, R / 2, n_mod * n_blk}, box {256, R / 2, 1}: one 128 x R block
   CUtensorMap b_map[kMaxModules];     // LoRA: 4D {64, R, module_cols / 64, n_slots}, box {64, R, 2, 1}, SW128
@@ -97,6 +99,7 @@ struct alignas(64) LinearParams {
   int32_t n_tiles_n;
   int32_t n_kb;
   int32_t act;        // LF_ACT_*
+  int32_t w_kn;       // 1: w is (K, N) (the transposed nn.Linear weight), read MN-major
   int32_t* status;
   const void* y_in;   // accumulate: y's current values (the output itself), row stride ldy
   int64_t ldy;
@@ -274,12 +277,12 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
 
   const uint32_t s_stage0 = base;
   const uint32_t s_out0 = base + kStages * kStageBytes;  // [warp] 2 KB staging tiles
-  const uint32_t s_delta = s_out0 + kEpiWarps * kOutBuf;  // the tile's first delta block (rank 16)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + (s_delta + kDeltaBuf - base));
+  const uint32_t s_delta = s_out0 + kEpiWarps * kOutBuf;  // a tile's first delta blocks
+  uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + (s_delta + kDeltaBufs * kDeltaBuf - base));
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   const int FULL = 0, EMPTY = kStages, ACC_FULL = 2 * kStages, ACC_EMPTY = 2 * kStages + 2,
-            DRAIN = 2 * kStages + 4, DFULL = DRAIN + 1, DEMPTY = DRAIN + 2, U_READY = DRAIN + 3,
-            N_BARS = DRAIN + 4;
+            DRAIN = 2 * kStages + 4, DFULL = DRAIN + 1, DEMPTY = DFULL + kDeltaBufs, U_READY = DEMPTY + kDeltaBufs,
+            N_BARS = U_READY + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(&bars[N_BARS]);
   int32_t* s_abort = reinterpret_cast<int32_t*>(tmem_slot + 1);
 
@@ -293,14 +296,21 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
       mbar_init(bar(ACC_EMPTY + i), 2 * kEpiWarps);  // both CTAs' epilogue warps
     }
     mbar_init(bar(DRAIN), 1);
-    mbar_init(bar(DFULL), 1);   // the leader's arrive, with both CTAs' bytes
-    mbar_init(bar(DEMPTY), 1);  // the leader's MMA commit
+    for (int i = 0; i < kDeltaBufs; ++i) {
+      mbar_init(bar(DFULL + i), 1);   // the leader's arrive, with both CTAs' bytes
+      mbar_init(bar(DEMPTY + i), 1);  // the leader's MMA commit
+    }
     mbar_init(bar(U_READY), kEpiWarps);  // this CTA's epilogue warps: a shrink pass's u is written
     *s_abort = 0;
     fence_mbar_init();
     prefetch_tmap(&p.x_map);
     prefetch_tmap(&p.w_map);
     prefetch_tmap(&p.y_map);
+    if (kLora) {  // the delta blocks' u and B maps, and the shrink's A map
+      prefetch_tmap(&p.u_map);
+      for (int i = 0; i < p.n_mod; ++i) prefetch_tmap(&p.b_map[i]);
+      if (p.shrink) prefetch_tmap(&p.a_map);
+    }
   }
   if (warp == 1) {  // the same warp in both CTAs allocates the pair's TMEM
     __syncwarp();
@@ -321,9 +331,12 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
     atomicExch(s_abort, 1);
   };
   constexpr bool lora = kLora;
-  // a tile's first delta block goes to its own buffer, loaded while the tile's K
-  // blocks stream, so it has landed when the MMA reaches it (later ones use the ring)
-  const bool dbuf = lora && 512 * p.rank <= kDeltaBuf;
+  // a tile's first delta blocks (as many as the delta buffer holds: 512 * rank bytes
+  // each per CTA) go to their own buffer, loaded while the tile's K blocks stream, so
+  // they have landed when the MMA reaches them; later ones use the ring, where a block
+  // in a stage carries a sixteenth of a K block's work and the ring's lead shrinks
+  const int n_dslots = lora ? kDeltaBuf / (512 * p.rank) : 0;
+  const bool dbuf = n_dslots > 0;
   auto dbuf_tile = [&](const Item& it) { return !(kLora && p.shrink && it.first); };
 
   if (warp == 0) {
@@ -415,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
         auto entry = [&](int q) {
           return Entry{__ldg(p.pairs + 3 * q), __ldg(p.pairs + 3 * q + 1), __ldg(p.pairs + 3 * q + 2)};
         };
-        auto load_delta = [&](uint32_t dst_u, uint32_t dst_b, uint32_t full_local, Entry e) {
+        auto load_delta = [&](uint32_t dst_u, uint32_t dst_b, uint32_t full_local, Entry e, uint32_t arm_bytes) {
           int j = e.j;
           const int32_t slot = e.slot;  // out of range: zero fill, no delta, reported
           const int32_t mask = e.mask;
@@ -427,15 +440,18 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
           const int32_t blk = (j >= 0 && ((mask >> rank) & 1)) ? mod * p.n_blk + 2 * it.rb + int32_t(rank) + j
                                                                : zero_blk;
           const uint32_t full = mapa_shared(full_local, 0);
-          if (rank == 0) mbar_arrive_expect_tx(full_local, 2 * 512 * p.rank);  // u 128 x R + B R x 128, twice
+          if (rank == 0 && arm_bytes) mbar_arrive_expect_tx(full_local, arm_bytes);  // every block's bytes, both CTAs
           tma_load_3d_pair(dst_u, &p.u_map, full, 0, 0, blk);
           tma_load_4d_pair(dst_b, &p.b_map[mod], full, 0, 0, (n_loc + half_cols) / 64, slot);
         };
-        // the first block is loaded once the MMA has started this tile (by then the
-        // previous tile's first block has been multiplied); not for a block's first tile
-        // when this launch writes u (its delta blocks wait for the shrink's epilogue)
+        // the first blocks go to the delta buffer half way through the tile's K blocks:
+        // the copies issue about kStages K blocks ahead of the MMA, so the previous
+        // tile's blocks were multiplied by then and these land before the MMA needs
+        // them; not for a block's first tile when this launch writes u (its delta
+        // blocks wait for the shrink's epilogue)
         const bool use_dbuf = dbuf && q1 > q0 && dbuf_tile(it);
-        const int d_after = (p.n_kb < kStages ? p.n_kb : kStages) - 1;
+        const int n_in = use_dbuf ? min(q1 - q0, n_dslots) : 0;
+        const int d_after = p.n_kb / 2;
         // the tile's first two delta entries, in flight while its K blocks stream
         Entry e_first{0, 0, 0}, e_second{0, 0, 0};
         if (q1 > q0) e_first = entry(q0);
@@ -447,19 +463,28 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
             break;
           }
           tma_load_2d_pair(st, &p.x_map, full, kb * kBK, m0);
-          tma_load_2d_pair(st + kABytes, &p.w_map, full, kb * kBK, n0 + half_cols);
+          if (p.w_kn)
+            tma_load_3d_pair(st + kABytes, &p.w_map, full, 0, kb * kBK, (n0 + half_cols) / 64);
+          else
+            tma_load_2d_pair(st + kABytes, &p.w_map, full, kb * kBK, n0 + half_cols);
           if (use_dbuf && kb == d_after) {
-            if (aborted_flag(s_abort) || !mbar_wait(bar(DEMPTY), (dk & 1) ^ 1)) {
+            const int db = dk % kDeltaBufs;
+            if (aborted_flag(s_abort) || !mbar_wait(bar(DEMPTY + db), ((dk / kDeltaBufs) & 1) ^ 1)) {
               if (!aborted_flag(s_abort)) fail();
               stop = true;
               ++kk;
               break;
             }
-            load_delta(s_delta, s_delta + 256 * p.rank, bar(DFULL), e_first);
+            const uint32_t blk_bytes = 512u * uint32_t(p.rank);
+            for (int i = 0; i < n_in; ++i) {
+              const uint32_t dst = s_delta + db * kDeltaBuf + i * blk_bytes;
+              load_delta(dst, dst + 256 * p.rank, bar(DFULL + db), i == 0 ? e_first : i == 1 ? e_second : entry(q0 + i),
+                         i == 0 ? 2u * blk_bytes * uint32_t(n_in) : 0u);
+            }
             ++dk;
           }
         }
-        if (use_dbuf) ++q0;
+        q0 += n_in;
         if (stop || q1 <= q0) continue;
         if (!wait_u()) {
           stop = true;
@@ -473,24 +498,27 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
             break;
           }
           const uint32_t st = s_stage0 + s * kStageBytes;
-          const int q_first = use_dbuf ? q0 - 1 : q0;  // the tile's first entry
+          const int q_first = q0 - n_in;  // the tile's first entry
           load_delta(st, st + kABytes, bar(FULL + s),
-                     q == q_first ? e_first : q == q_first + 1 ? e_second : entry(q));
+                     q == q_first ? e_first : q == q_first + 1 ? e_second : entry(q), 2u * 512u * uint32_t(p.rank));
         }
       }
       if (aborted_flag(s_abort)) {  // loads nobody consumed land before the CTA exits (bounded)
         if (rank == 0) {
           for (int q = (kk > kStages ? kk - kStages : 0); q < kk; ++q)
             mbar_wait(bar(FULL + q % kStages), (q / kStages) & 1);
-          if (dk > 0) mbar_wait(bar(DFULL), (dk - 1) & 1);
+          for (int q = (dk > kDeltaBufs ? dk - kDeltaBufs : 0); q < dk; ++q)
+            mbar_wait(bar(DFULL + q % kDeltaBufs), (q / kDeltaBufs) & 1);
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (the leader's lane 0)
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16(DT<T>::umma_fmt, 2 * kBM, kBN, 0, 0);
+      // the delta blocks' B is MN-major (the cache's (R, cols) rows); with w (K, N) the main
+      // loop's B is MN-major too, and every MMA of a tile has one instruction descriptor
       constexpr uint32_t idesc_d = umma_idesc_f16(DT<T>::umma_fmt, 2 * kBM, kBN, 0, 1);
+      const uint32_t idesc = p.w_kn ? idesc_d : umma_idesc_f16(DT<T>::umma_fmt, 2 * kBM, kBN, 0, 0);
       int kk = 0, n_it = 0, dk = 0;
       bool stop = false;
       auto wait = [&](uint32_t b, uint32_t parity) {
@@ -556,7 +584,9 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
           const uint32_t st = s_stage0 + s * kStageBytes;
 #pragma unroll
           for (int q = 0; q < kBK / 16; ++q)
-            umma_pair(tmem + a * kBN, smem_desc(st + q * 32, 16, 1024, 2), smem_desc(st + kABytes + q * 32, 16, 1024, 2),
+            umma_pair(tmem + a * kBN, smem_desc(st + q * 32, 16, 1024, 2),
+                      p.w_kn ? smem_desc(st + kABytes + q * 2048, 8192, 1024, 2)   // [N/64][K][64] MN-major
+                             : smem_desc(st + kABytes + q * 32, 16, 1024, 2),
                       idesc, (kb | q) != 0 ? 1u : 0u);
           umma_commit_pair(bar(EMPTY + s));
         }
@@ -568,14 +598,19 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
                       smem_desc(ba + q * 2048, p.rank * 128, 1024, 2), idesc_d, 1u);
         };
         int d = 0;
-        if (!stop && dbuf && n_delta > 0 && dbuf_tile(it)) {  // the first block, from the delta buffer
-          if (!wait(bar(DFULL), dk & 1)) {
+        if (!stop && dbuf && n_delta > 0 && dbuf_tile(it)) {  // the first blocks, from the delta buffer
+          const int db = dk % kDeltaBufs;
+          const int n_in = min(n_delta, n_dslots);
+          if (!wait(bar(DFULL + db), (dk / kDeltaBufs) & 1)) {
             stop = true;
           } else {
-            delta_mma(s_delta, s_delta + 256 * p.rank);
-            umma_commit_pair(bar(DEMPTY));
+            for (int i = 0; i < n_in; ++i) {
+              const uint32_t src = s_delta + db * kDeltaBuf + i * 512u * uint32_t(p.rank);
+              delta_mma(src, src + 256 * p.rank);
+            }
+            umma_commit_pair(bar(DEMPTY + db));
             ++dk;
-            d = 1;
+            d = n_in;
           }
         }
         for (; d < n_delta && !stop; ++d, ++kk) {
@@ -830,7 +865,7 @@ struct LoraArgs {
 
 static int linear_impl(const char* fn, void* stream, int dtype, const void* x, int64_t ldx, const void* w,
                        int64_t ldw, const void* bias, void* y, int64_t ldy, int64_t m, int n, int k, int act,
-                       const LoraArgs* lora, int32_t* status, bool accumulate = false) {
+                       const LoraArgs* lora, int32_t* status, bool accumulate = false, bool w_kn = false) {
   if (dtype != LF_DTYPE_BF16 && dtype != LF_DTYPE_F16)
     return set_error(LF_ERR_UNSUPPORTED, "%s: dtype %d (bf16 or f16 only)", fn, dtype);
   if (act != LF_ACT_NONE && act != LF_ACT_GELU) return set_error(LF_ERR_INVALID, "%s: unknown act %d", fn, act);
@@ -839,7 +874,8 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
   if (m < 0 || m > INT32_MAX || n <= 0 || k <= 0 || n % kBN != 0 || k % kBK != 0)
     return set_error(LF_ERR_UNSUPPORTED, "%s: n %d must be a multiple of 256 and k %d of 64", fn, n, k);
   if (x == nullptr || w == nullptr || y == nullptr) return set_error(LF_ERR_INVALID, "%s: null x, w or y", fn);
-  if (ldx < k || ldw < k || ldy < n) return set_error(LF_ERR_INVALID, "%s: a row stride is below its row", fn);
+  if (ldx < k || ldw < (w_kn ? n : k) || ldy < n)
+    return set_error(LF_ERR_INVALID, "%s: a row stride is below its row", fn);
   if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (bias != nullptr && !aligned16(bias)) || (ldx * 2) % 16 ||
       (ldw * 2) % 16 || (ldy * 2) % 16)
     return set_error(LF_ERR_INVALID, "%s: pointers and row strides must be 16-byte aligned", fn);
@@ -891,7 +927,12 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
     const cuuint32_t box[2] = {kBK, kBM};
     if ((rc = tmap(&p.x_map, 2, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "x"))) return rc;
   }
-  {
+  if (w_kn) {  // w (k, n): blocks of 64 output columns, each K rows of 128 bytes
+    const cuuint64_t dims[3] = {64, cuuint64_t(k), cuuint64_t(n / 64)};
+    const cuuint64_t strides[2] = {cuuint64_t(ldw) * 2, 128};
+    const cuuint32_t box[3] = {64, kBK, kBN / 128};
+    if ((rc = tmap(&p.w_map, 3, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "w"))) return rc;
+  } else {
     const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(n)};
     const cuuint64_t strides[1] = {cuuint64_t(ldw) * 2};
     const cuuint32_t box[2] = {kBK, kBN / 2};
@@ -963,6 +1004,7 @@ static int linear_impl(const char* fn, void* stream, int dtype, const void* x, i
   p.n_tiles = int64_t(p.n_rb) * p.n_tiles_n;
   p.n_kb = k / kBK;
   p.act = act;
+  p.w_kn = w_kn ? 1 : 0;
   p.status = status;
   p.y_in = accumulate ? y : nullptr;
   p.ldy = ldy;
@@ -1041,18 +1083,20 @@ extern "C" int lf_linear_accumulate(void* stream, int dtype, const void* x, int6
 }
 
 extern "C" int lf_linear_lora(void* stream, int dtype, const void* x, int64_t ldx, const void* w, int64_t ldw,
-                              const void* bias, void* y, int64_t ldy, int64_t m, int n, int k, int act,
+                              int w_kn, const void* bias, void* y, int64_t ldy, int64_t m, int n, int k, int act,
                               const void* u, int rank, const void* cache_b, int64_t b_slot_stride,
                               int64_t b_module_stride, int n_slots, int n_modules, const int32_t* modules,
                               int module_cols, int n_segs, const int32_t* tile_pairs, const int32_t* pairs,
                               int32_t* status) {
   LoraArgs L{u, rank, cache_b, b_slot_stride, b_module_stride, n_slots, n_modules, modules, module_cols,
              n_segs, tile_pairs, pairs, nullptr, 0, 0, nullptr, nullptr};
-  return linear_impl("lf_linear_lora", stream, dtype, x, ldx, w, ldw, bias, y, ldy, m, n, k, act, &L, status);
+  return linear_impl("lf_linear_lora", stream, dtype, x, ldx, w, ldw, bias, y, ldy, m, n, k, act, &L, status, false,
+                     w_kn != 0);
 }
 
 extern "C" int lf_linear_lora_shrink(void* stream, int dtype, const void* x, int64_t ldx, const void* w,
-                                     int64_t ldw, const void* bias, void* y, int64_t ldy, int64_t m, int n, int k,
+                                     int64_t ldw, int w_kn, const void* bias, void* y, int64_t ldy, int64_t m, int n,
+                                     int k,
                                      int act, void* u, int rank, const void* cache_a, int64_t a_slot_stride,
                                      int64_t a_module_stride, const void* cache_b, int64_t b_slot_stride,
                                      int64_t b_module_stride, int n_slots, int n_modules, const int32_t* modules,
@@ -1061,5 +1105,6 @@ extern "C" int lf_linear_lora_shrink(void* stream, int dtype, const void* x, int
   if (cache_a == nullptr) return set_error(LF_ERR_INVALID, "lf_linear_lora_shrink: null cache_a");
   LoraArgs L{u, rank, cache_b, b_slot_stride, b_module_stride, n_slots, n_modules, modules, module_cols,
              n_segs, tile_pairs, pairs, cache_a, a_slot_stride, a_module_stride, seg_start, seg_len};
-  return linear_impl("lf_linear_lora_shrink", stream, dtype, x, ldx, w, ldw, bias, y, ldy, m, n, k, act, &L, status);
+  return linear_impl("lf_linear_lora_shrink", stream, dtype, x, ldx, w, ldw, bias, y, ldy, m, n, k, act, &L, status,
+                     false, w_kn != 0);
 }

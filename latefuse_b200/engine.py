@@ -326,6 +326,11 @@ class EncoderWithLora(nn.Module):
         #: (``lf_linear_lora_shrink``); False runs ``lf_lora_shrink_blocked`` first; or
         #: the set of projections to fuse (``{"qkv"}``, ``{"dense"}``)
         self.fuse_shrink: bool | set = True
+        #: the LoRA'd projections read a (K, N) transposed copy of their weight (kept per
+        #: weight, rebuilt when it changes), in the delta factors' operand form; off by
+        #: default: it measured the same as the weight as given, at 8 MB more per layer
+        self.kn_weights = False
+        self._wt_cache: dict[int, tuple] = {}
         #: bf16/f16 FFN down projection on this library's GEMM accumulating onto its
         #: residual (``lf_linear_accumulate``) instead of torch's ``addmm_`` (cuBLAS,
         #: beta = 1).  Off by default: at the bge-m3 serving shape (17,410 tokens x 1,024
@@ -529,6 +534,18 @@ class EncoderWithLora(nn.Module):
         o = F.linear(mid, layer.wo2, layer.bo2)
         return add_layernorm(o, h1, layer.ln2.weight, layer.ln2.bias, self.eps, out=o)
 
+    def _transposed(self, w: Tensor) -> Tensor | None:
+        """``w``'s ``(K, N)`` transpose for :func:`linear_lora` (None when ``kn_weights`` is
+        off), cached per weight and rebuilt when the weight is replaced or changed in place."""
+        if not self.kn_weights:
+            return None
+        hit = self._wt_cache.get(id(w))
+        if hit is not None and hit[1] == w._version and hit[2] == w.data_ptr():
+            return hit[0]
+        t = w.detach().t().contiguous()
+        self._wt_cache[id(w)] = (t, w._version, w.data_ptr())
+        return t
+
     @staticmethod
     def _gemm_ok(dtype: torch.dtype, weight_shape) -> bool:
         """Whether this library's GEMM (``lf_linear``) takes a projection of this weight:
@@ -618,7 +635,7 @@ class EncoderWithLora(nn.Module):
                         ev[1].record()
                 ev = self._event_pair("qkv_gemm")
                 qkv = linear_lora(h, layer.wqkv, layer.bqkv, u_qkv, cache, segs, qkv_by_col, H, status=status,
-                                  shrink=fuse_qkv)
+                                  shrink=fuse_qkv, weight_t=self._transposed(layer.wqkv))
                 if ev is not None:
                     ev[1].record()
             else:
@@ -642,7 +659,7 @@ class EncoderWithLora(nn.Module):
                         ev[1].record()
                 ev = self._event_pair("dense_gemm")
                 ao = linear_lora(ctx, layer.wo, layer.bo, u_dense, cache, segs, dense_idx, H, status=status,
-                                 shrink=fuse_dense_shrink)
+                                 shrink=fuse_dense_shrink, weight_t=self._transposed(layer.wo))
                 if ev is not None:
                     ev[1].record()
                 h = self._ffn(layer, ao, h)

@@ -306,22 +306,28 @@ def lora_shrink_blocked(x: Tensor, u: Tensor, cache: FactorCache, segs: SegmentT
     nat.check(rc, "lf_lora_shrink_blocked")
 
 
-def linear_lora(x: Tensor, weight: Tensor, bias: Tensor | None, u: Tensor, cache: FactorCache,
+def linear_lora(x: Tensor, weight: Tensor | None, bias: Tensor | None, u: Tensor, cache: FactorCache,
                 segs: SegmentTable, modules, module_cols: int, act: int = 0, out: Tensor | None = None,
-                status: Tensor | None = None, shrink: bool = False) -> Tensor:
+                status: Tensor | None = None, shrink: bool = False, weight_t: Tensor | None = None) -> Tensor:
     """``act(x @ weight.T + bias + delta)`` on the tcgen05 GEMM with the LoRA delta in
     its accumulator: output columns ``[i * module_cols, (i + 1) * module_cols)`` get
     ``u[i] @ B(slot(t), modules[i])`` (``u`` from :func:`lora_shrink_blocked`).
     One rounding of the sum, where the reference rounds the projection and the delta
     apart; see ``lf_linear_lora``.  With ``shrink`` the same launch computes ``u`` first
-    (``lf_linear_lora_shrink``; ``u`` is then an output, in the same blocked layout)."""
-    dev = nat.require_cuda(x, weight, bias, u, segs.table, out, status)
+    (``lf_linear_lora_shrink``; ``u`` is then an output, in the same blocked layout).
+    ``weight_t``, the ``(K, N)`` transpose of ``weight`` (which may then be None), is
+    read in the delta factors' operand form instead (``w_kn`` of the C entry points)."""
+    dev = nat.require_cuda(x, weight, weight_t, bias, u, segs.table, out, status)
     x2, ldx = _rows(x)
-    N, K = weight.shape
+    if weight_t is not None:
+        K, N = weight_t.shape
+        w, w_kn = (weight_t if weight_t.stride(-1) == 1 else weight_t.contiguous()), 1
+    else:
+        N, K = weight.shape
+        w, w_kn = (weight if weight.stride(-1) == 1 else weight.contiguous()), 0
     if u.numel() < _blocked_elems(len(modules), x2.shape[0], segs.n_segs, cache.rank) or not u.is_contiguous() \
             or u.dtype != x.dtype:
         raise ValueError("u must be a contiguous blocked_u(n_modules, n_tokens, n_segs, rank) buffer of x's dtype")
-    w = weight if weight.stride(-1) == 1 else weight.contiguous()
     if out is None:
         out = torch.empty(*x.shape[:-1], N, dtype=x.dtype, device=x.device)
     o2 = out.reshape(-1, N)
@@ -336,7 +342,7 @@ def linear_lora(x: Tensor, weight: Tensor, bias: Tensor | None, u: Tensor, cache
             raise ValueError(f"the A factors take {cache.hidden} inputs, x has {K}")
         s_start, s_len, _, _, _, _ = segs.ptrs()
         rc = nat.lib().lf_linear_lora_shrink(
-            nat.stream_ptr(dev), nat.dtype_code(x.dtype), x2.data_ptr(), ldx, w.data_ptr(), w.stride(0),
+            nat.stream_ptr(dev), nat.dtype_code(x.dtype), x2.data_ptr(), ldx, w.data_ptr(), w.stride(0), w_kn,
             nat.ptr(b), o2.data_ptr(), o2.stride(0), x2.shape[0], N, K, int(act), u.data_ptr(), cache.rank,
             cache.a_ptr, cache.a_slot_stride, cache.a_module_stride, cache.b_ptr, cache.b_slot_stride,
             cache.b_module_stride, cache.n_slots, len(modules), nat.i32_array(modules), int(module_cols), s_start,
@@ -344,7 +350,7 @@ def linear_lora(x: Tensor, weight: Tensor, bias: Tensor | None, u: Tensor, cache
         nat.check(rc, "lf_linear_lora_shrink")
         return out
     rc = nat.lib().lf_linear_lora(
-        nat.stream_ptr(dev), nat.dtype_code(x.dtype), x2.data_ptr(), ldx, w.data_ptr(), w.stride(0), nat.ptr(b),
+        nat.stream_ptr(dev), nat.dtype_code(x.dtype), x2.data_ptr(), ldx, w.data_ptr(), w.stride(0), w_kn, nat.ptr(b),
         o2.data_ptr(), o2.stride(0), x2.shape[0], N, K, int(act), u.data_ptr(), cache.rank, cache.b_ptr,
         cache.b_slot_stride, cache.b_module_stride, cache.n_slots, len(modules), nat.i32_array(modules),
         int(module_cols), segs.n_segs, tp, pp, nat.ptr(status))

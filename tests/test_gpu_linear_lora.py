@@ -279,8 +279,16 @@ def test_shrink_in_the_gemm_launch_matches_the_two_launches(cuda, R, n_mod, max_
     two = linear_lora(x, W, b, u_two, fc, st, modules, H, status=status)
     u_one = torch.full_like(u_two, float("nan"))  # every block the table names must be written
     one = linear_lora(x, W, b, u_one, fc, st, modules, H, status=status, shrink=True)
+    # the transposed weight (read in the delta factors' operand form), with and without
+    # the shrink in the launch
+    Wt = W.t().contiguous()
+    two_kn = linear_lora(x, None, b, u_two, fc, st, modules, H, status=status, weight_t=Wt)
+    one_kn = linear_lora(x, None, b, torch.full_like(u_two, float("nan")), fc, st, modules, H, status=status,
+                         shrink=True, weight_t=Wt)
     torch.cuda.synchronize()
     assert status.item() == 0, nat.decode_status(status.item())
+    check(two_kn, two, two)
+    check(one_kn, two, two)
     got, want = _u_rows(u_one, st, n_mod, R), _u_rows(u_two, st, n_mod, R)
     assert got.keys() == want.keys()
     for k in want:
