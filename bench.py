@@ -76,12 +76,13 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--mode", choices=["serve", "op", "classify", "register", "xl"], default="serve",
+    ap.add_argument("--mode", choices=["serve", "op", "classify", "register", "xl", "mixed"], default="serve",
                     help="serve: the bge-m3 embedding workload; op: the isolated LoRA op "
                          "Y = X W + (X A_t) B_t at X (64, 256, 1024); classify: 128 x 128 rows, 2,000 tenants "
                          "with heads, rank 8 on query+value; register: adapter registration latency; xl: XLM-R-XL "
                          "shape, rank 32 on query+value, 512 x 256 rows (set --batch 512 --seq 256 --rank 32 "
-                         "--layers 36 --adapters 4000)")
+                         "--layers 36 --adapters 4000); mixed: ranks 8/16/32 from native-rank buckets against "
+                         "one padded store")
     ap.add_argument("--batch", type=int, default=64, help="rows per GPU")
     ap.add_argument("--seq", type=int, default=512)
     ap.add_argument("--adapters", type=int, default=10000)
@@ -795,6 +796,63 @@ def run_classify(args):
 
 
 # ---------------------------------------------------------------------------
+# mixed ranks: native-rank buckets against one padded store
+# ---------------------------------------------------------------------------
+def run_mixed(args):
+    """A fleet of ``--adapters`` adapters with ranks drawn uniformly from 8, 16 and 32
+    on the bge-m3 shape (q/k/v/dense), served at r_max 32 two ways (the reference's
+    ``benchmarks/profiling/mixed_rank_bench.py`` arms): every adapter zero-padded into
+    one rank-32 store, and each at its own rank in a rank bucket with the batch's
+    adapters gathered into an r_max staging cache per batch (``RankBucketStore``).
+    One step = ``embed_tokens`` of the 64 x 512 stratified batch from host tensors."""
+    import latefuse_b200 as lf
+    from latefuse_b200 import _native as nat
+    from latefuse_b200.rank_buckets import RankBucketStore
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n, mix = args.adapters, (8, 16, 32)
+    cfg, model, padded = build_ours(args, dev, rank=32, adapters=n)
+    g = torch.Generator().manual_seed(args.seed + 7)
+    ranks = [mix[int(i)] for i in torch.randint(0, len(mix), (n,), generator=g)]
+    fleet = RankBucketStore(cfg)
+    fleet.fill_random_(ranks, std=0.02, generator=torch.Generator(device=dev).manual_seed(args.seed + 8))
+    ids, mask, tenants = make_inputs(args, args.batch)
+    ids_h, mask_h = ids.pin_memory(), mask.pin_memory()
+    out = {}
+    for name, store in (("padded", padded), ("native_buckets", fleet)):
+        emb = lf.MultiTenantEmbedder(cfg, engine="bert", model=model, store=store, tokenizer=False)
+        for _ in range(args.warmup):
+            emb.embed_tokens(ids_h, mask_h, tenants)
+        torch.cuda.synchronize()
+        ev = events(1)[0]
+        t0 = time.perf_counter()
+        ev[0].record()
+        for _ in range(args.steps):
+            emb.embed_tokens(ids_h, mask_h, tenants)
+        ev[1].record()
+        torch.cuda.synchronize()
+        emb.check_device_status()
+        ms = ev[0].elapsed_time(ev[1]) / args.steps
+        out[name] = {"value": args.batch / (ms * 1e-3), "ms_per_step": ms,
+                     "wall_ms_per_step": (time.perf_counter() - t0) * 1e3 / args.steps,
+                     "adapter_bytes": store.memory_bytes()}
+    uniq = len(set(tenants))
+    print(json.dumps({
+        "mode": "mixed", "metric": "sequences/sec, bge-m3 shape, mixed-rank fleet (r in 8/16/32, r_max 32)",
+        "value": out["native_buckets"]["value"], "unit": "sequences/s", "steps": args.steps, "warmup": args.warmup,
+        "dtype": "bf16",
+        "config": {"workload": f"bge-m3 shape ({args.layers}L) bf16 embedding forward, LoRA on q/k/v/dense, {n} "
+                               f"adapters with ranks uniform over {list(mix)} served at r_max 32, {args.batch} rows x "
+                               f"{args.seq} (lengths U[{args.min_len},{args.seq}]), Zipf(1.1) tenants, CLS + L2",
+                   "unique_tenants": uniq, "rank_counts": {str(r): ranks.count(r) for r in mix}},
+        "arms": out,
+        "memory_native_over_padded": out["native_buckets"]["adapter_bytes"] / out["padded"]["adapter_bytes"],
+        "gpu_launches": nat.launch_count(),
+    }), flush=True)
+
+
+# ---------------------------------------------------------------------------
 # XLM-R-XL scale-out (rank 32 on query+value, 512 x 256 rows)
 # ---------------------------------------------------------------------------
 def xl_config(layers: int = 36):
@@ -1106,6 +1164,8 @@ def main():
         run_register(args)
     elif args.mode == "xl":
         run_xl(args)
+    elif args.mode == "mixed":
+        run_mixed(args)
     else:
         run_serve(args)
 

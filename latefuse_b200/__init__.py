@@ -30,6 +30,7 @@ from latefuse_b200.head import POOLING_STRATEGIES, LRHeadOps, pool_tokens, valid
 from latefuse_b200.heads import HeadStore, LRHead
 from latefuse_b200.loaders import load_peft_adapter, peft_key_fn
 from latefuse_b200.lora import LoraOps, SegmentTable, lora_apply
+from latefuse_b200.rank_buckets import RankBucketStore
 from latefuse_b200.store import AdapterStore, LoraWeight
 from latefuse_b200.tasks import (
     ASSEMBLERS,
@@ -63,6 +64,7 @@ __all__ = [
     "pool_tokens",
     # Stores.
     "AdapterStore",
+    "RankBucketStore",
     "LoraWeight",
     "HeadStore",
     "LRHead",

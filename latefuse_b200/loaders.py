@@ -361,6 +361,20 @@ def registrar_for(store: AdapterStore) -> AdapterRegistrar:
     return reg
 
 
+def peft_rank(path: str, config, adapter_name: str = "default") -> int:
+    """The rank of the PEFT adapter at ``path``: its ``adapter_config.json``'s ``r``, or
+    else the first target module's A in its weights file."""
+    directory = path if os.path.isdir(path) else (os.path.dirname(path) or ".")
+    meta = PeftAdapterConfig.read(directory)
+    if meta is not None and meta.rank is not None:
+        return int(meta.rank)
+    source = _TensorSource(_weights_file(path))
+    first = peft_key_fn(config.hf_config.model_type, adapter_name)(0, config.target_modules[0])[0]
+    if first not in source:
+        raise KeyError(f"the adapter at {path} has no tensor '{first}'")
+    return int(source.shape(first)[0])
+
+
 def load_peft_adapter(store: AdapterStore, adapter_id: str, path: str, *, adapter_name: str = "default",
                       lora_alpha: float | None = None, strict: bool = True, pad_rank: bool = False) -> None:
     """Make the PEFT adapter at ``path`` (directory or weights file) resident in ``store``.
@@ -375,5 +389,10 @@ def load_peft_adapter(store: AdapterStore, adapter_id: str, path: str, *, adapte
         FileNotFoundError: no weights file at ``path``.
         KeyError:          the weights lack a layer's key.
     """
+    from latefuse_b200.rank_buckets import RankBucketStore
+
+    if isinstance(store, RankBucketStore):  # kept at its own rank, in that rank's bucket
+        store.load_peft(adapter_id, path, adapter_name=adapter_name, lora_alpha=lora_alpha, strict=strict)
+        return
     registrar_for(store).register(adapter_id, path, adapter_name=adapter_name, lora_alpha=lora_alpha,
                                   strict=strict, pad_rank=pad_rank)

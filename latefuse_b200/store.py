@@ -334,10 +334,14 @@ class AdapterStore:
         )
 
     def fill_random_(self, n: int, std: float = 0.02, generator: torch.Generator | None = None,
-                     prefix: str = "adapter_") -> list[str]:
-        """Register ``n`` adapters ``{prefix}{i}`` with A and B both ~ N(0, std), drawn
-        in one pass over the cache (a fast path for large synthetic populations)."""
-        ids = [f"{prefix}{i}" for i in range(n)]
+                     prefix: str = "adapter_", ids: list[str] | None = None) -> list[str]:
+        """Register ``n`` adapters ``{prefix}{i}`` (or the given ``ids``) with A and B both
+        ~ N(0, std), drawn in one pass over the cache (a fast path for large synthetic
+        populations)."""
+        if ids is None:
+            ids = [f"{prefix}{i}" for i in range(n)]
+        elif len(ids) != n or len(set(ids)) != n:
+            raise ValueError(f"ids must be {n} distinct adapter ids")
         # every id is checked before any slot is drawn or committed, so a refused
         # call leaves the store exactly as it was
         clash = next((aid for aid in ids if aid in self._slot_of), None)

@@ -27,6 +27,7 @@ from latefuse_b200.config import LoraServingConfig
 from latefuse_b200.engine import EncoderWithLora, HFEncoderWithLora
 from latefuse_b200.head import head_forward, l2_normalize, validate_pooling
 from latefuse_b200.heads import HeadStore
+from latefuse_b200.rank_buckets import store_for_batch
 from latefuse_b200.store import AdapterStore
 
 T = TypeVar("T")
@@ -216,16 +217,23 @@ class TaskPipeline:
                     and input_ids.device.type == "cpu"
                     and (token_type_ids is None or token_type_ids.device.type == "cpu")
                     and getattr(self.model, "supports_packing", False))
+        # a store of native-rank buckets serves each batch from its r_max staging cache
+        store = store_for_batch(self.store, list(tenants))
         if packable:
             # padding-free forward: real tokens only, rows grouped by tenant
-            slots = self.store.slots(list(tenants))
+            slots = store.slots(list(tenants))
             pb = self.model.pack(input_ids, lengths, slots, token_type_ids)
             with torch.no_grad():
                 if head is None:
-                    return self.model.encode_pooled_packed(pb, self.store, pooling)
-                h = self.model.encode_packed(pb, self.store)
+                    return self.model.encode_pooled_packed(pb, store, pooling)
+                h = self.model.encode_packed(pb, store)
                 return self.model.heads_packed(h, pb, pooling, **head)
-        batch = self._get_assembler().batch_lora(list(tenants), input_ids.shape[1], lengths)
+        if store is self.store:
+            assembler = self._get_assembler()
+        else:  # this batch's staging cache
+            kind = IndexSelectBatchAssembler if self._assembler_kind == "index_select" else BatchAssembler
+            assembler = kind(store, cfg)
+        batch = assembler.batch_lora(list(tenants), input_ids.shape[1], lengths)
 
         def dev(t):
             if t is None or t.device == cfg.device:

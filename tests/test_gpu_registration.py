@@ -128,3 +128,46 @@ def test_padded_lower_rank_adapter_serves_like_the_oracle(tmp_path, cuda):
                           .float(), dim=-1)
         assert row_rel(ours[rows], ref) < 2e-2, t
     oracle.close()
+
+
+def test_native_rank_buckets_serve_like_the_padded_store(tmp_path, cuda):
+    """Rank 4, 8 and 16 PEFT adapters kept at their own ranks (RankBucketStore) and
+    padded per batch: the packed forward gives the same bits as the same adapters
+    zero-padded into one rank-16 store, and matches the oracle's unpadded forward;
+    a following batch that puts a lower-rank tenant in a staging slot a rank-16 tenant
+    held gets no trace of it."""
+    from latefuse_b200.rank_buckets import RankBucketStore
+
+    base, cfg, emb_pad = small_pipeline(cuda, rank=16)
+    fleet = RankBucketStore(cfg)
+    emb = lf.MultiTenantEmbedder(cfg, engine="bert", model=emb_pad.model, store=fleet, tokenizer=False)
+    sds = {}
+    for t, r, alpha, seed in (("r4", 4, 8, 11), ("r8", 8, 24, 12), ("r16", 16, 16, 13)):
+        sds[t] = (peft_dir(tmp_path / t, cfg.num_layers, cfg.hidden_size, r, alpha, seed=seed), r, alpha)
+        emb.register_adapter(t, str(tmp_path / t))
+        emb_pad.register_adapter(t, str(tmp_path / t), pad_rank=True)
+    assert [fleet.rank_of(t) for t in ("r4", "r8", "r16")] == [4, 8, 16]
+    assert fleet.memory_bytes() * 48 == emb_pad.store.memory_bytes() * 28
+
+    gen = torch.Generator().manual_seed(6)
+    lengths = [400, 33, 257, 128, 7, 300]
+    ids = torch.randint(5, 1000, (6, 512), generator=gen)
+    ids[:, 0] = 0
+    mask = (torch.arange(512).unsqueeze(0) < torch.tensor(lengths).unsqueeze(1)).long()
+    ids = torch.where(mask.bool(), ids, torch.ones_like(ids))
+    for tenants in (["r16", "r8", "r16", "r4", "r8", "r4"], ["r4", "r4", "r8", "r8", "r4", "r8"]):
+        ours = emb.embed_tokens(ids, mask, tenants)
+        pad = emb_pad.embed_tokens(ids, mask, tenants)
+        emb.check_device_status()
+        assert torch.equal(ours, pad), tenants
+    adapters = {t: {"wa": {}, "wb": {}} for t in sds}
+    for t, (sd, r, alpha) in sds.items():
+        for m in TARGETS:
+            adapters[t]["wa"][m], adapters[t]["wb"][m] = reference_fold(sd, cfg.num_layers, r, alpha, m)
+    oracle = HookedEncoder(base, adapters, TARGETS)
+    for t in ("r4", "r8"):
+        rows = [i for i, x in enumerate(tenants) if x == t]
+        ref = F.normalize(oracle.encode_pooled(ids[rows].to(cuda), mask[rows].to(cuda), [t] * len(rows), "cls")
+                          .float(), dim=-1)
+        assert row_rel(ours[rows], ref) < 2e-2, t
+    oracle.close()

@@ -466,3 +466,62 @@ def test_stream_to_host_yields_every_result_in_order_with_bounded_lookahead():
     assert [h[0, 0].item() for h in stream_to_host(step, [(7,)], depth=1)] == [7.0]
     with pytest.raises(ValueError, match="depth"):
         list(stream_to_host(step, [(0,)], depth=0))
+
+
+# ------------------------------------------------------- native-rank buckets ---
+def test_rank_buckets_keep_each_adapter_at_its_own_rank(tmp_path):
+    """PEFT adapters of ranks 2 and 4 in an r_max-8 fleet: each in its own bucket at its
+    own rank (the padded store holds both at 8), re-registration at another rank moves
+    buckets, and the errors name the tenant or the rank."""
+    from latefuse_b200.rank_buckets import RankBucketStore
+
+    c = cfg(rank=8)
+    fleet = RankBucketStore(c)
+    d2, sd2 = _peft_dir(tmp_path, c, rank=2, alpha=4, seed=1)
+    d4, _ = _peft_dir(tmp_path, c, rank=4, alpha=8, seed=2)
+    lf.load_peft_adapter(fleet, "two", str(d2))
+    lf.load_peft_adapter(fleet, "four", str(d4))
+    assert fleet.rank_of("two") == 2 and fleet.rank_of("four") == 4 and fleet.ranks() == [2, 4]
+    assert fleet.get("two").wa["query"].shape == (c.num_layers, c.hidden_size, 2)
+    padded = lf.AdapterStore(c)
+    lf.load_peft_adapter(padded, "two", str(d2), pad_rank=True)
+    lf.load_peft_adapter(padded, "four", str(d4), pad_rank=True)
+    assert fleet.memory_bytes() * 8 == padded.memory_bytes() * (2 + 4) // 2
+    ka, kb = lf.peft_key_fn("bert")(1, "value")
+    torch.testing.assert_close(fleet.get("two").wb["value"][1], (sd2[kb] * 2).T.contiguous())
+    lf.load_peft_adapter(fleet, "two", str(d4))  # now rank 4: it leaves the rank-2 bucket
+    assert fleet.rank_of("two") == 4 and fleet.ranks() == [4] and len(fleet) == 2
+    fleet.evict("four")
+    assert "four" not in fleet and fleet.adapter_ids() == ["two"]
+    with pytest.raises(KeyError, match="nobody"):
+        fleet.batch_store(["two", "nobody"])
+    d16, _ = _peft_dir(tmp_path, c, rank=16, alpha=16, seed=3)
+    with pytest.raises(ValueError, match="rank"):
+        lf.load_peft_adapter(fleet, "big", str(d16))
+    assert "big" not in fleet
+
+
+def test_rank_bucket_batch_store_pads_to_r_max_and_reuses_slots_cleanly():
+    """The batch staging cache: slot u holds the batch's u-th distinct adapter, its A
+    columns and B rows beyond its rank zero, also when the slot held a higher-rank
+    adapter in the batch before; the padded slots equal a pad_rank store's."""
+    from latefuse_b200.rank_buckets import RankBucketStore
+
+    c = cfg(rank=8)
+    fleet = RankBucketStore(c)
+    ids = fleet.fill_random_([8, 2, 4, 8, 2], std=0.1, generator=torch.Generator().manual_seed(3))
+    assert [fleet.rank_of(a) for a in ids] == [8, 2, 4, 8, 2]
+    first = fleet.batch_store([ids[0], ids[3], ids[0]])
+    assert first.slots([ids[0], ids[3], ids[0]]) == [0, 1, 0]
+    stage = fleet.batch_store([ids[2], ids[1], ids[1], ids[4]])  # slots 0, 1 held rank-8 adapters
+    assert stage.slots([ids[1], ids[4], ids[2]]) == [0, 1, 2]  # grouped by rank
+    for a in (ids[1], ids[2], ids[4]):
+        r, mine, got = fleet.rank_of(a), fleet.get(a), stage.get(a)
+        for m in c.target_modules:
+            assert torch.equal(got.wa[m][..., :r], mine.wa[m]) and not got.wa[m][..., r:].any()
+            assert torch.equal(got.wb[m][:, :r], mine.wb[m]) and not got.wb[m][:, r:].any()
+    # the kernels' view of the staging cache is that of a padded store
+    fc = stage.factor_cache(1)
+    assert fc.rank == 8 and fc.n_slots >= 3
+    with pytest.raises(TypeError, match="batch_store"):
+        fleet.slots(ids)
