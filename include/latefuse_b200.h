@@ -439,6 +439,20 @@ int lf_add_layernorm(void* stream, int dtype, const void* a, int64_t lda, const 
                      const void* vec, const void* gamma, const void* beta, float eps, int64_t n_rows,
                      int hidden, void* out, int64_t ldo);
 
+/* The encoder's embeddings and their LayerNorm in one pass over gathered rows:
+ *     e = round(round(word[ids[r]] + type[types[r]]) + pos[positions[r]])
+ *     out[r] = LayerNorm(e) with gamma, beta, eps
+ * (each sum rounded to dtype as torch rounds it: src/latefuse/model/encoder.py:270-282,
+ * the HF embeddings `inputs_embeds + token_type_embeddings`, `+ position_embeddings`,
+ * `LayerNorm`).  ids / positions / types are device int32 (types may be NULL: row 0);
+ * an index outside its table reads row 0 and sets LF_STATUS_BAD_SLOT in status.
+ * Layout rules as lf_add_layernorm. */
+int lf_embed_layernorm(void* stream, int dtype, const void* word, int64_t ld_word, int64_t n_word,
+                       const int32_t* ids, const void* pos, int64_t ld_pos, int64_t n_pos,
+                       const int32_t* positions, const void* type, int64_t ld_type, int64_t n_type,
+                       const int32_t* types, const void* gamma, const void* beta, float eps,
+                       int64_t n_rows, int hidden, void* out, int64_t ldo, int32_t* status);
+
 /* out = x * 0.5 * (1 + erf(x / sqrt(2))) in f32, rounded to dtype: the exact
  * GELU of the FFN (ACT2FN["gelu"], src/latefuse/model/encoder.py:122,139).
  * n % 8 == 0; x and out 16-byte aligned; out may alias x. */

@@ -104,6 +104,10 @@ SIGNATURES: dict[str, tuple] = {
     "lf_add_layernorm": (c_int, [
         c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, ctypes.c_float,
         c_int64, c_int, c_void_p, c_int64]),
+    "lf_embed_layernorm": (c_int, [
+        c_void_p, c_int, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
+        c_int64, c_int64, c_void_p, c_void_p, c_void_p, ctypes.c_float, c_int64, c_int, c_void_p, c_int64,
+        c_void_p]),
     "lf_gelu": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int64]),
     "lf_attention_varlen": (c_int, [
         c_void_p, c_int, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_int,

@@ -133,6 +133,16 @@ struct NormParams {
   int32_t hidden;
   void* out;
   int64_t ldo;
+  // embeddings (MODE 3): row r is LN(round(round(a[ia[r]] + c[ic[r]]) + b[ib[r]])),
+  // tables a / b / c with n_a / n_b / n_c rows; an index outside its table reads row 0
+  // and sets LF_STATUS_BAD_SLOT
+  const int32_t* ia;
+  const int32_t* ib;
+  const int32_t* ic;
+  const void* c;
+  int64_t ldc;
+  int64_t n_a, n_b, n_c;
+  int32_t* status;
 };
 
 struct SimtParams {

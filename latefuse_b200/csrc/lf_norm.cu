@@ -99,7 +99,9 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 constexpr int kNormWarps = 8;
 
-// MODE 0: a alone; 1: a + b (a second matrix); 2: a + v (one row vector).
+// MODE 0: a alone; 1: a + b (a second matrix); 2: a + v (one row vector); 3: the
+// embeddings, round(round(a[ia] + c[ic]) + b[ib]) of gathered table rows (the
+// encoder's word + token type, then + position, each sum rounded as torch rounds it).
 template <typename T, int NC, int MODE>
 __global__ void __launch_bounds__(32 * kNormWarps)
 add_layernorm_kernel(const NormParams p, int full) {
@@ -109,22 +111,37 @@ add_layernorm_kernel(const NormParams p, int full) {
   const int lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * kNormWarps + (threadIdx.x >> 5);
   if (row >= p.n_rows) return;
-  const T* a = reinterpret_cast<const T*>(p.a) + row * p.lda;
-  const T* b = MODE == 1 ? reinterpret_cast<const T*>(p.b) + row * p.ldb
+  int64_t ra_row = row, rb_row = row, rc_row = 0;
+  if constexpr (MODE == 3) {
+    ra_row = __ldg(p.ia + row);
+    rb_row = __ldg(p.ib + row);
+    rc_row = p.ic != nullptr ? __ldg(p.ic + row) : 0;
+    const bool bad = ra_row < 0 || ra_row >= p.n_a || rb_row < 0 || rb_row >= p.n_b || rc_row < 0 || rc_row >= p.n_c;
+    if (bad) {
+      if (lane == 0) set_status(p.status, LF_STATUS_BAD_SLOT);
+      ra_row = (ra_row < 0 || ra_row >= p.n_a) ? 0 : ra_row;
+      rb_row = (rb_row < 0 || rb_row >= p.n_b) ? 0 : rb_row;
+      rc_row = (rc_row < 0 || rc_row >= p.n_c) ? 0 : rc_row;
+    }
+  }
+  const T* a = reinterpret_cast<const T*>(p.a) + ra_row * p.lda;
+  const T* b = MODE == 1 || MODE == 3 ? reinterpret_cast<const T*>(p.b) + rb_row * p.ldb
                : MODE == 2 ? reinterpret_cast<const T*>(p.vec) : nullptr;
+  const T* cc = MODE == 3 ? reinterpret_cast<const T*>(p.c) + rc_row * p.ldc : nullptr;
   const T* gamma = reinterpret_cast<const T*>(p.gamma);
   const T* beta = reinterpret_cast<const T*>(p.beta);
   T* out = reinterpret_cast<T*>(p.out) + row * p.ldo;
   const int H = p.hidden;
 
   // every load of the row (and gamma / beta) is issued before any arithmetic
-  Raw8<T> ra[NC], rb[NC];
+  Raw8<T> ra[NC], rb[NC], rc[MODE == 3 ? NC : 1];
 #pragma unroll
   for (int c = 0; c < NC; ++c) {
     const int col = c * 256 + lane * 8;
     if (full || col < H) {
       ra[c].load(a + col);
       if (HAS_B) rb[c].load(b + col);
+      if constexpr (MODE == 3) rc[c].load(cc + col);
     }
   }
   // gamma and beta too, so that their latency overlaps the reductions instead
@@ -149,6 +166,12 @@ add_layernorm_kernel(const NormParams p, int full) {
     const int col = c * 256 + lane * 8;
     if (full || col < H) {
       ra[c].unpack(v[c]);
+      if constexpr (MODE == 3) {
+        float w[8];
+        rc[c].unpack(w);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[c][i] = round_through<T>(v[c][i] + w[i]);
+      }
       if (HAS_B) {
         float w[8];
         rb[c].unpack(w);
@@ -254,7 +277,8 @@ int launch_norm(const NormParams& p, cudaStream_t s) {
   switch (nc) {
 #define LF_NORM_CASE(N)                                                                  \
   case N:                                                                                \
-    e = launch_pdl(p.b != nullptr ? add_layernorm_kernel<T, N, 1>                        \
+    e = launch_pdl(p.ia != nullptr ? add_layernorm_kernel<T, N, 3>                       \
+                   : p.b != nullptr ? add_layernorm_kernel<T, N, 1>                      \
                    : p.vec != nullptr ? add_layernorm_kernel<T, N, 2> : add_layernorm_kernel<T, N, 0>, \
                    grid, block, 0, s, p, full);                                          \
     break;
@@ -356,7 +380,7 @@ extern "C" int lf_add_layernorm(void* stream, int dtype, const void* a, int64_t 
       (lda * es) % 16 != 0 || (ldo * es) % 16 != 0 || (b != nullptr && (ldb * es) % 16 != 0))
     return set_error(LF_ERR_INVALID, "lf_add_layernorm: pointers and row strides must be 16-byte aligned");
   if (n_rows == 0) return LF_OK;
-  NormParams p;
+  NormParams p = {};
   p.a = a;
   p.b = b;
   p.lda = lda;
@@ -369,6 +393,53 @@ extern "C" int lf_add_layernorm(void* stream, int dtype, const void* a, int64_t 
   p.hidden = hidden;
   p.out = out;
   p.ldo = ldo;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == LF_DTYPE_BF16) return launch_norm<__nv_bfloat16>(p, s);
+  if (dtype == LF_DTYPE_F16) return launch_norm<__half>(p, s);
+  return launch_norm<float>(p, s);
+}
+
+extern "C" int lf_embed_layernorm(void* stream, int dtype, const void* word, int64_t ld_word, int64_t n_word,
+                                  const int32_t* ids, const void* pos, int64_t ld_pos, int64_t n_pos,
+                                  const int32_t* positions, const void* type, int64_t ld_type, int64_t n_type,
+                                  const int32_t* types, const void* gamma, const void* beta, float eps,
+                                  int64_t n_rows, int hidden, void* out, int64_t ldo, int32_t* status) {
+  if (dtype != LF_DTYPE_BF16 && dtype != LF_DTYPE_F16 && dtype != LF_DTYPE_F32)
+    return set_error(LF_ERR_INVALID, "lf_embed_layernorm: unknown dtype %d", dtype);
+  if (word == nullptr || pos == nullptr || type == nullptr || ids == nullptr || positions == nullptr ||
+      gamma == nullptr || beta == nullptr || out == nullptr)
+    return set_error(LF_ERR_INVALID, "lf_embed_layernorm: null table, index, gamma, beta or out");
+  if (n_rows < 0 || hidden <= 0 || hidden % 8 != 0 || n_word <= 0 || n_pos <= 0 || n_type <= 0)
+    return set_error(LF_ERR_INVALID, "lf_embed_layernorm: hidden %d must be a positive multiple of 8", hidden);
+  if (hidden > 4096) return set_error(LF_ERR_UNSUPPORTED, "lf_embed_layernorm: hidden %d above 4096", hidden);
+  if (ld_word < hidden || ld_pos < hidden || ld_type < hidden || ldo < hidden)
+    return set_error(LF_ERR_INVALID, "lf_embed_layernorm: a row stride is below hidden %d", hidden);
+  const int es = dtype == LF_DTYPE_F32 ? 4 : 2;
+  if (!aligned16(word) || !aligned16(pos) || !aligned16(type) || !aligned16(out) || !aligned16(gamma) ||
+      !aligned16(beta) || (ld_word * es) % 16 || (ld_pos * es) % 16 || (ld_type * es) % 16 || (ldo * es) % 16)
+    return set_error(LF_ERR_INVALID, "lf_embed_layernorm: pointers and row strides must be 16-byte aligned");
+  if (n_rows == 0) return LF_OK;
+  NormParams p = {};
+  p.a = word;
+  p.lda = ld_word;
+  p.n_a = n_word;
+  p.ia = ids;
+  p.b = pos;
+  p.ldb = ld_pos;
+  p.n_b = n_pos;
+  p.ib = positions;
+  p.c = type;
+  p.ldc = ld_type;
+  p.n_c = n_type;
+  p.ic = types;  // null: every row takes type row 0
+  p.gamma = gamma;
+  p.beta = beta;
+  p.eps = eps;
+  p.n_rows = n_rows;
+  p.hidden = hidden;
+  p.out = out;
+  p.ldo = ldo;
+  p.status = status;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == LF_DTYPE_BF16) return launch_norm<__nv_bfloat16>(p, s);
   if (dtype == LF_DTYPE_F16) return launch_norm<__half>(p, s);

@@ -45,6 +45,30 @@ def add_layernorm(a: Tensor, b: Tensor | None, weight: Tensor, bias: Tensor, eps
     return out
 
 
+def embed_layernorm(ids: Tensor, positions: Tensor, types: Tensor | None, word: Tensor, pos: Tensor,
+                    type_: Tensor, weight: Tensor, bias: Tensor, eps: float, status: Tensor | None = None) -> Tensor:
+    """``layer_norm((word[ids] + type_[types]) + pos[positions])`` for int32 index vectors
+    (each sum rounded to the tables' dtype, as torch's embedding adds are), one native
+    launch.  ``types`` None takes type row 0 everywhere.  Returns ``(len(ids), H)``."""
+    dev = nat.require_cuda(ids, positions, types, word, pos, type_, weight, bias, status)
+    for t in (ids, positions, types):
+        if t is not None and (t.dtype != torch.int32 or not t.is_contiguous()):
+            raise ValueError("ids, positions and types must be contiguous int32 tensors")
+    n, H = ids.shape[0], word.shape[1]
+    if positions.shape[0] != n or (types is not None and types.shape[0] != n):
+        raise ValueError(f"{n} ids but {positions.shape[0]} positions")
+    out = torch.empty(n, H, dtype=word.dtype, device=word.device)
+    w = weight if weight.dtype == word.dtype else weight.to(word.dtype)
+    bb = bias if bias.dtype == word.dtype else bias.to(word.dtype)
+    rc = nat.lib().lf_embed_layernorm(
+        nat.stream_ptr(dev), nat.dtype_code(word.dtype), word.data_ptr(), word.stride(0), word.shape[0],
+        ids.data_ptr(), pos.data_ptr(), pos.stride(0), pos.shape[0], positions.data_ptr(), type_.data_ptr(),
+        type_.stride(0), type_.shape[0], nat.ptr(types), w.contiguous().data_ptr(), bb.contiguous().data_ptr(),
+        float(eps), n, H, out.data_ptr(), out.stride(0), nat.ptr(status))
+    nat.check(rc, "lf_embed_layernorm")
+    return out
+
+
 def gelu(x: Tensor, out: Tensor | None = None) -> Tensor:
     """Exact (erf) GELU of a contiguous tensor."""
     dev = nat.require_cuda(x, out)

@@ -33,7 +33,8 @@ from latefuse_b200.config import LoraServingConfig
 from latefuse_b200.head import LRHeadOps, head_forward, head_forward_rows, pool_tokens, validate_pooling
 from latefuse_b200.lora import (FactorCache, SegmentTable, blocked_u, fused_shrink_ok, linear_lora, lora_apply,
                                  lora_apply_into, lora_shrink_blocked, per_row_cache, workspace_bytes)
-from latefuse_b200.encoder_ops import ACT_GELU, add_layernorm, attention_varlen, gelu, linear, linear_accumulate
+from latefuse_b200.encoder_ops import (ACT_GELU, add_layernorm, attention_varlen, embed_layernorm, gelu, linear,
+                                       linear_accumulate)
 from latefuse_b200.packing import PackedBatch, pack_rows
 
 # Per-layer module paths (relative to "encoder.layer.{i}.") for each logical target.
@@ -594,9 +595,16 @@ class EncoderWithLora(nn.Module):
         """
         T = pb.n_tokens
         H, nh, hd = self.config.hidden_size, self.num_heads, self.head_dim
-        x = self.word_embeddings(pb.ids) + self.token_type_embeddings(pb.token_types)
-        h = add_layernorm(x, self.position_embeddings(pb.positions), self.emb_ln.weight, self.emb_ln.bias,
-                          self.eps)
+        if self._runner.status is None or self._runner.status.device != pb.ids.device:
+            self._runner.status = torch.zeros(1, dtype=torch.int32, device=pb.ids.device)
+        if H % 8 == 0 and H <= 4096:  # gathers, both adds and the LayerNorm in one launch
+            h = embed_layernorm(pb.ids, pb.positions, pb.token_types, self.word_embeddings.weight,
+                                self.position_embeddings.weight, self.token_type_embeddings.weight,
+                                self.emb_ln.weight, self.emb_ln.bias, self.eps, status=self._runner.status)
+        else:
+            x = self.word_embeddings(pb.ids) + self.token_type_embeddings(pb.token_types)
+            h = add_layernorm(x, self.position_embeddings(pb.positions), self.emb_ln.weight, self.emb_ln.bias,
+                              self.eps)
 
         do_lora = apply_lora and store is not None and (self._qkv_targets or self._dense_target)
         if do_lora:

@@ -10,7 +10,7 @@ import torch
 import torch.nn.functional as F
 
 from latefuse_b200 import _native as nat
-from latefuse_b200.encoder_ops import add_layernorm, gelu
+from latefuse_b200.encoder_ops import add_layernorm, embed_layernorm, gelu
 
 pytestmark = pytest.mark.gpu
 
@@ -114,3 +114,40 @@ def test_layernorm_with_row_vector_matches_torch(cuda, dtype):
     tol = 1e-5 if dtype == torch.float32 else 2e-2
     torch.testing.assert_close(ours, ref, atol=tol, rtol=tol)
     assert (ours.float() - ref.float()).abs().max().item() <= (1e-5 if dtype == torch.float32 else 2 ** -6 * 8)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("H", [256, 1024, 2560])
+def test_embed_layernorm_is_the_gathers_adds_and_layernorm(cuda, dtype, H):
+    """One launch for the packed forward's embeddings: the same bits as this library's
+    add+LayerNorm on torch's own gathers and first add (the rounding points of the
+    encoder's embeddings), token types given or all zero; an index outside its table
+    is reported in the status word and reads row 0."""
+    g = torch.Generator(device=cuda).manual_seed(H)
+    V, P, n = 5000, 600, 3000
+    word = torch.randn(V, H, device=cuda, generator=g).to(dtype)
+    pos = torch.randn(P, H, device=cuda, generator=g).to(dtype)
+    typ = torch.randn(2, H, device=cuda, generator=g).to(dtype)
+    w = (1 + 0.1 * torch.randn(H, device=cuda, generator=g)).to(dtype)
+    b = (0.1 * torch.randn(H, device=cuda, generator=g)).to(dtype)
+    ids = torch.randint(0, V, (n,), device=cuda, generator=g, dtype=torch.int32)
+    positions = torch.randint(0, P, (n,), device=cuda, generator=g, dtype=torch.int32)
+    types = torch.randint(0, 2, (n,), device=cuda, generator=g, dtype=torch.int32)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    for tt in (types, None):
+        ours = embed_layernorm(ids, positions, tt, word, pos, typ, w, b, 1e-5, status=status)
+        x = word[ids.long()] + typ[tt.long() if tt is not None else torch.zeros_like(ids).long()]
+        want = add_layernorm(x, pos[positions.long()], w, b, 1e-5)
+        assert torch.equal(ours, want)
+        ref = F.layer_norm((x.float() + pos[positions.long()].float()).to(dtype).float(), (H,), w.float(), b.float(),
+                           1e-5)
+        lo, hi = TOL[dtype]
+        assert (ours.float() - ref).abs().max().item() <= lo
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    bad = ids.clone()
+    bad[7] = V + 3
+    ours = embed_layernorm(bad, positions, types, word, pos, typ, w, b, 1e-5, status=status)
+    torch.cuda.synchronize()
+    assert status.item() == nat.LF_STATUS_BAD_SLOT
+    assert torch.isfinite(ours.float()).all()
