@@ -99,6 +99,11 @@ extern "C" {
 #define LF_OPT_REQUIRE_TC 3     /* 1: fail with LF_ERR_UNSUPPORTED instead of running the
                                    CUDA-core kernels where the tcgen05 kernels do not apply */
 #define LF_OPT_PERSISTENT 4     /* 0: do not use the persistent expand kernel (default 1) */
+#define LF_OPT_FUSED_APPLY 5    /* 1 (default): lf_lora_apply runs as one launch (shrink and
+                                   expand in one kernel, u kept on chip) where that kernel
+                                   applies; 0: a shrink launch and an expand launch */
+#define LF_OPT_FUSED_SPLIT 6    /* 0 = automatic, else the column chunks each tile record of
+                                   the one-launch lf_lora_apply is split into */
 
 /* ------------------------------------------------------------------------ */
 /* library                                                                   */
@@ -188,7 +193,12 @@ size_t lf_lora_workspace_bytes(int dtype, int64_t n_tokens, int rank, int n_modu
  * y, i.e. y[t, off_m + :] += B(slot(t), m)^T (A(slot(t), m)^T x[t]) for up to 4
  * modules that share the input x (query/key/value of one layer share one read of
  * x).  One call replaces, per layer, the reference's cat -> bmm -> bmm -> add
- * sequence of every hook (src/latefuse/model/hf_wrapper.py:213-217). */
+ * sequence of every hook (src/latefuse/model/hf_wrapper.py:213-217).  With tile
+ * records, bf16/f16, rank 8/16/32/64, hidden a multiple of 64, 16-byte aligned
+ * buffers and x not overlapping y, it runs as ONE kernel that keeps u on chip
+ * (the workspace is then unused; LF_OPT_FUSED_APPLY = 0 selects the shrink and
+ * expand launches, which give the same bits); otherwise as a shrink launch into
+ * `workspace` and an expand launch. */
 int lf_lora_apply(void* stream, int dtype,
                   const void* x, int64_t ldx,
                   void* y, int64_t ldy,
@@ -208,7 +218,8 @@ int lf_lora_apply(void* stream, int dtype,
  * allocate device memory (a host framework that owns every allocation, or code
  * that must not call cudaMalloc while serving).  It has no counterpart in the
  * reference.  Same arguments, contract and results as lf_lora_apply minus the
- * workspace: the shrink output lives in a file-scope device array of
+ * workspace.  It always runs lf_lora_apply's shrink launch and expand launch
+ * (never the one-launch kernel), and the shrink output lives in a file-scope device array of
  * LF_NOALLOC_SCRATCH_BYTES that every GPU using the library holds until the
  * process exits.  Batches needing more scratch than that
  * (lf_lora_workspace_bytes) are rejected with LF_ERR_WORKSPACE.  The first call

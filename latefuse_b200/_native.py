@@ -25,6 +25,8 @@ LF_OPT_FORCE_SIMT = 1
 LF_OPT_SHRINK_CLUSTER = 2
 LF_OPT_REQUIRE_TC = 3
 LF_OPT_PERSISTENT = 4
+LF_OPT_FUSED_APPLY = 5
+LF_OPT_FUSED_SPLIT = 6
 
 LF_STATUS_BAD_SLOT, LF_STATUS_BAD_SEGMENT, LF_STATUS_TIMEOUT, LF_STATUS_BAD_HEAD = 1, 2, 4, 8
 

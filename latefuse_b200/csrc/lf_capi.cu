@@ -18,6 +18,8 @@ static std::atomic<int> g_force_simt{0};
 static std::atomic<int> g_shrink_cluster{0};
 static std::atomic<int> g_require_tc{0};
 static std::atomic<int> g_persistent{1};
+static std::atomic<int> g_fused_apply{1};
+static std::atomic<int> g_fused_split{0};
 
 int set_error(int code, const char* fmt, ...) {
   va_list ap;
@@ -421,6 +423,168 @@ static int expand_impl(cudaStream_t stream, int dtype, const void* u, void* y, i
   return run_expand_tc(dtype, p, rank, nt, stream);
 }
 
+// ---------------------------------------------------------------------------
+// one-launch apply
+// ---------------------------------------------------------------------------
+static bool ranges_overlap(const void* a, size_t na, const void* b, size_t nb) {
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
+  return a0 < b0 + nb && b0 < a0 + na;
+}
+
+// Column chunks per tile record: the fewest that give every SM an item, each a
+// multiple of 64 columns and at least 128 wide (or the LF_OPT_FUSED_SPLIT choice).
+static int fused_chunks(int hidden, int n_tiles) {
+  const int forced = g_fused_split.load();
+  if (forced > 0) return (hidden % (64 * forced) == 0) ? forced : -1;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int c = 1;
+  while (int64_t(n_tiles) * c < sms && hidden % (64 * 2 * c) == 0 && hidden / (2 * c) >= 128) c *= 2;
+  return c;
+}
+
+// Launches lf_lora_apply's one-launch kernel and returns LF_OK, an error code if the
+// launch failed, or -1 (nothing launched) where the two-launch path must run.
+static int fused_apply(cudaStream_t stream, int dtype, const void* x, int64_t ldx, void* y, int64_t ldy,
+                       int64_t n_tokens, int hidden, int rank, const void* cache_a, int64_t a_slot_stride,
+                       int64_t a_module_stride, const void* cache_b, int64_t b_slot_stride, int64_t b_module_stride,
+                       int n_slots, int n_modules, const int32_t* modules, const int64_t* y_col_offsets,
+                       const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot, int n_segs,
+                       const int32_t* tiles, int n_tiles, int32_t* status) {
+  if (!g_fused_apply.load() || !g_persistent.load() || option_force_simt()) return -1;
+  if (dtype == LF_DTYPE_F32 || !tc_rank(rank) || hidden % 64 != 0 || tiles == nullptr || n_tiles <= 0) return -1;
+  const int es = elem_size(dtype);
+  int64_t y_cols = 0;
+  for (int m = 0; m < n_modules; ++m) {
+    if (y_col_offsets[m] < 0 || y_col_offsets[m] % 8 != 0) return -1;
+    if (y_col_offsets[m] + hidden > y_cols) y_cols = y_col_offsets[m] + hidden;
+  }
+  if (ldy < y_cols) return -1;  // the two-launch path reports it
+  if (!aligned16(x) || !aligned16(y) || !aligned16(cache_a) || !aligned16(cache_b) || (ldx * es) % 16 != 0 ||
+      (ldy * es) % 16 != 0 || (a_slot_stride * es) % 16 != 0 || (a_module_stride * es) % 16 != 0 ||
+      (b_slot_stride * es) % 16 != 0 || (b_module_stride * es) % 16 != 0)
+    return -1;
+  if (n_slots > 1 && (a_slot_stride < int64_t(hidden) * rank || b_slot_stride < int64_t(hidden) * rank)) return -1;
+  // y is written while other items still read x: they must not share memory
+  if (ranges_overlap(x, size_t(((n_tokens - 1) * ldx + hidden) * es), y, size_t(((n_tokens - 1) * ldy + y_cols) * es)))
+    return -1;
+  const int chunks = fused_chunks(hidden, n_tiles);
+  if (chunks <= 0) return -1;
+  FusedApplyParams p;
+  memset(&p, 0, sizeof(p));
+  {
+    cuuint64_t dims[2] = {cuuint64_t(hidden), cuuint64_t(n_tokens)};
+    cuuint64_t strides[1] = {cuuint64_t(ldx) * es};
+    cuuint32_t box[2] = {64, 128};
+    int rc = encode(&p.x_map, dtype, 2, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "x");
+    if (rc) return rc;
+  }
+  {
+    cuuint64_t dims[2] = {cuuint64_t(y_cols), cuuint64_t(n_tokens)};
+    cuuint64_t strides[1] = {cuuint64_t(ldy) * es};
+    cuuint32_t box[2] = {64, 128};
+    int rc = encode(&p.y_map, dtype, 2, y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "y");
+    if (rc) return rc;
+    cuuint32_t sbox[2] = {64, 32};
+    rc = encode(&p.ys_map, dtype, 2, y, dims, strides, sbox, CU_TENSOR_MAP_SWIZZLE_128B, "y (stores)");
+    if (rc) return rc;
+  }
+  const int64_t a_ss = n_slots == 1 ? int64_t(hidden) * rank : a_slot_stride;
+  const int64_t b_ss = n_slots == 1 ? int64_t(hidden) * rank : b_slot_stride;
+  for (int m = 0; m < n_modules; ++m) {
+    const void* a = static_cast<const uint8_t*>(cache_a) + int64_t(modules[m]) * a_module_stride * es;
+    cuuint64_t adims[3] = {cuuint64_t(rank), cuuint64_t(hidden), cuuint64_t(n_slots)};
+    cuuint64_t astrides[2] = {cuuint64_t(rank) * es, cuuint64_t(a_ss) * es};
+    cuuint32_t abox[3] = {cuuint32_t(rank), 64, 1};
+    int rc = encode(&p.a_map[m], dtype, 3, a, adims, astrides, abox, a_tma_swizzle(rank), "a");
+    if (rc) return rc;
+    const void* b = static_cast<const uint8_t*>(cache_b) + int64_t(modules[m]) * b_module_stride * es;
+    cuuint64_t bdims[3] = {cuuint64_t(hidden), cuuint64_t(rank), cuuint64_t(n_slots)};
+    cuuint64_t bstrides[2] = {cuuint64_t(hidden) * es, cuuint64_t(b_ss) * es};
+    cuuint32_t bbox[3] = {64, cuuint32_t(rank), 1};
+    rc = encode(&p.b_map[m], dtype, 3, b, bdims, bstrides, bbox, CU_TENSOR_MAP_SWIZZLE_128B, "b");
+    if (rc) return rc;
+    p.y_col_off[m] = y_col_offsets[m];
+  }
+  // modules whose cache indices step evenly share one 4D map of A (as the shrink does)
+  int d = n_modules > 1 ? modules[1] - modules[0] : 1;
+  for (int m = 2; m < n_modules && d > 0; ++m)
+    if (modules[m] - modules[m - 1] != d) d = 0;
+  const int64_t mstride = n_modules == 1 ? int64_t(hidden) * rank * es : int64_t(d) * a_module_stride * es;
+  if (d > 0 && mstride >= int64_t(hidden) * rank * es && mstride % 16 == 0) {
+    const void* a = static_cast<const uint8_t*>(cache_a) + int64_t(modules[0]) * a_module_stride * es;
+    cuuint64_t dims[4] = {cuuint64_t(rank), cuuint64_t(hidden), cuuint64_t(n_modules), cuuint64_t(n_slots)};
+    cuuint64_t strides[3] = {cuuint64_t(rank) * es, cuuint64_t(mstride), cuuint64_t(a_ss) * es};
+    cuuint32_t box[4] = {cuuint32_t(rank), 64, cuuint32_t(n_modules), 1};
+    int rc = encode(&p.a_modules_map, dtype, 4, a, dims, strides, box, a_tma_swizzle(rank), "a (modules)");
+    if (rc) return rc;
+    p.a_one_box = 1;
+  }
+  p.n_tokens = n_tokens;
+  p.hidden = hidden;
+  p.n_modules = n_modules;
+  p.n_slots = n_slots;
+  p.n_tiles = n_tiles;
+  p.n_chunks = chunks;
+  p.chunk_cols = hidden / chunks;
+  p.tiles = tiles;
+  p.seg_start = seg_start;
+  p.seg_len = seg_len;
+  p.seg_slot = seg_slot;
+  p.n_segs = n_segs;
+  p.status = status;
+  const int rc = run_lora_fused(dtype, p, rank, stream);
+  return rc == LF_ERR_UNSUPPORTED ? -1 : rc;
+}
+
+// lf_lora_apply as a shrink launch into `workspace` and an expand launch that reads it.
+static int apply_two_launch(cudaStream_t s, int dtype, const void* x, int64_t ldx, void* y, int64_t ldy,
+                            int64_t n_tokens, int hidden, int rank, const void* cache_a, int64_t a_slot_stride,
+                            int64_t a_module_stride, const void* cache_b, int64_t b_slot_stride,
+                            int64_t b_module_stride, int n_slots, int n_modules, const int32_t* modules,
+                            const int64_t* y_col_offsets, const int32_t* seg_start, const int32_t* seg_len,
+                            const int32_t* seg_slot, int n_segs, const int32_t* tiles, int n_tiles, int n_multi,
+                            void* workspace, int32_t* status) {
+  int rc = shrink_impl(s, dtype, x, ldx, n_tokens, hidden, rank, cache_a, a_slot_stride, a_module_stride, n_slots,
+                       n_modules, modules, seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles, n_multi, workspace,
+                       status);
+  if (rc) return rc;
+  return expand_impl(s, dtype, workspace, y, ldy, n_tokens, hidden, rank, cache_b, b_slot_stride, b_module_stride,
+                     n_slots, n_modules, modules, y_col_offsets, seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles,
+                     n_multi, 1, true, status);
+}
+
+int apply_entry(bool allow_fused, void* stream, int dtype, const void* x, int64_t ldx, void* y, int64_t ldy,
+                int64_t n_tokens, int hidden, int rank, const void* cache_a, int64_t a_slot_stride,
+                int64_t a_module_stride, const void* cache_b, int64_t b_slot_stride, int64_t b_module_stride,
+                int n_slots, int n_modules, const int32_t* modules, const int64_t* y_col_offsets,
+                const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot, int n_segs,
+                const int32_t* tiles, int n_tiles, int n_multi, void* workspace, size_t workspace_bytes,
+                int32_t* status) {
+  int rc = check_common("lf_lora_apply", dtype, n_tokens, hidden, rank, n_slots, n_modules, modules, seg_start,
+                        seg_len, seg_slot, n_segs);
+  if (rc) return rc;
+  if ((rc = check_tiles("lf_lora_apply", tiles, n_tiles, n_multi, n_tokens))) return rc;
+  if (x == nullptr || y == nullptr || cache_a == nullptr || cache_b == nullptr || y_col_offsets == nullptr)
+    return set_error(LF_ERR_INVALID, "lf_lora_apply: NULL buffer");
+  if (ldx < hidden) return set_error(LF_ERR_INVALID, "lf_lora_apply: ldx < hidden");
+  if (n_tokens == 0) return LF_OK;
+  const size_t need = lf_lora_workspace_bytes(dtype, n_tokens, rank, n_modules);
+  if (workspace == nullptr || workspace_bytes < need)
+    return set_error(LF_ERR_WORKSPACE, "lf_lora_apply: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (allow_fused) {
+    rc = fused_apply(s, dtype, x, ldx, y, ldy, n_tokens, hidden, rank, cache_a, a_slot_stride, a_module_stride,
+                     cache_b, b_slot_stride, b_module_stride, n_slots, n_modules, modules, y_col_offsets, seg_start,
+                     seg_len, seg_slot, n_segs, tiles, n_tiles, status);
+    if (rc >= 0) return rc;
+  }
+  return apply_two_launch(s, dtype, x, ldx, y, ldy, n_tokens, hidden, rank, cache_a, a_slot_stride, a_module_stride,
+                          cache_b, b_slot_stride, b_module_stride, n_slots, n_modules, modules, y_col_offsets,
+                          seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles, n_multi, workspace, status);
+}
+
 }  // namespace lf
 
 using namespace lf;
@@ -442,6 +606,11 @@ int lf_set_option(int key, int value) {
     case LF_OPT_FORCE_SIMT: g_force_simt.store(value ? 1 : 0); return LF_OK;
     case LF_OPT_REQUIRE_TC: g_require_tc.store(value ? 1 : 0); return LF_OK;
     case LF_OPT_PERSISTENT: g_persistent.store(value ? 1 : 0); return LF_OK;
+    case LF_OPT_FUSED_APPLY: g_fused_apply.store(value ? 1 : 0); return LF_OK;
+    case LF_OPT_FUSED_SPLIT:
+      if (value < 0 || value > 16) return set_error(LF_ERR_INVALID, "LF_OPT_FUSED_SPLIT must be in [0, 16]");
+      g_fused_split.store(value);
+      return LF_OK;
     case LF_OPT_SHRINK_CLUSTER:
       if (value < 0 || value > 8 || (value & (value - 1)) != 0)
         return set_error(LF_ERR_INVALID, "LF_OPT_SHRINK_CLUSTER must be 0 or a power of two <= 8");
@@ -517,25 +686,10 @@ int lf_lora_apply(void* stream, int dtype, const void* x, int64_t ldx, void* y, 
                   const int32_t* modules, const int64_t* y_col_offsets, const int32_t* seg_start,
                   const int32_t* seg_len, const int32_t* seg_slot, int n_segs, const int32_t* tiles, int n_tiles,
                   int n_multi, void* workspace, size_t workspace_bytes, int32_t* status) {
-  int rc = check_common("lf_lora_apply", dtype, n_tokens, hidden, rank, n_slots, n_modules, modules, seg_start,
-                        seg_len, seg_slot, n_segs);
-  if (rc) return rc;
-  if ((rc = check_tiles("lf_lora_apply", tiles, n_tiles, n_multi, n_tokens))) return rc;
-  if (x == nullptr || y == nullptr || cache_a == nullptr || cache_b == nullptr || y_col_offsets == nullptr)
-    return set_error(LF_ERR_INVALID, "lf_lora_apply: NULL buffer");
-  if (ldx < hidden) return set_error(LF_ERR_INVALID, "lf_lora_apply: ldx < hidden");
-  if (n_tokens == 0) return LF_OK;
-  const size_t need = lf_lora_workspace_bytes(dtype, n_tokens, rank, n_modules);
-  if (workspace == nullptr || workspace_bytes < need)
-    return set_error(LF_ERR_WORKSPACE, "lf_lora_apply: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  rc = shrink_impl(s, dtype, x, ldx, n_tokens, hidden, rank, cache_a, a_slot_stride, a_module_stride, n_slots,
-                   n_modules, modules, seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles, n_multi, workspace,
-                   status);
-  if (rc) return rc;
-  return expand_impl(s, dtype, workspace, y, ldy, n_tokens, hidden, rank, cache_b, b_slot_stride, b_module_stride,
-                     n_slots, n_modules, modules, y_col_offsets, seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles,
-                     n_multi, 1, true, status);
+  return apply_entry(true, stream, dtype, x, ldx, y, ldy, n_tokens, hidden, rank, cache_a, a_slot_stride,
+                     a_module_stride, cache_b, b_slot_stride, b_module_stride, n_slots, n_modules, modules,
+                     y_col_offsets, seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles, n_multi, workspace,
+                     workspace_bytes, status);
 }
 
 int lf_lora_apply_into(void* stream, int dtype, const void* x, int64_t ldx, const void* r, int64_t ldr,

@@ -107,6 +107,37 @@ struct alignas(64) ShrinkPersistParams {
   int32_t u_blocked;
 };
 
+// One-launch late-fusion delta over the tile records (see lf_lora_fused.cu).
+struct alignas(64) FusedApplyParams {
+  CUtensorMap x_map;                 // 2D {hidden, n_tokens}, box {64, 128}, SW128
+  CUtensorMap a_map[kMaxModules];    // 3D {rank, hidden, n_slots}, box {rank, 64, 1}
+  CUtensorMap a_modules_map;         // 4D, as ShrinkPersistParams (a_one_box = 1)
+  CUtensorMap y_map;                 // 2D {y_cols, n_tokens}, box {64, 128}, SW128 (loads)
+  CUtensorMap ys_map;                // the same tensor, box {64, 32}: one warp's rows (stores)
+  CUtensorMap b_map[kMaxModules];    // 3D {hidden, rank, n_slots}, box {64, rank, 1}, SW128
+  int32_t a_one_box;
+  int64_t n_tokens;
+  int64_t y_col_off[kMaxModules];
+  int32_t hidden;
+  int32_t n_modules;
+  int32_t n_slots;
+  int32_t n_tiles;                   // tile records
+  int32_t n_chunks;                  // column chunks per record (items = n_tiles * n_chunks)
+  int32_t chunk_cols;                // hidden / n_chunks, a multiple of 64
+  int32_t kmax;                      // segments per round (one shrink pass + one expand pass)
+  int32_t stages;                    // ring stages (each an x box with A boxes or a y box with B boxes)
+  int32_t stage_bytes;
+  uint32_t u_cols;                   // TMEM columns of the u accumulator (kmax * n_modules * rank, padded)
+  uint32_t d_col;                    // first TMEM column of the 64-column delta accumulators
+  uint32_t tmem_alloc;               // TMEM columns allocated
+  const int32_t* tiles;              // records {tile, first segment, segment count, first slot}
+  const int32_t* seg_start;
+  const int32_t* seg_len;
+  const int32_t* seg_slot;
+  int32_t n_segs;
+  int32_t* status;
+};
+
 // Packed varlen attention, head_dim 64 (see lf_attention.cu).
 struct alignas(64) AttnParams {
   CUtensorMap qkv_map;               // 2D {ld_qkv, n_tokens}, box {64, 128}, SW128
@@ -186,6 +217,18 @@ CUtensorMapSwizzle a_tma_swizzle(int rank);
 int run_expand_persist(int dtype, const ExpandPersistParams& p, int rank, int nt, bool after_shrink,
                        cudaStream_t s);
 int run_shrink_persist(int dtype, const ShrinkPersistParams& p, int rank, cudaStream_t s);
+// Fills p's ring and round sizes for this rank and launches; LF_ERR_UNSUPPORTED
+// (nothing launched) when no configuration fits.
+int run_lora_fused(int dtype, FusedApplyParams& p, int rank, cudaStream_t s);
+// lf_lora_apply with its argument checks; allow_fused = false keeps it on the shrink
+// and expand launches, whose u goes through `workspace`.
+int apply_entry(bool allow_fused, void* stream, int dtype, const void* x, int64_t ldx, void* y, int64_t ldy,
+                int64_t n_tokens, int hidden, int rank, const void* cache_a, int64_t a_slot_stride,
+                int64_t a_module_stride, const void* cache_b, int64_t b_slot_stride, int64_t b_module_stride,
+                int n_slots, int n_modules, const int32_t* modules, const int64_t* y_col_offsets,
+                const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot, int n_segs,
+                const int32_t* tiles, int n_tiles, int n_multi, void* workspace, size_t workspace_bytes,
+                int32_t* status);
 
 // CUDA-core path
 int run_shrink_simt(int dtype, const SimtParams& p, cudaStream_t s);

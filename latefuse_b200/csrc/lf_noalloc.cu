@@ -68,8 +68,10 @@ extern "C" int lf_lora_apply_noalloc(void* stream, int dtype,
     }
     scratch = g_scratch_ptr[dev];
   }
-  return lf_lora_apply(stream, dtype, x, ldx, y, ldy, n_tokens, hidden, rank, cache_a, a_slot_stride,
-                       a_module_stride, cache_b, b_slot_stride, b_module_stride, n_slots, n_modules, modules,
-                       y_col_offsets, seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles, n_multi, scratch,
-                       LF_NOALLOC_SCRATCH_BYTES, status);
+  // the shrink + expand launches, with u in the static array (lf_lora_apply's one-launch
+  // kernel keeps u on chip and would not use it)
+  return apply_entry(false, stream, dtype, x, ldx, y, ldy, n_tokens, hidden, rank, cache_a, a_slot_stride,
+                     a_module_stride, cache_b, b_slot_stride, b_module_stride, n_slots, n_modules, modules,
+                     y_col_offsets, seg_start, seg_len, seg_slot, n_segs, tiles, n_tiles, n_multi, scratch,
+                     LF_NOALLOC_SCRATCH_BYTES, status);
 }
