@@ -27,8 +27,9 @@
 // One ring for both kinds of stage lets the producer run ahead: while the MMAs
 // still consume an item's x, its y boxes are already in flight, and while the
 // epilogue works through an item's y boxes, the next item's x is.  A stage is freed
-// by work on that stage (or on a later box of the same round) alone, and every
-// round frees all its stages when it ends, so the ring never waits on a later item.
+// by work on that stage (or, where the ring is deep enough, on a later box of the
+// same round) alone, and every round frees all its stages when it ends, so the ring
+// never waits on a stage it has not yet loaded.
 // x is read once per item (the items of one record run side by side, so their x
 // comes from L2 after the first), y is read and written once, u never leaves the
 // SM, and there is no second launch.
@@ -348,6 +349,10 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
     const bool reporter = row == 0 && eg == 0;
     int k = 0, rk = 0, dk = 0;
     int pend = -1;  // lane 0: ring position of this warp's last stored box, not yet freed
+    // A box's stage is freed after this warp's NEXT store, kGroups boxes later, only when
+    // the ring holds more than 2 * kGroups stages: the producer must be able to load
+    // that later box without the stage still held, or the two would wait on each other.
+    const bool defer = NS > 2 * kGroups;
     bool stop = false;
     auto release_pending = [&]() {  // lane 0: every store of this warp has read its rows
       tma_store_wait_read_all();
@@ -462,11 +467,16 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
                 tma_store_2d(&p.ys_map, st + uint32_t(quad * 32 * 128),
                              int32_t(p.y_col_off[m]) + ch * p.chunk_cols + b * 64, int32_t(r0));
                 tma_store_commit();
-                // the store before this one has read its rows: free that box's part of its
-                // stage (this box's part is freed after the next store, or at the round's end)
-                tma_store_wait_read_le1();
-                if (pend >= 0) mbar_arrive(bar(EMPTY + pend % NS));
-                pend = k;
+                if (defer) {
+                  // the store before this one has read its rows: free that box's part of its
+                  // stage (this box's part is freed after the next store, or at the round's end)
+                  tma_store_wait_read_le1();
+                  if (pend >= 0) mbar_arrive(bar(EMPTY + pend % NS));
+                  pend = k;
+                } else {
+                  tma_store_wait_read_all();
+                  mbar_arrive(bar(EMPTY + k % NS));
+                }
               } else {
                 mbar_arrive(bar(EMPTY + k % NS));  // nothing reads these rows
               }
