@@ -467,7 +467,7 @@ def run_serve(args):
         r16 = op["results"]["r16"]
         lora_hbm = {
             "kernel": "lf_lora_apply as the isolated op, one launch (shrink and expand in one kernel, u kept on "
-                      "chip): X (64, 256, 1024) bf16, rank 16, 10,000 resident adapters, L2 flushed before each call",
+                      "chip): X (64, 256, 1024) bf16, rank 16, 10,000 resident adapters, L2 flushed clean before each call",
             "achieved": r16["apply_flushed_gbs"], "peak": op.get("peak_gbs"), "unit": "GB/s",
             "frac": r16["apply_flushed_frac_of_hbm"], "algorithmic_bytes": r16["algorithmic_bytes"],
             "us": r16["apply_flushed_us"], "two_launch_us": r16["two_launch_flushed_us"],
@@ -649,7 +649,14 @@ def op_results(args, dev, steps: int, warmup: int) -> dict:
         segs = SegmentTable.for_padded(slots, S, dev)
         ws = torch.empty(workspace_bytes(torch.bfloat16, T, R, 1), dtype=torch.uint8, device=dev)
         y = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
-        flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > L2, written between steps
+        # L2 flush between steps: 256 MB written, then another 256 MB read, so that L2 holds no
+        # dirty lines whose write-back the timed kernel would otherwise pay for
+        flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+        flush_r = torch.ones(256 * 1024 * 1024 // 8, dtype=torch.int64, device=dev)
+
+        def flush_l2():
+            flush.zero_()
+            flush_r.max()
 
         def op(times=None):
             torch.matmul(x, w, out=y)
@@ -665,7 +672,7 @@ def op_results(args, dev, steps: int, warmup: int) -> dict:
         ev, ops = events(steps), events(steps)
         n0 = nat.launch_count()
         for i in range(steps):
-            flush.zero_()
+            flush_l2()
             ops[i][0].record()
             op(ev[i])
             ops[i][1].record()
@@ -686,7 +693,7 @@ def op_results(args, dev, steps: int, warmup: int) -> dict:
             for fn, acc in ((lambda: lora_apply(x, y, fc, segs, [0], [0], ws), ap), (two_launch, two),
                             (lambda: lora_shrink(x, u, fc, segs, [0]), sh),
                             (lambda: lora_expand(u, y, fc, segs, [0], [0], True), ex)):
-                flush.zero_()
+                flush_l2()
                 a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a_.record()
                 fn()
@@ -708,10 +715,11 @@ def op_results(args, dev, steps: int, warmup: int) -> dict:
                         "expand_us": expand_ms * 1e3,
                         "expand_gbs": (2 * T * H * 2 + U * 2 * H * R) / (expand_ms * 1e-3) / 1e9,
                         "launches_per_op": launches}
-        del cache, x, y, w, ws, flush
+        del cache, x, y, w, ws, flush, flush_r
         torch.cuda.empty_cache()
     return {"workload": "Y = X W + (X A_t) B_t, X (64,256,1024) bf16, 10,000 adapters, Zipf(1.1) tenants, "
-                        "L2 flushed between steps", "peak_gbs": peak, "results": out}
+                        "L2 flushed between steps (256 MB written, then 256 MB of another buffer read)", "peak_gbs": peak,
+            "results": out}
 
 
 def run_op(args):

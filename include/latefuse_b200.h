@@ -101,7 +101,8 @@ extern "C" {
 #define LF_OPT_PERSISTENT 4     /* 0: do not use the persistent expand kernel (default 1) */
 #define LF_OPT_FUSED_APPLY 5    /* 1 (default): lf_lora_apply runs as one launch (shrink and
                                    expand in one kernel, u kept on chip) where that kernel
-                                   applies; 0: a shrink launch and an expand launch */
+                                   applies and the call has one module; 2: also with several
+                                   modules; 0: a shrink launch and an expand launch */
 #define LF_OPT_FUSED_SPLIT 6    /* 0 = automatic, else the column chunks each tile record of
                                    the one-launch lf_lora_apply is split into */
 
@@ -193,9 +194,9 @@ size_t lf_lora_workspace_bytes(int dtype, int64_t n_tokens, int rank, int n_modu
  * y, i.e. y[t, off_m + :] += B(slot(t), m)^T (A(slot(t), m)^T x[t]) for up to 4
  * modules that share the input x (query/key/value of one layer share one read of
  * x).  One call replaces, per layer, the reference's cat -> bmm -> bmm -> add
- * sequence of every hook (src/latefuse/model/hf_wrapper.py:213-217).  With tile
- * records, bf16/f16, rank 8/16/32/64, hidden a multiple of 64, 16-byte aligned
- * buffers and x not overlapping y, it runs as ONE kernel that keeps u on chip
+ * sequence of every hook (src/latefuse/model/hf_wrapper.py:213-217).  With one
+ * module, tile records, bf16/f16, rank 8/16/32/64, hidden a multiple of 64,
+ * 16-byte aligned buffers and x not overlapping y, it runs as ONE kernel that keeps u on chip
  * (the workspace is then unused; LF_OPT_FUSED_APPLY = 0 selects the shrink and
  * expand launches, which give the same bits); otherwise as a shrink launch into
  * `workspace` and an expand launch. */

@@ -35,7 +35,8 @@ def apply(x, y, fc, st, mods, offs, fused=True, split=0):
     ws = torch.empty(workspace_bytes(x.dtype, x.shape[0], fc.rank, len(mods)), dtype=torch.uint8, device=x.device)
     status = torch.zeros(1, dtype=torch.int32, device=x.device)
     out = y.clone()
-    nat.set_option(nat.LF_OPT_FUSED_APPLY, 1 if fused else 0)
+    # several modules take the one-launch kernel only when asked for (2)
+    nat.set_option(nat.LF_OPT_FUSED_APPLY, (1 if len(mods) == 1 else 2) if fused else 0)
     nat.set_option(nat.LF_OPT_FUSED_SPLIT, split)
     n0 = nat.launch_count()
     lora_apply(x, out, fc, st, mods, offs, ws, status)
@@ -63,7 +64,8 @@ def short_segments(n, gap_max, n_slots, g):
 def test_fused_equals_two_launches_many_segments(cuda, dtype, n_mod, R):
     """Tiles holding up to ~15 short segments with gaps (several rounds per record for
     every rank and module count), a partial last tile, every column chunking: the one
-    launch gives the two launches' bits."""
+    launch gives the two launches' bits.  Several modules run the kernel only under
+    LF_OPT_FUSED_APPLY = 2; by default they take the two launches."""
     H, n_slots = 512, 11
     g = torch.Generator().manual_seed(31 * n_mod + R)
     starts, lengths, slots, t = short_segments(40, 6, n_slots, g)
@@ -135,6 +137,13 @@ def test_fused_column_slices_of_a_wider_output(cuda):
     one, s1, _ = apply(x, y, fc, st, mods, offs)
     assert s1 == 0 and torch.equal(one, two)
     assert torch.equal(one[:, 2 * H:3 * H], y[:, 2 * H:3 * H])
+    # by default (LF_OPT_FUSED_APPLY = 1) several modules take the two launches
+    ws = torch.empty(workspace_bytes(dtype, T, R, 3), dtype=torch.uint8, device=cuda)
+    out = y.clone()
+    n0 = nat.launch_count()
+    lora_apply(x, out, fc, st, mods, offs, ws)
+    torch.cuda.synchronize()
+    assert nat.launch_count() - n0 == 2 and torch.equal(out, two)
     ref = segmented_apply(x.cpu(), y.cpu(), a_of, b_of, list(zip(starts, lengths, slots)), col_offsets=offs,
                           modules=mods)
     check(one.cpu(), ref, y.cpu(), dtype)
