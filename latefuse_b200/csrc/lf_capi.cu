@@ -490,11 +490,8 @@ static int fused_apply(cudaStream_t stream, int dtype, const void* x, int64_t ld
   {
     cuuint64_t dims[2] = {cuuint64_t(y_cols), cuuint64_t(n_tokens)};
     cuuint64_t strides[1] = {cuuint64_t(ldy) * es};
-    cuuint32_t box[2] = {64, 128};
-    int rc = encode(&p.y_map, dtype, 2, y, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, "y");
-    if (rc) return rc;
     cuuint32_t sbox[2] = {64, 32};
-    rc = encode(&p.ys_map, dtype, 2, y, dims, strides, sbox, CU_TENSOR_MAP_SWIZZLE_128B, "y (stores)");
+    int rc = encode(&p.ys_map, dtype, 2, y, dims, strides, sbox, CU_TENSOR_MAP_SWIZZLE_128B, "y (reductions)");
     if (rc) return rc;
   }
   const int64_t a_ss = n_slots == 1 ? int64_t(hidden) * rank : a_slot_stride;

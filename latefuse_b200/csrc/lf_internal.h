@@ -112,8 +112,7 @@ struct alignas(64) FusedApplyParams {
   CUtensorMap x_map;                 // 2D {hidden, n_tokens}, box {64, 128}, SW128
   CUtensorMap a_map[kMaxModules];    // 3D {rank, hidden, n_slots}, box {rank, 64, 1}
   CUtensorMap a_modules_map;         // 4D, as ShrinkPersistParams (a_one_box = 1)
-  CUtensorMap y_map;                 // 2D {y_cols, n_tokens}, box {64, 128}, SW128 (loads)
-  CUtensorMap ys_map;                // the same tensor, box {64, 32}: one warp's rows (stores)
+  CUtensorMap ys_map;                // 2D {y_cols, n_tokens}, box {64, 32}, SW128: one warp's rows (reductions)
   CUtensorMap b_map[kMaxModules];    // 3D {hidden, rank, n_slots}, box {64, rank, 1}, SW128
   int32_t a_one_box;
   int64_t n_tokens;

@@ -9,40 +9,30 @@
 // every module's hidden columns).  One persistent CTA per SM runs items one after
 // another with three roles around ONE ring of shared-memory stages:
 //   warp 0      producer: for each item, the x K-blocks with the A boxes of the
-//               round's segments ("x stages"), then the y boxes with the matching
-//               B boxes ("y stages"), by TMA, in that order, as far ahead as the
-//               ring allows;
+//               round's segments ("x stages"), then for each 64-column y box the
+//               matching B boxes ("B stages"), by TMA, as far ahead as the ring
+//               allows;
 //   warp 1      MMA issuer: u = x A into a TMEM accumulator (one MMA per K step,
-//               N = segments x modules x rank; an x stage is free once its MMAs
-//               complete), then for each y stage the delta u B (K = rank, N = 64)
-//               into one of four TMEM accumulators;
+//               N = segments x modules x rank), then for each y box the delta u B
+//               (K = rank, N = 64) into one of four TMEM accumulators; a stage is
+//               free as soon as its MMAs complete;
 //   warps 2..   epilogue, three groups of four warps (a warp per TMEM lane quadrant,
-//               a thread per tile row); the y boxes go round-robin to the groups,
-//               so three boxes are drained at once.  The groups round u and write
-//               each (segment, module) block into shared memory as the delta MMA's
-//               K-major operand (the product for rows of that segment, 0 for the
-//               others); then for each of its y stages a group adds the rounded
-//               delta to the staged box in place, stores each warp's 32 rows by TMA
-//               and frees its part of the stage once the store has read it.
-// One ring for both kinds of stage lets the producer run ahead: while the MMAs
-// still consume an item's x, its y boxes are already in flight, and while the
-// epilogue works through an item's y boxes, the next item's x is.  A stage is freed
-// by work on that stage (or, where the ring is deep enough, on a later box of the
-// same round) alone, and every round frees all its stages when it ends, so the ring
-// never waits on a stage it has not yet loaded.
-// x is read once per item (the items of one record run side by side, so their x
-// comes from L2 after the first), y is read and written once, u never leaves the
-// SM, and there is no second launch.
+//               a thread per tile row).  The groups round u and write each (segment,
+//               module) block into shared memory as the delta MMA's K-major operand
+//               (the product for rows of that segment, 0 for the others); then the y
+//               boxes go round-robin to the groups: each warp rounds its 32 rows of
+//               the delta, stages them and adds them to y in L2 with one TMA
+//               reduction (cp.reduce.async.bulk.tensor .add), which computes
+//               round(y + delta) element by element as the reference's add does.
+// y never passes through the SM: x is read once per item (the items of one record
+// run side by side, so their x comes from L2 after the first), y is read and written
+// once by L2, u never leaves the SM, and there is no second launch.  Rows of a
+// staged box outside the round's segments add -0, which leaves every value as it was
+// (-0 included); a warp whose 32 rows hold none of them adds nothing.
 //
 // A record with more than kmax segments takes several rounds, each a shrink pass
-// and an expand pass over the record's boxes; a round's y loads wait until the
-// previous round's stores have completed, since they read the rows it wrote.
-//
-// The shrink accumulates the full hidden dimension in one TMEM accumulator with
-// the same MMA sequence as lora_shrink_persist_kernel, and every rounding point
-// is the same as in the shrink + expand launches.  Every wait is bounded; a
-// timeout sets LF_STATUS_TIMEOUT and the roles unwind (loads drained, MMAs
-// finished, stores completed) before TMEM is released.
+// and a delta pass over the record's boxes; their reductions touch disjoint rows
+// with non-zero values, so the rounds need no ordering between them.
 #include "lf_common.cuh"
 #include "lf_internal.h"
 #include "lf_records.cuh"
@@ -59,6 +49,8 @@ constexpr int kDBufs = 4;                  // 64-column TMEM delta accumulators
 constexpr int kFusedThreads = 64 + 128 * kGroups;
 constexpr int kSmemMax = 227 * 1024;       // dynamic shared memory per CTA on sm_100
 constexpr int kFixedBytes = 2048;          // alignment slack + barriers
+constexpr int kStageOut = 32 * 128;        // one warp's 32 rows x 64 columns of the delta (SW128)
+constexpr int kOutBytes = (kFusedThreads / 32 - 2) * kStageOut;
 
 template <int R>
 struct FusedOps {
@@ -90,13 +82,13 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
   const int nyb = p.chunk_cols / 64;
   const uint32_t s_ring = base;
   const uint32_t s_u = s_ring + uint32_t(NS * p.stage_bytes);
-  const uint32_t s_zero = s_u + uint32_t(KM * n_mod * F::kUBlk);
+  const uint32_t s_out = s_u + uint32_t(KM * n_mod * F::kUBlk);  // a staging box per epilogue warp
+  const uint32_t s_zero = s_out + kOutBytes;
   const uint32_t s_meta = s_zero + F::kZeroBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + (s_meta - base));
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   const int FULL = 0, EMPTY = NS, DFULL = 2 * NS, DEMPTY = DFULL + kDBufs, UFULL = DEMPTY + kDBufs,
-            UEMPTY = UFULL + 1, UREADY = UEMPTY + 1, USFREE = UREADY + 1, RDONE = USFREE + 1, DRAIN = RDONE + 1,
-            NBAR = DRAIN + 1;
+            UEMPTY = UFULL + 1, UREADY = UEMPTY + 1, USFREE = UREADY + 1, DRAIN = USFREE + 1, NBAR = DRAIN + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(&bars[NBAR]);
   int32_t* s_abort = reinterpret_cast<int32_t*>(tmem_slot + 1);
   auto stage = [&](int k) { return s_ring + uint32_t((k % NS) * p.stage_bytes); };
@@ -108,10 +100,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
   if (tid == 0) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(bar(FULL + i), 1);
-      // four arrivals free a stage: an x stage gets three from the MMA thread and one
-      // from the commit of its MMAs, a y stage one from each warp of the epilogue group
-      // that stored it
-      mbar_init(bar(EMPTY + i), 4);
+      mbar_init(bar(EMPTY + i), 1);  // the commit of the MMAs that read the stage
     }
     for (int i = 0; i < kDBufs; ++i) {
       mbar_init(bar(DFULL + i), 1);
@@ -121,7 +110,6 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
     mbar_init(bar(UEMPTY), 4 * kGroups);
     mbar_init(bar(UREADY), 4 * kGroups);
     mbar_init(bar(USFREE), 1);
-    mbar_init(bar(RDONE), 4 * kGroups);
     mbar_init(bar(DRAIN), 1);
     *s_abort = 0;
     fence_mbar_init();
@@ -133,7 +121,6 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
   }
   if (tid == 0) {
     prefetch_tmap(&p.x_map);
-    prefetch_tmap(&p.y_map);
     prefetch_tmap(&p.ys_map);
   }
   if (warp == 1) {
@@ -161,7 +148,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      int k = 0, rd = 0;  // ring position, rounds waited for
+      int k = 0;  // ring position
       bool stop = false;
       auto acquire = [&](int kk) {  // the stage at ring position kk is free
         if (aborted(s_abort) || !mbar_wait(bar(EMPTY + kk % NS), ((kk / NS) & 1) ^ 1)) {
@@ -198,14 +185,6 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
             }
           }
           if (stop) break;
-          if (j0 > 0) {  // this round's y boxes hold rows the previous round stored
-            if (aborted(s_abort) || !mbar_wait(bar(RDONE), rd & 1)) {
-              if (!aborted(s_abort)) fail();
-              stop = true;
-              break;
-            }
-            ++rd;
-          }
           for (int m = 0; m < n_mod && !stop; ++m) {
             for (int b = 0; b < nyb; ++b, ++k) {
               if (!acquire(k)) {
@@ -215,10 +194,9 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
               const uint32_t st = stage(k);
               const uint32_t full = bar(FULL + k % NS);
               const int32_t hcol = ch * p.chunk_cols + b * 64;
-              mbar_arrive_expect_tx(full, uint32_t(kBoxBytes + kp * F::kBBox));
-              tma_load_2d(st, &p.y_map, full, int32_t(p.y_col_off[m]) + hcol, row0);
+              mbar_arrive_expect_tx(full, uint32_t(kp * F::kBBox));
               for (int jj = 0; jj < kp; ++jj)
-                tma_load_3d(st + kBoxBytes + uint32_t(jj * F::kBBox), &p.b_map[m], full, hcol, 0,
+                tma_load_3d(st + uint32_t(jj * F::kBBox), &p.b_map[m], full, hcol, 0,
                             sub_slot(rc, j0 + jj, p.seg_slot, p.n_segs));
             }
           }
@@ -286,8 +264,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
               }
             }
             issued = true;
-            mbar_arrive_cnt(bar(EMPTY + k % NS), 3);
-            umma_commit(bar(EMPTY + k % NS));  // the fourth arrival: these MMAs have read the stage
+            umma_commit(bar(EMPTY + k % NS));  // the stage is free once these MMAs have read it
           }
           if (stop) break;
           umma_commit(bar(UFULL));
@@ -311,7 +288,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
               const uint32_t d = tmem + p.d_col + uint32_t(a * 64);
               for (int jj = 0; jj < kp; ++jj) {
                 const uint32_t ub = s_u + uint32_t((jj * n_mod + m) * F::kUBlk);
-                const uint32_t bb = st + kBoxBytes + uint32_t(jj * F::kBBox);
+                const uint32_t bb = st + uint32_t(jj * F::kBBox);
                 if (R == 8) {
                   const uint64_t ad = smem_desc(ub, s_zero_u - ub, 128, 0);  // K 8..15 read zeros
                   const uint64_t bd = smem_desc(bb, F::kBBox, s_zero_b - bb, 2);
@@ -327,6 +304,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
               }
               issued = true;
               umma_commit(bar(DFULL + a));
+              umma_commit(bar(EMPTY + k % NS));
             }
           }
           if (!stop) umma_commit(bar(USFREE));  // the u blocks may be rewritten once these MMAs finish
@@ -341,24 +319,16 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
     // ------------------------------------------------------------ epilogue (warps 2..)
     // kGroups groups of four warps, one warp per TMEM lane quadrant in each; group g
     // takes every kGroups-th y box (and every kGroups-th u block), so that several
-    // boxes are read, added and stored at once.
+    // boxes are drained and reduced into y at once.
     const int eg = (warp - 2) >> 2;
     const int quad = warp & 3;  // the TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
     const uint32_t lane_base = uint32_t(quad * 32) << 16;
+    const uint32_t s_mine = s_out + uint32_t((warp - 2) * kStageOut);
+    uint8_t* my_line = gbase + (s_mine - base) + lane * 128;  // this row in the warp's SW128 staging box
     const bool reporter = row == 0 && eg == 0;
-    int k = 0, rk = 0, dk = 0;
-    int pend = -1;  // lane 0: ring position of this warp's last stored box, not yet freed
-    // A box's stage is freed after this warp's NEXT store, kGroups boxes later, only when
-    // the ring holds more than 2 * kGroups stages: the producer must be able to load
-    // that later box without the stage still held, or the two would wait on each other.
-    const bool defer = NS > 2 * kGroups;
+    int rk = 0, dk = 0;
     bool stop = false;
-    auto release_pending = [&]() {  // lane 0: every store of this warp has read its rows
-      tma_store_wait_read_all();
-      if (pend >= 0) mbar_arrive(bar(EMPTY + pend % NS));
-      pend = -1;
-    };
     for (int item = blockIdx.x; item < n_items && !stop; item += gridDim.x) {
       const int4 rc = __ldg(recs + item / C);
       const int ch = item % C;
@@ -368,16 +338,18 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
       }
       const int ns = sub_items(rc, p.n_segs);
       const int64_t row0 = int64_t(rc.x) * kTile;
+      const int64_t r0 = row0 + quad * 32;  // this warp's first row
       const int4 seg0 = first_seg(rc, p.seg_start, p.seg_len, p.seg_slot, p.n_segs);
       for (int j0 = 0; j0 < ns && !stop; j0 += KM, ++rk) {
         const int kp = min(KM, ns - j0);
-        k += nkb;  // the round's x stages are the MMA's
         int j_row = -1;  // this row's segment within the round
         for (int jj = 0; jj < kp; ++jj) {
           const SubRows sr = rows_of(rc, j0 + jj, seg0, row0, p.n_tokens, p.seg_start, p.seg_len, p.seg_slot,
                                      p.n_segs, p.n_slots, p.status, reporter && ch == 0);
           if (row >= sr.lo && row < sr.hi) j_row = jj;
         }
+        // a warp with none of the round's rows adds nothing to y
+        const bool warp_rows = __any_sync(0xffffffffu, j_row >= 0) && r0 < p.n_tokens;
         // (1) u, rounded: the row's product in its own segment's blocks, 0 in the others
         bool ok = !aborted(s_abort);
         if (ok && !(mbar_wait(bar(UFULL), rk & 1) && mbar_wait(bar(USFREE), (rk & 1) ^ 1))) {
@@ -420,12 +392,11 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
         }
         // (2) the delta, one 64-column y box at a time, the boxes dealt round-robin
         for (int m = 0; m < n_mod && !stop; ++m) {
-          for (int b = 0; b < nyb; ++b, ++k, ++dk) {
+          for (int b = 0; b < nyb; ++b, ++dk) {
             if (dk % kGroups != eg) continue;
             const int a = dk % kDBufs;
             bool ok2 = !aborted(s_abort);
-            if (ok2 &&
-                !(mbar_wait(bar(DFULL + a), (dk / kDBufs) & 1) && mbar_wait(bar(FULL + k % NS), (k / NS) & 1))) {
+            if (ok2 && !mbar_wait(bar(DFULL + a), (dk / kDBufs) & 1)) {
               fail();
               ok2 = false;
             }
@@ -439,62 +410,36 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(DEMPTY + a));
-            const uint32_t st = stage(k);
-            if (j_row >= 0) {
-              // y + round(delta), rounded: the reference's two rounding points.  The
-              // box is SW128: chunk c of row r sits at 16 * (c ^ (r % 8)) in its line.
-              uint8_t* line = gbase + (st - base) + row * 128;
+            if (!warp_rows) continue;
+            if (lane == 0) tma_store_wait_read_all();  // the warp's previous reduction has read the box
+            __syncwarp();
+            // round(delta) for the round's rows, -0 for the others (y + -0 is y).  The box
+            // is SW128: chunk c of row r sits at 16 * (c ^ (r % 8)) in its 128-byte line.
+            const bool in = j_row >= 0;
 #pragma unroll
-              for (int c = 0; c < 8; ++c) {
-                uint4* pv = reinterpret_cast<uint4*>(line + ((c ^ (row & 7)) << 4));
-                uint4 yv = *pv;
-                uint32_t* w = reinterpret_cast<uint32_t*>(&yv);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  const float2 yf = Pack2<T>::unpack(w[i]);
-                  const float2 d = Pack2<T>::unpack(
-                      Pack2<T>::pack(__uint_as_float(acc[c * 8 + 2 * i]), __uint_as_float(acc[c * 8 + 2 * i + 1])));
-                  w[i] = Pack2<T>::pack(yf.x + d.x, yf.y + d.y);
-                }
-                *pv = yv;
+            for (int c = 0; c < 8; ++c) {
+              uint4 pk = make_uint4(0x80008000u, 0x80008000u, 0x80008000u, 0x80008000u);
+              if (in) {
+                pk.x = Pack2<T>::pack(__uint_as_float(acc[c * 8 + 0]), __uint_as_float(acc[c * 8 + 1]));
+                pk.y = Pack2<T>::pack(__uint_as_float(acc[c * 8 + 2]), __uint_as_float(acc[c * 8 + 3]));
+                pk.z = Pack2<T>::pack(__uint_as_float(acc[c * 8 + 4]), __uint_as_float(acc[c * 8 + 5]));
+                pk.w = Pack2<T>::pack(__uint_as_float(acc[c * 8 + 6]), __uint_as_float(acc[c * 8 + 7]));
               }
+              *reinterpret_cast<uint4*>(my_line + ((c ^ (lane & 7)) << 4)) = pk;
             }
-            fence_proxy_async_smem();  // the rows are read by the TMA store (async proxy)
+            fence_proxy_async_smem();  // the rows are read by the TMA reduction (async proxy)
             __syncwarp();
             if (lane == 0) {
-              const int64_t r0 = row0 + quad * 32;
-              if (r0 < p.n_tokens) {  // rows past the end are clipped; a box wholly past it is not stored
-                tma_store_2d(&p.ys_map, st + uint32_t(quad * 32 * 128),
-                             int32_t(p.y_col_off[m]) + ch * p.chunk_cols + b * 64, int32_t(r0));
-                tma_store_commit();
-                if (defer) {
-                  // the store before this one has read its rows: free that box's part of its
-                  // stage (this box's part is freed after the next store, or at the round's end)
-                  tma_store_wait_read_le1();
-                  if (pend >= 0) mbar_arrive(bar(EMPTY + pend % NS));
-                  pend = k;
-                } else {
-                  tma_store_wait_read_all();
-                  mbar_arrive(bar(EMPTY + k % NS));
-                }
-              } else {
-                mbar_arrive(bar(EMPTY + k % NS));  // nothing reads these rows
-              }
+              // rows past the end of the tokens are clipped
+              tma_reduce_add_2d(&p.ys_map, s_mine, int32_t(p.y_col_off[m]) + ch * p.chunk_cols + b * 64,
+                                int32_t(r0));
+              tma_store_commit();
             }
-          }
-        }
-        if (stop) break;
-        if (lane == 0) {
-          // a round's boxes are all freed before the next round or item needs the ring
-          release_pending();
-          if (j0 + KM < ns) {  // the next round reloads these boxes: its loads follow our stores
-            tma_store_wait_all();
-            mbar_arrive(bar(RDONE));
           }
         }
       }
     }
-    if (lane == 0) tma_store_wait_all();
+    if (lane == 0) tma_store_wait_all();  // every reduction has completed
   }
 
   __syncthreads();
@@ -515,14 +460,12 @@ int launch_fused(FusedApplyParams& p, cudaStream_t stream) {
   // segments per round: two where the ring then keeps at least 7 stages (one where it
   // would not), so that u for all of them (kmax * n_modules * RP TMEM columns) and the
   // four 64-column delta accumulators fit in TMEM; a stage holds an x box with the
-  // round's A boxes or a y box with its B boxes, whichever is larger
+  // round's A boxes, or the B boxes of one y box
   int chosen = 0, stages = 0, sb = 0, fixed = 0;
   for (int km = 2; km >= 1; --km) {
     if (km * p.n_modules * RP > 256) continue;
-    const int xs = kBoxBytes + km * p.n_modules * F::kABox;
-    const int ys = kBoxBytes + km * F::kBBox;
-    sb = xs > ys ? xs : ys;
-    fixed = kFixedBytes + F::kZeroBytes + km * p.n_modules * F::kUBlk;
+    sb = kBoxBytes + km * p.n_modules * F::kABox;  // an x stage; a B stage (km * kBBox) is smaller
+    fixed = kFixedBytes + F::kZeroBytes + km * p.n_modules * F::kUBlk + kOutBytes;
     const int st = (kSmemMax - fixed) / sb;
     if (st >= 7 || (km == 1 && st >= 2)) {
       chosen = km;
