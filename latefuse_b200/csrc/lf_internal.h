@@ -124,7 +124,8 @@ struct alignas(64) FusedApplyParams {
   int32_t n_chunks;                  // column chunks per record (items = n_tiles * n_chunks)
   int32_t chunk_cols;                // hidden / n_chunks, a multiple of 64
   int32_t kmax;                      // segments per round (one shrink pass + one expand pass)
-  int32_t stages;                    // ring stages (each an x box with A boxes or a y box with B boxes)
+  int32_t stages;                    // ring stages (each an x box with A boxes, or the B boxes of a y box)
+  int32_t out_bufs;                  // staging boxes per epilogue warp (1 or 2)
   int32_t stage_bytes;
   uint32_t u_cols;                   // TMEM columns of the u accumulator (kmax * n_modules * rank, padded)
   uint32_t d_col;                    // first TMEM column of the 64-column delta accumulators

@@ -21,7 +21,8 @@
 //               module) block into shared memory as the delta MMA's K-major operand
 //               (the product for rows of that segment, 0 for the others); then the y
 //               boxes go round-robin to the groups: each warp rounds its 32 rows of
-//               the delta, stages them and adds them to y in L2 with one TMA
+//               the delta, stages them (two staging boxes per warp, so two
+//               reductions are in flight) and adds them to y in L2 with one TMA
 //               reduction (cp.reduce.async.bulk.tensor .add), which computes
 //               round(y + delta) element by element as the reference's add does.
 // y never passes through the SM: x is read once per item (the items of one record
@@ -50,7 +51,7 @@ constexpr int kFusedThreads = 64 + 128 * kGroups;
 constexpr int kSmemMax = 227 * 1024;       // dynamic shared memory per CTA on sm_100
 constexpr int kFixedBytes = 2048;          // alignment slack + barriers
 constexpr int kStageOut = 32 * 128;        // one warp's 32 rows x 64 columns of the delta (SW128)
-constexpr int kOutBytes = (kFusedThreads / 32 - 2) * kStageOut;
+constexpr int kEpiWarps = kFusedThreads / 32 - 2;
 
 template <int R>
 struct FusedOps {
@@ -83,7 +84,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
   const uint32_t s_ring = base;
   const uint32_t s_u = s_ring + uint32_t(NS * p.stage_bytes);
   const uint32_t s_out = s_u + uint32_t(KM * n_mod * F::kUBlk);  // a staging box per epilogue warp
-  const uint32_t s_zero = s_out + kOutBytes;
+  const uint32_t s_zero = s_out + uint32_t(kEpiWarps * p.out_bufs * kStageOut);
   const uint32_t s_meta = s_zero + F::kZeroBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + (s_meta - base));
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
@@ -324,8 +325,8 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
     const int quad = warp & 3;  // the TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
     const uint32_t lane_base = uint32_t(quad * 32) << 16;
-    const uint32_t s_mine = s_out + uint32_t((warp - 2) * kStageOut);
-    uint8_t* my_line = gbase + (s_mine - base) + lane * 128;  // this row in the warp's SW128 staging box
+    const uint32_t s_mine = s_out + uint32_t((warp - 2) * p.out_bufs * kStageOut);  // this warp's staging boxes
+    int nbox = 0;  // reductions this warp has issued
     const bool reporter = row == 0 && eg == 0;
     int rk = 0, dk = 0;
     bool stop = false;
@@ -411,7 +412,16 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(DEMPTY + a));
             if (!warp_rows) continue;
-            if (lane == 0) tma_store_wait_read_all();  // the warp's previous reduction has read the box
+            const uint32_t sbox = s_mine + uint32_t((nbox % p.out_bufs) * kStageOut);
+            uint8_t* my_line = gbase + (sbox - base) + lane * 128;  // this row in the SW128 staging box
+            // with two staging boxes two reductions are in flight per warp: the one issued two
+            // boxes ago has read this box; with one, the previous one has
+            if (lane == 0) {
+              if (p.out_bufs == 2)
+                tma_store_wait_read_le1();
+              else
+                tma_store_wait_read_all();
+            }
             __syncwarp();
             // round(delta) for the round's rows, -0 for the others (y + -0 is y).  The box
             // is SW128: chunk c of row r sits at 16 * (c ^ (r % 8)) in its 128-byte line.
@@ -431,10 +441,11 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
             __syncwarp();
             if (lane == 0) {
               // rows past the end of the tokens are clipped
-              tma_reduce_add_2d(&p.ys_map, s_mine, int32_t(p.y_col_off[m]) + ch * p.chunk_cols + b * 64,
+              tma_reduce_add_2d(&p.ys_map, sbox, int32_t(p.y_col_off[m]) + ch * p.chunk_cols + b * 64,
                                 int32_t(r0));
               tma_store_commit();
             }
+            ++nbox;
           }
         }
       }
@@ -457,25 +468,31 @@ template <typename T, int R>
 int launch_fused(FusedApplyParams& p, cudaStream_t stream) {
   using F = FusedOps<R>;
   constexpr int RP = F::RP;
-  // segments per round: two where the ring then keeps at least 7 stages (one where it
+  // segments per round: two where the ring then keeps at least 6 stages (one where it
   // would not), so that u for all of them (kmax * n_modules * RP TMEM columns) and the
   // four 64-column delta accumulators fit in TMEM; a stage holds an x box with the
   // round's A boxes, or the B boxes of one y box
-  int chosen = 0, stages = 0, sb = 0, fixed = 0;
-  for (int km = 2; km >= 1; --km) {
-    if (km * p.n_modules * RP > 256) continue;
-    sb = kBoxBytes + km * p.n_modules * F::kABox;  // an x stage; a B stage (km * kBBox) is smaller
-    fixed = kFixedBytes + F::kZeroBytes + km * p.n_modules * F::kUBlk + kOutBytes;
-    const int st = (kSmemMax - fixed) / sb;
-    if (st >= 7 || (km == 1 && st >= 2)) {
-      chosen = km;
-      stages = st > 12 ? 12 : st;
-      break;
+  // each epilogue warp stages its delta rows in two boxes where they fit (two reductions
+  // in flight), else in one
+  int chosen = 0, stages = 0, sb = 0, fixed = 0, bufs = 0;
+  for (int ob = 2; ob >= 1 && chosen == 0; --ob) {
+    for (int km = 2; km >= 1; --km) {
+      if (km * p.n_modules * RP > 256) continue;
+      sb = kBoxBytes + km * p.n_modules * F::kABox;  // an x stage; a B stage (km * kBBox) is smaller
+      fixed = kFixedBytes + F::kZeroBytes + km * p.n_modules * F::kUBlk + kEpiWarps * ob * kStageOut;
+      const int st = (kSmemMax - fixed) / sb;
+      if (st >= 6 || (km == 1 && st >= 2)) {
+        chosen = km;
+        bufs = ob;
+        stages = st > 12 ? 12 : st;
+        break;
+      }
     }
   }
   if (chosen == 0)
     return set_error(LF_ERR_UNSUPPORTED, "fused LoRA: %d modules of rank %d do not fit", p.n_modules, R);
   p.kmax = chosen;
+  p.out_bufs = bufs;
   p.stages = stages;
   p.stage_bytes = sb;
   p.u_cols = uint32_t(chosen * p.n_modules * RP);
