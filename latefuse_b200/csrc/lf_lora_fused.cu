@@ -7,11 +7,14 @@
 //
 // An item is one tile record (128 tokens) times one column chunk (chunk_cols of
 // every module's hidden columns).  One persistent CTA per SM runs items one after
-// another with three roles around ONE ring of shared-memory stages:
-//   warp 0      producer: for each item, the x K-blocks with the A boxes of the
-//               round's segments ("x stages"), then for each 64-column y box the
-//               matching B boxes ("B stages"), by TMA, as far ahead as the ring
-//               allows;
+// another with four roles around two rings of shared-memory stages:
+//   warp 0      x producer: for each item, the x K-blocks with the A boxes of the
+//               round's segments, by TMA, through a ring of x stages;
+//   warp 14     B producer: for each 64-column y box the matching B boxes, through
+//               a separate, deeper ring of small stages, from the start of the
+//               item: the B factors (scattered 2 KB boxes of the slot cache, whose
+//               latency set the pace when they shared the x ring) are in shared
+//               memory by the time the shrink is done;
 //   warp 1      MMA issuer: u = x A into a TMEM accumulator (one MMA per K step,
 //               N = segments x modules x rank), then for each y box the delta u B
 //               (K = rank, N = 64) into one of four TMEM accumulators; a stage is
@@ -47,11 +50,12 @@ using namespace rec;
 constexpr int kBoxBytes = kTile * 64 * 2;  // one 128 x 64 box of x or y, 16 KB
 constexpr int kGroups = 3;                 // epilogue groups: y boxes go round-robin to them
 constexpr int kDBufs = 4;                  // 64-column TMEM delta accumulators
-constexpr int kFusedThreads = 64 + 128 * kGroups;
+constexpr int kEpiWarps = 4 * kGroups;       // warps 2 .. 2 + kEpiWarps - 1
+constexpr int kBWarp = 2 + kEpiWarps;         // the B producer
+constexpr int kFusedThreads = 32 * (kBWarp + 1);
 constexpr int kSmemMax = 227 * 1024;       // dynamic shared memory per CTA on sm_100
 constexpr int kFixedBytes = 2048;          // alignment slack + barriers
 constexpr int kStageOut = 32 * 128;        // one warp's 32 rows x 64 columns of the delta (SW128)
-constexpr int kEpiWarps = kFusedThreads / 32 - 2;
 
 template <int R>
 struct FusedOps {
@@ -81,18 +85,22 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
   const int NS = p.stages, KM = p.kmax, n_mod = p.n_modules;
   const int nkb = p.hidden / 64;
   const int nyb = p.chunk_cols / 64;
+  const int NB = p.b_stages;
   const uint32_t s_ring = base;
-  const uint32_t s_u = s_ring + uint32_t(NS * p.stage_bytes);
+  const uint32_t s_bring = s_ring + uint32_t(NS * p.stage_bytes);
+  const uint32_t s_u = s_bring + uint32_t(NB * p.b_stage_bytes);
   const uint32_t s_out = s_u + uint32_t(KM * n_mod * F::kUBlk);  // a staging box per epilogue warp
   const uint32_t s_zero = s_out + uint32_t(kEpiWarps * p.out_bufs * kStageOut);
   const uint32_t s_meta = s_zero + F::kZeroBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + (s_meta - base));
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  const int FULL = 0, EMPTY = NS, DFULL = 2 * NS, DEMPTY = DFULL + kDBufs, UFULL = DEMPTY + kDBufs,
-            UEMPTY = UFULL + 1, UREADY = UEMPTY + 1, USFREE = UREADY + 1, DRAIN = USFREE + 1, NBAR = DRAIN + 1;
+  const int FULL = 0, EMPTY = NS, BFULL = 2 * NS, BEMPTY = BFULL + NB, DFULL = BEMPTY + NB,
+            DEMPTY = DFULL + kDBufs, UFULL = DEMPTY + kDBufs, UEMPTY = UFULL + 1, UREADY = UEMPTY + 1,
+            USFREE = UREADY + 1, DRAIN = USFREE + 1, NBAR = DRAIN + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(&bars[NBAR]);
   int32_t* s_abort = reinterpret_cast<int32_t*>(tmem_slot + 1);
   auto stage = [&](int k) { return s_ring + uint32_t((k % NS) * p.stage_bytes); };
+  auto bstage = [&](int k) { return s_bring + uint32_t((k % NB) * p.b_stage_bytes); };
 
   const int C = p.n_chunks;
   const int n_items = p.n_tiles * C;
@@ -102,6 +110,10 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(bar(FULL + i), 1);
       mbar_init(bar(EMPTY + i), 1);  // the commit of the MMAs that read the stage
+    }
+    for (int i = 0; i < NB; ++i) {
+      mbar_init(bar(BFULL + i), 1);
+      mbar_init(bar(BEMPTY + i), 1);
     }
     for (int i = 0; i < kDBufs; ++i) {
       mbar_init(bar(DFULL + i), 1);
@@ -147,7 +159,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
   };
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------------ x producer
     if (lane == 0) {
       int k = 0;  // ring position
       bool stop = false;
@@ -160,7 +172,6 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
       };
       for (int item = blockIdx.x; item < n_items && !stop; item += gridDim.x) {
         const int4 rc = __ldg(recs + item / C);
-        const int ch = item % C;
         if (!rec_valid(rc)) continue;
         const int ns = sub_items(rc, p.n_segs);
         const int32_t row0 = rc.x * kTile;
@@ -185,17 +196,36 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
                 for (int m = 0; m < n_mod; ++m) tma_load_3d(ab + m * F::kABox, &p.a_map[m], full, 0, kb * 64, slot);
             }
           }
-          if (stop) break;
+        }
+      }
+      if (aborted(s_abort)) {  // copies nobody consumed land before the CTA exits (bounded)
+        for (int q = (k > NS ? k - NS : 0); q < k; ++q) mbar_wait(bar(FULL + q % NS), (q / NS) & 1);
+      }
+    }
+  } else if (warp == kBWarp) {
+    // ------------------------------------------------------------ B producer
+    if (lane == 0) {
+      int kb = 0;  // B ring position
+      bool stop = false;
+      for (int item = blockIdx.x; item < n_items && !stop; item += gridDim.x) {
+        const int4 rc = __ldg(recs + item / C);
+        const int ch = item % C;
+        if (!rec_valid(rc)) continue;
+        const int ns = sub_items(rc, p.n_segs);
+        for (int j0 = 0; j0 < ns && !stop; j0 += KM) {
+          const int kp = min(KM, ns - j0);
           for (int m = 0; m < n_mod && !stop; ++m) {
-            for (int b = 0; b < nyb; ++b, ++k) {
-              if (!acquire(k)) {
+            for (int b = 0; b < nyb; ++b, ++kb) {
+              if (aborted(s_abort) || !mbar_wait(bar(BEMPTY + kb % NB), ((kb / NB) & 1) ^ 1)) {
+                if (!aborted(s_abort)) fail();
                 stop = true;
                 break;
               }
-              const uint32_t st = stage(k);
-              const uint32_t full = bar(FULL + k % NS);
+              const uint32_t st = bstage(kb);
+              const uint32_t full = bar(BFULL + kb % NB);
               const int32_t hcol = ch * p.chunk_cols + b * 64;
               mbar_arrive_expect_tx(full, uint32_t(kp * F::kBBox));
+              // an out-of-range slot reads zeros (TMA fill); its rows get no delta
               for (int jj = 0; jj < kp; ++jj)
                 tma_load_3d(st + uint32_t(jj * F::kBBox), &p.b_map[m], full, hcol, 0,
                             sub_slot(rc, j0 + jj, p.seg_slot, p.n_segs));
@@ -204,7 +234,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
         }
       }
       if (aborted(s_abort)) {  // copies nobody consumed land before the CTA exits (bounded)
-        for (int q = (k > NS ? k - NS : 0); q < k; ++q) mbar_wait(bar(FULL + q % NS), (q / NS) & 1);
+        for (int q = (kb > NB ? kb - NB : 0); q < kb; ++q) mbar_wait(bar(BFULL + q % NB), (q / NB) & 1);
       }
     }
   } else if (warp == 1) {
@@ -213,7 +243,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
       constexpr uint32_t idesc_d = umma_idesc_f16(DT<T>::umma_fmt, kTile, 64, /*a_mn=*/0, /*b_mn=*/1);
       constexpr uint32_t idesc16 = umma_idesc_f16(DT<T>::umma_fmt, kTile, RP, /*a_mn=*/0, /*b_mn=*/1);
       const uint32_t s_zero_s = s_zero, s_zero_b = s_zero + 1024, s_zero_u = s_zero + 2048;
-      int k = 0, rk = 0, dk = 0;
+      int k = 0, kb = 0, rk = 0, dk = 0;  // x ring position, B ring position, round, y box
       bool stop = false, issued = false;
       auto full_wait = [&](int kk) {
         if (aborted(s_abort) || !mbar_wait(bar(FULL + kk % NS), (kk / NS) & 1)) {
@@ -234,7 +264,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
             stop = true;
             break;
           }
-          for (int kb = 0; kb < nkb; ++kb, ++k) {
+          for (int kx = 0; kx < nkb; ++kx, ++k) {
             if (!full_wait(k)) {
               stop = true;
               break;
@@ -250,7 +280,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
                   const uint64_t ad = smem_desc(st + q * 32, 16, 1024, 2);
                   const uint32_t bstart = ab + q * 16 * (R * 2);
                   const uint64_t bd = smem_desc(bstart, 128, s_zero_s + q * 256 - bstart, 0);
-                  umma_f16(tmem + jm * RP, ad, bd, idesc16, (kb | q) != 0 ? 1u : 0u);
+                  umma_f16(tmem + jm * RP, ad, bd, idesc16, (kx | q) != 0 ? 1u : 0u);
                 }
               }
             } else {
@@ -261,7 +291,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
               for (int q = 0; q < 4; ++q) {
                 const uint64_t ad = smem_desc(st + q * 32, 16, 1024, 2);
                 const uint64_t bd = smem_desc(st + kBoxBytes + q * 16 * (R * 2), F::kABox, 8 * R * 2, F::kALayout);
-                umma_f16(tmem, ad, bd, idesc, (kb | q) != 0 ? 1u : 0u);
+                umma_f16(tmem, ad, bd, idesc, (kx | q) != 0 ? 1u : 0u);
               }
             }
             issued = true;
@@ -277,15 +307,16 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
           }
           tc_fence_after();
           for (int m = 0; m < n_mod && !stop; ++m) {
-            for (int b = 0; b < nyb; ++b, ++k, ++dk) {
+            for (int b = 0; b < nyb; ++b, ++kb, ++dk) {
               const int a = dk % kDBufs;
-              if (!full_wait(k) || !mbar_wait(bar(DEMPTY + a), ((dk / kDBufs) & 1) ^ 1)) {
+              if (aborted(s_abort) || !mbar_wait(bar(BFULL + kb % NB), (kb / NB) & 1) ||
+                  !mbar_wait(bar(DEMPTY + a), ((dk / kDBufs) & 1) ^ 1)) {
                 if (!aborted(s_abort)) fail();
                 stop = true;
                 break;
               }
               tc_fence_after();
-              const uint32_t st = stage(k);
+              const uint32_t st = bstage(kb);
               const uint32_t d = tmem + p.d_col + uint32_t(a * 64);
               for (int jj = 0; jj < kp; ++jj) {
                 const uint32_t ub = s_u + uint32_t((jj * n_mod + m) * F::kUBlk);
@@ -305,7 +336,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
               }
               issued = true;
               umma_commit(bar(DFULL + a));
-              umma_commit(bar(EMPTY + k % NS));
+              umma_commit(bar(BEMPTY + kb % NB));
             }
           }
           if (!stop) umma_commit(bar(USFREE));  // the u blocks may be rewritten once these MMAs finish
@@ -468,24 +499,31 @@ template <typename T, int R>
 int launch_fused(FusedApplyParams& p, cudaStream_t stream) {
   using F = FusedOps<R>;
   constexpr int RP = F::RP;
-  // segments per round: two where the ring then keeps at least 6 stages (one where it
-  // would not), so that u for all of them (kmax * n_modules * RP TMEM columns) and the
-  // four 64-column delta accumulators fit in TMEM; a stage holds an x box with the
-  // round's A boxes, or the B boxes of one y box
-  // each epilogue warp stages its delta rows in two boxes where they fit (two reductions
-  // in flight), else in one
-  int chosen = 0, stages = 0, sb = 0, fixed = 0, bufs = 0;
-  for (int ob = 2; ob >= 1 && chosen == 0; --ob) {
-    for (int km = 2; km >= 1; --km) {
+  // Sizes, in order of preference: two segments per round (u for all of them, kmax *
+  // n_modules * RP TMEM columns, and the four 64-column delta accumulators fit in
+  // TMEM), the deepest B ring, two staging boxes per epilogue warp, with at least 4 x
+  // stages (4 stages of 16 KB per SM already stream x at the full HBM rate); where
+  // nothing gives 4, the smallest sizes with 2.
+  int chosen = 0, stages = 0, sb = 0, fixed = 0, bufs = 0, nbs = 0;
+  for (int pass = 0; pass < 2 && chosen == 0; ++pass) {
+    const int need = pass == 0 ? 4 : 2;
+    for (int km = 2; km >= 1 && chosen == 0; --km) {
       if (km * p.n_modules * RP > 256) continue;
-      sb = kBoxBytes + km * p.n_modules * F::kABox;  // an x stage; a B stage (km * kBBox) is smaller
-      fixed = kFixedBytes + F::kZeroBytes + km * p.n_modules * F::kUBlk + kEpiWarps * ob * kStageOut;
-      const int st = (kSmemMax - fixed) / sb;
-      if (st >= 6 || (km == 1 && st >= 2)) {
-        chosen = km;
-        bufs = ob;
-        stages = st > 12 ? 12 : st;
-        break;
+      for (int nb : {16, 12, 8, 6, 4, 2}) {
+        for (int ob = 2; ob >= 1; --ob) {
+          sb = kBoxBytes + km * p.n_modules * F::kABox;
+          fixed = kFixedBytes + F::kZeroBytes + km * p.n_modules * F::kUBlk + kEpiWarps * ob * kStageOut +
+                  nb * km * F::kBBox;
+          const int st = (kSmemMax - fixed) / sb;
+          if (st >= need) {
+            chosen = km;
+            bufs = ob;
+            nbs = nb;
+            stages = st > 12 ? 12 : st;
+            break;
+          }
+        }
+        if (chosen) break;
       }
     }
   }
@@ -495,6 +533,8 @@ int launch_fused(FusedApplyParams& p, cudaStream_t stream) {
   p.out_bufs = bufs;
   p.stages = stages;
   p.stage_bytes = sb;
+  p.b_stages = nbs;
+  p.b_stage_bytes = chosen * F::kBBox;
   p.u_cols = uint32_t(chosen * p.n_modules * RP);
   p.d_col = (p.u_cols + 63u) & ~63u;
   uint32_t alloc = 32;
