@@ -131,7 +131,6 @@ struct alignas(64) FusedApplyParams {
   int32_t out_bufs;                  // staging boxes per epilogue warp (1 or 2)
   uint32_t u_cols;                   // TMEM columns of the u accumulator (kmax * n_modules * rank, padded)
   uint32_t d_col;                    // first TMEM column of the 64-column delta accumulators
-  int32_t d_bufs;                    // delta accumulators (TMEM columns left by u, at most 8)
   uint32_t tmem_alloc;               // TMEM columns allocated
   const int32_t* tiles;              // records {tile, first segment, segment count, first slot}
   const int32_t* seg_start;

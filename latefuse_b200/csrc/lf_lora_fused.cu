@@ -17,11 +17,8 @@
 //               memory by the time the shrink is done;
 //   warp 1      MMA issuer: u = x A into a TMEM accumulator (one MMA per K step,
 //               N = segments x modules x rank), then for each y box the delta u B
-//               (K = rank, N = 64) into one of up to eight TMEM accumulators (every
-//               TMEM column u leaves free: a box's MMA waits for the box that many
-//               boxes earlier to be drained, so more buffers mean fewer round trips
-//               between the MMA thread and the epilogue); a stage is free as soon as
-//               its MMAs complete;
+//               (K = rank, N = 64) into one of four TMEM accumulators; a stage is
+//               free as soon as its MMAs complete;
 //   warps 2..   epilogue, three groups of four warps (a warp per TMEM lane quadrant,
 //               a thread per tile row).  The groups round u and write each (segment,
 //               module) block into shared memory as the delta MMA's K-major operand
@@ -52,7 +49,7 @@ using namespace rec;
 
 constexpr int kBoxBytes = kTile * 64 * 2;  // one 128 x 64 box of x or y, 16 KB
 constexpr int kGroups = 3;                 // epilogue groups: y boxes go round-robin to them
-constexpr int kMaxDBufs = 8;               // 64-column TMEM delta accumulators (every free TMEM column)
+constexpr int kDBufs = 4;                  // 64-column TMEM delta accumulators
 constexpr int kEpiWarps = 4 * kGroups;       // warps 2 .. 2 + kEpiWarps - 1
 constexpr int kBWarp = 2 + kEpiWarps;         // the B producer
 constexpr int kFusedThreads = 32 * (kBWarp + 1);
@@ -97,9 +94,8 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
   const uint32_t s_meta = s_zero + F::kZeroBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + (s_meta - base));
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  const int ND = p.d_bufs;
   const int FULL = 0, EMPTY = NS, BFULL = 2 * NS, BEMPTY = BFULL + NB, DFULL = BEMPTY + NB,
-            DEMPTY = DFULL + kMaxDBufs, UFULL = DEMPTY + kMaxDBufs, UEMPTY = UFULL + 1, UREADY = UEMPTY + 1,
+            DEMPTY = DFULL + kDBufs, UFULL = DEMPTY + kDBufs, UEMPTY = UFULL + 1, UREADY = UEMPTY + 1,
             USFREE = UREADY + 1, DRAIN = USFREE + 1, NBAR = DRAIN + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(&bars[NBAR]);
   int32_t* s_abort = reinterpret_cast<int32_t*>(tmem_slot + 1);
@@ -119,7 +115,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
       mbar_init(bar(BFULL + i), 1);
       mbar_init(bar(BEMPTY + i), 1);
     }
-    for (int i = 0; i < ND; ++i) {
+    for (int i = 0; i < kDBufs; ++i) {
       mbar_init(bar(DFULL + i), 1);
       mbar_init(bar(DEMPTY + i), 4);  // the four warps of the group that drained it
     }
@@ -312,9 +308,9 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
           tc_fence_after();
           for (int m = 0; m < n_mod && !stop; ++m) {
             for (int b = 0; b < nyb; ++b, ++kb, ++dk) {
-              const int a = dk % ND;
+              const int a = dk % kDBufs;
               if (aborted(s_abort) || !mbar_wait(bar(BFULL + kb % NB), (kb / NB) & 1) ||
-                  !mbar_wait(bar(DEMPTY + a), ((dk / ND) & 1) ^ 1)) {
+                  !mbar_wait(bar(DEMPTY + a), ((dk / kDBufs) & 1) ^ 1)) {
                 if (!aborted(s_abort)) fail();
                 stop = true;
                 break;
@@ -430,9 +426,9 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
         for (int m = 0; m < n_mod && !stop; ++m) {
           for (int b = 0; b < nyb; ++b, ++dk) {
             if (dk % kGroups != eg) continue;
-            const int a = dk % ND;
+            const int a = dk % kDBufs;
             bool ok2 = !aborted(s_abort);
-            if (ok2 && !mbar_wait(bar(DFULL + a), (dk / ND) & 1)) {
+            if (ok2 && !mbar_wait(bar(DFULL + a), (dk / kDBufs) & 1)) {
               fail();
               ok2 = false;
             }
@@ -504,7 +500,7 @@ int launch_fused(FusedApplyParams& p, cudaStream_t stream) {
   using F = FusedOps<R>;
   constexpr int RP = F::RP;
   // Sizes, in order of preference: two segments per round (u for all of them, kmax *
-  // n_modules * RP TMEM columns, and at least four 64-column delta accumulators fit in
+  // n_modules * RP TMEM columns, and the four 64-column delta accumulators fit in
   // TMEM), the deepest B ring, two staging boxes per epilogue warp, with at least 4 x
   // stages (4 stages of 16 KB per SM already stream x at the full HBM rate); where
   // nothing gives 4, the smallest sizes with 2.
@@ -541,9 +537,9 @@ int launch_fused(FusedApplyParams& p, cudaStream_t stream) {
   p.b_stage_bytes = chosen * F::kBBox;
   p.u_cols = uint32_t(chosen * p.n_modules * RP);
   p.d_col = (p.u_cols + 63u) & ~63u;
-  p.d_bufs = int((512u - p.d_col) / 64u);
-  if (p.d_bufs > kMaxDBufs) p.d_bufs = kMaxDBufs;
-  p.tmem_alloc = 512;
+  uint32_t alloc = 32;
+  while (alloc < p.d_col + 64u * kDBufs) alloc <<= 1;
+  p.tmem_alloc = alloc;
   // one CTA per SM: the request stays above half of the SM's shared memory, so a
   // second CTA of this kernel can never wait on TMEM the first one holds
   size_t smem = size_t(fixed) + size_t(stages) * size_t(sb);
