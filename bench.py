@@ -60,6 +60,10 @@ FALLBACK_BF16_TFLOPS = 1590.0
 # --warmup 1 --no-cpu-baseline --no-e2e --no-extras` (same tokens and segments as the
 # full workload; the adapters read are the batch's tenants in both).
 NCU_TRAFFIC_QKV_GEMM = 119.5e6
+# DRAM bytes (read 70.04 MB + write 0.15 MB) and duration (22.85 us) of one lf_lora_apply
+# launch (the one-launch kernel) on the isolated op at rank 16, from one ncu capture
+NCU_TRAFFIC_LORA_OP_R16 = 70.19e6
+NCU_DURATION_LORA_OP_R16 = 22.85
 
 
 def bge_m3_config(layers: int = 24):
@@ -471,6 +475,10 @@ def run_serve(args):
             "achieved": r16["apply_flushed_gbs"], "peak": op.get("peak_gbs"), "unit": "GB/s",
             "frac": r16["apply_flushed_frac_of_hbm"], "algorithmic_bytes": r16["algorithmic_bytes"],
             "us": r16["apply_flushed_us"], "two_launch_us": r16["two_launch_flushed_us"],
+            "traffic": NCU_TRAFFIC_LORA_OP_R16,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch (y's writes stay in L2)",
+            "ncu_duration_us": NCU_DURATION_LORA_OP_R16,
+            "ncu_frac": r16["algorithmic_bytes"] / (NCU_DURATION_LORA_OP_R16 * 1e-6) / 1e9 / op.get("peak_gbs"),
             "note": "in the serving step the shrink and the expand run inside the q/k/v and attention-output "
                     "projection GEMMs (lf_linear_lora_shrink): no separate launch exists to time, and their "
                     "in-step cost is lora_overhead",
