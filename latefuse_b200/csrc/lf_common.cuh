@@ -216,30 +216,6 @@ __device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t bar, uint32_t par
   return done != 0;
 }
 
-// Non-blocking test of an mbarrier phase.
-__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(done)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-
-// Bounded wait that polls instead of letting the thread be suspended, for hand-offs
-// whose latency sets a kernel's pace.  Returns false on timeout.
-__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity) {
-  if (mbar_test_wait(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_test_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && global_timer_ns() - t0 > LF_WAIT_LIMIT_NS) return false;
-  }
-}
-
 // Bounded wait on an mbarrier phase. Returns false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;

@@ -309,9 +309,8 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
           for (int m = 0; m < n_mod && !stop; ++m) {
             for (int b = 0; b < nyb; ++b, ++kb, ++dk) {
               const int a = dk % kDBufs;
-              // polled waits: these hand-offs set the pace of the delta boxes
-              if (aborted(s_abort) || !mbar_wait_spin(bar(BFULL + kb % NB), (kb / NB) & 1) ||
-                  !mbar_wait_spin(bar(DEMPTY + a), ((dk / kDBufs) & 1) ^ 1)) {
+              if (aborted(s_abort) || !mbar_wait(bar(BFULL + kb % NB), (kb / NB) & 1) ||
+                  !mbar_wait(bar(DEMPTY + a), ((dk / kDBufs) & 1) ^ 1)) {
                 if (!aborted(s_abort)) fail();
                 stop = true;
                 break;
@@ -429,7 +428,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
             if (dk % kGroups != eg) continue;
             const int a = dk % kDBufs;
             bool ok2 = !aborted(s_abort);
-            if (ok2 && !mbar_wait_spin(bar(DFULL + a), (dk / kDBufs) & 1)) {
+            if (ok2 && !mbar_wait(bar(DFULL + a), (dk / kDBufs) & 1)) {
               fail();
               ok2 = false;
             }
