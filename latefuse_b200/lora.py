@@ -8,8 +8,10 @@ each targeted projection output gets
 The reference computes this with a per-layer ``torch.cat``/``index_select``
 gather of the per-row factors followed by two ``torch.bmm`` calls and an add
 (``src/latefuse/ops/lora.py:57,75``, ``src/latefuse/model/hf_wrapper.py:213-217``).
-Here one :func:`lora_apply` call runs the sm_100a shrink and expand kernels,
-which read each tenant's factors in place from the slot cache.
+Here one :func:`lora_apply` call runs the sm_100a kernels, which read each
+tenant's factors in place from the slot cache: for one module, a single kernel
+that keeps the shrink output on chip and adds the delta to y in L2; for several
+modules sharing x, a shrink launch and an expand launch (same bits either way).
 """
 
 from __future__ import annotations
