@@ -55,11 +55,11 @@ TARGETS = ["query", "key", "value", "dense"]
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 # DRAM bytes (read + write) of one q/k/v lf_linear_lora_shrink launch at 17,410 tokens x
-# 3072 x 1024, rank 16, 39 segments, from one ncu capture (dram__bytes_read.sum 52.9 MB +
-# dram__bytes_write.sum 66.7 MB) of `bench.py --layers 2 --adapters 500 --steps 1
+# 3072 x 1024, rank 16, 39 segments, from one ncu capture (dram__bytes_read.sum 52.6 MB +
+# dram__bytes_write.sum 63.2 MB) of `bench.py --layers 2 --adapters 500 --steps 1
 # --warmup 1 --no-cpu-baseline --no-e2e --no-extras` (same tokens and segments as the
 # full workload; the adapters read are the batch's tenants in both).
-NCU_TRAFFIC_QKV_GEMM = 119.5e6
+NCU_TRAFFIC_QKV_GEMM = 115.9e6
 # DRAM bytes (read 70.04 MB + write 0.15 MB) and duration (22.85 us) of one lf_lora_apply
 # launch (the one-launch kernel) on the isolated op at rank 16, from one ncu capture
 NCU_TRAFFIC_LORA_OP_R16 = 70.19e6
