@@ -195,7 +195,7 @@ size_t lf_lora_workspace_bytes(int dtype, int64_t n_tokens, int rank, int n_modu
  * modules that share the input x (query/key/value of one layer share one read of
  * x).  One call replaces, per layer, the reference's cat -> bmm -> bmm -> add
  * sequence of every hook (src/latefuse/model/hf_wrapper.py:213-217).  With one
- * module, tile records, bf16/f16, rank 8/16/32/64, hidden a multiple of 64,
+ * module, tile records, bf16/f16, rank 8/16/32/64, hidden a multiple of 128,
  * 16-byte aligned buffers and x not overlapping y, it runs as ONE kernel that keeps u on chip
  * (the workspace is then unused; LF_OPT_FUSED_APPLY = 0 selects the shrink and
  * expand launches, which give the same bits); otherwise as a shrink launch into

@@ -432,17 +432,17 @@ static bool ranges_overlap(const void* a, size_t na, const void* b, size_t nb) {
 }
 
 // Column chunks per tile record: doubled while the items still fit on the SMs at one
-// each (a split item reads the record's x again, from L2), each chunk a multiple of 64
-// columns and at least 128 wide; or the LF_OPT_FUSED_SPLIT choice.  At 128 records of
+// each (a split item reads the record's x again, from L2), each chunk a multiple of 128
+// columns; or the LF_OPT_FUSED_SPLIT choice.  At 128 records of
 // the isolated op one chunk measured 29 us, two 33.
 static int fused_chunks(int hidden, int n_tiles) {
   const int forced = g_fused_split.load();
-  if (forced > 0) return (hidden % (64 * forced) == 0) ? forced : -1;
+  if (forced > 0) return (hidden % (128 * forced) == 0) ? forced : -1;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   int c = 1;
-  while (int64_t(n_tiles) * c * 2 <= sms && hidden % (64 * 2 * c) == 0 && hidden / (2 * c) >= 128) c *= 2;
+  while (int64_t(n_tiles) * c * 2 <= sms && hidden % (128 * 2 * c) == 0) c *= 2;
   return c;
 }
 
@@ -455,7 +455,7 @@ static int fused_apply(cudaStream_t stream, int dtype, const void* x, int64_t ld
                        const int32_t* seg_start, const int32_t* seg_len, const int32_t* seg_slot, int n_segs,
                        const int32_t* tiles, int n_tiles, int32_t* status) {
   if (!g_fused_apply.load() || !g_persistent.load() || option_force_simt()) return -1;
-  if (dtype == LF_DTYPE_F32 || !tc_rank(rank) || hidden % 64 != 0 || tiles == nullptr || n_tiles <= 0) return -1;
+  if (dtype == LF_DTYPE_F32 || !tc_rank(rank) || hidden % 128 != 0 || tiles == nullptr || n_tiles <= 0) return -1;
   // one module per call (the hf engine's hooks, the isolated op): with three modules
   // sharing x (q/k/v, 17,369 tokens) the shrink + expand launches measured faster
   // (68.6 vs 82.0 us), the expand's 128-column items draining y faster than the

@@ -122,15 +122,16 @@ struct alignas(64) FusedApplyParams {
   int32_t n_slots;
   int32_t n_tiles;                   // tile records
   int32_t n_chunks;                  // column chunks per record (items = n_tiles * n_chunks)
-  int32_t chunk_cols;                // hidden / n_chunks, a multiple of 64
+  int32_t chunk_cols;                // hidden / n_chunks, a multiple of 128
   int32_t kmax;                      // segments per round (one shrink pass + one expand pass)
   int32_t stages;                    // x ring stages (each an x box with the round's A boxes)
   int32_t stage_bytes;
-  int32_t b_stages;                  // B ring stages (each the round's B boxes of one y box)
+  int32_t b_stages;                  // B ring stages (each the round's B boxes of one 128-column step)
   int32_t b_stage_bytes;
   int32_t out_bufs;                  // staging boxes per epilogue warp (1 or 2)
   uint32_t u_cols;                   // TMEM columns of the u accumulator (kmax * n_modules * rank, padded)
-  uint32_t d_col;                    // first TMEM column of the 64-column delta accumulators
+  uint32_t d_col;                    // first TMEM column of the 128-column delta accumulators
+  int32_t d_bufs;                    // delta accumulators (2 or 3)
   uint32_t tmem_alloc;               // TMEM columns allocated
   const int32_t* tiles;              // records {tile, first segment, segment count, first slot}
   const int32_t* seg_start;

@@ -10,20 +10,23 @@
 // another with four roles around two rings of shared-memory stages:
 //   warp 0      x producer: for each item, the x K-blocks with the A boxes of the
 //               round's segments, by TMA, through a ring of x stages;
-//   warp 14     B producer: for each 64-column y box the matching B boxes, through
+//   warp 14     B producer: for each 128-column step of y the matching B boxes, through
 //               a separate, deeper ring of small stages, from the start of the
 //               item: the B factors (scattered 2 KB boxes of the slot cache, whose
 //               latency set the pace when they shared the x ring) are in shared
 //               memory by the time the shrink is done;
 //   warp 1      MMA issuer: u = x A into a TMEM accumulator (one MMA per K step,
-//               N = segments x modules x rank), then for each y box the delta u B
-//               (K = rank, N = 64) into one of four TMEM accumulators; a stage is
-//               free as soon as its MMAs complete;
+//               N = segments x modules x rank), then for each 128-column step of y
+//               the delta u B (K = rank, N = 128: two 64-column boxes per MMA, which
+//               halves this thread's waits, MMAs and commits, whose latency set the
+//               pace at one box per step) into one of up to three TMEM accumulators;
+//               a stage is free as soon as its MMAs complete;
 //   warps 2..   epilogue, three groups of four warps (a warp per TMEM lane quadrant,
 //               a thread per tile row).  The groups round u and write each (segment,
 //               module) block into shared memory as the delta MMA's K-major operand
 //               (the product for rows of that segment, 0 for the others); then the y
-//               boxes go round-robin to the groups: each warp rounds its 32 rows of
+//               steps go round-robin to the groups; for each 64-column half of a step
+//               each warp rounds its 32 rows of
 //               the delta, stages them (two staging boxes per warp, so two
 //               reductions are in flight) and adds them to y in L2 with one TMA
 //               reduction (cp.reduce.async.bulk.tensor .add), which computes
@@ -49,7 +52,7 @@ using namespace rec;
 
 constexpr int kBoxBytes = kTile * 64 * 2;  // one 128 x 64 box of x or y, 16 KB
 constexpr int kGroups = 3;                 // epilogue groups: y boxes go round-robin to them
-constexpr int kDBufs = 4;                  // 64-column TMEM delta accumulators
+constexpr int kMaxDBufs = 3;               // 128-column TMEM delta accumulators (fewer where u needs the room)
 constexpr int kEpiWarps = 4 * kGroups;       // warps 2 .. 2 + kEpiWarps - 1
 constexpr int kBWarp = 2 + kEpiWarps;         // the B producer
 constexpr int kFusedThreads = 32 * (kBWarp + 1);
@@ -65,8 +68,9 @@ struct FusedOps {
   static constexpr int kUBlk = kTile * R * 2;   // u block: 128 rows of R (K-major, no swizzle)
   static constexpr uint32_t kALayout = (R == 8) ? 0u : (R == 16) ? 6u : (R == 32) ? 4u : 2u;
   // rank 8 pads K or N to 16 with zero operands: [0, 1 KB) the shrink's A columns
-  // 8..15, [1, 2 KB) the delta's B rows 8..15, [2, 4 KB) the u blocks' columns 8..15
-  static constexpr int kZeroBytes = (R == 8) ? 4096 : 0;
+  // 8..15, [1, 3 KB) the delta's B rows 8..15 (two 64-column atoms), [3, 5 KB) the u
+  // blocks' columns 8..15
+  static constexpr int kZeroBytes = (R == 8) ? 5120 : 0;
 };
 
 }  // namespace
@@ -84,7 +88,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int NS = p.stages, KM = p.kmax, n_mod = p.n_modules;
   const int nkb = p.hidden / 64;
-  const int nyb = p.chunk_cols / 64;
+  const int nys = p.chunk_cols / 128;  // 128-column steps of y per module
   const int NB = p.b_stages;
   const uint32_t s_ring = base;
   const uint32_t s_bring = s_ring + uint32_t(NS * p.stage_bytes);
@@ -95,12 +99,13 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
   uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + (s_meta - base));
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   const int FULL = 0, EMPTY = NS, BFULL = 2 * NS, BEMPTY = BFULL + NB, DFULL = BEMPTY + NB,
-            DEMPTY = DFULL + kDBufs, UFULL = DEMPTY + kDBufs, UEMPTY = UFULL + 1, UREADY = UEMPTY + 1,
+            DEMPTY = DFULL + kMaxDBufs, UFULL = DEMPTY + kMaxDBufs, UEMPTY = UFULL + 1, UREADY = UEMPTY + 1,
             USFREE = UREADY + 1, DRAIN = USFREE + 1, NBAR = DRAIN + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(&bars[NBAR]);
   int32_t* s_abort = reinterpret_cast<int32_t*>(tmem_slot + 1);
   auto stage = [&](int k) { return s_ring + uint32_t((k % NS) * p.stage_bytes); };
   auto bstage = [&](int k) { return s_bring + uint32_t((k % NB) * p.b_stage_bytes); };
+  const int ND = p.d_bufs;
 
   const int C = p.n_chunks;
   const int n_items = p.n_tiles * C;
@@ -115,7 +120,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
       mbar_init(bar(BFULL + i), 1);
       mbar_init(bar(BEMPTY + i), 1);
     }
-    for (int i = 0; i < kDBufs; ++i) {
+    for (int i = 0; i < ND; ++i) {
       mbar_init(bar(DFULL + i), 1);
       mbar_init(bar(DEMPTY + i), 4);  // the four warps of the group that drained it
     }
@@ -215,7 +220,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
         for (int j0 = 0; j0 < ns && !stop; j0 += KM) {
           const int kp = min(KM, ns - j0);
           for (int m = 0; m < n_mod && !stop; ++m) {
-            for (int b = 0; b < nyb; ++b, ++kb) {
+            for (int b = 0; b < nys; ++b, ++kb) {
               if (aborted(s_abort) || !mbar_wait(bar(BEMPTY + kb % NB), ((kb / NB) & 1) ^ 1)) {
                 if (!aborted(s_abort)) fail();
                 stop = true;
@@ -223,12 +228,14 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
               }
               const uint32_t st = bstage(kb);
               const uint32_t full = bar(BFULL + kb % NB);
-              const int32_t hcol = ch * p.chunk_cols + b * 64;
-              mbar_arrive_expect_tx(full, uint32_t(kp * F::kBBox));
+              const int32_t hcol = ch * p.chunk_cols + b * 128;
+              mbar_arrive_expect_tx(full, uint32_t(kp * 2 * F::kBBox));
               // an out-of-range slot reads zeros (TMA fill); its rows get no delta
-              for (int jj = 0; jj < kp; ++jj)
-                tma_load_3d(st + uint32_t(jj * F::kBBox), &p.b_map[m], full, hcol, 0,
-                            sub_slot(rc, j0 + jj, p.seg_slot, p.n_segs));
+              for (int jj = 0; jj < kp; ++jj) {
+                const int32_t slot = sub_slot(rc, j0 + jj, p.seg_slot, p.n_segs);
+                for (int h = 0; h < 2; ++h)  // the step's two 64-column atoms, kBBox apart
+                  tma_load_3d(st + uint32_t((jj * 2 + h) * F::kBBox), &p.b_map[m], full, hcol + h * 64, 0, slot);
+              }
             }
           }
         }
@@ -240,9 +247,9 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_d = umma_idesc_f16(DT<T>::umma_fmt, kTile, 64, /*a_mn=*/0, /*b_mn=*/1);
+      constexpr uint32_t idesc_d = umma_idesc_f16(DT<T>::umma_fmt, kTile, 128, /*a_mn=*/0, /*b_mn=*/1);
       constexpr uint32_t idesc16 = umma_idesc_f16(DT<T>::umma_fmt, kTile, RP, /*a_mn=*/0, /*b_mn=*/1);
-      const uint32_t s_zero_s = s_zero, s_zero_b = s_zero + 1024, s_zero_u = s_zero + 2048;
+      const uint32_t s_zero_s = s_zero, s_zero_b = s_zero + 1024, s_zero_u = s_zero + 3072;
       int k = 0, kb = 0, rk = 0, dk = 0;  // x ring position, B ring position, round, y box
       bool stop = false, issued = false;
       auto full_wait = [&](int kk) {
@@ -307,20 +314,20 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
           }
           tc_fence_after();
           for (int m = 0; m < n_mod && !stop; ++m) {
-            for (int b = 0; b < nyb; ++b, ++kb, ++dk) {
-              const int a = dk % kDBufs;
+            for (int b = 0; b < nys; ++b, ++kb, ++dk) {
+              const int a = dk % ND;
               if (aborted(s_abort) || !mbar_wait(bar(BFULL + kb % NB), (kb / NB) & 1) ||
-                  !mbar_wait(bar(DEMPTY + a), ((dk / kDBufs) & 1) ^ 1)) {
+                  !mbar_wait(bar(DEMPTY + a), ((dk / ND) & 1) ^ 1)) {
                 if (!aborted(s_abort)) fail();
                 stop = true;
                 break;
               }
               tc_fence_after();
               const uint32_t st = bstage(kb);
-              const uint32_t d = tmem + p.d_col + uint32_t(a * 64);
+              const uint32_t d = tmem + p.d_col + uint32_t(a * 128);
               for (int jj = 0; jj < kp; ++jj) {
                 const uint32_t ub = s_u + uint32_t((jj * n_mod + m) * F::kUBlk);
-                const uint32_t bb = st + uint32_t(jj * F::kBBox);
+                const uint32_t bb = st + uint32_t(jj * 2 * F::kBBox);
                 if (R == 8) {
                   const uint64_t ad = smem_desc(ub, s_zero_u - ub, 128, 0);  // K 8..15 read zeros
                   const uint64_t bd = smem_desc(bb, F::kBBox, s_zero_b - bb, 2);
@@ -422,13 +429,13 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
           mbar_arrive(bar(UEMPTY));
           mbar_arrive(bar(UREADY));
         }
-        // (2) the delta, one 64-column y box at a time, the boxes dealt round-robin
+        // (2) the delta, one 128-column step of y at a time, the steps dealt round-robin
         for (int m = 0; m < n_mod && !stop; ++m) {
-          for (int b = 0; b < nyb; ++b, ++dk) {
+          for (int b = 0; b < nys; ++b, ++dk) {
             if (dk % kGroups != eg) continue;
-            const int a = dk % kDBufs;
+            const int a = dk % ND;
             bool ok2 = !aborted(s_abort);
-            if (ok2 && !mbar_wait(bar(DFULL + a), (dk / kDBufs) & 1)) {
+            if (ok2 && !mbar_wait(bar(DFULL + a), (dk / ND) & 1)) {
               fail();
               ok2 = false;
             }
@@ -437,46 +444,50 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
               break;
             }
             tc_fence_after();
-            uint32_t acc[64];
-            tmem_ld64(tmem + lane_base + p.d_col + uint32_t(a * 64), acc);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(DEMPTY + a));
-            if (!warp_rows) continue;
-            const uint32_t sbox = s_mine + uint32_t((nbox % p.out_bufs) * kStageOut);
-            uint8_t* my_line = gbase + (sbox - base) + lane * 128;  // this row in the SW128 staging box
-            // with two staging boxes two reductions are in flight per warp: the one issued two
-            // boxes ago has read this box; with one, the previous one has
-            if (lane == 0) {
-              if (p.out_bufs == 2)
-                tma_store_wait_read_le1();
-              else
-                tma_store_wait_read_all();
-            }
-            __syncwarp();
-            // round(delta) for the round's rows, -0 for the others (y + -0 is y).  The box
-            // is SW128: chunk c of row r sits at 16 * (c ^ (r % 8)) in its 128-byte line.
-            const bool in = j_row >= 0;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-              uint4 pk = make_uint4(0x80008000u, 0x80008000u, 0x80008000u, 0x80008000u);
-              if (in) {
-                pk.x = Pack2<T>::pack(__uint_as_float(acc[c * 8 + 0]), __uint_as_float(acc[c * 8 + 1]));
-                pk.y = Pack2<T>::pack(__uint_as_float(acc[c * 8 + 2]), __uint_as_float(acc[c * 8 + 3]));
-                pk.z = Pack2<T>::pack(__uint_as_float(acc[c * 8 + 4]), __uint_as_float(acc[c * 8 + 5]));
-                pk.w = Pack2<T>::pack(__uint_as_float(acc[c * 8 + 6]), __uint_as_float(acc[c * 8 + 7]));
+            for (int h = 0; h < 2; ++h) {  // the step's two 64-column halves
+              uint32_t acc[64];
+              tmem_ld64(tmem + lane_base + p.d_col + uint32_t(a * 128 + h * 64), acc);
+              if (h == 1) {  // both halves are in registers: the accumulator is free
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(DEMPTY + a));
               }
-              *reinterpret_cast<uint4*>(my_line + ((c ^ (lane & 7)) << 4)) = pk;
+              if (!warp_rows) continue;
+              const uint32_t sbox = s_mine + uint32_t((nbox % p.out_bufs) * kStageOut);
+              uint8_t* my_line = gbase + (sbox - base) + lane * 128;  // this row in the SW128 staging box
+              // with two staging boxes two reductions are in flight per warp: the one issued
+              // two boxes ago has read this box; with one, the previous one has
+              if (lane == 0) {
+                if (p.out_bufs == 2)
+                  tma_store_wait_read_le1();
+                else
+                  tma_store_wait_read_all();
+              }
+              __syncwarp();
+              // round(delta) for the round's rows, -0 for the others (y + -0 is y).  The box
+              // is SW128: chunk c of row r sits at 16 * (c ^ (r % 8)) in its 128-byte line.
+              const bool in = j_row >= 0;
+#pragma unroll
+              for (int c = 0; c < 8; ++c) {
+                uint4 pk = make_uint4(0x80008000u, 0x80008000u, 0x80008000u, 0x80008000u);
+                if (in) {
+                  pk.x = Pack2<T>::pack(__uint_as_float(acc[c * 8 + 0]), __uint_as_float(acc[c * 8 + 1]));
+                  pk.y = Pack2<T>::pack(__uint_as_float(acc[c * 8 + 2]), __uint_as_float(acc[c * 8 + 3]));
+                  pk.z = Pack2<T>::pack(__uint_as_float(acc[c * 8 + 4]), __uint_as_float(acc[c * 8 + 5]));
+                  pk.w = Pack2<T>::pack(__uint_as_float(acc[c * 8 + 6]), __uint_as_float(acc[c * 8 + 7]));
+                }
+                *reinterpret_cast<uint4*>(my_line + ((c ^ (lane & 7)) << 4)) = pk;
+              }
+              fence_proxy_async_smem();  // the rows are read by the TMA reduction (async proxy)
+              __syncwarp();
+              if (lane == 0) {
+                // rows past the end of the tokens are clipped
+                tma_reduce_add_2d(&p.ys_map, sbox,
+                                  int32_t(p.y_col_off[m]) + ch * p.chunk_cols + b * 128 + h * 64, int32_t(r0));
+                tma_store_commit();
+              }
+              ++nbox;
             }
-            fence_proxy_async_smem();  // the rows are read by the TMA reduction (async proxy)
-            __syncwarp();
-            if (lane == 0) {
-              // rows past the end of the tokens are clipped
-              tma_reduce_add_2d(&p.ys_map, sbox, int32_t(p.y_col_off[m]) + ch * p.chunk_cols + b * 64,
-                                int32_t(r0));
-              tma_store_commit();
-            }
-            ++nbox;
           }
         }
       }
@@ -500,7 +511,7 @@ int launch_fused(FusedApplyParams& p, cudaStream_t stream) {
   using F = FusedOps<R>;
   constexpr int RP = F::RP;
   // Sizes, in order of preference: two segments per round (u for all of them, kmax *
-  // n_modules * RP TMEM columns, and the four 64-column delta accumulators fit in
+  // n_modules * RP TMEM columns, and at least two 128-column delta accumulators fit in
   // TMEM), the deepest B ring, two staging boxes per epilogue warp, with at least 4 x
   // stages (4 stages of 16 KB per SM already stream x at the full HBM rate); where
   // nothing gives 4, the smallest sizes with 2.
@@ -513,7 +524,7 @@ int launch_fused(FusedApplyParams& p, cudaStream_t stream) {
         for (int ob = 2; ob >= 1; --ob) {
           sb = kBoxBytes + km * p.n_modules * F::kABox;
           fixed = kFixedBytes + F::kZeroBytes + km * p.n_modules * F::kUBlk + kEpiWarps * ob * kStageOut +
-                  nb * km * F::kBBox;
+                  nb * km * 2 * F::kBBox;
           const int st = (kSmemMax - fixed) / sb;
           if (st >= need) {
             chosen = km;
@@ -534,12 +545,12 @@ int launch_fused(FusedApplyParams& p, cudaStream_t stream) {
   p.stages = stages;
   p.stage_bytes = sb;
   p.b_stages = nbs;
-  p.b_stage_bytes = chosen * F::kBBox;
+  p.b_stage_bytes = chosen * 2 * F::kBBox;
   p.u_cols = uint32_t(chosen * p.n_modules * RP);
   p.d_col = (p.u_cols + 63u) & ~63u;
-  uint32_t alloc = 32;
-  while (alloc < p.d_col + 64u * kDBufs) alloc <<= 1;
-  p.tmem_alloc = alloc;
+  p.d_bufs = int((512u - p.d_col) / 128u);  // 2 or 3 (u takes at most 256 columns)
+  if (p.d_bufs > kMaxDBufs) p.d_bufs = kMaxDBufs;
+  p.tmem_alloc = 512;
   // one CTA per SM: the request stays above half of the SM's shared memory, so a
   // second CTA of this kernel can never wait on TMEM the first one holds
   size_t smem = size_t(fixed) + size_t(stages) * size_t(sb);
