@@ -513,11 +513,13 @@ int launch_fused(FusedApplyParams& p, cudaStream_t stream) {
   // Sizes, in order of preference: two segments per round (u for all of them, kmax *
   // n_modules * RP TMEM columns, and at least two 128-column delta accumulators fit in
   // TMEM), the deepest B ring, two staging boxes per epilogue warp, with at least 4 x
-  // stages (4 stages of 16 KB per SM already stream x at the full HBM rate); where
-  // nothing gives 4, the smallest sizes with 2.
+  // stages (4 stages of 16 KB per SM already stream x at the full HBM rate).  Where
+  // nothing gives 4 (three or four modules of rank 64) the call takes the two launches:
+  // sizes with 2 x stages and 2 B stages timed out in a test (the status word reported
+  // it; the cause was not found), so they are not used.
   int chosen = 0, stages = 0, sb = 0, fixed = 0, bufs = 0, nbs = 0;
-  for (int pass = 0; pass < 2 && chosen == 0; ++pass) {
-    const int need = pass == 0 ? 4 : 2;
+  for (int pass = 0; pass < 1 && chosen == 0; ++pass) {
+    const int need = 4;
     for (int km = 2; km >= 1 && chosen == 0; --km) {
       if (km * p.n_modules * RP > 256) continue;
       for (int nb : {16, 12, 8, 6, 4, 2}) {

@@ -78,10 +78,13 @@ def test_fused_equals_two_launches_many_segments(cuda, dtype, n_mod, R):
     assert st.n_multi > 0
     two, s2, l2 = apply(x, y, fc, st, mods, offs, fused=False)
     assert s2 == 0 and l2 == 2
+    # three or four modules of rank 64 do not fit the one-launch kernel's rings and take
+    # the two launches even under LF_OPT_FUSED_APPLY = 2
+    fits = n_mod * R < 192
     for split in (0, 1, 2, 4):
         one, s1, l1 = apply(x, y, fc, st, mods, offs, split=split)
         assert s1 == 0, nat.decode_status(s1)
-        assert l1 == 1
+        assert l1 == (1 if fits else 2)
         assert torch.equal(one, two), f"split {split}"
     ref = segmented_apply(x.cpu(), y.cpu(), a_of, b_of, list(zip(starts, lengths, slots)), col_offsets=offs,
                           modules=mods)
