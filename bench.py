@@ -60,10 +60,10 @@ FALLBACK_BF16_TFLOPS = 1590.0
 # --warmup 1 --no-cpu-baseline --no-e2e --no-extras` (same tokens and segments as the
 # full workload; the adapters read are the batch's tenants in both).
 NCU_TRAFFIC_QKV_GEMM = 115.9e6
-# DRAM bytes (read 70.04 MB + write 0.15 MB) and duration (22.85 us) of one lf_lora_apply
+# DRAM bytes (read 70.05 MB + write 0.13 MB) and duration (21.66 us) of one lf_lora_apply
 # launch (the one-launch kernel) on the isolated op at rank 16, from one ncu capture
-NCU_TRAFFIC_LORA_OP_R16 = 70.19e6
-NCU_DURATION_LORA_OP_R16 = 22.85
+NCU_TRAFFIC_LORA_OP_R16 = 70.18e6
+NCU_DURATION_LORA_OP_R16 = 21.66
 
 
 def bge_m3_config(layers: int = 24):
