@@ -11,7 +11,8 @@
 //   warp 0      x producer: for each item, the x K-blocks with the A boxes of the
 //               round's segments, by TMA, through a ring of x stages;
 //   warp 14     B producer: for each 128-column step of y the matching B boxes, through
-//               a separate, deeper ring of small stages, from the start of the
+//               a separate, deeper ring of small stages (freed by the epilogue group
+//               that drains the step), from the start of the
 //               item: the B factors (scattered 2 KB boxes of the slot cache, whose
 //               latency set the pace when they shared the x ring) are in shared
 //               memory by the time the shrink is done;
@@ -118,7 +119,9 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
     }
     for (int i = 0; i < NB; ++i) {
       mbar_init(bar(BFULL + i), 1);
-      mbar_init(bar(BEMPTY + i), 1);
+      // the four warps of the epilogue group that saw the step's delta complete (the MMAs
+      // that read the stage are done then), so the MMA thread commits once per step
+      mbar_init(bar(BEMPTY + i), 4);
     }
     for (int i = 0; i < ND; ++i) {
       mbar_init(bar(DFULL + i), 1);
@@ -343,7 +346,6 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
               }
               issued = true;
               umma_commit(bar(DFULL + a));
-              umma_commit(bar(BEMPTY + kb % NB));
             }
           }
           if (!stop) umma_commit(bar(USFREE));  // the u blocks may be rewritten once these MMAs finish
@@ -444,6 +446,8 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
               break;
             }
             tc_fence_after();
+            // the step's MMAs are done: its B stage (ring position = step index) is free
+            if (lane == 0) mbar_arrive(bar(BEMPTY + dk % NB));
             for (int h = 0; h < 2; ++h) {  // the step's two 64-column halves
               uint32_t acc[64];
               tmem_ld64(tmem + lane_base + p.d_col + uint32_t(a * 128 + h * 64), acc);
