@@ -50,6 +50,15 @@ def test_version_and_options(lib):
     assert lib.lf_set_option(999, 1) == LF_ERR_INVALID
     assert b"unknown option" in lib.lf_last_error()
     assert lib.lf_set_option(nat.LF_OPT_SHRINK_CLUSTER, 3) == LF_ERR_INVALID
+    # the one-launch lf_lora_apply: 0 off, 1 one-module calls (default), 2 every module count
+    for v in (0, 2, 1):
+        assert lib.lf_set_option(nat.LF_OPT_FUSED_APPLY, v) == 0
+    assert lib.lf_set_option(nat.LF_OPT_FUSED_APPLY, 3) == LF_ERR_INVALID
+    assert b"LF_OPT_FUSED_APPLY" in lib.lf_last_error()
+    for v in (4, 1, 0):  # column chunks per tile record, 0 = automatic
+        assert lib.lf_set_option(nat.LF_OPT_FUSED_SPLIT, v) == 0
+    assert lib.lf_set_option(nat.LF_OPT_FUSED_SPLIT, 17) == LF_ERR_INVALID
+    assert lib.lf_set_option(nat.LF_OPT_FUSED_SPLIT, -1) == LF_ERR_INVALID
 
 
 def test_argument_validation_happens_before_any_device_work(lib):
