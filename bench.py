@@ -479,6 +479,8 @@ def run_serve(args):
             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch (y's writes stay in L2)",
             "ncu_duration_us": NCU_DURATION_LORA_OP_R16,
             "ncu_frac": r16["algorithmic_bytes"] / (NCU_DURATION_LORA_OP_R16 * 1e-6) / 1e9 / op.get("peak_gbs"),
+            # the same call timed inside the op, right after the base GEMM (Y = X W + delta)
+            "in_op_us": r16["delta_us"], "in_op_frac": r16["delta_frac_of_hbm"],
             "note": "in the serving step the shrink and the expand run inside the q/k/v and attention-output "
                     "projection GEMMs (lf_linear_lora_shrink): no separate launch exists to time, and their "
                     "in-step cost is lora_overhead",
