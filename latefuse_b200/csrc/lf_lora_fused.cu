@@ -9,29 +9,29 @@
 // every module's hidden columns).  One persistent CTA per SM runs items one after
 // another with four roles around two rings of shared-memory stages:
 //   warp 0      x producer: for each item, the x K-blocks with the A boxes of the
-//               round's segments, by TMA, through a ring of x stages;
-//   warp 14     B producer: for each 128-column step of y the matching B boxes, through
-//               a separate, deeper ring of small stages (freed by the epilogue group
-//               that drains the step), from the start of the
-//               item: the B factors (scattered 2 KB boxes of the slot cache, whose
-//               latency set the pace when they shared the x ring) are in shared
-//               memory by the time the shrink is done;
+//               round's segments, by TMA, through a ring of at least 4 x stages;
+//   warp 14     B producer: for each 128-column step of y the matching B boxes,
+//               through a separate, deeper ring of small stages (freed by the
+//               epilogue group that drains the step), from the start of the item:
+//               the B factors (scattered 2 KB boxes of the slot cache, whose latency
+//               set the pace when they shared the x ring) are in shared memory by the
+//               time the shrink is done;
 //   warp 1      MMA issuer: u = x A into a TMEM accumulator (one MMA per K step,
 //               N = segments x modules x rank), then for each 128-column step of y
 //               the delta u B (K = rank, N = 128: two 64-column boxes per MMA, which
 //               halves this thread's waits, MMAs and commits, whose latency set the
 //               pace at one box per step) into one of up to three TMEM accumulators;
-//               a stage is free as soon as its MMAs complete;
-//   warps 2..   epilogue, three groups of four warps (a warp per TMEM lane quadrant,
+//               an x stage is free as soon as its MMAs complete;
+//   warps 2..13 epilogue, three groups of four warps (a warp per TMEM lane quadrant,
 //               a thread per tile row).  The groups round u and write each (segment,
 //               module) block into shared memory as the delta MMA's K-major operand
 //               (the product for rows of that segment, 0 for the others); then the y
-//               steps go round-robin to the groups; for each 64-column half of a step
-//               each warp rounds its 32 rows of
-//               the delta, stages them (two staging boxes per warp, so two
-//               reductions are in flight) and adds them to y in L2 with one TMA
-//               reduction (cp.reduce.async.bulk.tensor .add), which computes
-//               round(y + delta) element by element as the reference's add does.
+//               steps go round-robin to the groups: for each 64-column half of a step
+//               each warp rounds its 32 rows of the delta, stages them (in one or two
+//               staging boxes per warp; with two, two reductions are in flight) and
+//               adds them to y in L2 with one TMA reduction
+//               (cp.reduce.async.bulk.tensor .add), which computes round(y + delta)
+//               element by element as the reference's add does.
 // y never passes through the SM: x is read once per item (the items of one record
 // run side by side, so their x comes from L2 after the first), y is read and written
 // once by L2, u never leaves the SM, and there is no second launch.  Rows of a
@@ -253,7 +253,7 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
       constexpr uint32_t idesc_d = umma_idesc_f16(DT<T>::umma_fmt, kTile, 128, /*a_mn=*/0, /*b_mn=*/1);
       constexpr uint32_t idesc16 = umma_idesc_f16(DT<T>::umma_fmt, kTile, RP, /*a_mn=*/0, /*b_mn=*/1);
       const uint32_t s_zero_s = s_zero, s_zero_b = s_zero + 1024, s_zero_u = s_zero + 3072;
-      int k = 0, kb = 0, rk = 0, dk = 0;  // x ring position, B ring position, round, y box
+      int k = 0, kb = 0, rk = 0, dk = 0;  // x ring position, B ring position, round, y step
       bool stop = false, issued = false;
       auto full_wait = [&](int kk) {
         if (aborted(s_abort) || !mbar_wait(bar(FULL + kk % NS), (kk / NS) & 1)) {
@@ -359,8 +359,8 @@ lora_fused_kernel(const __grid_constant__ FusedApplyParams p) {
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..)
     // kGroups groups of four warps, one warp per TMEM lane quadrant in each; group g
-    // takes every kGroups-th y box (and every kGroups-th u block), so that several
-    // boxes are drained and reduced into y at once.
+    // takes every kGroups-th y step (and every kGroups-th u block), so that several
+    // steps are drained and reduced into y at once.
     const int eg = (warp - 2) >> 2;
     const int quad = warp & 3;  // the TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
