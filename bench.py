@@ -126,13 +126,22 @@ def measured_hbm_peak() -> tuple[float, str]:
 
 
 def measured_tensor_peak() -> tuple[float, str]:
-    """Dense bf16 TFLOP/s for a kernel timed inside the step.  The burst figure: the
-    sustained one was measured at a median SM clock of 1,305 MHz under the power
-    cap, while this step's clocks stay near their maximum (see ``clocks``)."""
+    """Dense bf16 TFLOP/s for a kernel timed inside the step: the burst figure, the
+    stricter denominator (the sustained figure comes from a GEMM loop whose clocks
+    settled lower than this step's; both clocks are recorded)."""
     pk = _peaks()
     if "bf16_tflops" in pk:
         return float(pk["bf16_tflops"]), "measured burst (MEASURED_PEAKS.json bf16_tflops)"
     return FALLBACK_BF16_TFLOPS, "fallback (burst)"
+
+
+def measured_tensor_peak_sustained() -> float | None:
+    """The sustained dense bf16 TFLOP/s (a seconds-long GEMM loop under the power cap), if measured."""
+    v = _peaks().get("bf16_tflops_sustained")
+    try:
+        return float(v) if v else None
+    except (TypeError, ValueError):
+        return None
 
 
 class ClockSampler:
@@ -399,6 +408,9 @@ def run_serve(args):
             "algorithmic_flops_per_launch": gemm_flops, "launch_ms": gemm_ms, "tokens_per_launch": T_tok,
             "peak_source": tpeak_src,
         }
+        tsus = measured_tensor_peak_sustained()
+        roofline["frac_of_sustained"] = tach / tsus if tsus else None
+        roofline["peak_sustained"] = tsus
     else:
         roofline = {"bound": "tensor", "achieved": None, "peak": None, "unit": "TFLOP/s", "frac": None,
                     "traffic": None, "kernel": "cuBLAS projections (this configuration does not use lf_linear_lora)"}
