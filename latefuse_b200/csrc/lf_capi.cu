@@ -539,7 +539,11 @@ static int fused_apply(cudaStream_t stream, int dtype, const void* x, int64_t ld
   p.n_segs = n_segs;
   p.status = status;
   const int rc = run_lora_fused(dtype, p, rank, stream);
-  return rc == LF_ERR_UNSUPPORTED ? -1 : rc;
+  if (rc == LF_ERR_UNSUPPORTED) {  // no size fits: the two launches run, and the call does not fail
+    g_err[0] = '\0';
+    return -1;
+  }
+  return rc;
 }
 
 // lf_lora_apply as a shrink launch into `workspace` and an expand launch that reads it.
